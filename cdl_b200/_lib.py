@@ -1,0 +1,128 @@
+"""ctypes binding of ``libcdlb200.so`` (the C ABI in ``include/cdlb200.h``).
+
+The library is loaded from the package directory.  There is no fallback: if
+the shared library is missing or the tensors are not on a CUDA device, calls
+raise instead of computing anything on the CPU.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libcdlb200.so")
+
+OK = 0
+ERR_INVALID_ARG = -1
+ERR_ALIGNMENT = -2
+ERR_UNSUPPORTED = -3
+ERR_LAUNCH = -4
+ERR_TIMEOUT = -5
+ERR_WORKSPACE = -6
+ERR_CUDA = -7
+
+SCALE_LINEAR = 0
+SCALE_SWIZZLED = 1
+
+_lib = None
+_lock = threading.Lock()
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I = ctypes.c_int
+_SZ = ctypes.c_size_t
+
+# name -> (restype, argtypes); every symbol declared in include/cdlb200.h
+SIGNATURES: dict[str, tuple] = {
+    "cdlb200_status_string": (ctypes.c_char_p, [_I]),
+    "cdlb200_version": (_I, []),
+    "cdlb200_nvfp4_quant_workspace_bytes": (_SZ, [_I64, _I64]),
+    "cdlb200_nvfp4_quant": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P, _P, _P, _SZ, _P]),
+    "cdlb200_mxfp4_quant": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P]),
+    "cdlb200_mxfp8_quant": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P]),
+    "cdlb200_fp4_dequant": (_I, [_P, _P, _P, _I64, _I64, _I, _I, _P, _P]),
+    "cdlb200_mxfp8_dequant": (_I, [_P, _P, _P, _I64, _I64, _P, _P]),
+    "cdlb200_swizzle_scales": (_I, [_P, _I64, _I64, _P, _P]),
+}
+
+
+class CdlB200Error(RuntimeError):
+    """A libcdlb200 call returned a non-zero status."""
+
+    def __init__(self, fn: str, status: int, msg: str):
+        super().__init__(f"{fn} failed: {msg} (status {status})")
+        self.status = status
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the shared library; raises if it is not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise ImportError(
+                    f"{LIB_PATH} is not built; run `python -m cdl_b200.build` "
+                    "(there is no CPU fallback for the cdl_b200 kernels)"
+                )
+            handle = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = handle
+    return _lib
+
+
+def call(name: str, *args) -> None:
+    status = getattr(lib(), name)(*args)
+    if status != OK:
+        msg = lib().cdlb200_status_string(status).decode()
+        if status in (ERR_INVALID_ARG, ERR_ALIGNMENT, ERR_WORKSPACE):
+            raise ValueError(f"{name}: {msg} (status {status})")
+        raise CdlB200Error(name, status, msg)
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def require_cuda(*tensors: torch.Tensor) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(
+                "cdl_b200 kernels run on CUDA tensors only (no CPU fallback); got a tensor on "
+                f"{t.device}"
+            )
+        dev = t.device if dev is None else dev
+    return dev
+
+
+_WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def nvfp4_workspace(device: torch.device) -> torch.Tensor:
+    """Per-(device, stream) scratch of the NVFP4 global amax (zeroed once).
+
+    The kernels leave it re-armed, so one buffer serves every stream-ordered
+    call.  Calls on different streams get different buffers.
+    """
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream(device))
+    ws = _WORKSPACES.get(key)
+    if ws is None:
+        nbytes = lib().cdlb200_nvfp4_quant_workspace_bytes(0, 0)
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws

@@ -1,0 +1,89 @@
+"""Block-scaled quantize: the drop-in for ``cdl.core.kernel.quant``.
+
+Same public functions, arguments, return types and errors as the reference
+(``cdl/core/kernel/quant.py:126-146``):
+
+* ``nvfp4_quant(x)`` -> ``(packed u8[rows, nb*8], scale u8[rows, nb], alpha f32[1])``
+* ``mxfp4_quant(x)`` -> ``(packed u8[rows, nb*16], scale u8[rows, nb], alpha = ones(1))``
+* ``mxfp8_quant(x)`` -> ``(packed e4m3[rows, nb*32], scale u8[rows, nb], None)``
+
+raising ``ValueError`` for a non-2-D input (quant.py:79-80).  ``block_chunk``
+was a Triton tiling knob and is accepted and ignored.  Two keyword extensions
+serve the GEMM path: ``transpose=True`` quantizes ``x.T`` along dim 0 without
+materialising the transpose (the wgrad requantize), and ``swizzled=True``
+writes the scales directly in the 128x4 tiled GEMM layout.
+
+The input must be a bf16 CUDA tensor; there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from cdl_b200 import _lib
+
+NVFP4, MXFP4, MXFP8 = 0, 1, 2
+_BLOCK = {NVFP4: 16, MXFP4: 32, MXFP8: 32}
+
+
+def scale_shape(r: int, nb: int, swizzled: bool) -> tuple[int, int]:
+    if swizzled:
+        return ((r + 127) // 128 * 128, (nb + 3) // 4 * 4)
+    return (r, nb)
+
+
+def _quant(
+    x: torch.Tensor, fmt: int, transpose: bool = False, swizzled: bool = False
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]:
+    if x.ndim != 2:
+        raise ValueError(f"expected a 2D tensor [rows, k], got shape {tuple(x.shape)}")
+    dev = _lib.require_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise TypeError(f"cdl_b200 quantize takes bfloat16 input, got {x.dtype}")
+    if x.stride(1) != 1 or x.stride(0) < x.shape[1] or x.data_ptr() % 16:
+        x = x.contiguous()
+    rows, k = x.shape
+    r, c = (k, rows) if transpose else (rows, k)
+    B = _BLOCK[fmt]
+    nb = (c + B - 1) // B
+    pstride = nb * B if fmt == MXFP8 else nb * B // 2
+    packed = torch.empty((r, pstride), dtype=torch.float8_e4m3fn if fmt == MXFP8 else torch.uint8, device=dev)
+    scale = torch.empty(scale_shape(r, nb, swizzled), dtype=torch.uint8, device=dev)
+    layout = _lib.SCALE_SWIZZLED if swizzled else _lib.SCALE_LINEAR
+    ld = max(x.stride(0), 1)
+    st = _lib.stream(dev)
+    if fmt == NVFP4:
+        alpha = torch.empty(1, dtype=torch.float32, device=dev)
+        ws = _lib.nvfp4_workspace(dev)
+        _lib.call(
+            "cdlb200_nvfp4_quant", _lib.ptr(x), rows, k, ld, int(transpose), _lib.ptr(packed),
+            _lib.ptr(scale), layout, None, _lib.ptr(alpha), _lib.ptr(ws), ws.numel(), st,
+        )
+        return packed, scale, alpha
+    name = "cdlb200_mxfp4_quant" if fmt == MXFP4 else "cdlb200_mxfp8_quant"
+    _lib.call(name, _lib.ptr(x), rows, k, ld, int(transpose), _lib.ptr(packed), _lib.ptr(scale), layout, st)
+    alpha = torch.ones(1, dtype=torch.float32, device=dev) if fmt == MXFP4 else None
+    return packed, scale, alpha
+
+
+def nvfp4_quant(
+    x: torch.Tensor, block_chunk: int = 32, *, transpose: bool = False, swizzled: bool = False
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    packed, scale, alpha = _quant(x, NVFP4, transpose, swizzled)
+    assert alpha is not None
+    return packed, scale, alpha
+
+
+def mxfp4_quant(
+    x: torch.Tensor, block_chunk: int = 32, *, transpose: bool = False, swizzled: bool = False
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    packed, scale, alpha = _quant(x, MXFP4, transpose, swizzled)
+    assert alpha is not None
+    return packed, scale, alpha
+
+
+def mxfp8_quant(
+    x: torch.Tensor, block_chunk: int = 32, *, transpose: bool = False, swizzled: bool = False
+) -> tuple[torch.Tensor, torch.Tensor, None]:
+    packed, scale, _ = _quant(x, MXFP8, transpose, swizzled)
+    return packed, scale, None

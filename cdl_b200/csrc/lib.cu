@@ -1,0 +1,35 @@
+// lib.cu -- library-wide helpers of libcdlb200: status strings, version,
+// per-device SM count cache.
+#include "common.cuh"
+
+namespace cdlb200 {
+
+int num_sms() {
+    static int cache[128] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 148;
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+}  // namespace cdlb200
+
+extern "C" const char* cdlb200_status_string(int status) {
+    switch (status) {
+        case CDLB200_OK: return "ok";
+        case CDLB200_ERR_INVALID_ARG: return "invalid argument";
+        case CDLB200_ERR_ALIGNMENT: return "misaligned pointer or leading dimension";
+        case CDLB200_ERR_UNSUPPORTED: return "unsupported device (needs sm_100)";
+        case CDLB200_ERR_LAUNCH: return "CUDA kernel launch failed";
+        case CDLB200_ERR_TIMEOUT: return "bounded device-side wait timed out";
+        case CDLB200_ERR_WORKSPACE: return "workspace missing or too small";
+        case CDLB200_ERR_CUDA: return "CUDA runtime error";
+        default: return "unknown status";
+    }
+}
+
+extern "C" int cdlb200_version(void) { return 100; }

@@ -1,0 +1,459 @@
+// quant.cu -- block-scaled NVFP4 / MXFP4 / MXFP8 quantize kernels (sm_100a).
+//
+// Replaces cdl's Triton `_quant_kernel` + host `_quant`
+// (cdl/core/kernel/quant.py:13-146) and the torch global amax it launches
+// (quant.py:96-101).  Results are bit-identical to cdl's torch nearest-round
+// path (cdl/core/ecdl.py:46-131 with fp32 format tables).
+//
+// Layout in HBM.  A row-major bf16 [rows, k] matrix with k % block == 0 is one
+// flat array of blocks; so are its packed codes (k/2 or k bytes per row) and
+// its linear scales (one byte per block).  The fast path therefore streams
+// 16-byte vectors: one vector = 8 elements, a block = 2 (NVFP4) or 4 (MX)
+// adjacent lanes of a warp, reduced with one or two shuffles.  Every global
+// load and store of a warp covers one contiguous span (512 B in, 128 B or
+// 256 B out).
+//
+// E2M1 encoding without a per-element divide.  cdl computes v = RN(x / s) and
+// counts the e2m1 midpoints mid_j in {.25,.75,1.25,1.75,2.5,3.5,5} that
+// |v| exceeds (strict '>', so ties round toward zero; cdl/core/format/
+// fp4.py:15-17).  All mid_j have an even last mantissa bit, so
+//     RN(|x|/s) > mid_j  <=>  |x|/s > mid_j + ulp(mid_j)/2  =: U_j
+//                        <=>  |x| > RD(U_j * s)               (|x| is an fp32)
+// and RD(U_j * s) = fma_rd(mid_j, s, s * ulp(mid_j)/2) is exact whenever
+// s * ulp(mid_j)/2 does not underflow (s >= 2^-100).  Each block therefore
+// computes seven thresholds once and each element does seven compares.  For
+// power-of-two MX scales the threshold is exactly mid_j * s.  Blocks whose
+// NVFP4 scale is tiny or non-finite fall back to the literal IEEE divide.
+#include "common.cuh"
+
+namespace cdlb200 {
+
+namespace {
+
+// e2m1 midpoints mid_j and ulp(mid_j) / 2 = 2^(floor(log2(mid_j)) - 24)
+__device__ __forceinline__ constexpr float mid_j(int j) {
+    return j == 0 ? 0.25f : j == 1 ? 0.75f : j == 2 ? 1.25f : j == 3 ? 1.75f : j == 4 ? 2.5f : j == 5 ? 3.5f : 5.0f;
+}
+__device__ __forceinline__ constexpr float half_ulp_j(int j) {
+    return j == 0 ? 0x1p-26f : j == 1 ? 0x1p-25f : j <= 3 ? 0x1p-24f : j <= 5 ? 0x1p-23f : 0x1p-22f;
+}
+constexpr int kWsCounterOff = 0;
+constexpr int kWsPartialOff = 256;
+constexpr int kMaxAmaxGrid = 1024;
+
+struct BlockCode {
+    float t[7];      // e2m1 thresholds on |x| (FP4) ; t[0] = 1/scale (FP8)
+    float s;         // block scale (NVFP4 fallback divide)
+    bool exact_div;  // NVFP4 fallback: divide literally
+    uint32_t byte;   // stored scale byte
+};
+
+// max |x| of 8 bf16 values as bf16 magnitude bits (NaN sorts above Inf).
+__device__ __forceinline__ uint32_t amax8(const uint4& w) {
+    const uint32_t M = 0x7fff7fffu;
+    uint32_t a, b, c;
+    asm("max.u16x2 %0, %1, %2;" : "=r"(a) : "r"(w.x & M), "r"(w.y & M));
+    asm("max.u16x2 %0, %1, %2;" : "=r"(b) : "r"(w.z & M), "r"(w.w & M));
+    asm("max.u16x2 %0, %1, %2;" : "=r"(c) : "r"(a), "r"(b));
+    return max(c & 0xffffu, c >> 16);
+}
+
+__device__ __forceinline__ float mag_to_f32(uint32_t mag) { return u2f(mag << 16); }
+
+template <int FMT>
+__device__ __forceinline__ void block_setup(uint32_t mag, float gmax, float alpha, BlockCode& bc) {
+    if constexpr (FMT == kNVFP4) {
+        // cdl/core/ecdl.py:55  q = bamax * 448 / gmax (two roundings, as cdl)
+        float bamax = mag > 0x7f80u ? u2f(0x7fc00000u) : mag_to_f32(mag);
+        float q = __fdiv_rn(__fmul_rn(bamax, 448.0f), gmax);
+        bc.byte = ue4m3_scale_byte(q);
+        float s = __fmul_rn(e4m3_to_f32(bc.byte), alpha);  // ecdl.py:129
+        bc.s = s;
+        bc.exact_div = !(s >= 0x1p-100f && s <= 3.4028234e38f);
+#pragma unroll
+        for (int j = 0; j < 7; ++j) bc.t[j] = __fmaf_rd(mid_j(j), s, __fmul_rn(s, half_ulp_j(j)));
+    } else {
+        bc.byte = e8m0_byte_from_bf16_mag<FmtTraits<FMT>::kEmax>(mag);
+        bc.exact_div = false;
+        if constexpr (FMT == kMXFP4) {
+            float s = e8m0_to_f32(bc.byte);
+            bc.s = s;
+#pragma unroll
+            for (int j = 0; j < 7; ++j) bc.t[j] = __fmul_rn(mid_j(j), s);
+        } else {
+            bc.s = e8m0_inv(bc.byte);  // RN(x / 2^e) == x * 2^-e exactly
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t e2m1_mag_thresh(float a, const float* t) {
+    uint32_t m = 0;
+#pragma unroll
+    for (int j = 0; j < 7; ++j) m += (a > t[j]) ? 1u : 0u;
+    return m;
+}
+
+// nibble of one bf16 element (given as its 16 bits in the low half of h)
+__device__ __forceinline__ uint32_t e2m1_nibble(uint32_t h, const BlockCode& bc) {
+    if (!bc.exact_div) {
+        uint32_t m = e2m1_mag_thresh(u2f((h & 0x7fffu) << 16), bc.t);
+        return m | ((h >> 12) & 8u);
+    }
+    float v = __fdiv_rn(u2f(h << 16), bc.s);
+    float a = fabsf(v);
+    uint32_t m = 0;
+#pragma unroll
+    for (int j = 0; j < 7; ++j) m += (a > mid_j(j)) ? 1u : 0u;
+    return m | (signbit(v) ? 8u : 0u);
+}
+
+// 8 elements -> 8 nibbles (element e at bits 4e..4e+3)
+__device__ __forceinline__ uint32_t encode8_fp4(const uint4& w, const BlockCode& bc) {
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    uint32_t out = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        uint32_t lo = e2m1_nibble(ws[i] & 0xffffu, bc);
+        uint32_t hi = e2m1_nibble(ws[i] >> 16, bc);
+        out |= (lo | (hi << 4)) << (8 * i);
+    }
+    return out;
+}
+
+// 8 elements -> 8 e4m3 bytes
+__device__ __forceinline__ uint2 encode8_fp8(const uint4& w, const BlockCode& bc) {
+    const float inv = bc.s;
+    uint32_t b01 = cvt_e4m3x2(__fmul_rn(bf16hi(w.x), inv), __fmul_rn(bf16lo(w.x), inv));
+    uint32_t b23 = cvt_e4m3x2(__fmul_rn(bf16hi(w.y), inv), __fmul_rn(bf16lo(w.y), inv));
+    uint32_t b45 = cvt_e4m3x2(__fmul_rn(bf16hi(w.z), inv), __fmul_rn(bf16lo(w.z), inv));
+    uint32_t b67 = cvt_e4m3x2(__fmul_rn(bf16hi(w.w), inv), __fmul_rn(bf16lo(w.w), inv));
+    return make_uint2(b01 | (b23 << 16), b45 | (b67 << 16));
+}
+
+// ---------------------------------------------------------------------------
+// global amax (NVFP4): per-CTA partial maxima, the last CTA to finish reduces
+// them and writes gmax / alpha, then re-arms the counter for the next call.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(512) amax_kernel(const uint16_t* __restrict__ x, int64_t rows,
+                                                   int64_t k, int64_t ldx, int vec_ok,
+                                                   uint32_t* __restrict__ partial,
+                                                   uint32_t* __restrict__ counter,
+                                                   float* __restrict__ gmax_out,
+                                                   float* __restrict__ alpha_out) {
+    uint32_t m = 0;
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t nthr = (int64_t)gridDim.x * blockDim.x;
+    if (vec_ok) {  // contiguous, 16-byte aligned: flat vector loop + scalar tail
+        const int64_t n = rows * k;
+        const int64_t nvec = n >> 3;
+        const uint4* xv = reinterpret_cast<const uint4*>(x);
+        int64_t v = tid;
+        for (; v + 3 * nthr < nvec; v += 4 * nthr) {
+            uint4 a = ldg_stream(xv + v), b = ldg_stream(xv + v + nthr);
+            uint4 c = ldg_stream(xv + v + 2 * nthr), d = ldg_stream(xv + v + 3 * nthr);
+            m = max(m, max(max(amax8(a), amax8(b)), max(amax8(c), amax8(d))));
+        }
+        for (; v < nvec; v += nthr) m = max(m, amax8(ldg_stream(xv + v)));
+        for (int64_t i = (nvec << 3) + tid; i < n; i += nthr) m = max(m, (uint32_t)(x[i] & 0x7fffu));
+    } else {
+        for (int64_t r = blockIdx.x; r < rows; r += gridDim.x)
+            for (int64_t c = threadIdx.x; c < k; c += blockDim.x)
+                m = max(m, (uint32_t)(x[r * ldx + c] & 0x7fffu));
+    }
+    m = __reduce_max_sync(0xffffffffu, m);
+    __shared__ uint32_t warp_max[16];
+    __shared__ bool is_last;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) warp_max[warp] = m;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t wm = lane < (int)(blockDim.x >> 5) ? warp_max[lane] : 0u;
+        wm = __reduce_max_sync(0xffffffffu, wm);
+        if (lane == 0) {
+            partial[blockIdx.x] = wm;
+            __threadfence();
+            uint32_t prev = atomicAdd(counter, 1u);
+            is_last = prev == gridDim.x - 1;
+        }
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    uint32_t g = 0;
+    for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) g = max(g, __ldcg(partial + i));
+    g = __reduce_max_sync(0xffffffffu, g);
+    if (lane == 0) warp_max[warp] = g;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t gm = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) gm = max(gm, warp_max[w]);
+        float gmax;
+        if (gm > 0x7f80u) gmax = u2f(0x7fc00000u);
+        else gmax = fmaxf(mag_to_f32(gm), 1.1754943508222875e-38f);  // clamp_min(tiny)
+        if (gmax_out) *gmax_out = gmax;
+        *alpha_out = __fdiv_rn(gmax, 2688.0f);  // gmax / (6 * 448)
+        *counter = 0u;
+    }
+}
+
+// gmax for an empty tensor (quant.py:99-101): tiny, alpha = tiny / 2688
+__global__ void empty_alpha_kernel(float* gmax_out, float* alpha_out) {
+    const float tiny = 1.1754943508222875e-38f;
+    if (gmax_out) *gmax_out = tiny;
+    *alpha_out = __fdiv_rn(tiny, 2688.0f);
+}
+
+// ---------------------------------------------------------------------------
+// fast path: contiguous rows, k % block == 0, 16-byte aligned input
+// ---------------------------------------------------------------------------
+template <int FMT, bool SWZ, int U>
+__global__ void __launch_bounds__(256) quant_flat_kernel(const uint4* __restrict__ x, int64_t nvec,
+                                                         uint8_t* __restrict__ packed,
+                                                         uint8_t* __restrict__ scale, int64_t nb,
+                                                         int64_t c4, const float* __restrict__ gmax_p,
+                                                         const float* __restrict__ alpha_p) {
+    constexpr int B = FmtTraits<FMT>::kBlock;
+    constexpr int VPB = B / 8;
+    float gmax = 0.f, alpha = 0.f;
+    if constexpr (FMT == kNVFP4) {
+        gmax = *gmax_p;
+        alpha = *alpha_p;
+    }
+    const int lane = threadIdx.x & 31;
+    const int64_t warp_base = (int64_t)blockIdx.x * blockDim.x * U + (threadIdx.x & ~31) * U;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x * U;
+    for (int64_t base = warp_base; base < nvec; base += stride) {
+        uint4 w[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            int64_t v = base + 32 * u + lane;
+            w[u] = v < nvec ? ldg_stream(x + v) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t v = base + 32 * u + lane;
+            uint32_t mag = amax8(w[u]);
+            mag = max(mag, __shfl_xor_sync(0xffffffffu, mag, 1));
+            if constexpr (VPB == 4) mag = max(mag, __shfl_xor_sync(0xffffffffu, mag, 2));
+            if (v < nvec) {
+                BlockCode bc;
+                block_setup<FMT>(mag, gmax, alpha, bc);
+                if constexpr (FmtTraits<FMT>::kFp4) {
+                    reinterpret_cast<uint32_t*>(packed)[v] = encode8_fp4(w[u], bc);
+                } else {
+                    reinterpret_cast<uint2*>(packed)[v] = encode8_fp8(w[u], bc);
+                }
+                if ((lane & (VPB - 1)) == 0) {
+                    const int64_t blk = v / VPB;
+                    int64_t off = blk;
+                    if constexpr (SWZ) off = swizzle_offset(blk / nb, blk % nb, c4);
+                    scale[off] = (uint8_t)bc.byte;
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// general path: any leading dimension, ragged k, transposed (dim-0) blocks.
+// One thread per (output row r, block b); element (r, c) is x[r*sr + c*sc].
+// Threads are ordered r-fastest so a transposed input is read coalesced.
+// ---------------------------------------------------------------------------
+template <int FMT, bool SWZ>
+__global__ void __launch_bounds__(256) quant_strided_kernel(const uint16_t* __restrict__ x, int64_t R,
+                                                            int64_t C, int64_t sr, int64_t sc,
+                                                            uint8_t* __restrict__ packed,
+                                                            int64_t pstride,
+                                                            uint8_t* __restrict__ scale, int64_t nb,
+                                                            int64_t c4,
+                                                            const float* __restrict__ gmax_p,
+                                                            const float* __restrict__ alpha_p) {
+    constexpr int B = FmtTraits<FMT>::kBlock;
+    float gmax = 0.f, alpha = 0.f;
+    if constexpr (FMT == kNVFP4) {
+        gmax = *gmax_p;
+        alpha = *alpha_p;
+    }
+    const int64_t total = R * nb;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = idx % R, b = idx / R;
+        uint32_t h[B];
+        uint32_t mag = 0;
+#pragma unroll
+        for (int i = 0; i < B; ++i) {
+            const int64_t c = b * B + i;
+            h[i] = c < C ? (uint32_t)x[r * sr + c * sc] : 0u;
+            mag = max(mag, h[i] & 0x7fffu);
+        }
+        BlockCode bc;
+        block_setup<FMT>(mag, gmax, alpha, bc);
+        uint8_t* prow = packed + r * pstride;
+        if constexpr (FmtTraits<FMT>::kFp4) {
+#pragma unroll
+            for (int i = 0; i < B; i += 2)
+                prow[(b * B + i) / 2] = (uint8_t)(e2m1_nibble(h[i], bc) | (e2m1_nibble(h[i + 1], bc) << 4));
+        } else {
+#pragma unroll
+            for (int i = 0; i < B; i += 2) {
+                uint32_t p = cvt_e4m3x2(__fmul_rn(u2f(h[i + 1] << 16), bc.s), __fmul_rn(u2f(h[i] << 16), bc.s));
+                prow[b * B + i] = (uint8_t)(p & 0xffu);
+                prow[b * B + i + 1] = (uint8_t)(p >> 8);
+            }
+        }
+        const int64_t off = SWZ ? swizzle_offset(r, b, c4) : r * nb + b;
+        scale[off] = (uint8_t)bc.byte;
+    }
+}
+
+bool aligned(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) & (uintptr_t)(a - 1)) == 0; }
+
+int device_ok() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return CDLB200_ERR_CUDA;
+    static int cc_major[128] = {0};
+    if (dev < 0 || dev >= 128) return CDLB200_ERR_CUDA;
+    if (cc_major[dev] == 0) {
+        int major = 0;
+        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+            return CDLB200_ERR_CUDA;
+        cc_major[dev] = major;
+    }
+    return cc_major[dev] == 10 ? CDLB200_OK : CDLB200_ERR_UNSUPPORTED;
+}
+
+template <int FMT, bool SWZ>
+int launch_encode(const void* x, int64_t rows, int64_t k, int64_t ldx, int transpose, void* packed,
+                  void* scale, const float* gmax, const float* alpha, cudaStream_t st) {
+    constexpr int B = FmtTraits<FMT>::kBlock;
+    const int64_t R = transpose ? k : rows, C = transpose ? rows : k;
+    const int64_t nb = (C + B - 1) / B;
+    const int64_t c4 = (nb + 3) / 4;
+    const int64_t pstride = FmtTraits<FMT>::kFp4 ? nb * B / 2 : nb * B;
+    const int sms = num_sms();
+    const bool flat = !transpose && ldx == k && (k % B) == 0 && aligned(x, 16) &&
+                      aligned(packed, FmtTraits<FMT>::kFp4 ? 4 : 8);
+    if (flat) {
+        constexpr int U = 4;
+        const int64_t nvec = rows * k / 8;
+        int64_t grid = (nvec + 256 * U - 1) / (256 * U);
+        grid = grid < (int64_t)sms * 8 ? grid : (int64_t)sms * 8;
+        quant_flat_kernel<FMT, SWZ, U><<<(unsigned)grid, 256, 0, st>>>(
+            reinterpret_cast<const uint4*>(x), nvec, static_cast<uint8_t*>(packed),
+            static_cast<uint8_t*>(scale), nb, c4, gmax, alpha);
+    } else {
+        const int64_t sr = transpose ? 1 : ldx, sc = transpose ? ldx : 1;
+        int64_t grid = (R * nb + 255) / 256;
+        grid = grid < (int64_t)sms * 16 ? grid : (int64_t)sms * 16;
+        quant_strided_kernel<FMT, SWZ><<<(unsigned)grid, 256, 0, st>>>(
+            static_cast<const uint16_t*>(x), R, C, sr, sc, static_cast<uint8_t*>(packed), pstride,
+            static_cast<uint8_t*>(scale), nb, c4, gmax, alpha);
+    }
+    CDLB200_CHECK_LAUNCH();
+    return CDLB200_OK;
+}
+
+template <int FMT>
+int quant_entry(const void* x, int64_t rows, int64_t k, int64_t ldx, int transpose, void* packed,
+                void* scale, int scale_layout, const float* gmax, const float* alpha, cudaStream_t st) {
+    constexpr int B = FmtTraits<FMT>::kBlock;
+    if (scale_layout == CDLB200_SCALE_SWIZZLED) {
+        const int64_t R = transpose ? k : rows, C = transpose ? rows : k;
+        const int64_t nb = (C + B - 1) / B;
+        if ((R % 128) != 0 || (nb % 4) != 0) {
+            const size_t bytes = (size_t)((R + 127) / 128 * 128) * (size_t)((nb + 3) / 4 * 4);
+            if (cudaMemsetAsync(scale, 0, bytes, st) != cudaSuccess) return CDLB200_ERR_CUDA;
+        }
+        return launch_encode<FMT, true>(x, rows, k, ldx, transpose, packed, scale, gmax, alpha, st);
+    }
+    return launch_encode<FMT, false>(x, rows, k, ldx, transpose, packed, scale, gmax, alpha, st);
+}
+
+int check_args(const void* x, int64_t rows, int64_t k, int64_t ldx, int transpose, const void* packed,
+               const void* scale, int scale_layout) {
+    if (rows < 0 || k < 0) return CDLB200_ERR_INVALID_ARG;
+    if (transpose != 0 && transpose != 1) return CDLB200_ERR_INVALID_ARG;
+    if (scale_layout != CDLB200_SCALE_LINEAR && scale_layout != CDLB200_SCALE_SWIZZLED)
+        return CDLB200_ERR_INVALID_ARG;
+    if (rows == 0 || k == 0) return CDLB200_OK;
+    if (!x || !packed || !scale) return CDLB200_ERR_INVALID_ARG;
+    if (ldx < k) return CDLB200_ERR_INVALID_ARG;
+    if (!aligned(x, 2)) return CDLB200_ERR_ALIGNMENT;
+    return CDLB200_OK;
+}
+
+}  // namespace
+
+// Launches the global amax reduction; shared with the no-workspace variants.
+int launch_amax(const void* x, int64_t rows, int64_t k, int64_t ldx, uint32_t* partial,
+                uint32_t* counter, float* gmax, float* alpha, cudaStream_t st) {
+    if (rows == 0 || k == 0) {
+        empty_alpha_kernel<<<1, 1, 0, st>>>(gmax, alpha);
+        CDLB200_CHECK_LAUNCH();
+        return CDLB200_OK;
+    }
+    const int sms = num_sms();
+    const int vec_ok = ldx == k && aligned(x, 16);
+    int64_t want = vec_ok ? (rows * k / 8 + 512 * 4 - 1) / (512 * 4) : rows;
+    int64_t cap = (int64_t)sms * 2 < kMaxAmaxGrid ? (int64_t)sms * 2 : kMaxAmaxGrid;
+    int grid = (int)(want < 1 ? 1 : (want < cap ? want : cap));
+    amax_kernel<<<grid, 512, 0, st>>>(static_cast<const uint16_t*>(x), rows, k, ldx, vec_ok, partial,
+                                      counter, gmax, alpha);
+    CDLB200_CHECK_LAUNCH();
+    return CDLB200_OK;
+}
+
+int launch_nvfp4_encode(const void* x, int64_t rows, int64_t k, int64_t ldx, int transpose,
+                        void* packed, void* scale, int scale_layout, const float* gmax,
+                        const float* alpha, cudaStream_t st) {
+    return quant_entry<kNVFP4>(x, rows, k, ldx, transpose, packed, scale, scale_layout, gmax, alpha,
+                               st);
+}
+
+}  // namespace cdlb200
+
+using namespace cdlb200;
+
+extern "C" size_t cdlb200_nvfp4_quant_workspace_bytes(int64_t, int64_t) {
+    return (size_t)kWsPartialOff + sizeof(uint32_t) * kMaxAmaxGrid + sizeof(float);
+}
+
+extern "C" int cdlb200_nvfp4_quant(const void* x, int64_t rows, int64_t k, int64_t ldx, int transpose,
+                                   void* packed, void* scale, int scale_layout, float* gmax,
+                                   float* alpha, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+    int rc = check_args(x, rows, k, ldx, transpose, packed, scale, scale_layout);
+    if (rc != CDLB200_OK) return rc;
+    if (!alpha) return CDLB200_ERR_INVALID_ARG;
+    if (!workspace || workspace_bytes < cdlb200_nvfp4_quant_workspace_bytes(rows, k))
+        return CDLB200_ERR_WORKSPACE;
+    if (!aligned(workspace, 256)) return CDLB200_ERR_ALIGNMENT;
+    if ((rc = device_ok()) != CDLB200_OK) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    uint32_t* counter = reinterpret_cast<uint32_t*>(ws + kWsCounterOff);
+    uint32_t* partial = reinterpret_cast<uint32_t*>(ws + kWsPartialOff);
+    // gmax goes to the caller's buffer if given, else to the workspace tail
+    float* g = gmax ? gmax : reinterpret_cast<float*>(ws + kWsPartialOff + sizeof(uint32_t) * kMaxAmaxGrid);
+    rc = launch_amax(x, rows, k, ldx, partial, counter, g, alpha, st);
+    if (rc != CDLB200_OK || rows == 0 || k == 0) return rc;
+    return launch_nvfp4_encode(x, rows, k, ldx, transpose, packed, scale, scale_layout, g, alpha, st);
+}
+
+extern "C" int cdlb200_mxfp4_quant(const void* x, int64_t rows, int64_t k, int64_t ldx, int transpose,
+                                   void* packed, void* scale, int scale_layout, void* stream) {
+    int rc = check_args(x, rows, k, ldx, transpose, packed, scale, scale_layout);
+    if (rc != CDLB200_OK || rows == 0 || k == 0) return rc;
+    if ((rc = device_ok()) != CDLB200_OK) return rc;
+    return quant_entry<kMXFP4>(x, rows, k, ldx, transpose, packed, scale, scale_layout, nullptr,
+                               nullptr, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cdlb200_mxfp8_quant(const void* x, int64_t rows, int64_t k, int64_t ldx, int transpose,
+                                   void* packed, void* scale, int scale_layout, void* stream) {
+    int rc = check_args(x, rows, k, ldx, transpose, packed, scale, scale_layout);
+    if (rc != CDLB200_OK || rows == 0 || k == 0) return rc;
+    if ((rc = device_ok()) != CDLB200_OK) return rc;
+    return quant_entry<kMXFP8>(x, rows, k, ldx, transpose, packed, scale, scale_layout, nullptr,
+                               nullptr, static_cast<cudaStream_t>(stream));
+}

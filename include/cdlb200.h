@@ -1,0 +1,123 @@
+/*
+ * cdlb200.h -- C ABI of the B200-native (sm_100a) cdl low-precision hot path.
+ *
+ * Every entry point takes device pointers owned by the caller, sizes in
+ * elements, and a CUDA stream (as `void*`, a cudaStream_t; NULL = legacy
+ * default stream).  Calls are asynchronous: they enqueue kernels on `stream`,
+ * never synchronize the host and never allocate device memory (scratch space
+ * is passed in as `workspace`).  They return CDLB200_OK (0) or a negative
+ * CDLB200_ERR_* code; argument errors are detected on the host before any
+ * launch.
+ *
+ * Formats follow cdl (FelysNeko/cdl):
+ *   NVFP4 : e2m1 elements, blocks of 16 along the last dim, e4m3 (UE4M3, zero
+ *           excluded) block scales, per-tensor fp32 alpha = amax / (6 * 448).
+ *   MXFP4 : e2m1 elements, blocks of 32, e8m0 scales (alpha = 1).
+ *   MXFP8 : e4m3 elements, blocks of 32, e8m0 scales (no alpha).
+ * Packed FP4 stores element 2j in the low nibble of byte j.  Block scales are
+ * written either linear row-major [rows, nb] (what cdl's quantizers return) or
+ * in the 128x4-tiled layout consumed by the block-scaled GEMM (cdl's
+ * swizzle_scale_factors, zero-padded to [ceil(rows/128)*128, ceil(nb/4)*4]).
+ * A K that is not a multiple of the block is zero-padded to whole blocks, so
+ * packed rows hold nb*B/2 (FP4) or nb*B (FP8) bytes, as in cdl.
+ *
+ * Numerics: codes and scales are bit-identical to cdl's torch nearest-round
+ * path with fp32 format tables for finite inputs.  NaN/Inf are outside that
+ * contract (cdl itself gives platform-dependent results for them), except
+ * +-Inf in the MX formats, which follows cdl's torch path.
+ */
+#ifndef CDLB200_H_
+#define CDLB200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CDLB200_OK 0
+#define CDLB200_ERR_INVALID_ARG (-1)  /* bad shape, null pointer, bad flag */
+#define CDLB200_ERR_ALIGNMENT (-2)    /* pointer / leading dimension alignment */
+#define CDLB200_ERR_UNSUPPORTED (-3)  /* device is not sm_100 */
+#define CDLB200_ERR_LAUNCH (-4)       /* CUDA launch error (cudaGetLastError) */
+#define CDLB200_ERR_TIMEOUT (-5)      /* a bounded device-side wait gave up */
+#define CDLB200_ERR_WORKSPACE (-6)    /* workspace too small */
+#define CDLB200_ERR_CUDA (-7)         /* other CUDA runtime error */
+
+/* scale_layout values */
+#define CDLB200_SCALE_LINEAR 0    /* [rows, nb] row-major */
+#define CDLB200_SCALE_SWIZZLED 1  /* 128x4 tiles, zero-padded */
+
+/* Human-readable name of a status code. */
+const char* cdlb200_status_string(int status);
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int cdlb200_version(void);
+
+/*
+ * NVFP4 quantize of a bf16 matrix.
+ * Replaces cdl/core/kernel/quant.py:126-131 `nvfp4_quant` (its `_quant` host
+ * code at quant.py:71-123 with group 16, e4m3 scales, and the torch global
+ * amax at quant.py:96-101) and the Triton `_quant_kernel` (quant.py:13-68).
+ *
+ *   x        bf16 [rows, k], row stride `ldx` elements (ldx >= k)
+ *   transpose 0: quantize x along its last dim (blocks of 16 along k);
+ *            1: quantize x^T, i.e. blocks of 16 along `rows`; outputs are then
+ *               laid out for the [k, rows] matrix (the wgrad requantize).
+ *   packed   uint8 [R, nb*8]   (R, C = rows, k or k, rows; nb = ceil(C/16))
+ *   scale    uint8 [R, nb] or swizzled (scale_layout)
+ *   gmax     optional fp32 [1] output: max|x| clamped to FLT_MIN (may be NULL)
+ *   alpha    fp32 [1] output: gmax / 2688
+ *   workspace device scratch of cdlb200_nvfp4_quant_workspace_bytes() bytes,
+ *            zero-filled before its first use; the call leaves it re-usable
+ *            (calls sharing one workspace must be stream-ordered).
+ */
+size_t cdlb200_nvfp4_quant_workspace_bytes(int64_t rows, int64_t k);
+int cdlb200_nvfp4_quant(const void* x, int64_t rows, int64_t k, int64_t ldx, int transpose,
+                        void* packed, void* scale, int scale_layout, float* gmax, float* alpha,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * MXFP4 / MXFP8 quantize of a bf16 matrix (blocks of 32, e8m0 scales).
+ * Replaces cdl/core/kernel/quant.py:134-139 `mxfp4_quant` and :142-146
+ * `mxfp8_quant` (their `_quant_kernel` e8m0 branch, quant.py:39-46, 56-68).
+ * MXFP4 packed: uint8 [R, nb*16]; MXFP8 packed: e4m3 bytes [R, nb*32].
+ * cdl's MXFP4 alpha (a constant 1.0) and MXFP8 alpha (None) are host-side.
+ */
+int cdlb200_mxfp4_quant(const void* x, int64_t rows, int64_t k, int64_t ldx, int transpose,
+                        void* packed, void* scale, int scale_layout, void* stream);
+int cdlb200_mxfp8_quant(const void* x, int64_t rows, int64_t k, int64_t ldx, int transpose,
+                        void* packed, void* scale, int scale_layout, void* stream);
+
+/*
+ * FP4 dequantize: out[r, c] = bf16((e2m1 * scale) * alpha).
+ * Replaces cdl/core/kernel/dequant.py:103-109 `nvfp4_dequant` (block 16, e4m3
+ * scale) and :112-118 `mxfp4_dequant` (block 32, e8m0 scale), i.e. the Triton
+ * `_fp4_dequant_kernel` (dequant.py:25-47).  k must be a multiple of `block`.
+ *   packed uint8 [rows, k/2], scale uint8 [rows, k/block] linear,
+ *   alpha fp32 [1] (device), out bf16 [rows, k].
+ */
+int cdlb200_fp4_dequant(const void* packed, const void* scale, const float* alpha, int64_t rows,
+                        int64_t k, int block, int scale_is_e8m0, void* out, void* stream);
+
+/*
+ * MXFP8 dequantize: out = bf16(e4m3 * e8m0 [* alpha]).
+ * Replaces cdl/core/kernel/dequant.py:121-143 `mxfp8_dequant` / the Triton
+ * `_mxfp8_dequant_kernel` (dequant.py:50-72).  alpha may be NULL (None).
+ */
+int cdlb200_mxfp8_dequant(const void* packed, const void* scale, const float* alpha, int64_t rows,
+                          int64_t k, void* out, void* stream);
+
+/*
+ * Scale-factor swizzle of a linear uint8 [m, b] scale matrix into the 128x4
+ * tiled layout, zero-padded to [ceil(m/128)*128, ceil(b/4)*4].
+ * Replaces cdl/core/mm/swizzle.py:5-14 `swizzle_scale_factors`.
+ */
+int cdlb200_swizzle_scales(const void* sf, int64_t m, int64_t b, void* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CDLB200_H_ */

@@ -1,0 +1,72 @@
+"""CPU-side checks of the C-ABI boundary: the library loads, exports every
+symbol the header declares, validates arguments on the host, and the Python
+API refuses CPU tensors instead of falling back."""
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from cdl_b200 import _lib
+
+ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+
+
+def _declared_symbols():
+    names = set()
+    for f in os.listdir(os.path.join(ROOT, "include")):
+        if f.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", f)).read()
+            names |= set(re.findall(r"\b(cdlb200_\w+)\s*\(", text))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    declared = _declared_symbols()
+    assert len(declared) >= 9
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert declared <= set(_lib.SIGNATURES), declared - set(_lib.SIGNATURES)
+
+
+def test_status_strings_and_version():
+    lib = _lib.lib()
+    assert lib.cdlb200_version() >= 100
+    for code in range(-7, 1):
+        assert lib.cdlb200_status_string(code)
+    assert lib.cdlb200_nvfp4_quant_workspace_bytes(4096, 4096) >= 256
+
+
+def test_host_side_argument_errors_need_no_gpu():
+    lib = _lib.lib()
+    # negative sizes, bad layout flag, bad transpose flag: rejected before any CUDA call
+    assert lib.cdlb200_mxfp4_quant(None, -1, 16, 16, 0, None, None, 0, None) == _lib.ERR_INVALID_ARG
+    assert lib.cdlb200_mxfp8_quant(None, 4, 32, 32, 0, None, None, 7, None) == _lib.ERR_INVALID_ARG
+    assert lib.cdlb200_mxfp8_quant(None, 4, 32, 32, 2, None, None, 0, None) == _lib.ERR_INVALID_ARG
+    assert lib.cdlb200_fp4_dequant(None, None, None, 4, 32, 8, 0, None, None) == _lib.ERR_INVALID_ARG
+    assert lib.cdlb200_swizzle_scales(None, -3, 4, None, None) == _lib.ERR_INVALID_ARG
+    # empty problems are valid no-ops for the MX formats
+    assert lib.cdlb200_mxfp4_quant(None, 0, 16, 16, 0, None, None, 0, None) == _lib.OK
+    # ld < k is invalid
+    dummy = ctypes.c_void_p(16)
+    assert lib.cdlb200_mxfp4_quant(dummy, 4, 64, 32, 0, dummy, dummy, 0, None) == _lib.ERR_INVALID_ARG
+    # NVFP4 needs a workspace of the stated size
+    assert lib.cdlb200_nvfp4_quant(dummy, 4, 64, 64, 0, dummy, dummy, 0, None, dummy, dummy, 8, None) in (
+        _lib.ERR_WORKSPACE,
+    )
+
+
+def test_python_api_refuses_cpu_tensors():
+    from cdl_b200.core.kernel import dequant, quant
+
+    x = torch.randn(4, 32).bfloat16()
+    for fn in (quant.nvfp4_quant, quant.mxfp4_quant, quant.mxfp8_quant):
+        with pytest.raises(RuntimeError, match="no CPU fallback"):
+            fn(x)
+    with pytest.raises(ValueError, match="2D"):
+        quant.nvfp4_quant(torch.randn(2, 3, 4).bfloat16())
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        dequant.nvfp4_dequant(torch.zeros(4, 16, dtype=torch.uint8), torch.zeros(4, 2, dtype=torch.uint8), torch.ones(1))
