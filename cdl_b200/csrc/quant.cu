@@ -16,14 +16,31 @@
 // E2M1 encoding without a per-element divide.  cdl computes v = RN(x / s) and
 // counts the e2m1 midpoints mid_j in {.25,.75,1.25,1.75,2.5,3.5,5} that
 // |v| exceeds (strict '>', so ties round toward zero; cdl/core/format/
-// fp4.py:15-17).  All mid_j have an even last mantissa bit, so
-//     RN(|x|/s) > mid_j  <=>  |x|/s > mid_j + ulp(mid_j)/2  =: U_j
-//                        <=>  |x| > RD(U_j * s)               (|x| is an fp32)
-// and RD(U_j * s) = fma_rd(mid_j, s, s * ulp(mid_j)/2) is exact whenever
-// s * ulp(mid_j)/2 does not underflow (s >= 2^-100).  Each block therefore
-// computes seven thresholds once and each element does seven compares.  For
-// power-of-two MX scales the threshold is exactly mid_j * s.  Blocks whose
-// NVFP4 scale is tiny or non-finite fall back to the literal IEEE divide.
+// fp4.py:15-17).  The hardware cvt.rn.satfinite.e2m1x2 rounds ties to even
+// instead, so it is only used on a value nudged just below the true one:
+//
+//   MX (s = 2^e): x * 2^-e is exact (bf16 has 8 significant bits), it differs
+//   from every midpoint it is not equal to by >= 2^-9 relative, so
+//   v' = RN(x * 2^-e * (1 - 2^-20)) lies on the same side of every midpoint
+//   and strictly below a midpoint it equals.  cvt(v') is then exactly cdl's
+//   code, sign and -0 included.
+//
+//   NVFP4 (general fp32 s): all mid_j have an even last mantissa bit, so
+//       RN(|x|/s) > mid_j  <=>  |x| > T_j := RD((mid_j + ulp(mid_j)/2) * s)
+//   with T_j = fma_rd(mid_j, s, s*ulp(mid_j)/2) exact for s >= 2^-100.  A bf16
+//   |x| exceeds T_j iff it is >= n_j, the next bf16 value above T_j.  With
+//   c = RN(RN(1/s) * (1 - 2^-20)), RN(T_j*c) < mid_j always, and
+//   RN(n_j*c) > mid_j whenever n_j - T_j >= 64 ulp(T_j) (2^-18 relative).  A
+//   block whose seven T_j all keep that margin (about 99.3% of blocks) is
+//   encoded as cvt(RN(x*c)); the others compare |x| against T_j directly.
+//   Blocks with a tiny or non-finite s use the literal IEEE divide.
+//
+// The NVFP4 scale byte needs q = RN(RN(bamax*448) / gmax) only up to its e4m3
+// rounding.  RN(bamax*448) has <= 11 significant bits and gmax <= 8, so their
+// quotient either equals an e4m3 rounding boundary (<= 5 bits) exactly or is
+// >= 2^-14 away from it; one Markstein correction of RN(p * RN(1/gmax))
+// (exact when the quotient is representable, within 2 ulp otherwise) gives
+// the same byte as the IEEE divide.
 #include "common.cuh"
 
 namespace cdlb200 {
@@ -66,7 +83,7 @@ __device__ __forceinline__ void block_setup(uint32_t mag, float gmax, float alph
         // cdl/core/ecdl.py:55  q = bamax * 448 / gmax (two roundings, as cdl)
         float bamax = mag > 0x7f80u ? u2f(0x7fc00000u) : mag_to_f32(mag);
         float q = __fdiv_rn(__fmul_rn(bamax, 448.0f), gmax);
-        bc.byte = ue4m3_scale_byte(q);
+        bc.byte = ue4m3_scale_byte(q);  // same byte as nvfp4_scale_byte (see header)
         float s = __fmul_rn(e4m3_to_f32(bc.byte), alpha);  // ecdl.py:129
         bc.s = s;
         bc.exact_div = !(s >= 0x1p-100f && s <= 3.4028234e38f);
@@ -78,8 +95,11 @@ __device__ __forceinline__ void block_setup(uint32_t mag, float gmax, float alph
         if constexpr (FMT == kMXFP4) {
             float s = e8m0_to_f32(bc.byte);
             bc.s = s;
+            // mid_j * 2^127 overflows for mid_j >= 2.5; finite |x| / 2^127 < 2 never
+            // exceeds those midpoints while +-inf exceeds all of them, so FLT_MAX
+            // is the exact threshold there.
 #pragma unroll
-            for (int j = 0; j < 7; ++j) bc.t[j] = __fmul_rn(mid_j(j), s);
+            for (int j = 0; j < 7; ++j) bc.t[j] = fminf(__fmul_rn(mid_j(j), s), 3.4028234664e38f);
         } else {
             bc.s = e8m0_inv(bc.byte);  // RN(x / 2^e) == x * 2^-e exactly
         }
@@ -130,11 +150,101 @@ __device__ __forceinline__ uint2 encode8_fp8(const uint4& w, const BlockCode& bc
     return make_uint2(b01 | (b23 << 16), b45 | (b67 << 16));
 }
 
+// Per-tensor NVFP4 constants shared by every block of one call.
+struct Nvfp4Tensor {
+    float gmax, alpha, yg;  // yg = RN(1 / gmax)
+    bool markstein;         // gmax in [2^-100, 1e35]: p / gmax via one Markstein step
+};
+
+__device__ __forceinline__ Nvfp4Tensor nvfp4_tensor(const float* gmax_p, const float* alpha_p) {
+    Nvfp4Tensor g;
+    g.gmax = *gmax_p;
+    g.alpha = *alpha_p;
+    g.markstein = g.gmax >= 0x1p-100f && g.gmax <= 1.0e35f;
+    g.yg = g.markstein ? __frcp_rn(g.gmax) : 0.0f;
+    return g;
+}
+
+// e4m3 scale byte of a block with bf16 amax bits `mag` (cdl/core/ecdl.py:52-55).
+__device__ __forceinline__ uint32_t nvfp4_scale_byte(uint32_t mag, const Nvfp4Tensor& g) {
+    const float bamax = mag > 0x7f80u ? u2f(0x7fc00000u) : u2f(mag << 16);
+    const float p = __fmul_rn(bamax, 448.0f);
+    float q;
+    if (g.markstein) {
+        const float q0 = __fmul_rn(p, g.yg);
+        const float r = __fmaf_rn(-q0, g.gmax, p);
+        q = __fmaf_rn(r, g.yg, q0);
+    } else {
+        q = __fdiv_rn(p, g.gmax);
+    }
+    return ue4m3_scale_byte(q);
+}
+
+// 8 fp32 values -> 8 e2m1 nibbles, element i at bits 4i..4i+3 (RNE, saturating).
+__device__ __forceinline__ uint32_t cvt_e2m1x8(float f0, float f1, float f2, float f3, float f4,
+                                               float f5, float f6, float f7) {
+    uint32_t out;
+    asm("{\n"
+        ".reg .b8 b0, b1, b2, b3;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n"
+        "mov.b32 %0, {b0, b1, b2, b3};\n"
+        "}"
+        : "=r"(out)
+        : "f"(f0), "f"(f1), "f"(f2), "f"(f3), "f"(f4), "f"(f5), "f"(f6), "f"(f7));
+    return out;
+}
+
+// 8 bf16 (one uint4) times c -> 8 nibbles via the hardware converter.
+__device__ __forceinline__ uint32_t cvt8_scaled(const uint4& w, float c) {
+    return cvt_e2m1x8(__fmul_rn(bf16lo(w.x), c), __fmul_rn(bf16hi(w.x), c), __fmul_rn(bf16lo(w.y), c),
+                      __fmul_rn(bf16hi(w.y), c), __fmul_rn(bf16lo(w.z), c), __fmul_rn(bf16hi(w.z), c),
+                      __fmul_rn(bf16lo(w.w), c), __fmul_rn(bf16hi(w.w), c));
+}
+
+// One NVFP4 block of 16 elements (w0, w1) with amax bits `mag`: returns the
+// scale byte and writes the 8 code bytes to out.x / out.y.
+__device__ __forceinline__ uint32_t nvfp4_block16(const uint4& w0, const uint4& w1, uint32_t mag,
+                                                  const Nvfp4Tensor& g, uint2& out) {
+    const uint32_t byte = nvfp4_scale_byte(mag, g);
+    const float s = __fmul_rn(e4m3_to_f32(byte), g.alpha);  // cdl/core/ecdl.py:129
+    if (s >= 0x1p-100f && s <= 3.4028234e38f) {
+        float t[7];
+        uint32_t hi = 0;
+#pragma unroll
+        for (int j = 0; j < 7; ++j) {
+            t[j] = __fmaf_rd(mid_j(j), s, __fmul_rn(s, half_ulp_j(j)));
+            hi = max(hi, f2u(t[j]) & 0xffffu);
+        }
+        if (hi <= 0xffc0u) {  // every threshold keeps >= 64 ulp below the next bf16
+            const float c = __fmul_rn(__frcp_rn(s), 0.99999904632568359375f);  // 1 - 2^-20
+            out.x = cvt8_scaled(w0, c);
+            out.y = cvt8_scaled(w1, c);
+        } else {
+            BlockCode bc;
+#pragma unroll
+            for (int j = 0; j < 7; ++j) bc.t[j] = t[j];
+            bc.exact_div = false;
+            out.x = encode8_fp4(w0, bc);
+            out.y = encode8_fp4(w1, bc);
+        }
+    } else {
+        BlockCode bc;
+        bc.s = s;
+        bc.exact_div = true;
+        out.x = encode8_fp4(w0, bc);
+        out.y = encode8_fp4(w1, bc);
+    }
+    return byte;
+}
+
 // ---------------------------------------------------------------------------
 // global amax (NVFP4): per-CTA partial maxima, the last CTA to finish reduces
 // them and writes gmax / alpha, then re-arms the counter for the next call.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(512) amax_kernel(const uint16_t* __restrict__ x, int64_t rows,
+__global__ void __launch_bounds__(512, 2) amax_kernel(const uint16_t* __restrict__ x, int64_t rows,
                                                    int64_t k, int64_t ldx, int vec_ok,
                                                    uint32_t* __restrict__ partial,
                                                    uint32_t* __restrict__ counter,
@@ -237,10 +347,13 @@ __global__ void __launch_bounds__(256) quant_flat_kernel(const uint4* __restrict
             if constexpr (VPB == 4) mag = max(mag, __shfl_xor_sync(0xffffffffu, mag, 2));
             if (v < nvec) {
                 BlockCode bc;
-                block_setup<FMT>(mag, gmax, alpha, bc);
-                if constexpr (FmtTraits<FMT>::kFp4) {
-                    reinterpret_cast<uint32_t*>(packed)[v] = encode8_fp4(w[u], bc);
+                if constexpr (FMT == kMXFP4) {
+                    bc.byte = e8m0_byte_from_bf16_mag<FmtTraits<FMT>::kEmax>(mag);
+                    // 2^-e * (1 - 2^-20): exact, also for the subnormal 2^-127
+                    const float c = __fmul_rn(e8m0_inv(bc.byte), 0.99999904632568359375f);
+                    reinterpret_cast<uint32_t*>(packed)[v] = cvt8_scaled(w[u], c);
                 } else {
+                    block_setup<FMT>(mag, gmax, alpha, bc);
                     reinterpret_cast<uint2*>(packed)[v] = encode8_fp8(w[u], bc);
                 }
                 if ((lane & (VPB - 1)) == 0) {
@@ -249,6 +362,42 @@ __global__ void __launch_bounds__(256) quant_flat_kernel(const uint4* __restrict
                     if constexpr (SWZ) off = swizzle_offset(blk / nb, blk % nb, c4);
                     scale[off] = (uint8_t)bc.byte;
                 }
+            }
+        }
+    }
+}
+
+// NVFP4 fast path: one thread per 16-element block (two 16-byte loads, one
+// 8-byte code store, one scale byte), so the per-block scale and threshold
+// set-up is computed once per block.  U blocks per thread per iteration.
+template <bool SWZ, int U>
+__global__ void __launch_bounds__(256) nvfp4_flat_kernel(const uint4* __restrict__ x, int64_t nblk,
+                                                         uint2* __restrict__ packed,
+                                                         uint8_t* __restrict__ scale, int64_t nb,
+                                                         int64_t c4, const float* __restrict__ gmax_p,
+                                                         const float* __restrict__ alpha_p) {
+    const Nvfp4Tensor g = nvfp4_tensor(gmax_p, alpha_p);
+    const int64_t nthr = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < nblk; base += nthr * U) {
+        uint4 w0[U], w1[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t b = base + u * nthr;
+            if (b < nblk) {
+                w0[u] = ldg_stream(x + 2 * b);
+                w1[u] = ldg_stream(x + 2 * b + 1);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t b = base + u * nthr;
+            if (b < nblk) {
+                uint2 out;
+                const uint32_t byte = nvfp4_block16(w0[u], w1[u], max(amax8(w0[u]), amax8(w1[u])), g, out);
+                packed[b] = out;
+                int64_t off = b;
+                if constexpr (SWZ) off = swizzle_offset(b / nb, b % nb, c4);
+                scale[off] = (uint8_t)byte;
             }
         }
     }
@@ -332,8 +481,16 @@ int launch_encode(const void* x, int64_t rows, int64_t k, int64_t ldx, int trans
     const int64_t pstride = FmtTraits<FMT>::kFp4 ? nb * B / 2 : nb * B;
     const int sms = num_sms();
     const bool flat = !transpose && ldx == k && (k % B) == 0 && aligned(x, 16) &&
-                      aligned(packed, FmtTraits<FMT>::kFp4 ? 4 : 8);
-    if (flat) {
+                      aligned(packed, (FmtTraits<FMT>::kFp4 && FMT != kNVFP4) ? 4 : 8);
+    if (flat && FMT == kNVFP4) {
+        constexpr int U = 2;
+        const int64_t nblk = rows * k / 16;
+        int64_t grid = (nblk + 256 * U - 1) / (256 * U);
+        grid = grid < (int64_t)sms * 8 ? grid : (int64_t)sms * 8;
+        nvfp4_flat_kernel<SWZ, U><<<(unsigned)grid, 256, 0, st>>>(
+            reinterpret_cast<const uint4*>(x), nblk, static_cast<uint2*>(packed),
+            static_cast<uint8_t*>(scale), nb, c4, gmax, alpha);
+    } else if (flat) {
         constexpr int U = 4;
         const int64_t nvec = rows * k / 8;
         int64_t grid = (nvec + 256 * U - 1) / (256 * U);
