@@ -42,6 +42,7 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_version": (_I, []),
     "cdlb200_nvfp4_quant_workspace_bytes": (_SZ, [_I64, _I64]),
     "cdlb200_nvfp4_quant": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P, _P, _P, _SZ, _P]),
+    "cdlb200_nvfp4_quant_noalloc": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P, _P, _P]),
     "cdlb200_mxfp4_quant": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P]),
     "cdlb200_mxfp8_quant": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P]),
     "cdlb200_fp4_dequant": (_I, [_P, _P, _P, _I64, _I64, _I, _I, _P, _P]),

@@ -79,6 +79,23 @@ int cdlb200_nvfp4_quant(const void* x, int64_t rows, int64_t k, int64_t ldx, int
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * NVFP4 quantize that allocates nothing and takes no workspace.  It has no
+ * counterpart in the reference: it exists for callers that cannot allocate
+ * device memory (a host binding this C ABI from another runtime without a
+ * CUDA allocator, or a runtime that owns all device memory in a fixed arena).
+ * Same arguments and results as cdlb200_nvfp4_quant minus the workspace; the
+ * scratch is a fixed 8 KiB array in the library's device memory, held on
+ * every GPU that loads the library until it is unloaded.  Returns
+ * CDLB200_ERR_WORKSPACE if a call would need more scratch than that.  The
+ * first call on a device looks up that array's address, so make it before
+ * any stream capture.  All calls on a device share the array: calls that
+ * overlap on the GPU race.
+ */
+int cdlb200_nvfp4_quant_noalloc(const void* x, int64_t rows, int64_t k, int64_t ldx, int transpose,
+                                void* packed, void* scale, int scale_layout, float* gmax,
+                                float* alpha, void* stream);
+
+/*
  * MXFP4 / MXFP8 quantize of a bf16 matrix (blocks of 32, e8m0 scales).
  * Replaces cdl/core/kernel/quant.py:134-139 `mxfp4_quant` and :142-146
  * `mxfp8_quant` (their `_quant_kernel` e8m0 branch, quant.py:39-46, 56-68).
