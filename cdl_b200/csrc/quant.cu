@@ -54,7 +54,12 @@ __device__ __forceinline__ constexpr float mid_j(int j) {
 __device__ __forceinline__ constexpr float half_ulp_j(int j) {
     return j == 0 ? 0x1p-26f : j == 1 ? 0x1p-25f : j <= 3 ? 0x1p-24f : j <= 5 ? 0x1p-23f : 0x1p-22f;
 }
+// NVFP4 workspace: [0] arrival counter, [4] departure counter (fused kernel),
+// [8] status word (non-zero after a timed-out grid barrier), [256..) partial maxima.
 constexpr int kWsCounterOff = 0;
+constexpr int kWsDepartOff = 4;
+constexpr int kWsStatusOff = 8;
+constexpr int kWsGmaxOff = 12;  // fused kernel: running max of the CTA maxima (bf16 magnitude bits)
 constexpr int kWsPartialOff = 256;
 constexpr int kMaxAmaxGrid = 1024;
 
@@ -204,28 +209,43 @@ __device__ __forceinline__ uint32_t cvt8_scaled(const uint4& w, float c) {
                       __fmul_rn(bf16lo(w.w), c), __fmul_rn(bf16hi(w.w), c));
 }
 
+// RN(1/s) to within 2^-22 relative: hardware approximation refined by one
+// Newton-Raphson step (y1 = y0 + y0 * (1 - s*y0)).  The fast encoder's bounds
+// hold for any reciprocal within 2^-21.
+__device__ __forceinline__ float recip_nr(float s) {
+    float y0;
+    asm("rcp.approx.f32 %0, %1;" : "=f"(y0) : "f"(s));
+    const float e = __fmaf_rn(-s, y0, 1.0f);
+    return __fmaf_rn(y0, e, y0);
+}
+
 // One NVFP4 block of 16 elements (w0, w1) with amax bits `mag`: returns the
 // scale byte and writes the 8 code bytes to out.x / out.y.
+//
+// The fast-path check needs only four thresholds: T_0 = RD(0.25 s (1+2^-24))
+// = 0.25 s, and T_4 = 2 T_2, T_5 = 2 T_3, T_6 = 4 T_2 (directed rounding
+// commutes with scaling by 2), so the low 16 bits of s, T_1, T_2, T_3 cover
+// all seven.
 __device__ __forceinline__ uint32_t nvfp4_block16(const uint4& w0, const uint4& w1, uint32_t mag,
                                                   const Nvfp4Tensor& g, uint2& out) {
     const uint32_t byte = nvfp4_scale_byte(mag, g);
     const float s = __fmul_rn(e4m3_to_f32(byte), g.alpha);  // cdl/core/ecdl.py:129
     if (s >= 0x1p-100f && s <= 3.4028234e38f) {
-        float t[7];
-        uint32_t hi = 0;
-#pragma unroll
-        for (int j = 0; j < 7; ++j) {
-            t[j] = __fmaf_rd(mid_j(j), s, __fmul_rn(s, half_ulp_j(j)));
-            hi = max(hi, f2u(t[j]) & 0xffffu);
-        }
-        if (hi <= 0xffc0u) {  // every threshold keeps >= 64 ulp below the next bf16
-            const float c = __fmul_rn(__frcp_rn(s), 0.99999904632568359375f);  // 1 - 2^-20
+        const float t1 = __fmaf_rd(0.75f, s, __fmul_rn(s, 0x1p-25f));
+        const float t2 = __fmaf_rd(1.25f, s, __fmul_rn(s, 0x1p-24f));
+        const float t3 = __fmaf_rd(1.75f, s, __fmul_rn(s, 0x1p-24f));
+        uint32_t a, b, hi;
+        asm("max.u16x2 %0, %1, %2;" : "=r"(a) : "r"(f2u(s)), "r"(f2u(t1)));
+        asm("max.u16x2 %0, %1, %2;" : "=r"(b) : "r"(f2u(t2)), "r"(f2u(t3)));
+        asm("max.u16x2 %0, %1, %2;" : "=r"(hi) : "r"(a), "r"(b));
+        if ((hi & 0xffffu) <= 0xffc0u) {  // every threshold keeps >= 64 ulp below the next bf16
+            const float c = __fmul_rn(recip_nr(s), 0.99999904632568359375f);  // (1 - 2^-20) / s
             out.x = cvt8_scaled(w0, c);
             out.y = cvt8_scaled(w1, c);
         } else {
             BlockCode bc;
 #pragma unroll
-            for (int j = 0; j < 7; ++j) bc.t[j] = t[j];
+            for (int j = 0; j < 7; ++j) bc.t[j] = __fmaf_rd(mid_j(j), s, __fmul_rn(s, half_ulp_j(j)));
             bc.exact_div = false;
             out.x = encode8_fp4(w0, bc);
             out.y = encode8_fp4(w1, bc);
@@ -403,6 +423,278 @@ __global__ void __launch_bounds__(256) nvfp4_flat_kernel(const uint4* __restrict
     }
 }
 
+constexpr uint32_t kBarrierSpins = 1u << 20;
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Per-CTA table of everything an NVFP4 block needs besides its codes, indexed
+// by the block's scale byte (1..126), built once per CTA after the barrier.
+//
+//   tt[j]  t_j, the largest bf16 value <= T_j, in both halves of a word: a
+//          bf16 |x| has code > j iff |x| > t_j (exact; used by the packed
+//          binary search below).
+//   c      the encoder multiplier, when one separates every threshold: let
+//          n_j be the bf16 value after t_j; if RN(t_j*c) < mid_j and
+//          RN(n_j*c) > mid_j for all seven j, then, a -> RN(a*c) being
+//          monotone, cvt.rn(RN(|x|*c)) equals cdl's code for every bf16 x and
+//          no product lands on a midpoint.  The 14 products are evaluated with
+//          the encoder's own rounding for a few c = RN(1/s)*(1 - nu).
+//   kind   kCvt (c separates every threshold), kSearch (no candidate does:
+//          thresholds pinched against the bf16 grid from both sides, which
+//          happens for whole tensors because gmax/2688 has short periodic
+//          binary expansions), kDivide (s below 2^-100 or not finite:
+//          literal IEEE divide).
+// The table is identical on every CTA, so the encoding mode chosen from it is
+// uniform across the grid: cvt when no entry has exceptions, otherwise the
+// packed search (and the divide for kDivide entries).
+constexpr uint32_t kCvt = 0u, kSearch = 1u, kDivide = 2u;
+struct ScaleEntry {
+    float c, s;
+    uint32_t kind, pad;
+    uint32_t tt[8];
+};
+
+// Scale entry of `byte` built cooperatively by 4 adjacent lanes of a warp:
+// lane i tries c = RN(1/s)*(1 - nu_i) (nu = 2^-20, 2^-21, 2^-19, 2^-22) and
+// the first candidate that separates all seven thresholds wins.
+__device__ __forceinline__ ScaleEntry make_scale_entry(uint32_t byte, float alpha, int cand) {
+    ScaleEntry e;
+    e.s = __fmul_rn(e4m3_to_f32(byte), alpha);
+    e.c = 0.0f;
+    e.pad = 0u;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) e.tt[j] = 0u;
+    const bool divide = !(e.s >= 0x1p-100f && e.s <= 3.4028234e38f);
+    // T_0 = RD(0.25 s (1 + 2^-24)) = 0.25 s; T_4 = 2 T_2, T_5 = 2 T_3, T_6 = 4 T_2
+    float T[7];
+    T[0] = __fmul_rn(e.s, 0.25f);
+    T[1] = __fmaf_rd(0.75f, e.s, __fmul_rn(e.s, 0x1p-25f));
+    T[2] = __fmaf_rd(1.25f, e.s, __fmul_rn(e.s, 0x1p-24f));
+    T[3] = __fmaf_rd(1.75f, e.s, __fmul_rn(e.s, 0x1p-24f));
+    T[4] = __fmul_rn(T[2], 2.0f);
+    T[5] = __fmul_rn(T[3], 2.0f);
+    T[6] = __fmul_rn(T[2], 4.0f);
+#pragma unroll
+    for (int j = 0; j < 7; ++j) {
+        const uint32_t t16 = f2u(T[j]) >> 16;
+        e.tt[j] = t16 | (t16 << 16);
+    }
+    const float nu = cand == 0 ? 0x1p-20f : cand == 1 ? 0x1p-21f : cand == 2 ? 0x1p-19f : cand == 3 ? 0x1p-22f
+                   : cand == 4 ? 0x1p-18f : cand == 5 ? 0x1p-23f : cand == 6 ? 0x1p-17f : 0x1p-24f;
+    const float c = __fmul_rn(recip_nr(e.s), 1.0f - nu);
+    bool ok = !divide;
+#pragma unroll
+    for (int j = 0; j < 7; ++j) {
+        const uint32_t tb = f2u(T[j]) & 0xffff0000u;
+        ok = ok && (__fmul_rn(u2f(tb), c) < mid_j(j)) && (__fmul_rn(u2f(tb + 0x10000u), c) > mid_j(j));
+    }
+    const uint32_t lane = threadIdx.x & 31, grp = lane & ~3u;
+    const uint32_t votes = (__ballot_sync(0xffffffffu, ok) >> grp) & 0xfu;
+    const int first = votes ? __ffs(votes) - 1 : -1;
+    e.c = __shfl_sync(0xffffffffu, c, (int)grp + (first < 0 ? 0 : first));
+    e.kind = divide ? kDivide : (first < 0 ? kSearch : kCvt);
+    return e;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_gt(uint32_t a, uint32_t b) {
+    uint32_t m;
+    asm("set.gt.u32.bf16x2 %0, %1, %2;" : "=r"(m) : "r"(a), "r"(b));
+    return m;  // 0xffff in each half where a > b
+}
+
+// 8 elements (one uint4: pairs (x0,x1) .. (x6,x7)) -> 8 nibbles, exact, by a
+// three-level binary search of each bf16 magnitude against the thresholds.
+// Words are regrouped as (x_k, x_k+4) so that each lane's result bits land in
+// its own 16-bit half: nibble k in bits 4k.., nibble k+4 in bits 16+4k...
+__device__ __forceinline__ uint32_t search8(const uint4& w, const uint32_t* tt) {
+    const uint32_t r[4] = {__byte_perm(w.x, w.z, 0x5410), __byte_perm(w.x, w.z, 0x7632),
+                           __byte_perm(w.y, w.w, 0x5410), __byte_perm(w.y, w.w, 0x7632)};
+    uint32_t out = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint32_t a = r[k] & 0x7fff7fffu;
+        const uint32_t c3 = bf16x2_gt(a, tt[3]);
+        const uint32_t c2 = bf16x2_gt(a, (c3 & tt[5]) | (~c3 & tt[1]));
+        const uint32_t hi = (c2 & tt[6]) | (~c2 & tt[4]);
+        const uint32_t lo = (c2 & tt[2]) | (~c2 & tt[0]);
+        const uint32_t c1 = bf16x2_gt(a, (c3 & hi) | (~c3 & lo));
+        const uint32_t sh = 4 * k;
+        out |= (c1 & (0x00010001u << sh)) | (c2 & (0x00020002u << sh)) | (c3 & (0x00040004u << sh)) |
+               ((r[k] >> (12 - sh)) & (0x00080008u << sh));
+    }
+    return out;
+}
+
+// NVFP4 fused path: global amax and encode in ONE persistent cooperative
+// launch, two 512-thread CTAs per SM.  The input is cut into chunks of 512
+// blocks (16 KiB), dealt round-robin to the CTAs so that each CTA streams
+// from every part of the tensor.
+//   phase 1  stream own chunks from HBM (four 32-byte blocks in flight per
+//            thread), reduce max|x|, keep every block's amax in shared
+//            memory, fold the CTA maximum into one global word (atomicMax)
+//            and arrive on a grid barrier;
+//   phase 2  every CTA reads the global amax, builds the 126-entry scale
+//            table (4 lanes per entry), and re-encodes its chunks in reverse
+//            order -- most recently streamed first, so they come from L2.
+// The grid-barrier wait is bounded (kBarrierSpins polls, about a second): on
+// a timeout the CTA writes a non-zero status word into the workspace and
+// carries on, so a failed wait never hangs the GPU.  The last CTA to finish
+// re-arms the barrier words for the next stream-ordered call.
+constexpr int kFusedThreads = 512;  // threads of the fused NVFP4 kernel (two CTAs per SM)
+constexpr int kChunkBlocks = kFusedThreads;  // one block per thread per chunk (16 KiB)
+constexpr int kAmaxChunks = 16;  // chunks whose per-block amax phase 1 keeps for phase 2
+
+__device__ __forceinline__ uint2 encode_block(const uint4& a0, const uint4& a1, uint32_t byte,
+                                              const ScaleEntry& e, int mode) {
+    uint2 out;
+    if (mode == 0) {
+        out.x = cvt8_scaled(a0, e.c);
+        out.y = cvt8_scaled(a1, e.c);
+    } else if (mode == 2 || e.kind != kDivide) {
+        uint32_t tt[7];
+#pragma unroll
+        for (int j = 0; j < 7; ++j) tt[j] = e.tt[j];
+        out.x = search8(a0, tt);
+        out.y = search8(a1, tt);
+    } else {
+        BlockCode bc;
+        bc.s = e.s;
+        bc.exact_div = true;
+        out.x = encode8_fp4(a0, bc);
+        out.y = encode8_fp4(a1, bc);
+    }
+    return out;
+}
+
+template <bool SWZ>
+__global__ void __launch_bounds__(kFusedThreads, 2) nvfp4_fused_kernel(
+    const uint4* __restrict__ x, int64_t nblk, uint2* __restrict__ packed, uint8_t* __restrict__ scale,
+    int64_t nb, int64_t c4, uint8_t* __restrict__ ws, float* __restrict__ gmax_out,
+    float* __restrict__ alpha_out) {
+    __shared__ uint32_t red[kFusedThreads / 32];
+    __shared__ ScaleEntry table[128];
+    __shared__ float s_gmax;
+    __shared__ int s_mode;
+    __shared__ uint16_t amax_s[kAmaxChunks * kChunkBlocks];
+    uint32_t* arrive = reinterpret_cast<uint32_t*>(ws + kWsCounterOff);
+    uint32_t* depart = reinterpret_cast<uint32_t*>(ws + kWsDepartOff);
+    uint32_t* status = reinterpret_cast<uint32_t*>(ws + kWsStatusOff);
+    uint32_t* gmax_bits = reinterpret_cast<uint32_t*>(ws + kWsGmaxOff);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t G = gridDim.x;
+    const int64_t nchunk = (nblk + kChunkBlocks - 1) / kChunkBlocks;
+    const int nmine = nchunk > (int64_t)blockIdx.x ? (int)((nchunk - 1 - blockIdx.x) / G + 1) : 0;
+    auto blk = [&](int q) { return ((int64_t)blockIdx.x + (int64_t)q * G) * kChunkBlocks + tid; };
+
+    // ---- phase 1: stream own chunks (four blocks in flight per thread),
+    //      reduce max|x|, keep each block's amax in shared memory
+    uint32_t m = 0;
+    for (int q0 = 0; q0 < nmine; q0 += 4) {
+        uint4 v[8];
+        bool ok[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t b = blk(q0 + u);
+            ok[u] = q0 + u < nmine && b < nblk;
+            if (ok[u]) {
+                v[2 * u] = ldg_stream(x + 2 * b);
+                v[2 * u + 1] = ldg_stream(x + 2 * b + 1);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (!ok[u]) continue;
+            const uint32_t bm = max(amax8(v[2 * u]), amax8(v[2 * u + 1]));
+            if (q0 + u < kAmaxChunks) amax_s[(q0 + u) * kChunkBlocks + tid] = (uint16_t)bm;
+            m = max(m, bm);
+        }
+    }
+    m = __reduce_max_sync(0xffffffffu, m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (tid == 0) {
+        uint32_t cm = 0;
+        for (int w = 0; w < kFusedThreads / 32; ++w) cm = max(cm, red[w]);
+        atomicMax(gmax_bits, cm);
+        __threadfence();
+        atomicAdd(arrive, 1u);
+        uint32_t spins = 0;
+        while (ld_acquire_u32(arrive) < G) {
+            if (++spins > kBarrierSpins) {
+                atomicExch(status, 1u);
+                break;
+            }
+            __nanosleep(32);
+        }
+        // ---- global amax: one word, folded in by every CTA before it arrived
+        const uint32_t gm = __ldcg(gmax_bits);
+        const float gmax = gm > 0x7f80u ? u2f(0x7fc00000u) : fmaxf(u2f(gm << 16), 1.1754943508222875e-38f);
+        s_gmax = gmax;
+        s_mode = 0;
+        if (blockIdx.x == 0) {
+            if (gmax_out) *gmax_out = gmax;
+            *alpha_out = __fdiv_rn(gmax, 2688.0f);
+        }
+    }
+    __syncthreads();
+    Nvfp4Tensor t;
+    t.gmax = s_gmax;
+    t.alpha = __fdiv_rn(t.gmax, 2688.0f);
+    t.markstein = t.gmax >= 0x1p-100f && t.gmax <= 1.0e35f;
+    t.yg = t.markstein ? __frcp_rn(t.gmax) : 0.0f;
+    {  // 4 lanes per scale byte, one candidate multiplier each
+        const uint32_t byte = (uint32_t)(tid >> 2);
+        const ScaleEntry e = make_scale_entry(byte < 1 ? 1u : (byte > 126 ? 126u : byte), t.alpha, tid & 3);
+        if ((tid & 3) == 0 && byte >= 1 && byte <= 126) {
+            table[byte] = e;
+            // mode bits: 2 = some kSearch, 4 = some kDivide
+            const int bit = e.kind == kSearch ? 2 : (e.kind == kDivide ? 4 : 0);
+            if (bit) atomicOr(&s_mode, bit);
+        }
+    }
+    __syncthreads();
+    // 0: cvt; 2: packed search; 3: search + divide
+    const int mode = s_mode == 0 ? 0 : (s_mode < 4 ? 2 : 3);
+
+    // ---- phase 2: encode own chunks, last-streamed first (they come from L2)
+    for (int q1 = nmine - 1; q1 >= 0; q1 -= 2) {
+        uint4 v[4];
+        int64_t bs[2];
+        bool ok[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            bs[u] = blk(q1 - u);
+            ok[u] = q1 - u >= 0 && bs[u] < nblk;
+            if (ok[u]) {
+                v[2 * u] = ldg_stream(x + 2 * bs[u]);
+                v[2 * u + 1] = ldg_stream(x + 2 * bs[u] + 1);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            if (!ok[u]) continue;
+            const int q = q1 - u;
+            const uint32_t mag = q < kAmaxChunks ? (uint32_t)amax_s[q * kChunkBlocks + tid]
+                                                 : max(amax8(v[2 * u]), amax8(v[2 * u + 1]));
+            const uint32_t byte = nvfp4_scale_byte(mag, t);
+            const int64_t b = bs[u];
+            packed[b] = encode_block(v[2 * u], v[2 * u + 1], byte, table[byte], mode);
+            scale[SWZ ? swizzle_offset(b / nb, b % nb, c4) : b] = (uint8_t)byte;
+        }
+    }
+
+    // ---- leave the grid barrier; the last CTA out re-arms it for the next call
+    if (tid == 0 && atomicAdd(depart, 1u) == G - 1) {
+        *arrive = 0u;
+        *gmax_bits = 0u;
+        *depart = 0u;
+    }
+}
+
 // ---------------------------------------------------------------------------
 // general path: any leading dimension, ragged k, transposed (dim-0) blocks.
 // One thread per (output row r, block b); element (r, c) is x[r*sr + c*sc].
@@ -560,6 +852,65 @@ int launch_amax(const void* x, int64_t rows, int64_t k, int64_t ldx, uint32_t* p
     return CDLB200_OK;
 }
 
+namespace {
+
+template <bool SWZ>
+int launch_fused_impl(const void* x, int64_t rows, int64_t k, void* packed, void* scale, float* gmax,
+                      float* alpha, uint8_t* ws, cudaStream_t st) {
+    static int occ_cache[128][2] = {{0}};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return CDLB200_ERR_CUDA;
+    int& per_sm = occ_cache[dev][SWZ ? 1 : 0];
+    if (per_sm == 0) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, nvfp4_fused_kernel<SWZ>, kFusedThreads, 0) !=
+                cudaSuccess || n < 1)
+            return CDLB200_ERR_CUDA;
+        per_sm = n > 2 ? 2 : n;
+    }
+    const int64_t nblk = rows * k / 16;
+    const int64_t nchunk = (nblk + kChunkBlocks - 1) / kChunkBlocks;
+    int64_t grid = (int64_t)num_sms() * per_sm;
+    if (grid > kMaxAmaxGrid) grid = kMaxAmaxGrid;
+    if (grid > nchunk) grid = nchunk;
+    const int64_t nb = k / 16, c4 = (nb + 3) / 4;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kFusedThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident, or the launch fails
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, nvfp4_fused_kernel<SWZ>, reinterpret_cast<const uint4*>(x),
+                                             nblk, static_cast<uint2*>(packed), static_cast<uint8_t*>(scale),
+                                             nb, c4, ws, gmax, alpha);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        return CDLB200_ERR_LAUNCH;
+    }
+    return CDLB200_OK;
+}
+
+}  // namespace
+
+// Fused single-launch NVFP4 quantize of a contiguous, 16-byte aligned bf16
+// matrix with k % 16 == 0 (row-wise blocks).
+int launch_nvfp4_fused(const void* x, int64_t rows, int64_t k, void* packed, void* scale,
+                       int scale_layout, float* gmax, float* alpha, uint8_t* ws, cudaStream_t st) {
+    if (scale_layout == CDLB200_SCALE_SWIZZLED) {
+        const int64_t nb = k / 16;
+        if ((rows % 128) != 0 || (nb % 4) != 0) {
+            const size_t bytes = (size_t)((rows + 127) / 128 * 128) * (size_t)((nb + 3) / 4 * 4);
+            if (cudaMemsetAsync(scale, 0, bytes, st) != cudaSuccess) return CDLB200_ERR_CUDA;
+        }
+        return launch_fused_impl<true>(x, rows, k, packed, scale, gmax, alpha, ws, st);
+    }
+    return launch_fused_impl<false>(x, rows, k, packed, scale, gmax, alpha, ws, st);
+}
+
 int launch_nvfp4_encode(const void* x, int64_t rows, int64_t k, int64_t ldx, int transpose,
                         void* packed, void* scale, int scale_layout, const float* gmax,
                         const float* alpha, cudaStream_t st) {
@@ -592,6 +943,8 @@ extern "C" int cdlb200_nvfp4_quant(const void* x, int64_t rows, int64_t k, int64
     uint32_t* partial = reinterpret_cast<uint32_t*>(ws + kWsPartialOff);
     // gmax goes to the caller's buffer if given, else to the workspace tail
     float* g = gmax ? gmax : reinterpret_cast<float*>(ws + kWsPartialOff + sizeof(uint32_t) * kMaxAmaxGrid);
+    if (!transpose && rows > 0 && k > 0 && ldx == k && (k % 16) == 0 && aligned(x, 16) && aligned(packed, 8))
+        return launch_nvfp4_fused(x, rows, k, packed, scale, scale_layout, gmax, alpha, ws, st);
     rc = launch_amax(x, rows, k, ldx, partial, counter, g, alpha, st);
     if (rc != CDLB200_OK || rows == 0 || k == 0) return rc;
     return launch_nvfp4_encode(x, rows, k, ldx, transpose, packed, scale, scale_layout, g, alpha, st);

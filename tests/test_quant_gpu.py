@@ -197,3 +197,20 @@ def test_repeated_calls_reuse_workspace():
     op, os_, oa = oracle.quant(_bits(y.cpu()), oracle.NVFP4)
     np.testing.assert_array_equal(_np(p), op)
     np.testing.assert_array_equal(_np(s), os_)
+
+
+def test_nvfp4_many_global_scales_vs_oracle():
+    """Sweep the per-tensor scale so that many distinct block scales (and the
+    encoder's rare exact patch-up and divide paths) are exercised."""
+    base = workloads.c1_nvfp4(128, 1024, seed=77)
+    g = torch.Generator().manual_seed(78)
+    exps = torch.randint(-120, 100, (48,), generator=g).tolist()
+    mants = (1.0 + torch.rand(48, generator=g)).tolist()
+    for e, mnt in zip(exps, mants):
+        x = (base.float() * (mnt * 2.0 ** e)).to(torch.bfloat16)
+        xb = _bits(x)
+        packed, scale, alpha = _q()[oracle.NVFP4](x.cuda())
+        op, os_, oa = oracle.quant(xb, oracle.NVFP4)
+        np.testing.assert_array_equal(_np(scale), os_, err_msg=f"scale 2^{e}*{mnt}")
+        np.testing.assert_array_equal(_np(packed), op, err_msg=f"scale 2^{e}*{mnt}")
+        assert alpha.cpu().numpy().view(np.uint32)[0] == oa.view(np.uint32)[0]
