@@ -313,7 +313,7 @@ def main() -> None:
     per_step_s = ms_max / 1e3 / args.steps
     achieved = alg_bytes / per_step_s / 1e9
     traffic = profile_traffic(args.workload)
-    launches_per_step = 2 if fmt_name == "nvfp4" else 1
+    launches_per_step = 1
     if rank == 0:
         print(json.dumps({
             "metric": f"{fmt_name.upper()} quant GB/s", "value": round(value, 2), "unit": "GB/s",
@@ -327,7 +327,7 @@ def main() -> None:
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                          "traffic": traffic, "peak_source": peak_src,
-                         "kernel": "amax_kernel + quant_flat_kernel" if fmt_name == "nvfp4" else "quant_flat_kernel"},
+                         "kernel": "nvfp4_fused_kernel" if fmt_name == "nvfp4" else "quant_flat_kernel"},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
