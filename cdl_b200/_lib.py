@@ -48,6 +48,8 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_fp4_dequant": (_I, [_P, _P, _P, _I64, _I64, _I, _I, _P, _P]),
     "cdlb200_mxfp8_dequant": (_I, [_P, _P, _P, _I64, _I64, _P, _P]),
     "cdlb200_swizzle_scales": (_I, [_P, _I64, _I64, _P, _P]),
+    "cdlb200_mm_fp4": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _P, _I64, _P, _P]),
+    "cdlb200_mm_mxfp8": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _I64, _P, _P]),
 }
 
 

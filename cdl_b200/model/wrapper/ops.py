@@ -1,0 +1,88 @@
+"""Block-scaled GEMM custom ops: the drop-in for ``cdl.model.wrapper.flashinfer``.
+
+``torch.ops.cdl_b200.mm_fp4`` and ``torch.ops.cdl_b200.mm_mxfp8`` take the same
+arguments as cdl's ``cdl::mm_fp4`` / ``cdl::mm_mxfp8``
+(``cdl/model/wrapper/flashinfer.py:5-62``) and return bf16 ``[M, N]``; they run
+the tcgen05 block-scaled kernel of ``libcdlb200.so`` instead of FlashInfer's
+sm_120-only ``b12x`` backend.  Both have fake (meta) implementations for
+tracing, as in the reference.
+
+Argument conventions (cdl's): ``a`` is the row-major operand codes ``[M, K/2]``
+(FP4) or ``[M, K]`` (FP8); ``b`` is ``w_codes.T``, a ``[K', N]`` column-major
+view whose storage is the row-major ``[N, K']`` weight codes; the scales are
+``swizzle_scale_factors`` outputs (``b_scale`` possibly transposed, as cdl
+passes ``swizzle_scale_factors(w_q).T``), flattened for FP8.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from cdl_b200 import _lib
+
+
+def _storage_rows(t: torch.Tensor) -> torch.Tensor:
+    """Row-major [N, K'] storage behind cdl's column-major [K', N] view."""
+    if t.dim() == 2 and t.t().is_contiguous():
+        return t.t()
+    return t.t().contiguous()
+
+
+def _flat(t: torch.Tensor) -> torch.Tensor:
+    """The bytes of a swizzled scale tensor in storage order."""
+    if t.dim() == 2 and not t.is_contiguous() and t.t().is_contiguous():
+        t = t.t()
+    return t.contiguous().view(torch.uint8)
+
+
+@torch.library.custom_op("cdl_b200::mm_fp4", mutates_args=())
+def mm_fp4(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    a_scale: torch.Tensor,
+    b_scale: torch.Tensor,
+    alpha: torch.Tensor,
+    block_size: int,
+    use_nvfp4: bool,
+) -> torch.Tensor:
+    dev = _lib.require_cuda(a, b, a_scale, b_scale, alpha)
+    a = a.contiguous().view(torch.uint8)
+    brows = _storage_rows(b).view(torch.uint8)
+    m, k = a.shape[0], a.shape[1] * 2
+    n = brows.shape[0]
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    if m == 0 or n == 0:
+        return out
+    al = alpha.reshape(-1).float().contiguous()
+    _lib.call(
+        "cdlb200_mm_fp4", _lib.ptr(a), _lib.ptr(brows), _lib.ptr(_flat(a_scale)), _lib.ptr(_flat(b_scale)),
+        _lib.ptr(al), m, n, k, int(block_size), int(bool(use_nvfp4)), _lib.ptr(out), n, None, _lib.stream(dev),
+    )
+    return out
+
+
+@mm_fp4.register_fake
+def _(a, b, a_scale, b_scale, alpha, block_size, use_nvfp4):
+    return torch.empty(a.shape[0], b.shape[1], dtype=torch.bfloat16, device=a.device)
+
+
+@torch.library.custom_op("cdl_b200::mm_mxfp8", mutates_args=())
+def mm_mxfp8(a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor, b_scale: torch.Tensor) -> torch.Tensor:
+    dev = _lib.require_cuda(a, b, a_scale, b_scale)
+    a = a.contiguous().view(torch.uint8)
+    brows = _storage_rows(b).view(torch.uint8)
+    m, k = a.shape
+    n = brows.shape[0]
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    if m == 0 or n == 0:
+        return out
+    _lib.call(
+        "cdlb200_mm_mxfp8", _lib.ptr(a), _lib.ptr(brows), _lib.ptr(_flat(a_scale)), _lib.ptr(_flat(b_scale)),
+        None, m, n, k, _lib.ptr(out), n, None, _lib.stream(dev),
+    )
+    return out
+
+
+@mm_mxfp8.register_fake
+def _(a, b, a_scale, b_scale):
+    return torch.empty(a.shape[0], b.shape[1], dtype=torch.bfloat16, device=a.device)

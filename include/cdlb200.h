@@ -133,6 +133,37 @@ int cdlb200_mxfp8_dequant(const void* packed, const void* scale, const float* al
  */
 int cdlb200_swizzle_scales(const void* sf, int64_t m, int64_t b, void* out, void* stream);
 
+/*
+ * Block-scaled FP4 GEMM on the tcgen05 tensor cores:
+ *   out[m, n] = bf16(alpha * sum_k deq(a)[m, k] * deq(b)[n, k])
+ * Replaces cdl/model/wrapper/flashinfer.py:5-25 `cdl::mm_fp4` (FlashInfer
+ * mm_fp4, backend "b12x", sm_120 only) as called by cdl/core/mm/nvfp4.py:36-44
+ * and mxfp4.py:36-44.
+ *   a        packed e2m1 [m, k/2] row-major (16-byte aligned)
+ *   b        packed e2m1 [n, k/2] row-major, i.e. the storage of cdl's
+ *            [k/2, n] column-major `w_theta.T`
+ *   a_scale, b_scale  128x4-tiled scales of a and b (swizzle_scale_factors)
+ *   alpha    fp32 [1] device scalar (x_alpha * w_alpha), NULL = 1
+ *   block_size 16 with use_nvfp4 = 1 (e4m3 scales) or 32 with use_nvfp4 = 0
+ *            (e8m0 scales); k must be a multiple of 32
+ *   out      bf16 [m, ldo], ldo >= n
+ *   status   optional device uint32: set non-zero if a bounded wait timed out
+ */
+int cdlb200_mm_fp4(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                   const float* alpha, int64_t m, int64_t n, int64_t k, int block_size, int use_nvfp4,
+                   void* out, int64_t ldo, void* status, void* stream);
+
+/*
+ * Block-scaled MXFP8 GEMM (e4m3 elements, e8m0 scales, blocks of 32):
+ * replaces cdl/model/wrapper/flashinfer.py:41-52 `cdl::mm_mxfp8` as called by
+ * cdl/core/mm/mxfp8.py:36-51.  a: e4m3 [m, k], b: e4m3 [n, k] (storage of the
+ * [k, n] column-major view), scales 128x4-tiled, k a multiple of 16; alpha
+ * as above (cdl's op takes none: pass NULL).
+ */
+int cdlb200_mm_mxfp8(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                     const float* alpha, int64_t m, int64_t n, int64_t k, void* out, int64_t ldo,
+                     void* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
