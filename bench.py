@@ -2,25 +2,31 @@
 """Benchmark of the cdl_b200 hot path; prints ONE JSON line on rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload nvfp4_quant|mxfp4_quant|mxfp8_quant]
+                    [--workload nvfp4_quant|mxfp4_quant|mxfp8_quant|fp4_gemm|qat_135m|qat_1.7b]
 
-Default workload (``nvfp4_quant``): one step = NVFP4 quantize of one 4096x4096
-bf16 activation tensor (N(0,1), seed 0, 0.1% x20
-outliers; 16-element blocks, e4m3 scales, per-tensor alpha) through the
-public ``nvfp4_quant`` API.  Inputs cycle through a pool of distinct tensors
-totalling more than twice the 126 MB L2, so every step reads cold HBM.
-Metric: algorithmic GB/s = 2.5625 B/element (2 B read, 0.5 B codes, 1/16 B
-scales) x elements / time.
+Workloads (synthetic data everywhere):
 
-``value`` is timed with CUDA events over exactly K steps with the inputs
-resident in HBM (max over ranks; each rank quantizes its own tensors, so
-scaling is weak).  ``e2e`` is the same metric through the same API with the
-input in pinned host memory: every step copies it host->device, quantizes,
-and copies codes, scales and alpha back.
+* ``nvfp4_quant`` (default) -- one step = NVFP4 quantize of one 4096x4096
+  bf16 activation tensor (config C1: N(0,1), 0.1% x20 outliers) through the
+  public ``nvfp4_quant`` API.  Inputs cycle through a pool of distinct
+  tensors totalling more than twice the 126 MB L2, so every step reads cold
+  HBM.  Metric: algorithmic GB/s at 2.5625 B/element.
+* ``mxfp4_quant`` / ``mxfp8_quant`` -- config C2 shape [16384, 8192].
+* ``fp4_gemm`` -- config C3: NVFP4 GEMM 8192^3, one step = quantize the bf16
+  activations A (the GEMM prologue) + the tcgen05 block-scaled GEMM against
+  pre-quantized NVFP4 weights.  Metric: TFLOP/s (2 M N K per step).
+* ``qat_135m`` / ``qat_1.7b`` -- configs C4 / C5: one SmolLM2 NVFP4 QAT
+  training step (forward, backward, AdamW) on uniform random tokens; for
+  N > 1 data parallel with an NCCL bf16 gradient all-reduce.  Metric:
+  tokens/s over all ranks.
 
-``--impl reference`` times the CPU implementation of the path (the oracle in
-``oracle/``, a C restatement of cdl's torch quantize path, run on all host
-threads) on rank 0 for the same metric.
+Every step sequence is timed with CUDA events over exactly K steps with the
+inputs resident in HBM (max over ranks; each rank processes its own data, so
+scaling is weak).  ``e2e`` is the same metric through the same public API
+with host-resident inputs: each step copies its input host->device and its
+result back.  ``--impl reference`` times the CPU implementation of the path
+(``oracle/``, a C restatement of cdl's torch path, on all host threads) on
+rank 0.
 """
 
 from __future__ import annotations
@@ -39,26 +45,32 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 L2_BYTES = 126 * 1024 * 1024
-PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
-
-WORKLOADS = {
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+QUANT = {
     # name: (fmt, rows, k, bytes per element, config id)
     "nvfp4_quant": ("nvfp4", 4096, 4096, 2.5625, "C1"),
     "mxfp4_quant": ("mxfp4", 16384, 8192, 2.53125, "C2"),
     "mxfp8_quant": ("mxfp8", 16384, 8192, 3.03125, "C2"),
 }
+WORKLOADS = sorted(list(QUANT) + ["fp4_gemm", "qat_135m", "qat_1.7b"])
 
 
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="nvfp4_quant")
+    ap.add_argument("--workload", choices=WORKLOADS, default="nvfp4_quant")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--spinup-s", type=float, default=1.0, help="untimed clock ramp before warm-up")
-    return ap.parse_args()
+    a = ap.parse_args()
+    qat = a.workload.startswith("qat")
+    if a.steps is None:
+        a.steps = 10 if qat else (20 if a.workload == "fp4_gemm" else 200)
+    if a.warmup is None:
+        a.warmup = 3 if qat else 10
+    return a
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -108,11 +120,8 @@ class ClockSampler:
         time.sleep(0.25)
         self.proc.terminate()
         self.proc.wait()
-        rows = []
-        for line in open(self.path):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
+        rows = [[p.strip() for p in line.split(",")] for line in open(self.path)]
+        rows = [r for r in rows if len(r) >= 9]
         os.unlink(self.path)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
@@ -148,17 +157,13 @@ def cpu_quant_threads(x_bits, fmt_name: str, threads: int):
     if fmt == oracle.NVFP4:
         chunks = np.array_split(x_bits, threads)
         with concurrent.futures.ThreadPoolExecutor(threads) as ex:
-            gms = list(ex.map(lambda c: oracle.nvfp4_global(c)[0], chunks))
-        gmax = max(gms)
+            gmax = max(ex.map(lambda c: oracle.nvfp4_global(c)[0], chunks))
     parts = np.array_split(np.arange(x_bits.shape[0]), threads)
     with concurrent.futures.ThreadPoolExecutor(threads) as ex:
-        outs = list(ex.map(lambda idx: oracle.quant(x_bits[idx[0]: idx[-1] + 1], fmt, gmax), parts))
-    return outs
+        return list(ex.map(lambda idx: oracle.quant(x_bits[idx[0]: idx[-1] + 1], fmt, gmax), parts))
 
 
-def cpu_rate(fmt_name: str, rows: int, k: int, bpe: float, steps: int, warmup: int, threads: int,
-             target_s: float | None = None):
-    """(GB/s, sample description, seconds) of the oracle on a bounded sample."""
+def cpu_quant_rate(fmt_name, rows, k, bpe, steps, warmup, threads, target_s=None):
     import numpy as np
     import torch
 
@@ -173,167 +178,332 @@ def cpu_rate(fmt_name: str, rows: int, k: int, bpe: float, steps: int, warmup: i
     while n < steps or (target_s is not None and time.perf_counter() - t0 < target_s):
         cpu_quant_threads(bits, fmt_name, threads)
         n += 1
-        if target_s is not None and n >= steps and time.perf_counter() - t0 >= target_s:
-            break
     dt = time.perf_counter() - t0
-    gbs = bpe * rows * k * n / dt / 1e9
-    return gbs, f"{n} x {fmt_name} quantize of [{rows},{k}] bf16 ({threads} threads)", dt
+    return bpe * rows * k * n / dt / 1e9, f"{n} x {fmt_name} quantize of [{rows},{k}] bf16 ({threads} threads)"
+
+
+def cpu_gemm_rate(threads, target_s=10.0):
+    """Oracle NVFP4 GEMM (quantize A, dequantize, fp32 matmul) on a 2048^3 sample."""
+    import numpy as np
+    import torch
+
+    import oracle
+    from cdl_b200 import workloads
+
+    torch.set_num_threads(threads)
+    m = n = k = 2048
+    a, w = workloads.c3_gemm(m, n, k)
+    ab = a.view(torch.int16).numpy().view(np.uint16)
+    wb = w.view(torch.int16).numpy().view(np.uint16)
+    wp, ws, wa = oracle.quant(wb, oracle.NVFP4)
+    t0, cnt = time.perf_counter(), 0
+    while cnt < 1 or time.perf_counter() - t0 < target_s:
+        ap, as_, aa = oracle.quant(ab, oracle.NVFP4)
+        oracle.mm(ap, as_, wp, ws, oracle.NVFP4, float(aa[0] * wa[0]))
+        cnt += 1
+    dt = time.perf_counter() - t0
+    return (2.0 * m * n * k * cnt / dt / 1e12,
+            f"{cnt} x NVFP4 quantize(A) + dequantize + fp32 matmul at {m}^3 ({threads} threads)")
+
+
+def cpu_qat_rate(spec_name, threads, target_s=20.0):
+    """CPU restatement of the QAT step (unquantized, fp32 on CPU) at reduced size."""
+    import torch
+
+    from cdl_b200.train import qat
+
+    torch.set_num_threads(threads)
+    spec = qat.SPECS[spec_name]
+    step = qat.QatStep(spec, torch.device("cpu"), backend="none", seed=0)
+    step.model.float()
+    step.opt = torch.optim.AdamW(step.params, lr=3e-4, betas=(0.9, 0.95))
+    batch, seq = 1, 256
+    ids = qat.random_tokens(batch, seq, spec.vocab, seed=0, device=torch.device("cpu"))
+    step.step(ids)
+    t0, cnt = time.perf_counter(), 0
+    while cnt < 1 or time.perf_counter() - t0 < target_s:
+        step.step(ids)
+        cnt += 1
+    dt = time.perf_counter() - t0
+    return (batch * seq * cnt / dt,
+            f"{cnt} fp32 train steps of {spec.name} on {batch}x{seq} tokens ({threads} threads, unquantized)")
+
+
+# ---------------------------------------------------------------------------
+# GPU workloads
+# ---------------------------------------------------------------------------
+def quant_workload(name, dev, rank):
+    import torch
+
+    from cdl_b200 import workloads
+    from cdl_b200.core.kernel import quant
+
+    fmt, rows, k, bpe, cfg = QUANT[name]
+    qfn = {"nvfp4": quant.nvfp4_quant, "mxfp4": quant.mxfp4_quant, "mxfp8": quant.mxfp8_quant}[fmt]
+    in_bytes = rows * k * 2
+    pool_n = max(2, -(-2 * L2_BYTES // in_bytes))
+    gen = workloads.c1_nvfp4 if fmt == "nvfp4" else workloads.c2_mx
+    pool = [gen(rows, k, seed=1000 * rank + i, device=str(dev)) for i in range(pool_n)]
+    host_in = pool[0].cpu().pin_memory()
+    p0, s0, a0 = qfn(pool[0])
+    host_p = torch.empty(p0.shape, dtype=p0.dtype, pin_memory=True)
+    host_s = torch.empty(s0.shape, dtype=s0.dtype, pin_memory=True)
+    host_a = torch.empty(1, dtype=torch.float32, pin_memory=True)
+
+    def e2e_step():
+        p, s, a = qfn(host_in.to(dev, non_blocking=True))
+        host_p.copy_(p, non_blocking=True)
+        host_s.copy_(s, non_blocking=True)
+        if a is not None:
+            host_a.copy_(a, non_blocking=True)
+
+    return {
+        "step": lambda i: qfn(pool[i % pool_n]), "e2e_step": e2e_step, "graph": True,
+        "units_per_step": bpe * rows * k / 1e9, "unit": "GB/s", "metric": f"{fmt.upper()} quant GB/s",
+        "dtype": "bf16->e2m1/e4m3" if fmt != "mxfp8" else "bf16->e4m3/e8m0",
+        "config": {"workload": f"{name} {cfg} [{rows},{k}] bf16 per rank",
+                   "l2": f"inputs cycled over {pool_n} tensors ({pool_n * in_bytes >> 20} MiB > 2x L2)"},
+        "h2d": host_in.numel() * 2, "d2h": p0.numel() * p0.element_size() + s0.numel() + (4 if a0 is not None else 0),
+        "bound": "hbm", "kernel": "nvfp4_fused_kernel" if fmt == "nvfp4" else "quant_flat_kernel",
+        "launches_per_step": 1,
+    }
+
+
+def gemm_workload(dev, rank):
+    import torch
+
+    from cdl_b200 import workloads
+    from cdl_b200.core.kernel import quant
+    from cdl_b200.core.mm.swizzle import swizzle_scale_factors
+    from cdl_b200.model.wrapper.ops import mm_fp4
+
+    m = n = k = 8192
+    pool_n = 2  # 2 x (128 MiB bf16 A) > L2
+    pool = []
+    for i in range(pool_n):
+        a, w = workloads.c3_gemm(m, n, k, seed=100 * rank + i, device=str(dev))
+        pool.append(a)
+    wp, wsf, wal = quant.nvfp4_quant(w)
+    wsw = swizzle_scale_factors(wsf)
+
+    def step(i):
+        ap, asf, aal = quant.nvfp4_quant(pool[i % pool_n], swizzled=True)
+        return mm_fp4(ap, wp.T, asf, wsw.T, aal * wal, 16, True)
+
+    host_a = pool[0].cpu().pin_memory()
+    host_out = torch.empty(m, n, dtype=torch.bfloat16, pin_memory=True)
+
+    def e2e_step():
+        ap, asf, aal = quant.nvfp4_quant(host_a.to(dev, non_blocking=True), swizzled=True)
+        host_out.copy_(mm_fp4(ap, wp.T, asf, wsw.T, aal * wal, 16, True), non_blocking=True)
+
+    return {
+        "step": step, "e2e_step": e2e_step, "graph": True,
+        "units_per_step": 2.0 * m * n * k / 1e12, "unit": "TFLOP/s", "metric": "FP4 GEMM TFLOPS",
+        "dtype": "e2m1 x e2m1 (ue4m3 block scales) -> fp32 acc -> bf16",
+        "config": {"workload": f"fp4_gemm C3 NVFP4 {m}x{n}x{k}: quantize bf16 A + tcgen05 GEMM vs pre-quantized W",
+                   "l2": f"A cycled over {pool_n} tensors of 128 MiB (> L2)"},
+        "h2d": host_a.numel() * 2, "d2h": m * n * 2, "bound": "tensor",
+        "kernel": "bs_gemm_kernel<NVFP4> (+ nvfp4_fused_kernel prologue)", "launches_per_step": 3,
+    }
+
+
+def qat_workload(name, dev, rank, world):
+    import torch
+
+    from cdl_b200.train import qat
+
+    spec = qat.SPECS["135m" if name == "qat_135m" else "1.7b"]
+    batch, seq = (8, 2048) if name == "qat_135m" else (4, 2048)
+    step = qat.QatStep(spec, dev, backend="nvfp4", seed=0, ddp=world > 1)
+    pool = [qat.random_tokens(batch, seq, spec.vocab, seed=1000 * rank + i, device=dev) for i in range(4)]
+    host_ids = pool[0].cpu().pin_memory()
+    host_loss = torch.empty(1, dtype=torch.float32, pin_memory=True)
+
+    def e2e_step():
+        loss, _ = step.step(host_ids.to(dev, non_blocking=True))
+        host_loss.copy_(loss.float().reshape(1), non_blocking=True)
+
+    return {
+        "step": lambda i: step.step(pool[i % len(pool)]), "e2e_step": e2e_step, "graph": False,
+        "units_per_step": batch * seq, "unit": "tokens/s", "metric": "SmolLM2 NVFP4 QAT tokens/s",
+        "dtype": "nvfp4 fwd GEMMs (e2m1/ue4m3), bf16 bwd, bf16 params + AdamW",
+        "config": {"workload": f"{name} {'C4' if name == 'qat_135m' else 'C5'} {spec.name} QAT step, "
+                               f"{batch}x{seq} tokens per rank, AdamW lr 3e-4",
+                   "model": spec.name, "global_batch": batch * world, "seq_len": seq,
+                   "parallelism": f"dp{world}" if world > 1 else "single", "l2": "activations >> L2"},
+        "h2d": host_ids.numel() * 8, "d2h": 4, "bound": "tensor",
+        "flops_per_unit": qat.flops_per_token(spec, seq), "kernel": "full QAT step",
+        # per QLinear: quantize x and w, swizzle both scale sets, GEMM; backward: dequantize w and x
+        "launches_per_step": 7 * step.n_quant,
+    }
+
+
+def time_steps(w, steps, dev):
+    """Returns a callable running exactly `steps` steps (graph-captured when
+    the workload allows it) and the captured outputs to keep alive."""
+    import torch
+
+    if not w["graph"]:
+        def run():
+            for i in range(steps):
+                w["step"](i)
+
+        return run, None
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for i in range(3):
+            w["step"](i)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        outs = [w["step"](i) for i in range(steps)]
+    g.replay()
+    torch.cuda.synchronize()
+    return g.replay, (g, outs)
 
 
 # ---------------------------------------------------------------------------
 def main() -> None:
     args = parse_args()
-    fmt_name, rows, k, bpe, cfg = WORKLOADS[args.workload]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     threads = len(os.sched_getaffinity(0))
+    wl = args.workload
 
     if args.impl == "reference":
         if rank != 0:
             return
-        gbs, sample, _ = cpu_rate(fmt_name, rows, k, bpe, max(args.steps // 20, 3), min(args.warmup, 1), threads)
+        if wl in QUANT:
+            fmt, rows, k, bpe, cfg = QUANT[wl]
+            val, sample = cpu_quant_rate(fmt, rows, k, bpe, max(args.steps // 20, 3), min(args.warmup, 1), threads)
+            unit, metric = "GB/s", f"{fmt.upper()} quant GB/s"
+        elif wl == "fp4_gemm":
+            val, sample = cpu_gemm_rate(threads, target_s=5.0)
+            unit, metric = "TFLOP/s", "FP4 GEMM TFLOPS"
+        else:
+            val, sample = cpu_qat_rate("135m" if wl == "qat_135m" else "1.7b", threads, target_s=10.0)
+            unit, metric = "tokens/s", "SmolLM2 NVFP4 QAT tokens/s"
         print(json.dumps({
-            "impl": "reference", "metric": f"{args.workload.replace('_quant', '')} quant GB/s",
-            "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16->e2m1/e4m3", "data": "synthetic",
-            "config": {"workload": f"{args.workload} {cfg} [{rows},{k}] bf16"},
-            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                             "sample": sample},
-            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "impl": "reference", "metric": metric, "value": round(val, 4), "unit": unit, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "data": "synthetic", "config": {"workload": wl},
+            "cpu_baseline": {"value": round(val, 4), "unit": unit, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": round(val, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }), flush=True)
         return
 
     import torch
     import torch.distributed as dist
 
-    from cdl_b200 import workloads
-    from cdl_b200.core.kernel import quant
-
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    qfn = {"nvfp4": quant.nvfp4_quant, "mxfp4": quant.mxfp4_quant, "mxfp8": quant.mxfp8_quant}[fmt_name]
-    in_bytes = rows * k * 2
-    pool_n = max(2, -(-2 * L2_BYTES // in_bytes))
-    gen = workloads.c1_nvfp4 if fmt_name == "nvfp4" else workloads.c2_mx
-    pool = [gen(rows, k, seed=1000 * rank + i, device=str(dev)) for i in range(pool_n)]
-    alg_bytes = bpe * rows * k
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    if wl in QUANT:
+        w = quant_workload(wl, dev, rank)
+    elif wl == "fp4_gemm":
+        w = gemm_workload(dev, rank)
+    else:
+        w = qat_workload(wl, dev, rank, world)
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    # spin-up (clock ramp + sampler coverage), then W warm-up steps
-    sampler = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local])
-                           if os.environ.get("CUDA_VISIBLE_DEVICES") else local).start()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    sampler = ClockSampler(int(vis.split(",")[local]) if vis else local).start()
     t_end = time.time() + args.spinup_s
     i = 0
-    while time.time() < t_end:
-        qfn(pool[i % pool_n])
+    while time.time() < t_end and not wl.startswith("qat"):
+        w["step"](i)
         i += 1
-        if i % 64 == 0:
+        if i % 16 == 0:
             torch.cuda.synchronize()
     for i in range(args.warmup):
-        qfn(pool[i % pool_n])
+        w["step"](i)
     torch.cuda.synchronize()
 
-    # device-resident timed region: exactly K steps, captured in one CUDA graph
-    # (the API is capture-safe: no host sync, no cudaMalloc inside)
-    side = torch.cuda.Stream(dev)
-    side.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(side):
-        for i in range(3):
-            qfn(pool[i % pool_n])
-    torch.cuda.current_stream(dev).wait_stream(side)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        graph_outs = [qfn(pool[i % pool_n]) for i in range(args.steps)]
-    graph.replay()  # one full untimed replay on top of the W eager warm-up steps
-    torch.cuda.synchronize()
+    run, keep = time_steps(w, args.steps, dev)
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    graph.replay()
+    run()
     e1.record()
     torch.cuda.synchronize()
     barrier()
     ms = e0.elapsed_time(e1)
     clocks = sampler.stop()
-    del graph_outs
+    del keep, run
     ms_t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms_max = float(ms_t.item())
-    value = alg_bytes * args.steps * world / (ms_max / 1e3) / 1e9
+    value = w["units_per_step"] * args.steps * world / (ms_max / 1e3)
 
     # end to end through the public API with host buffers
-    host_in = pool[0].cpu().pin_memory()
-    p0, s0, a0 = qfn(pool[0])
-    host_p = torch.empty(p0.shape, dtype=p0.dtype, pin_memory=True)
-    host_s = torch.empty(s0.shape, dtype=s0.dtype, pin_memory=True)
-    host_a = torch.empty(1, dtype=torch.float32, pin_memory=True)
-    h2d = host_in.numel() * host_in.element_size()
-    d2h = p0.numel() * p0.element_size() + s0.numel() + (4 if a0 is not None else 0)
-    e2e_steps = max(3, min(args.steps, 50))
-
-    def e2e_step():
-        xd = host_in.to(dev, non_blocking=True)
-        p, s, a = qfn(xd)
-        host_p.copy_(p, non_blocking=True)
-        host_s.copy_(s, non_blocking=True)
-        if a is not None:
-            host_a.copy_(a, non_blocking=True)
-
-    for _ in range(3):
-        e2e_step()
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(2):
+        w["e2e_step"]()
     barrier()
     torch.cuda.synchronize()
     e0.record()
     for _ in range(e2e_steps):
-        e2e_step()
+        w["e2e_step"]()
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
     if world > 1:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = alg_bytes * e2e_steps * world / (float(e2e_ms.item()) / 1e3) / 1e9
+    e2e_value = w["units_per_step"] * e2e_steps * world / (float(e2e_ms.item()) / 1e3)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        gbs, sample, _ = cpu_rate(fmt_name, rows, k, bpe, 3, 1, threads, target_s=10.0)
-        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample}
+        if wl in QUANT:
+            fmt, rows, k, bpe, cfg = QUANT[wl]
+            val, sample = cpu_quant_rate(fmt, rows, k, bpe, 3, 1, threads, target_s=10.0)
+        elif wl == "fp4_gemm":
+            val, sample = cpu_gemm_rate(threads, target_s=10.0)
+        else:
+            val, sample = cpu_qat_rate("135m" if wl == "qat_135m" else "1.7b", threads, target_s=10.0)
+        cpu = {"value": round(val, 4), "unit": w["unit"], "cores": threads, "kind": "port", "sample": sample}
 
     peaks, peak_src = load_peaks()
     per_step_s = ms_max / 1e3 / args.steps
-    achieved = alg_bytes / per_step_s / 1e9
-    traffic = profile_traffic(args.workload)
-    launches_per_step = 1
+    if w["bound"] == "hbm":
+        achieved, peak, punit = w["units_per_step"] / per_step_s, peaks["hbm_gbs"], "GB/s"
+    elif wl == "fp4_gemm":
+        achieved, peak, punit = w["units_per_step"] / per_step_s, peaks["bf16_tflops"], "TFLOP/s"
+    else:
+        achieved = w["units_per_step"] * w["flops_per_unit"] / per_step_s / 1e12
+        peak, punit = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]), "TFLOP/s"
+    line = {
+        "metric": w["metric"], "value": round(value, 3), "unit": w["unit"], "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic",
+        "config": dict(w["config"], parallelism=w["config"].get("parallelism", f"replicas x{world}")),
+        "roofline": {"bound": w["bound"], "achieved": round(achieved, 2), "peak": peak, "unit": punit,
+                     "frac": round(achieved / peak, 4), "traffic": profile_traffic(wl),
+                     "peak_source": peak_src, "kernel": w["kernel"]},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_value, 3), "unit": w["unit"], "h2d_bytes_per_step": w["h2d"],
+                "d2h_bytes_per_step": w["d2h"]},
+        "gpu_launches": (w["launches_per_step"] * args.steps) if w["launches_per_step"] else None,
+        "clocks": clocks,
+    }
+    if wl == "fp4_gemm":
+        line["roofline"]["peak_note"] = ("denominator = measured cuBLAS bf16 peak (no measured FP4 peak; "
+                                         "nominal dense FP4 is 9 PFLOP/s)")
+    if wl.startswith("qat"):
+        line["roofline"]["peak_note"] = "model FLOPs (6P + 12 L d s per token) vs measured sustained bf16 peak"
     if rank == 0:
-        print(json.dumps({
-            "metric": f"{fmt_name.upper()} quant GB/s", "value": round(value, 2), "unit": "GB/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16->e2m1/e4m3" if fmt_name != "mxfp8" else "bf16->e4m3/e8m0",
-            "data": "synthetic",
-            "config": {"workload": f"{args.workload} {cfg} [{rows},{k}] bf16 per rank",
-                       "l2": f"inputs cycled over {pool_n} tensors ({pool_n * in_bytes >> 20} MiB > 2x L2)",
-                       "parallelism": f"replicas x{world}"},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
-                         "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                         "traffic": traffic, "peak_source": peak_src,
-                         "kernel": "nvfp4_fused_kernel" if fmt_name == "nvfp4" else "quant_flat_kernel"},
-            "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
-            "gpu_launches": launches_per_step * args.steps,
-            "clocks": clocks,
-        }), flush=True)
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
 

@@ -1,0 +1,5 @@
+"""``mxfp8`` backend: the drop-in for ``cdl.core.mm.mxfp8`` (cdl/core/mm/mxfp8.py:9)."""
+
+from cdl_b200.core.mm.blockscaled import make_matmul
+
+matmul = make_matmul("mxfp8")

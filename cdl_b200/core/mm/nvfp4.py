@@ -1,0 +1,5 @@
+"""``nvfp4`` backend: the drop-in for ``cdl.core.mm.nvfp4`` (cdl/core/mm/nvfp4.py:9)."""
+
+from cdl_b200.core.mm.blockscaled import make_matmul
+
+matmul = make_matmul("nvfp4")

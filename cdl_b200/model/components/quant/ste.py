@@ -1,0 +1,80 @@
+"""Straight-through-estimator quantizer, mirroring
+``cdl.model.components.quant.ste`` (cdl/model/components/quant/ste.py:13-89).
+
+``SteTensor`` quantizes its ``theta`` (flattened to 2-D) with the B200
+kernels under ``no_grad``; ``proxy()`` is ``theta`` itself, so gradients pass
+straight through (identity, no clipping mask); ``dequantize()`` serves the
+``native`` backend.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Literal
+
+import torch
+
+from cdl_b200.api.quant import QTensor, Quant
+from cdl_b200.core.kernel.dequant import mxfp4_dequant, mxfp8_dequant, nvfp4_dequant
+from cdl_b200.core.kernel.quant import mxfp4_quant, mxfp8_quant, nvfp4_quant
+
+Simulation = Literal["nvfp4", "mxfp4", "mxfp8"]
+
+
+@dataclass
+class SteTensor(QTensor):
+    theta: torch.Tensor
+    simulation: Simulation | None
+
+    @property
+    def leading_shape(self) -> torch.Size:
+        return self.theta.shape[:-1]
+
+    @property
+    def k(self) -> int:
+        return self.theta.shape[-1]
+
+    def _encode(self, fn):
+        with torch.no_grad():
+            packed, scale, alpha = fn(self.theta.reshape(-1, self.k))
+            packed = packed.reshape(*self.leading_shape, packed.shape[-1])
+            scale = scale.reshape(*self.leading_shape, scale.shape[-1])
+            return packed, scale, alpha
+
+    def nvfp4(self):
+        return self._encode(nvfp4_quant)
+
+    def mxfp4(self):
+        return self._encode(mxfp4_quant)
+
+    def mxfp8(self):
+        return self._encode(mxfp8_quant)
+
+    def dequantize(self) -> torch.Tensor:
+        if self.simulation is None:
+            return self.theta
+        if self.simulation == "nvfp4":
+            packed, scale, alpha = self.nvfp4()
+            fn = nvfp4_dequant
+        elif self.simulation == "mxfp4":
+            packed, scale, alpha = self.mxfp4()
+            fn = mxfp4_dequant
+        elif self.simulation == "mxfp8":
+            packed, scale, alpha = self.mxfp8()
+            fn = mxfp8_dequant
+        else:
+            raise ValueError(f"{self.simulation} is not supported")
+        out = fn(packed.reshape(-1, packed.shape[-1]), scale.reshape(-1, scale.shape[-1]), alpha)
+        return out.reshape(*self.leading_shape, out.shape[-1])[..., : self.k].to(self.theta.dtype)
+
+    def proxy(self) -> torch.Tensor | None:
+        return self.theta
+
+
+class SteQuant(Quant):
+    def __init__(self, simulation: Simulation | None):
+        super().__init__()
+        self.simulation = simulation
+
+    def forward(self, x: torch.Tensor) -> QTensor:
+        return SteTensor(theta=x, simulation=self.simulation)

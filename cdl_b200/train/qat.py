@@ -1,0 +1,166 @@
+"""SmolLM2 quantization-aware training step on the B200 path.
+
+Mirrors what cdl's training driver does per micro-batch (smollm2.py:667-677
+``lm_loss``, :638-659 ``_step_optimizer``, :408-424 ``apply_quant``): every
+``q/k/v/o/gate/up/down_proj`` linear of a Llama decoder becomes a
+``QLinear`` whose activation and weight pass through ``SteQuant`` and whose
+matmul backend is ``nvfp4`` (or ``mxfp4`` / ``mxfp8`` / ``native``); the loss
+is next-token cross entropy through the unquantized LM head; the optimizer
+is AdamW (betas 0.9/0.95) with gradient-norm clipping at 1.0.
+
+Models are built from the BASELINE configurations with random init (std
+0.02) -- no checkpoint is loaded -- and trained on uniform random tokens.
+
+Data parallel: one process per GPU; the model is wrapped in
+``DistributedDataParallel`` (NCCL), which all-reduces the bf16 gradients in
+buckets while the backward pass is still running.  Each rank quantizes its
+own activations (per-rank amax, as a single-GPU run would).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from cdl_b200.model.components.linear import QLinear
+from cdl_b200.model.components.quant.ste import SteQuant
+
+QUANT_TARGETS = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+
+
+@dataclass(frozen=True)
+class ModelSpec:
+    name: str
+    layers: int
+    hidden: int
+    heads: int
+    kv_heads: int
+    intermediate: int
+    vocab: int = 49152
+    rope_theta: float = 10000.0
+    tied: bool = True
+    max_pos: int = 8192
+
+
+SPECS = {
+    # SmolLM2-135M
+    "135m": ModelSpec("SmolLM2-135M", 30, 576, 9, 3, 1536, rope_theta=10000.0),
+    # SmolLM2-1.7B
+    "1.7b": ModelSpec("SmolLM2-1.7B", 24, 2048, 32, 32, 8192, rope_theta=130000.0),
+    # small stand-in for tests
+    "tiny": ModelSpec("tiny-llama", 2, 256, 4, 2, 512, vocab=1024, rope_theta=10000.0),
+}
+
+
+def build_model(spec: ModelSpec, device: torch.device, seed: int = 0) -> nn.Module:
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    cfg = LlamaConfig(
+        vocab_size=spec.vocab, hidden_size=spec.hidden, intermediate_size=spec.intermediate,
+        num_hidden_layers=spec.layers, num_attention_heads=spec.heads, num_key_value_heads=spec.kv_heads,
+        head_dim=spec.hidden // spec.heads, max_position_embeddings=spec.max_pos, rope_theta=spec.rope_theta,
+        rms_norm_eps=1e-5, tie_word_embeddings=spec.tied, initializer_range=0.02, hidden_act="silu",
+        attention_bias=False, mlp_bias=False, use_cache=False,
+    )
+    cfg._attn_implementation = "sdpa"
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = LlamaForCausalLM(cfg)
+    return model.to(dtype=torch.bfloat16)
+
+
+def apply_quant(model: nn.Module, backend: str = "nvfp4", simulation: str | None = None) -> int:
+    """Swap every target nn.Linear for an STE-quantized QLinear (smollm2.py:408-424).
+
+    ``backend="none"`` leaves the model unquantized (bf16 reference runs)."""
+    if backend == "none":
+        return 0
+    sim = simulation or (backend if backend.startswith("mx") else "nvfp4")
+    count = 0
+    for name, module in list(model.named_modules()):
+        parent_name, _, leaf = name.rpartition(".")
+        if leaf not in QUANT_TARGETS or not isinstance(module, nn.Linear):
+            continue
+        parent = model.get_submodule(parent_name) if parent_name else model
+        q = QLinear.from_linear(module)
+        q.set_activation_quant(SteQuant(sim))
+        q.set_weight_quant(SteQuant(sim))
+        q.set_backend(backend)
+        setattr(parent, leaf, q)
+        count += 1
+    return count
+
+
+def lm_loss(model: nn.Module, input_ids: torch.Tensor) -> torch.Tensor:
+    """Mean next-token cross entropy through the LM head (smollm2.py:667-677)."""
+    hidden = model.model(input_ids=input_ids, use_cache=False).last_hidden_state[:, :-1]
+    logits = model.lm_head(hidden.reshape(-1, hidden.shape[-1]))
+    return F.cross_entropy(logits.float(), input_ids[:, 1:].reshape(-1), reduction="mean")
+
+
+class LossModule(nn.Module):
+    """Model + loss as one module, so data parallelism wraps the whole forward."""
+
+    def __init__(self, model: nn.Module):
+        super().__init__()
+        self.model = model
+
+    def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
+        return lm_loss(self.model, input_ids)
+
+
+def flops_per_token(spec: ModelSpec, seq: int) -> float:
+    """6 * params + 12 * layers * hidden * seq (training FLOPs per token)."""
+    h, L = spec.hidden, spec.layers
+    kvd = spec.kv_heads * (h // spec.heads)
+    per_layer = h * h * 2 + 2 * h * kvd + 3 * h * spec.intermediate
+    params = L * per_layer + spec.vocab * h * (1 if spec.tied else 2)
+    return 6.0 * params + 12.0 * L * h * seq
+
+
+class QatStep:
+    """One QAT training step: forward, loss, backward (+ DP all-reduce), clip, AdamW."""
+
+    def __init__(self, spec: ModelSpec, device: torch.device, backend: str = "nvfp4", lr: float = 3e-4,
+                 grad_clip: float = 1.0, seed: int = 0, ddp: bool = False, bucket_mb: int = 64):
+        self.spec = spec
+        self.device = device
+        self.model = build_model(spec, device, seed)
+        self.n_quant = apply_quant(self.model, backend)
+        self.model.train()
+        params = [p for p in self.model.parameters() if p.requires_grad]
+        self.params = params
+        decay = [p for p in params if p.ndim > 1]
+        no_decay = [p for p in params if p.ndim <= 1]
+        self.opt = torch.optim.AdamW(
+            [{"params": decay, "weight_decay": 0.0}, {"params": no_decay, "weight_decay": 0.0}],
+            lr=lr, betas=(0.9, 0.95), foreach=True)
+        self.grad_clip = grad_clip
+        self.net = LossModule(self.model)
+        if ddp:
+            from torch.nn.parallel import DistributedDataParallel as DDP
+
+            self.net = DDP(self.net, device_ids=[device.index] if device.type == "cuda" else None,
+                           bucket_cap_mb=bucket_mb, gradient_as_bucket_view=True, static_graph=True)
+
+    def step(self, input_ids: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        loss = self.net(input_ids)
+        loss.backward()
+        gnorm = torch.nn.utils.clip_grad_norm_(self.params, self.grad_clip, foreach=True)
+        self.opt.step()
+        self.opt.zero_grad(set_to_none=True)
+        return loss.detach(), gnorm.detach()
+
+
+def random_tokens(batch: int, seq: int, vocab: int, seed: int, device: torch.device) -> torch.Tensor:
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    return torch.randint(0, vocab, (batch, seq), generator=g, device=device)
+
+
+def expected_initial_loss(spec: ModelSpec) -> float:
+    return math.log(spec.vocab)
