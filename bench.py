@@ -6,7 +6,10 @@
 
 Workloads (synthetic data everywhere):
 
-* ``nvfp4_quant`` (default) -- one step = NVFP4 quantize of one 4096x4096
+* ``qat_1.7b`` (default) -- config C5, see below.  At N=1 the line also
+  carries ``components``: the NVFP4 quantize GB/s (C1) and FP4 GEMM TFLOP/s
+  (C3 8192^3) of the other two BASELINE metrics, each with its roofline.
+* ``nvfp4_quant`` -- one step = NVFP4 quantize of one 4096x4096
   bf16 activation tensor (config C1: N(0,1), 0.1% x20 outliers) through the
   public ``nvfp4_quant`` API.  Inputs cycle through a pool of distinct
   tensors totalling more than twice the 126 MB L2, so every step reads cold
@@ -61,7 +64,9 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=WORKLOADS, default="nvfp4_quant")
+    ap.add_argument("--workload", choices=WORKLOADS, default="qat_1.7b")
+    ap.add_argument("--no-components", action="store_true",
+                    help="skip the N=1 component measurements (quantize GB/s, GEMM TFLOP/s)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--spinup-s", type=float, default=1.0, help="untimed clock ramp before warm-up")
     a = ap.parse_args()
@@ -364,6 +369,31 @@ def time_steps(w, steps, dev):
     return g.replay, (g, outs)
 
 
+def measure_component(name, dev, steps, warmup, peaks):
+    """Device-timed throughput and roofline of one kernel-level workload (N=1)."""
+    import torch
+
+    w = quant_workload(name, dev, 0) if name in QUANT else gemm_workload(dev, 0)
+    for i in range(warmup):
+        w["step"](i)
+    torch.cuda.synchronize()
+    run, keep = time_steps(w, steps, dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    del keep, run
+    value = w["units_per_step"] * steps / (ms / 1e3)
+    peak, punit = (peaks["hbm_gbs"], "GB/s") if w["bound"] == "hbm" else (peaks["bf16_tflops"], "TFLOP/s")
+    return {"metric": w["metric"], "value": round(value, 2), "unit": w["unit"], "steps": steps,
+            "ms_per_step": round(ms / steps, 5), "config": w["config"]["workload"],
+            "roofline": {"bound": w["bound"], "achieved": round(value, 2), "peak": peak, "unit": punit,
+                         "frac": round(value / peak, 4), "traffic": profile_traffic(name), "kernel": w["kernel"]},
+            "gpu_launches": w["launches_per_step"] * steps}
+
+
 # ---------------------------------------------------------------------------
 def main() -> None:
     args = parse_args()
@@ -502,6 +532,13 @@ def main() -> None:
                                          "nominal dense FP4 is 9 PFLOP/s)")
     if wl.startswith("qat"):
         line["roofline"]["peak_note"] = "model FLOPs (6P + 12 L d s per token) vs measured sustained bf16 peak"
+    if world == 1 and wl.startswith("qat") and not args.no_components:
+        line["components"] = {
+            "nvfp4_quant": measure_component("nvfp4_quant", dev, 200, 10, peaks),
+            "fp4_gemm": measure_component("fp4_gemm", dev, 20, 5, peaks),
+        }
+        line["components"]["fp4_gemm"]["roofline"]["peak_note"] = (
+            "denominator = measured cuBLAS bf16 peak (no measured FP4 peak; nominal dense FP4 is 9 PFLOP/s)")
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
