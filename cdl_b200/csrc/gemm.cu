@@ -41,7 +41,8 @@ constexpr int kSfAtomBytes = 512;               // 128 rows x 4 scale bytes
 constexpr int kSfStageBytes = 4 * kSfAtomBytes;  // up to 4 atoms per K tile
 constexpr int kStageBytes = 2 * kTileBytes + 2 * kSfStageBytes;
 constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 256;  // 128 accumulator + 16 SFA + 16 SFB (power of 2)
+constexpr int kSfBufs = 4;  // scale-factor TMEM buffers, rotated per K tile
+constexpr uint32_t kTmemCols = 256;  // 128 accumulator + 4 x 16 SFA + 4 x 16 SFB
 constexpr uint32_t kSpinLimit = 1u << 20;
 
 enum Kind : int { kNv = 0, kMx4 = 1, kMx8 = 2 };
@@ -219,7 +220,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_base_s;
-    const uint32_t tmem_acc = tmem, tmem_sfa = tmem + 128, tmem_sfb = tmem + 144;
+    // scale factors live in kSfBufs rotating 16-column buffers, so the copy for
+    // a K tile never overwrites columns that the previous tile's MMAs read
+    const uint32_t tmem_acc = tmem, tmem_sfa0 = tmem + 128, tmem_sfb0 = tmem + 128 + 16 * kSfBufs;
 
     // K tile kt holds kbytes_in_tile bytes of each row; the last may be partial
     auto tile_mmas = [&](int kt) {
@@ -264,6 +267,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const int nmma = tile_mmas(kt), natoms = tile_atoms(nmma);
                 const uint32_t st = smem_addr(smem + (size_t)s * kStageBytes);
+                const uint32_t tmem_sfa = tmem_sfa0 + 16u * (uint32_t)(kt % kSfBufs);
+                const uint32_t tmem_sfb = tmem_sfb0 + 16u * (uint32_t)(kt % kSfBufs);
                 for (int a = 0; a < natoms; ++a) {
                     const uint64_t dsa = desc_sf_atom(st + 2 * kTileBytes + a * kSfAtomBytes);
                     const uint64_t dsb = desc_sf_atom(st + 2 * kTileBytes + kSfStageBytes + a * kSfAtomBytes);
