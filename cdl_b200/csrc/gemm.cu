@@ -295,12 +295,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {  // ---- epilogue warps 2..5
         const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
-        const bool ok = mbar_wait(&acc_bar, 0);
+        bool ok = mbar_wait(&acc_bar, 0);
         if (!ok) atomicExch(&abort_s, 1);
+        ok = __all_sync(0xffffffffu, ok && !*(volatile int*)&abort_s);  // tcgen05.ld is warp-collective
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const float alpha = args.alpha ? *args.alpha : 1.0f;
         const int row = m0 + 32 * q + lane;
-        if (ok && !*(volatile int*)&abort_s) {
+        if (ok) {
 #pragma unroll 1
             for (int c0 = 0; c0 < kBN; c0 += 32) {
                 uint32_t v[32];
@@ -352,6 +353,448 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Pair kernel: two CTAs of a cluster (one per SM) compute a 256 x 256 tile
+// with cta_group::2 MMAs (M = 256, N = 256).  CTA rank r holds rows
+// [m0 + 128 r, +128) of A and rows [n0 + 128 r, +128) of B in its shared
+// memory; the tensor cores of the pair read both halves of B, so every SM
+// loads 32 KiB per K tile instead of the 48 KiB a single-SM 128 x 256 tile
+// needs -- the TMA engine of one SM is what bounds this GEMM.
+//
+// Scale factors do not go through the tensor-memory copy engine (whose
+// per-instruction cost would exceed the MMA time at N = 256): the four
+// epilogue warps write them into TMEM with tcgen05.st while the MMAs of the
+// previous stages run.  Layout the block-scaled MMA reads (M = 128 per SM):
+//   A row r       -> TMEM lane r,              column tsfa + r/32
+//   B column n    -> lane 32 (r/32) + n % 32,  column tsfb + n/32
+// i.e. each lane quarter needs every column's B scales; one 4-byte cell holds
+// the scales of four consecutive K blocks (the sf_id selects the byte for the
+// MX kinds).  Warp q (lanes 32q..32q+31) therefore stores, per cell, its own
+// A scales in all four columns of the cell and both 128-column B atoms' rows.
+//
+// Barriers: full[s] lives in the leader (rank 0) and collects the A/B TMA
+// bytes of both CTAs; sfdata[s] is local (this CTA's scale bytes landed);
+// sffull[s] (leader) collects one arrival per CTA once its scales are in
+// TMEM; empty[s] and acc_full are signalled in both CTAs by a multicast
+// tcgen05.commit of the leader.  No TMA load uses multicast.
+// ---------------------------------------------------------------------------
+constexpr int k2Stages = 4;
+constexpr int k2TileBytes = 128 * kBKBytes;                     // 16 KiB
+constexpr int k2SfaBytes = 4 * kSfAtomBytes;                    // 2 KiB
+constexpr int k2SfbBytes = 8 * kSfAtomBytes;                    // 4 KiB: two 128-column blocks
+constexpr int k2StageBytes = 2 * k2TileBytes + k2SfaBytes + k2SfbBytes;  // 38 KiB
+constexpr int k2OutBytes = 128 * 256 * 2;  // bf16 staging of one CTA's 128 x 256 output tile
+// TMEM columns: accumulator [0, 256); per stage s the B scales at 256 + 32 s
+// (32 columns) and the A scales at 416 + 16 s (16 columns), so every
+// tcgen05.st / MMA scale address is aligned to its width.
+constexpr uint32_t k2TmemCols = 512;
+constexpr uint32_t k2SfbCol0 = 256, k2SfaCol0 = 256 + 32 * k2Stages;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// shared::cluster address of the same shared variable in CTA `rank`
+__device__ __forceinline__ uint32_t map_rank(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_addr(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(bar_cluster)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_addr(bar)),
+        "h"((uint16_t)3)
+        : "memory");
+}
+
+template <int KIND>
+__device__ __forceinline__ void mma_issue_pair(uint32_t tmem_c, uint64_t da, uint64_t db, uint32_t idesc, uint32_t tsfa,
+                                               uint32_t tsfb, uint32_t accumulate) {
+    if constexpr (KIND == kNv) {
+        asm volatile(
+            "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+            "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n}" ::"r"(
+                tmem_c),
+            "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb));
+    } else if constexpr (KIND == kMx4) {
+        asm volatile(
+            "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+            "tcgen05.mma.cta_group::2.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n}" ::"r"(
+                tmem_c),
+            "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb));
+    } else {
+        asm volatile(
+            "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+            "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n}" ::"r"(
+                tmem_c),
+            "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb));
+    }
+}
+
+template <int KIND>
+__device__ __forceinline__ uint32_t instr_desc_pair(uint32_t sf_id) {
+    using T = KindTraits<KIND>;
+    uint32_t d = 0;
+    d |= (sf_id & 3u) << 4;
+    d |= (uint32_t)T::kFmt << 7;
+    d |= (uint32_t)T::kFmt << 10;
+    d |= (uint32_t)(256 >> 3) << 17;  // N = 256
+    d |= (uint32_t)T::kSfFmt << 23;
+    d |= (uint32_t)(256 >> 4) << 24;  // M = 256 (128 per CTA)
+    d |= (sf_id & 3u) << 29;
+    return d;
+}
+
+// tcgen05.st.32x32b of N consecutive columns (one 32-bit value per lane and column).
+template <int N>
+__device__ __forceinline__ void tmem_st(uint32_t addr, const uint32_t* r);
+template <>
+__device__ __forceinline__ void tmem_st<4>(uint32_t addr, const uint32_t* r) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(r[0]), "r"(r[1]), "r"(r[2]),
+                 "r"(r[3])
+                 : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_st<8>(uint32_t addr, const uint32_t* r) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(addr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_st<16>(uint32_t addr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            addr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_st<32>(uint32_t addr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(addr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+// Scales of one K tile (CELLS 4-byte cells) for this warp's 32 lanes: A cell g
+// in columns ta + 4g .. +3 (the MMA reads column ta + 4g + quarter), B cell g
+// of the two 128-column blocks in columns tb + 8g .. +7.
+template <int CELLS>
+__device__ __forceinline__ void store_scales(uint32_t ta, uint32_t tb, const uint32_t (&a)[4], const uint4 (&b)[8]) {
+    uint32_t ra[4 * CELLS], rb[8 * CELLS];
+#pragma unroll
+    for (int g = 0; g < CELLS; ++g) {
+        ra[4 * g] = ra[4 * g + 1] = ra[4 * g + 2] = ra[4 * g + 3] = a[g];
+        rb[8 * g + 0] = b[2 * g].x;
+        rb[8 * g + 1] = b[2 * g].y;
+        rb[8 * g + 2] = b[2 * g].z;
+        rb[8 * g + 3] = b[2 * g].w;
+        rb[8 * g + 4] = b[2 * g + 1].x;
+        rb[8 * g + 5] = b[2 * g + 1].y;
+        rb[8 * g + 6] = b[2 * g + 1].z;
+        rb[8 * g + 7] = b[2 * g + 1].w;
+    }
+    tmem_st<4 * CELLS>(ta, ra);
+    tmem_st<8 * CELLS>(tb, rb);
+}
+
+// OR of `v` over the 128 threads of named barrier ID (one four-warp group).
+template <int ID>
+__device__ __forceinline__ bool group_any(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n.reg .pred p, q;\nsetp.ne.u32 p, %1, 0;\nbar.red.or.pred q, %2, 128, p;\nselp.u32 %0, 1, 0, q;\n}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(ID)
+        : "memory");
+    return r != 0;
+}
+
+template <int ID>
+__device__ __forceinline__ void group_sync() {
+    asm volatile("bar.sync %0, 128;" ::"n"(ID) : "memory");
+}
+
+__device__ __forceinline__ void arrive_remote(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+// 2-D TMA store of a 64-column x 128-row bf16 box (128-byte swizzled in shared
+// memory); the tensor map clips rows and columns outside the output.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int x, int y, const void* src) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(x),
+                 "r"(y), "r"(smem_addr(src))
+                 : "memory");
+}
+
+constexpr int k2Threads = 320;  // warp 0 TMA, 1 MMA, 2-5 scale factors, 6-9 epilogue
+
+// Persistent: cluster c (of gridDim.x / 2) computes pair tiles c, c + C, c + 2C, ...
+// (row-major over 256 x 256 tiles).  The shared-memory stage ring and the
+// scale-factor TMEM buffers run on across tiles; the epilogue warps drain the
+// accumulator into registers, release it (acc_empty) and store while the
+// MMAs of the next tile already run.
+template <int KIND>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
+    bs_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                        const __grid_constant__ CUtensorMap map_out, const GemmArgs args, int tiles_n,
+                        int tiles_total) {
+    using T = KindTraits<KIND>;
+    constexpr int kMmaPerTile = (kBKBytes * (KIND == kMx8 ? 1 : 2)) / T::kKmma;  // 4
+    constexpr int kSfPerMma = T::kKmma / T::kVec;                               // scale bytes per row per MMA
+    constexpr int kCells = kMmaPerTile * kSfPerMma / 4;                         // 4-byte cells per K tile
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    __shared__ __align__(8) uint64_t full_bar[k2Stages], empty_bar[k2Stages], sfdata_bar[k2Stages], sffull_bar[k2Stages],
+        acc_full, acc_empty, done_bar;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int abort_s;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const int cluster = (int)(blockIdx.x >> 1), nclusters = (int)(gridDim.x >> 1);
+    const int my_tiles = cluster < tiles_total ? (tiles_total - 1 - cluster) / nclusters + 1 : 0;
+    const int nk = (args.kbytes + kBKBytes - 1) / kBKBytes;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < k2Stages; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+            mbar_init(&sfdata_bar[s], 1);
+            mbar_init(&sffull_bar[s], 2);
+        }
+        mbar_init(&acc_full, 1);
+        mbar_init(&acc_empty, 2);
+        mbar_init(&done_bar, 1);
+        abort_s = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base_s)),
+                     "r"(k2TmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base_s;
+
+    auto tile_origin = [&](int i, int& m0, int& n0) {
+        const int t = cluster + i * nclusters;
+        n0 = (t % tiles_n) * 256;
+        m0 = (t / tiles_n) * 256;
+    };
+    auto tile_mmas = [&](int kt) {
+        const int kb = args.kbytes - kt * kBKBytes < kBKBytes ? args.kbytes - kt * kBKBytes : kBKBytes;
+        const int kel = kb * (KIND == kMx8 ? 1 : 2);
+        return (kel + T::kKmma - 1) / T::kKmma;
+    };
+    auto tile_atoms = [&](int nmma) { return (nmma * kSfPerMma + 3) / 4; };
+    auto aborted = [&]() { return *(volatile int*)&abort_s != 0; };
+
+    if (warp == 0) {
+        if (lane == 0) {  // ---- TMA producer (both CTAs)
+            const uint32_t full0 = map_rank(&full_bar[0], 0);
+            int g = 0;
+            for (int i = 0; i < my_tiles && !aborted(); ++i) {
+                int m0, n0;
+                tile_origin(i, m0, n0);
+                const int mblk = (m0 >> 7) + (int)rank, nblk = n0 >> 7;
+                const bool a_ok = mblk * 128 < args.m;
+                const bool b0_ok = nblk * 128 < args.n, b1_ok = (nblk + 1) * 128 < args.n;
+                for (int kt = 0; kt < nk; ++kt, ++g) {
+                    const int s = g % k2Stages;
+                    const uint32_t ph = (uint32_t)(g / k2Stages) & 1u;
+                    if (!mbar_wait(&empty_bar[s], ph ^ 1u)) atomicExch(&abort_s, 1);
+                    if (aborted()) break;
+                    uint8_t* st = smem + (size_t)s * k2StageBytes;
+                    if (rank == 0) mbar_expect_tx(&full_bar[s], 4u * k2TileBytes);
+                    tma_load_2d_pair(st, &map_a, kt * kBKBytes, m0 + 128 * (int)rank, full0 + 8u * s);
+                    tma_load_2d_pair(st + k2TileBytes, &map_b, kt * kBKBytes, n0 + 128 * (int)rank, full0 + 8u * s);
+                    const int natoms = tile_atoms(tile_mmas(kt));
+                    const uint32_t sfb = (uint32_t)(natoms * kSfAtomBytes);
+                    mbar_expect_tx(&sfdata_bar[s], (a_ok ? sfb : 0u) + (b0_ok ? sfb : 0u) + (b1_ok ? sfb : 0u));
+                    uint8_t* sf = st + 2 * k2TileBytes;
+                    const size_t at = (size_t)kt * kCells;
+                    if (a_ok)
+                        bulk_load(sf, args.sfa + ((size_t)mblk * args.c4a + at) * kSfAtomBytes, sfb, &sfdata_bar[s]);
+                    if (b0_ok)
+                        bulk_load(sf + k2SfaBytes, args.sfb + ((size_t)nblk * args.c4b + at) * kSfAtomBytes, sfb,
+                                  &sfdata_bar[s]);
+                    if (b1_ok)
+                        bulk_load(sf + k2SfaBytes + 4 * kSfAtomBytes,
+                                  args.sfb + ((size_t)(nblk + 1) * args.c4b + at) * kSfAtomBytes, sfb, &sfdata_bar[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (rank == 0 && lane == 0) {  // ---- MMA issuer (leader CTA only)
+            int g = 0;
+            for (int i = 0; i < my_tiles && !aborted(); ++i) {
+                // both CTAs' epilogues have drained the accumulator of tile i - 1
+                if (i > 0 && !mbar_wait(&acc_empty, (uint32_t)(i - 1) & 1u)) {
+                    atomicExch(&abort_s, 1);
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                for (int kt = 0; kt < nk; ++kt, ++g) {
+                    const int s = g % k2Stages;
+                    const uint32_t ph = (uint32_t)(g / k2Stages) & 1u;
+                    if (!mbar_wait(&full_bar[s], ph) || !mbar_wait(&sffull_bar[s], ph)) {
+                        atomicExch(&abort_s, 1);
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const int nmma = tile_mmas(kt);
+                    const uint32_t st = smem_addr(smem + (size_t)s * k2StageBytes);
+                    const uint32_t tsfa0 = tmem + k2SfaCol0 + 16u * (uint32_t)s;
+                    const uint32_t tsfb0 = tmem + k2SfbCol0 + 32u * (uint32_t)s;
+                    for (int kk = 0; kk < nmma; ++kk) {
+                        const uint64_t da = desc_sw128(st + kk * 32);
+                        const uint64_t db = desc_sw128(st + k2TileBytes + kk * 32);
+                        const uint32_t sfi = (uint32_t)(kk * kSfPerMma);
+                        const uint32_t cell = sfi >> 2, byte = sfi & 3u;
+                        mma_issue_pair<KIND>(tmem, da, db, instr_desc_pair<KIND>(byte),
+                                             (tsfa0 + 4u * cell) | (byte << 30), (tsfb0 + 8u * cell) | (byte << 30),
+                                             (kt > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    mma_commit_pair(&empty_bar[s]);
+                }
+                if (aborted()) break;
+                mma_commit_pair(&acc_full);
+            }
+            mma_commit_pair(&done_bar);  // completes once every MMA issued above has
+        }
+    } else if (warp < 6) {  // ---- warps 2..5: scale factors into TMEM
+        const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
+        const uint32_t lane_off = (uint32_t)(32 * q) << 16;
+        const uint32_t sffull0 = map_rank(&sffull_bar[0], 0);
+        const int total = my_tiles * nk;
+        for (int g = 0; g < total; ++g) {
+            const int s = g % k2Stages, kt = g % nk;
+            const uint32_t ph = (uint32_t)(g / k2Stages) & 1u;
+            bool ok = mbar_wait(&sfdata_bar[s], ph);
+            // the MMAs that last read this stage's scale columns have completed
+            if (ok && g >= k2Stages) ok = mbar_wait(&empty_bar[s], ph ^ 1u);
+            if (!ok) atomicExch(&abort_s, 1);
+            if (group_any<1>(!ok || aborted())) break;  // the four warps leave together
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            (void)kt;
+            const uint8_t* sf = smem + (size_t)s * k2StageBytes + 2 * k2TileBytes;
+            uint32_t a[4];
+            uint4 b[8];
+#pragma unroll
+            for (int c = 0; c < kCells; ++c) {
+                a[c] = *reinterpret_cast<const uint32_t*>(sf + c * kSfAtomBytes + 16 * lane + 4 * q);
+                b[2 * c] = *reinterpret_cast<const uint4*>(sf + k2SfaBytes + c * kSfAtomBytes + 16 * lane);
+                b[2 * c + 1] = *reinterpret_cast<const uint4*>(sf + k2SfaBytes + (4 + c) * kSfAtomBytes + 16 * lane);
+            }
+            store_scales<kCells>(tmem + lane_off + k2SfaCol0 + 16u * (uint32_t)s,
+                                 tmem + lane_off + k2SfbCol0 + 32u * (uint32_t)s, a, b);
+            // the stores are complete once wait::st returns; a relaxed arrive is
+            // enough to publish them (a cluster-scope release would also wait
+            // for this CTA's in-flight TMA loads, ~1 us per K tile)
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            group_sync<1>();
+            if (threadIdx.x == 64) arrive_remote(sffull0 + 8u * s);
+        }
+    } else {  // ---- warps 6..9: epilogue, 128 rows x 256 columns of this CTA per tile
+        const int q = warp & 3;
+        const int r = 32 * q + lane;  // row of the tile = TMEM lane
+        const uint32_t lane_off = (uint32_t)(32 * q) << 16;
+        const uint32_t acc_empty0 = map_rank(&acc_empty, 0);
+        const float alpha = args.alpha ? *args.alpha : 1.0f;
+        // staging: four 64-column blocks of 128 rows x 128 bytes, 16-byte chunk c
+        // of row r at chunk c ^ (r & 7) (the TMA 128-byte swizzle)
+        uint8_t* out_s = smem + (size_t)k2Stages * k2StageBytes;
+        for (int i = 0; i < my_tiles; ++i) {
+            const bool ok = mbar_wait(&acc_full, (uint32_t)i & 1u);
+            if (!ok) atomicExch(&abort_s, 1);
+            // the TMA stores of tile i - 1 have finished reading the staging buffer
+            if (threadIdx.x == 192) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+            if (group_any<2>(!ok || aborted())) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll 1
+            for (int c = 0; c < 8; ++c) {  // 32 columns per step
+                uint32_t v[32];
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                      "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+                      "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]),
+                      "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]),
+                      "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+                    : "r"(tmem + lane_off + (uint32_t)(32 * c)));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                uint32_t pk[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const float lo = __fmul_rn(u2f(v[2 * j]), alpha), hi = __fmul_rn(u2f(v[2 * j + 1]), alpha);
+                    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(pk[j]) : "f"(hi), "f"(lo));
+                }
+                uint8_t* blk = out_s + (c >> 1) * (128 * 128) + r * 128;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {  // 16-byte chunks (c & 1) * 4 + j of the 128-byte row
+                    const int chunk = ((c & 1) * 4 + j) ^ (r & 7);
+                    *reinterpret_cast<uint4*>(blk + chunk * 16) =
+                        make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+                }
+            }
+            // accumulator drained: the next tile's MMAs may overwrite it
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // staging visible to the TMA engine
+            group_sync<2>();
+            if (threadIdx.x == 192) {
+                arrive_remote(acc_empty0);
+                int m0, n0;
+                tile_origin(i, m0, n0);
+                const int y = m0 + 128 * (int)rank;
+                if (y < args.m) {
+                    for (int b = 0; b < 4; ++b)
+                        if (n0 + 64 * b < args.n) tma_store_2d(&map_out, n0 + 64 * b, y, out_s + b * (128 * 128));
+                }
+                asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            }
+        }
+        if (threadIdx.x == 192) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // output written
+    }
+
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x == 0 && abort_s && args.status) atomicExch(args.status, 1u);
+    if (warp == 1) (void)mbar_wait(&done_bar, 0);  // every MMA of the pair has completed
+    cluster_sync_all();  // neither CTA touches the other's barriers or TMEM any more
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(k2TmemCols) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -383,6 +826,20 @@ bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t row_byte
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// bf16 output [rows, cols] with row pitch ldo elements, 64-column x 128-row
+// boxes, 128-byte swizzle (the layout the pair kernel stages its tile in).
+bool make_out_map(CUtensorMap* map, void* base, int64_t rows, int64_t cols, int64_t ldo) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ldo * 2)};
+    cuuint32_t box[2] = {64u, 128u};
+    cuuint32_t estr[2] = {1u, 1u};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int KIND>
 int launch_gemm(const void* a, const void* b, const void* sfa, const void* sfb, const float* alpha, int64_t m,
                 int64_t n, int64_t k, void* out, int64_t ldo, void* status, cudaStream_t st) {
@@ -410,6 +867,27 @@ int launch_gemm(const void* a, const void* b, const void* sfa, const void* sfb, 
     const int64_t nb = (k + T::kVec - 1) / T::kVec;
     args.c4a = args.c4b = (int)((nb + 3) / 4);
     args.status = static_cast<uint32_t*>(status);
+    // pair kernel: 256 x 256 tiles on SM pairs (its TMA store needs a 16-byte
+    // aligned output with a row pitch that is a multiple of 16 bytes)
+    CUtensorMap mo;
+    if (n > kBN && ((reinterpret_cast<uintptr_t>(out) & 15u) == 0) && (ldo % 8) == 0 &&
+        make_out_map(&mo, out, m, n, ldo)) {
+        static bool pair_attr_set[3] = {false, false, false};
+        const int smem2 = k2Stages * k2StageBytes + k2OutBytes + 1024;
+        if (!pair_attr_set[KIND]) {
+            if (cudaFuncSetAttribute(bs_gemm_pair_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2) !=
+                cudaSuccess)
+                return CDLB200_ERR_CUDA;
+            pair_attr_set[KIND] = true;
+        }
+        const int64_t tiles_n = (n + 255) / 256, tiles_m = (m + 255) / 256, tiles = tiles_n * tiles_m;
+        if (tiles > (int64_t)INT32_MAX) return CDLB200_ERR_INVALID_ARG;
+        const int64_t clusters = tiles < num_sms() / 2 ? tiles : num_sms() / 2;
+        bs_gemm_pair_kernel<KIND><<<(unsigned)(2 * clusters), k2Threads, smem2, st>>>(ma, mb, mo, args, (int)tiles_n,
+                                                                                           (int)tiles);
+        CDLB200_CHECK_LAUNCH();
+        return CDLB200_OK;
+    }
     dim3 grid((unsigned)((n + kBN - 1) / kBN), (unsigned)((m + kBM - 1) / kBM));
     bs_gemm_kernel<KIND><<<grid, kThreads, smem, st>>>(ma, mb, args);
     CDLB200_CHECK_LAUNCH();

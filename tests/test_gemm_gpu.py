@@ -44,7 +44,9 @@ def _rel_l2(x, y):
 
 
 @pytest.mark.parametrize("fmt_name", ["nvfp4", "mxfp4", "mxfp8"])
-@pytest.mark.parametrize("shape", [(128, 128, 256), (256, 384, 512), (200, 136, 576), (512, 1024, 2048)])
+@pytest.mark.parametrize("shape", [(128, 128, 256), (256, 384, 512), (200, 136, 576), (512, 1024, 2048),
+                                   (384, 520, 1088), (64, 300, 4096), (1000, 2048, 1024),
+                                   (2300, 2600, 320)])
 def test_gemm_vs_oracle(fmt_name, shape):
     got, ref = _run(fmt_name, *shape)
     ref_bf16 = torch.from_numpy(ref).bfloat16().float().numpy()
