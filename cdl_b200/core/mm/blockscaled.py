@@ -4,9 +4,18 @@
 Forward: both operands are quantized by the B200 kernels, their scales
 swizzled into the 128x4 GEMM layout, and the tcgen05 block-scaled GEMM
 produces bf16 ``alpha * deq(x) @ deq(w)^T`` (MXFP8 applies alpha outside the
-GEMM, as cdl does).  Backward, as cdl: ``dx = g @ deq(w)``, ``dw = g^T @
-deq(x)`` with bf16 operands (the straight-through estimator: gradients flow
-to the unquantized proxies).
+GEMM, as cdl does).
+
+Backward, two variants (the straight-through estimator in both: gradients
+flow to the unquantized proxies):
+
+* reference numerics (backends ``nvfp4`` / ``mxfp4`` / ``mxfp8``), as cdl:
+  ``dx = g @ deq(w)``, ``dw = g^T @ deq(x)`` with bf16 operands;
+* quantized backward (backends ``*_qbwd``): the dgrad and wgrad GEMMs run in
+  the same block-scaled format on the tensor cores --
+  ``dx = Q(g) . Q(w^T)^T`` (both quantized along N) and
+  ``dw = Q(g^T) . Q(x^T)^T`` (both quantized along M, the transposed
+  requantize) -- so all three GEMMs of a linear layer are FP4 (FP8).
 """
 
 from __future__ import annotations
@@ -15,16 +24,43 @@ import torch
 
 from cdl_b200.api.quant import QTensor
 from cdl_b200.core.kernel.dequant import mxfp4_dequant, mxfp8_dequant, nvfp4_dequant
+from cdl_b200.core.kernel.quant import mxfp4_quant, mxfp8_quant, nvfp4_quant
 from cdl_b200.core.mm.swizzle import expand_rows, pad_k, pad_n, swizzle_scale_factors
 from cdl_b200.model.wrapper.ops import mm_fp4, mm_mxfp8
 
 _DEQ = {"nvfp4": nvfp4_dequant, "mxfp4": mxfp4_dequant, "mxfp8": mxfp8_dequant}
+_QUANT = {"nvfp4": nvfp4_quant, "mxfp4": mxfp4_quant, "mxfp8": mxfp8_quant}
+
+
+def _qmm(fmt: str, a, b) -> torch.Tensor:
+    """``alpha * deq(a) @ deq(b)^T`` for two ``(codes, swizzled scales, alpha)``
+    triples quantized along their common last dimension."""
+    (ap, asf, aal), (bp, bsf, bal) = a, b
+    if fmt == "mxfp8":
+        return mm_mxfp8(ap.view(torch.uint8), bp.view(torch.uint8).T, asf.flatten(), bsf.flatten())
+    return mm_fp4(ap, bp.T, asf, bsf.T, aal * bal, 16 if fmt == "nvfp4" else 32, fmt == "nvfp4")
+
+
+def _quantized_grads(fmt: str, g: torch.Tensor, x: torch.Tensor | None, w: torch.Tensor | None):
+    """dgrad / wgrad of ``g = d(x @ w^T)`` with both GEMMs in ``fmt``."""
+    q = _QUANT[fmt]
+    dx = dw = None
+    if w is not None:  # [M, N] x [N, K]: reduce over N
+        dx = _qmm(fmt, q(g, swizzled=True), q(w, transpose=True, swizzled=True))
+    if x is not None:  # [N, M] x [M, K]: reduce over M
+        dw = _qmm(fmt, q(g, transpose=True, swizzled=True), q(x, transpose=True, swizzled=True))
+    return dx, dw
 
 
 class BlockScaledMatMul(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, fmt: str, x: QTensor, x_proxy, w: QTensor, w_proxy):
+    def forward(ctx, fmt: str, x: QTensor, x_proxy, w: QTensor, w_proxy, quantized_backward: bool = False):
         ctx.fmt = fmt
+        # the quantized backward needs every GEMM dimension to be a multiple of 32
+        ctx.qbwd = bool(quantized_backward) and x_proxy is not None and w_proxy is not None and all(
+            d % 32 == 0 for d in (*x_proxy.shape, w_proxy.shape[0]))
+        if ctx.qbwd:
+            ctx.proxies = (x_proxy.reshape(-1, x_proxy.shape[-1]), w_proxy)
         ctx.x_k = x_proxy.shape[-1] if x_proxy is not None else None
         ctx.w_k = w_proxy.shape[-1] if w_proxy is not None else None
         x_theta, x_q, x_alpha = getattr(x, fmt)()
@@ -38,7 +74,8 @@ class BlockScaledMatMul(torch.autograd.Function):
             block = 16 if fmt == "nvfp4" else 32
             x_theta, x_q = pad_k(x_theta, x_q, 2, block, 32)
             w_theta, w_q = pad_k(w_theta, w_q, 2, block, 32)
-        ctx.save_for_backward(x_theta, x_q, x_alpha, w_theta, w_q, w_alpha)
+        if not ctx.qbwd:  # the quantized backward requantizes the proxies instead
+            ctx.save_for_backward(x_theta, x_q, x_alpha, w_theta, w_q, w_alpha)
         n = w_theta.shape[0]
         w_theta, w_q = pad_n(w_theta, w_q, 8, 128 if fmt == "mxfp8" else 0)
         if fmt == "mxfp8":
@@ -54,6 +91,11 @@ class BlockScaledMatMul(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_output):
         grad_output = grad_output.contiguous()
+        if ctx.qbwd:
+            x_src, w_src = ctx.proxies
+            dx, dw = _quantized_grads(ctx.fmt, grad_output, x_src if ctx.w_k is not None else None,
+                                      w_src if ctx.x_k is not None else None)
+            return None, None, dx, None, dw, None
         x_theta, x_q, x_alpha, w_theta, w_q, w_alpha = ctx.saved_tensors
         deq = _DEQ[ctx.fmt]
         dx = dw = None
@@ -64,11 +106,11 @@ class BlockScaledMatMul(torch.autograd.Function):
             dx = grad_output @ deq(w_theta, w_q, w_alpha)[:, : ctx.x_k]
         if ctx.w_k is not None:
             dw = grad_output.T @ deq(x_theta, x_q, x_alpha)[:, : ctx.w_k]
-        return None, None, dx, None, dw
+        return None, None, dx, None, dw, None
 
 
-def make_matmul(fmt: str):
+def make_matmul(fmt: str, quantized_backward: bool = False):
     def matmul(x: QTensor, w: QTensor) -> torch.Tensor:
-        return BlockScaledMatMul.apply(fmt, x, x.proxy(), w, w.proxy())
+        return BlockScaledMatMul.apply(fmt, x, x.proxy(), w, w.proxy(), quantized_backward)
 
     return matmul

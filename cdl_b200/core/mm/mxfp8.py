@@ -3,3 +3,5 @@
 from cdl_b200.core.mm.blockscaled import make_matmul
 
 matmul = make_matmul("mxfp8")
+# dgrad and wgrad in mxfp8 as well (see blockscaled.py)
+matmul_qbwd = make_matmul("mxfp8", quantized_backward=True)

@@ -747,6 +747,114 @@ __global__ void __launch_bounds__(256) quant_strided_kernel(const uint16_t* __re
     }
 }
 
+// ---------------------------------------------------------------------------
+// transposed path (the wgrad requantize): blocks run along dim 0 of x[rows, k],
+// output row r is input column r.  A CTA stages a [TR x 64] tile of x in
+// shared memory with coalesced 16-byte loads, encodes one (column, block) pair
+// per thread from the shared-memory columns, collects the codes of its 64
+// output rows in shared memory and writes each row's segment contiguously.
+// TR = 256 input rows for FP4 (16 NVFP4 / 8 MXFP4 blocks), 128 for MXFP8
+// (4 blocks): 128 output bytes per row and tile either way.
+// ---------------------------------------------------------------------------
+constexpr int kTrCols = 64, kTrPitch = kTrCols + 8;  // staged row: 64 bf16 + 16 bytes of padding
+template <int FMT>
+struct TrTile {
+    static constexpr int kRows = FmtTraits<FMT>::kFp4 ? 256 : 128;
+    static constexpr int kBlocks = kRows / FmtTraits<FMT>::kBlock;
+    static constexpr int kOutBytes = 128;  // codes per output row and tile
+};
+
+template <int FMT, bool SWZ>
+__global__ void __launch_bounds__(256) quant_transpose_kernel(const uint16_t* __restrict__ x, int64_t rows, int64_t k,
+                                                              int64_t ldx, uint8_t* __restrict__ packed,
+                                                              int64_t pstride, uint8_t* __restrict__ scale,
+                                                              int64_t nb, int64_t c4, const float* __restrict__ gmax_p,
+                                                              const float* __restrict__ alpha_p) {
+    using G = TrTile<FMT>;
+    constexpr int B = FmtTraits<FMT>::kBlock, TR = G::kRows, NBT = G::kBlocks;
+    constexpr int BB = FmtTraits<FMT>::kFp4 ? B / 2 : B;  // code bytes per block
+    __shared__ __align__(16) uint16_t xs[TR * kTrPitch];
+    __shared__ __align__(16) uint8_t os[kTrCols * (G::kOutBytes + 16)];
+    constexpr int kOutPitch = G::kOutBytes + 16;
+    float gmax = 0.f, alpha = 0.f;
+    if constexpr (FMT == kNVFP4) {
+        gmax = *gmax_p;
+        alpha = *alpha_p;
+    }
+    const int tid = threadIdx.x;
+    const int64_t tiles_c = (k + kTrCols - 1) / kTrCols, tiles_r = (rows + TR - 1) / TR;
+    const bool vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (ldx & 7) == 0;
+    for (int64_t tile = blockIdx.x; tile < tiles_c * tiles_r; tile += gridDim.x) {
+        const int64_t col0 = (tile % tiles_c) * kTrCols, row0 = (tile / tiles_c) * TR;
+        // ---- stage x[row0 .. +TR, col0 .. +64) (zeros outside x)
+        for (int e = tid; e < TR * (kTrCols / 8); e += 256) {
+            const int r = e >> 3, c8 = (e & 7) * 8;
+            const int64_t gr = row0 + r, gc = col0 + c8;
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (gr < rows) {
+                const uint16_t* src = x + gr * ldx + gc;
+                if (vec && gc + 8 <= k) {
+                    v = ldg_stream(src);
+                } else {
+                    uint16_t h[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) h[i] = gc + i < k ? src[i] : (uint16_t)0;
+                    v = make_uint4(h[0] | (uint32_t)h[1] << 16, h[2] | (uint32_t)h[3] << 16, h[4] | (uint32_t)h[5] << 16,
+                                   h[6] | (uint32_t)h[7] << 16);
+                }
+            }
+            *reinterpret_cast<uint4*>(&xs[r * kTrPitch + c8]) = v;
+        }
+        __syncthreads();
+        // ---- encode: thread (j, b) = column col0 + j, block b of this tile (a warp shares b)
+        for (int p = tid; p < kTrCols * NBT; p += 256) {
+            const int j = p % kTrCols, b = p / kTrCols;
+            uint32_t h[B];
+            uint32_t mag = 0;
+#pragma unroll
+            for (int i = 0; i < B; ++i) {
+                h[i] = xs[(b * B + i) * kTrPitch + j];
+                mag = max(mag, h[i] & 0x7fffu);
+            }
+            BlockCode bc;
+            block_setup<FMT>(mag, gmax, alpha, bc);
+            uint8_t* o = os + j * kOutPitch + b * BB;
+            if constexpr (FmtTraits<FMT>::kFp4) {
+#pragma unroll
+                for (int i = 0; i < B; i += 2)
+                    o[i / 2] = (uint8_t)(e2m1_nibble(h[i], bc) | (e2m1_nibble(h[i + 1], bc) << 4));
+            } else {
+#pragma unroll
+                for (int i = 0; i < B; i += 2) {
+                    const uint32_t q2 =
+                        cvt_e4m3x2(__fmul_rn(u2f(h[i + 1] << 16), bc.s), __fmul_rn(u2f(h[i] << 16), bc.s));
+                    o[i] = (uint8_t)(q2 & 0xffu);
+                    o[i + 1] = (uint8_t)(q2 >> 8);
+                }
+            }
+            const int64_t r_out = col0 + j, blk = row0 / B + b;
+            if (r_out < k && blk < nb) scale[SWZ ? swizzle_offset(r_out, blk, c4) : r_out * nb + blk] = (uint8_t)bc.byte;
+        }
+        __syncthreads();
+        // ---- write each output row's segment: blocks row0/B .. (clipped to nb)
+        const int64_t blk0 = row0 / B;
+        const int nbytes = (int)((nb - blk0 < NBT ? nb - blk0 : NBT) * BB);
+        for (int e = tid; e < kTrCols * (G::kOutBytes / 8); e += 256) {
+            const int j = e / (G::kOutBytes / 8), o8 = (e % (G::kOutBytes / 8)) * 8;
+            const int64_t r_out = col0 + j;
+            if (r_out >= k || o8 >= nbytes) continue;
+            uint8_t* dst = packed + r_out * pstride + blk0 * BB + o8;
+            const uint8_t* srcb = os + j * kOutPitch + o8;
+            if (o8 + 8 <= nbytes && (reinterpret_cast<uintptr_t>(dst) & 7u) == 0) {
+                *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(srcb);
+            } else {
+                for (int i = 0; i < 8 && o8 + i < nbytes; ++i) dst[i] = srcb[i];
+            }
+        }
+        __syncthreads();
+    }
+}
+
 bool aligned(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) & (uintptr_t)(a - 1)) == 0; }
 
 int device_ok() {
@@ -789,6 +897,12 @@ int launch_encode(const void* x, int64_t rows, int64_t k, int64_t ldx, int trans
         grid = grid < (int64_t)sms * 8 ? grid : (int64_t)sms * 8;
         quant_flat_kernel<FMT, SWZ, U><<<(unsigned)grid, 256, 0, st>>>(
             reinterpret_cast<const uint4*>(x), nvec, static_cast<uint8_t*>(packed),
+            static_cast<uint8_t*>(scale), nb, c4, gmax, alpha);
+    } else if (transpose) {
+        const int64_t tiles = ((k + kTrCols - 1) / kTrCols) * ((rows + TrTile<FMT>::kRows - 1) / TrTile<FMT>::kRows);
+        int64_t grid = tiles < (int64_t)sms * 4 ? tiles : (int64_t)sms * 4;
+        quant_transpose_kernel<FMT, SWZ><<<(unsigned)grid, 256, 0, st>>>(
+            static_cast<const uint16_t*>(x), rows, k, ldx, static_cast<uint8_t*>(packed), pstride,
             static_cast<uint8_t*>(scale), nb, c4, gmax, alpha);
     } else {
         const int64_t sr = transpose ? 1 : ldx, sc = transpose ? ldx : 1;

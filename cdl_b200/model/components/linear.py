@@ -4,7 +4,9 @@
 ``QLinear`` quantizes its activation and (LoRA-merged) weight through its
 ``Quant`` modules and multiplies them with the matmul backend named by
 ``backend``: ``native`` (dequantize, then bf16 matmul), ``nvfp4`` / ``mxfp4``
-/ ``mxfp8`` (B200 block-scaled GEMM).
+/ ``mxfp8`` (B200 block-scaled GEMM forward, bf16 backward as cdl), and
+``nvfp4_qbwd`` / ``mxfp4_qbwd`` / ``mxfp8_qbwd`` (dgrad and wgrad in the same
+block-scaled format too).
 """
 
 from __future__ import annotations
@@ -19,7 +21,7 @@ from cdl_b200.api.quant import MatMul, Quant
 from cdl_b200.core.mm import mxfp4, mxfp8, native, nvfp4
 from cdl_b200.model.components.quant.ste import SteQuant
 
-Backend = Literal["native", "nvfp4", "mxfp4", "mxfp8"]
+Backend = Literal["native", "nvfp4", "mxfp4", "mxfp8", "nvfp4_qbwd", "mxfp4_qbwd", "mxfp8_qbwd"]
 
 
 class MergedLoRALayer(nn.Module):
@@ -41,6 +43,9 @@ _BACKENDS: dict[str, MatMul] = {
     "nvfp4": nvfp4.matmul,
     "mxfp4": mxfp4.matmul,
     "mxfp8": mxfp8.matmul,
+    "nvfp4_qbwd": nvfp4.matmul_qbwd,
+    "mxfp4_qbwd": mxfp4.matmul_qbwd,
+    "mxfp8_qbwd": mxfp8.matmul_qbwd,
 }
 
 

@@ -5,8 +5,11 @@ Mirrors what cdl's training driver does per micro-batch (smollm2.py:667-677
 ``q/k/v/o/gate/up/down_proj`` linear of a Llama decoder becomes a
 ``QLinear`` whose activation and weight pass through ``SteQuant`` and whose
 matmul backend is ``nvfp4`` (or ``mxfp4`` / ``mxfp8`` / ``native``); the loss
-is next-token cross entropy through the unquantized LM head; the optimizer
-is AdamW (betas 0.9/0.95) with gradient-norm clipping at 1.0.
+is next-token cross entropy through the unquantized LM head, computed the way
+cdl's Liger fused linear cross entropy does it (chunks of tokens; the logits
+are never materialised for the whole batch, and the gradients of the hidden
+states and of the head weight are formed in the same pass); the optimizer is
+AdamW (betas 0.9/0.95, fused on CUDA) with gradient-norm clipping at 1.0.
 
 Models are built from the BASELINE configurations with random init (std
 0.02) -- no checkpoint is loaded -- and trained on uniform random tokens.
@@ -79,7 +82,8 @@ def apply_quant(model: nn.Module, backend: str = "nvfp4", simulation: str | None
     ``backend="none"`` leaves the model unquantized (bf16 reference runs)."""
     if backend == "none":
         return 0
-    sim = simulation or (backend if backend.startswith("mx") else "nvfp4")
+    base = backend.split("_")[0]  # "nvfp4_qbwd" quantizes like "nvfp4"
+    sim = simulation or (base if base.startswith("mx") else "nvfp4")
     count = 0
     for name, module in list(model.named_modules()):
         parent_name, _, leaf = name.rpartition(".")
@@ -95,11 +99,50 @@ def apply_quant(model: nn.Module, backend: str = "nvfp4", simulation: str | None
     return count
 
 
-def lm_loss(model: nn.Module, input_ids: torch.Tensor) -> torch.Tensor:
+class LinearCrossEntropy(torch.autograd.Function):
+    """Mean cross entropy of ``h @ w^T`` against ``targets``, ``chunk`` tokens
+    at a time (the algorithm of Liger's fused linear cross entropy, which cdl
+    uses for its LM head, smollm2.py:667-677).  Per chunk: fp32 logits, the
+    log-sum-exp and the loss, then ``d loss / d logits = (softmax - onehot) / n``
+    in the hidden dtype, ``grad_h = dl @ w`` and ``grad_w += dl^T @ h``.  The
+    backward only scales the stored gradients."""
+
+    @staticmethod
+    def forward(ctx, h: torch.Tensor, w: torch.Tensor, targets: torch.Tensor, chunk: int) -> torch.Tensor:
+        n = h.shape[0]
+        grad_h = torch.empty_like(h) if ctx.needs_input_grad[0] else None
+        grad_w = torch.zeros_like(w) if ctx.needs_input_grad[1] else None
+        total = torch.zeros((), dtype=torch.float32, device=h.device)
+        for s in range(0, n, chunk):
+            hc, tc = h[s:s + chunk], targets[s:s + chunk]
+            logits = (hc @ w.t()).float()
+            lse = torch.logsumexp(logits, dim=1)
+            total += (lse - logits.gather(1, tc[:, None])[:, 0]).sum()
+            p = logits.sub_(lse[:, None]).exp_()
+            p[torch.arange(p.shape[0], device=p.device), tc] -= 1.0
+            dl = p.div_(n).to(h.dtype)
+            if grad_h is not None:
+                torch.mm(dl, w, out=grad_h[s:s + chunk])
+            if grad_w is not None:
+                grad_w.addmm_(dl.t(), hc)
+        ctx.save_for_backward(grad_h, grad_w)
+        return total / n
+
+    @staticmethod
+    def backward(ctx, grad_loss: torch.Tensor):
+        grad_h, grad_w = ctx.saved_tensors
+        gl = grad_loss.to(grad_h.dtype if grad_h is not None else grad_w.dtype)
+        return (grad_h * gl if grad_h is not None else None, grad_w * gl if grad_w is not None else None, None, None)
+
+
+def lm_loss(model: nn.Module, input_ids: torch.Tensor, chunk: int = 2048) -> torch.Tensor:
     """Mean next-token cross entropy through the LM head (smollm2.py:667-677)."""
     hidden = model.model(input_ids=input_ids, use_cache=False).last_hidden_state[:, :-1]
-    logits = model.lm_head(hidden.reshape(-1, hidden.shape[-1]))
-    return F.cross_entropy(logits.float(), input_ids[:, 1:].reshape(-1), reduction="mean")
+    h = hidden.reshape(-1, hidden.shape[-1])
+    targets = input_ids[:, 1:].reshape(-1)
+    if chunk <= 0:  # plain path: full fp32 logits
+        return F.cross_entropy(model.lm_head(h).float(), targets, reduction="mean")
+    return LinearCrossEntropy.apply(h, model.lm_head.weight, targets, chunk)
 
 
 class LossModule(nn.Module):
@@ -136,9 +179,10 @@ class QatStep:
         self.params = params
         decay = [p for p in params if p.ndim > 1]
         no_decay = [p for p in params if p.ndim <= 1]
+        fused = device.type == "cuda"
         self.opt = torch.optim.AdamW(
             [{"params": decay, "weight_decay": 0.0}, {"params": no_decay, "weight_decay": 0.0}],
-            lr=lr, betas=(0.9, 0.95), foreach=True)
+            lr=lr, betas=(0.9, 0.95), fused=fused, foreach=not fused)
         self.grad_clip = grad_clip
         self.net = LossModule(self.model)
         if ddp:

@@ -61,3 +61,77 @@ def test_loss_curve_nvfp4_vs_native():
         assert abs(a - b) / b < 5e-3, (a, b)
     for a, b in zip(norms["nvfp4"][:10], norms["native"][:10]):
         assert abs(a - b) / b < 5e-2, (a, b)
+
+
+@pytest.mark.parametrize("fmt", ["nvfp4", "mxfp4", "mxfp8"])
+def test_quantized_backward_gemms_vs_oracle(fmt):
+    """dgrad = Q(g).Q(w^T)^T and wgrad = Q(g^T).Q(x^T)^T against the fp32
+    dequantize-then-matmul oracle of the same quantized operands."""
+    import numpy as np
+
+    import oracle
+    from cdl_b200.core.mm.blockscaled import _quantized_grads
+
+    ofmt = {"nvfp4": oracle.NVFP4, "mxfp4": oracle.MXFP4, "mxfp8": oracle.MXFP8}[fmt]
+    gen = torch.Generator("cuda").manual_seed(5)
+    m, n, k = 256, 320, 576
+    g = torch.randn(m, n, device="cuda", generator=gen).bfloat16()
+    x = torch.randn(m, k, device="cuda", generator=gen).bfloat16()
+    w = (0.02 * torch.randn(n, k, device="cuda", generator=gen)).bfloat16()
+    dx, dw = _quantized_grads(fmt, g, x, w)
+    assert dx.shape == (m, k) and dw.shape == (n, k)
+
+    def bits(t):
+        return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+    def qmm(a, b):  # oracle of alpha * deq(Q(a)) @ deq(Q(b))^T, both quantized along their rows
+        ap, asf, aal = oracle.quant(bits(a), ofmt)
+        bp, bsf, bal = oracle.quant(bits(b), ofmt)
+        alpha = 1.0 if aal is None else float(aal[0]) * float(bal[0])
+        return oracle.mm(ap, asf, bp, bsf, ofmt, alpha)
+
+    for got, ref in ((dx, qmm(g, w.t())), (dw, qmm(g.t(), x.t()))):
+        ref_bf16 = torch.from_numpy(ref).bfloat16().float()
+        assert _rel(got.cpu(), ref_bf16) <= 1e-3
+
+
+@pytest.mark.parametrize("fmt", ["nvfp4", "mxfp8"])
+def test_qlinear_quantized_backward_close_to_reference_grads(fmt):
+    """The *_qbwd backends' gradients stay within the quantization error of
+    the reference (bf16) backward."""
+    from cdl_b200.model.components.linear import QLinear
+    from cdl_b200.model.components.quant.ste import SteQuant
+
+    torch.manual_seed(0)
+    lin = torch.nn.Linear(576, 320, bias=False).cuda().bfloat16()
+    grads = {}
+    for be in (fmt, fmt + "_qbwd"):
+        q = QLinear.from_linear(lin)
+        q.set_activation_quant(SteQuant(fmt))
+        q.set_weight_quant(SteQuant(fmt))
+        q.set_backend(be)
+        x = torch.randn(3, 128, 576, device="cuda", dtype=torch.bfloat16, generator=torch.Generator("cuda").manual_seed(1))
+        x.requires_grad_(True)
+        y = q(x)
+        y.backward(torch.randn_like(y, generator=torch.Generator("cuda").manual_seed(2)))
+        grads[be] = (x.grad.detach(), q.weight.grad.detach())
+    bound = 0.25 if fmt == "nvfp4" else 0.08
+    for a, b in zip(grads[fmt + "_qbwd"], grads[fmt]):
+        assert _rel(a, b) < bound, _rel(a, b)
+
+
+def test_loss_curve_quantized_backward():
+    """NVFP4 fwd/dgrad/wgrad (nvfp4_qbwd) against NVFP4 fwd + bf16 backward
+    (cdl's numerics): same seed and data, 60 steps on the small model."""
+    from cdl_b200.train import qat
+
+    spec = qat.SPECS["tiny"]
+    dev = torch.device("cuda")
+    curves = {}
+    for be in ("nvfp4", "nvfp4_qbwd"):
+        step = qat.QatStep(spec, dev, backend=be, lr=3e-4, seed=0)
+        curves[be] = [float(step.step(qat.random_tokens(8, 256, spec.vocab, seed=100 + i, device=dev))[0])
+                      for i in range(60)]
+    worst = max(abs(a - b) / b for a, b in zip(curves["nvfp4_qbwd"], curves["nvfp4"]))
+    print("max relative loss difference, quantized vs bf16 backward:", worst)
+    assert worst < 2e-2
