@@ -68,6 +68,8 @@ def parse_args():
     ap.add_argument("--no-components", action="store_true",
                     help="skip the N=1 component measurements (quantize GB/s, GEMM TFLOP/s)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--backend", default="nvfp4", choices=["nvfp4", "nvfp4_qbwd", "mxfp4", "mxfp8"],
+                    help="QAT workloads: QLinear backend (nvfp4 = cdl's numerics: bf16 backward)")
     ap.add_argument("--spinup-s", type=float, default=1.0, help="untimed clock ramp before warm-up")
     a = ap.parse_args()
     qat = a.workload.startswith("qat")
@@ -295,6 +297,14 @@ def gemm_workload(dev, rank):
         ap, asf, aal = quant.nvfp4_quant(pool[i % pool_n], swizzled=True)
         return mm_fp4(ap, wp.T, asf, wsw.T, aal * wal, 16, True)
 
+    # the GEMM kernel alone (A already quantized), for the roofline of the dominant kernel
+    pre = [quant.nvfp4_quant(a, swizzled=True) for a in pool]
+    alphas = [p[2] * wal for p in pre]
+
+    def kernel_step(i):
+        ap, asf, _ = pre[i % pool_n]
+        return mm_fp4(ap, wp.T, asf, wsw.T, alphas[i % pool_n], 16, True)
+
     host_a = pool[0].cpu().pin_memory()
     host_out = torch.empty(m, n, dtype=torch.bfloat16, pin_memory=True)
 
@@ -303,24 +313,26 @@ def gemm_workload(dev, rank):
         host_out.copy_(mm_fp4(ap, wp.T, asf, wsw.T, aal * wal, 16, True), non_blocking=True)
 
     return {
-        "step": step, "e2e_step": e2e_step, "graph": True,
+        "step": step, "e2e_step": e2e_step, "kernel_step": kernel_step, "graph": True,
         "units_per_step": 2.0 * m * n * k / 1e12, "unit": "TFLOP/s", "metric": "FP4 GEMM TFLOPS",
         "dtype": "e2m1 x e2m1 (ue4m3 block scales) -> fp32 acc -> bf16",
         "config": {"workload": f"fp4_gemm C3 NVFP4 {m}x{n}x{k}: quantize bf16 A + tcgen05 GEMM vs pre-quantized W",
                    "l2": f"A cycled over {pool_n} tensors of 128 MiB (> L2)"},
         "h2d": host_a.numel() * 2, "d2h": m * n * 2, "bound": "tensor",
-        "kernel": "bs_gemm_kernel<NVFP4> (+ nvfp4_fused_kernel prologue)", "launches_per_step": 3,
+        "kernel": "bs_gemm_pair_kernel<NVFP4> (persistent 2-SM tcgen05 block-scaled GEMM)",
+        "launches_per_step": 3,  # nvfp4_fused_kernel (A), the GEMM, the alpha product
     }
 
 
-def qat_workload(name, dev, rank, world):
+def qat_workload(name, dev, rank, world, backend="nvfp4"):
     import torch
 
     from cdl_b200.train import qat
 
     spec = qat.SPECS["135m" if name == "qat_135m" else "1.7b"]
     batch, seq = (8, 2048) if name == "qat_135m" else (4, 2048)
-    step = qat.QatStep(spec, dev, backend="nvfp4", seed=0, ddp=world > 1)
+    step = qat.QatStep(spec, dev, backend=backend, seed=0, ddp=world > 1)
+    qbwd = backend.endswith("_qbwd")
     pool = [qat.random_tokens(batch, seq, spec.vocab, seed=1000 * rank + i, device=dev) for i in range(4)]
     host_ids = pool[0].cpu().pin_memory()
     host_loss = torch.empty(1, dtype=torch.float32, pin_memory=True)
@@ -332,15 +344,19 @@ def qat_workload(name, dev, rank, world):
     return {
         "step": lambda i: step.step(pool[i % len(pool)]), "e2e_step": e2e_step, "graph": False,
         "units_per_step": batch * seq, "unit": "tokens/s", "metric": "SmolLM2 NVFP4 QAT tokens/s",
-        "dtype": "nvfp4 fwd GEMMs (e2m1/ue4m3), bf16 bwd, bf16 params + AdamW",
+        "dtype": ("nvfp4 fwd/dgrad/wgrad GEMMs (e2m1/ue4m3)" if qbwd else
+                  "nvfp4 fwd GEMMs (e2m1/ue4m3), bf16 dgrad/wgrad as cdl") + ", bf16 params + fused AdamW",
         "config": {"workload": f"{name} {'C4' if name == 'qat_135m' else 'C5'} {spec.name} QAT step, "
-                               f"{batch}x{seq} tokens per rank, AdamW lr 3e-4",
+                               f"{batch}x{seq} tokens per rank, AdamW lr 3e-4, backend {backend}",
+                   "backend": backend,
                    "model": spec.name, "global_batch": batch * world, "seq_len": seq,
                    "parallelism": f"dp{world}" if world > 1 else "single", "l2": "activations >> L2"},
         "h2d": host_ids.numel() * 8, "d2h": 4, "bound": "tensor",
         "flops_per_unit": qat.flops_per_token(spec, seq), "kernel": "full QAT step",
-        # per QLinear: quantize x and w, swizzle both scale sets, GEMM; backward: dequantize w and x
-        "launches_per_step": 7 * step.n_quant,
+        # per QLinear: quantize x and w, swizzle both scale sets, GEMM (5); backward: dequantize w and x
+        # (2), or with the quantized backward quantize g, g^T, w^T, x^T (1 + 3 x amax + transpose) and
+        # two GEMMs (9)
+        "launches_per_step": (14 if qbwd else 7) * step.n_quant,
     }
 
 
@@ -369,6 +385,27 @@ def time_steps(w, steps, dev):
     return g.replay, (g, outs)
 
 
+FP4_PEAK_NOTE = ("denominator = 4 x the measured cuBLAS bf16 burst peak: the block-scaled FP4 MMA retires "
+                 "4x the K of a bf16 MMA per cycle (measured on this pool: 128 cycles for M128 N256 K64 FP4 "
+                 "and for K16 bf16); nominal dense FP4 is 9 PFLOP/s")
+
+
+def time_kernel(fn, steps, dev):
+    """Average device time (ms) of ``fn(i)`` over ``steps`` launches on the current stream."""
+    import torch
+
+    for i in range(3):
+        fn(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        fn(i)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
 def measure_component(name, dev, steps, warmup, peaks):
     """Device-timed throughput and roofline of one kernel-level workload (N=1)."""
     import torch
@@ -386,11 +423,14 @@ def measure_component(name, dev, steps, warmup, peaks):
     ms = e0.elapsed_time(e1)
     del keep, run
     value = w["units_per_step"] * steps / (ms / 1e3)
-    peak, punit = (peaks["hbm_gbs"], "GB/s") if w["bound"] == "hbm" else (peaks["bf16_tflops"], "TFLOP/s")
+    achieved = value
+    if "kernel_step" in w:  # the dominant kernel alone
+        achieved = w["units_per_step"] / (time_kernel(w["kernel_step"], steps, dev) / 1e3)
+    peak, punit = (peaks["hbm_gbs"], "GB/s") if w["bound"] == "hbm" else (4 * peaks["bf16_tflops"], "TFLOP/s")
     return {"metric": w["metric"], "value": round(value, 2), "unit": w["unit"], "steps": steps,
             "ms_per_step": round(ms / steps, 5), "config": w["config"]["workload"],
-            "roofline": {"bound": w["bound"], "achieved": round(value, 2), "peak": peak, "unit": punit,
-                         "frac": round(value / peak, 4), "traffic": profile_traffic(name), "kernel": w["kernel"]},
+            "roofline": {"bound": w["bound"], "achieved": round(achieved, 2), "peak": peak, "unit": punit,
+                         "frac": round(achieved / peak, 4), "traffic": profile_traffic(name), "kernel": w["kernel"]},
             "gpu_launches": w["launches_per_step"] * steps}
 
 
@@ -440,7 +480,7 @@ def main() -> None:
     elif wl == "fp4_gemm":
         w = gemm_workload(dev, rank)
     else:
-        w = qat_workload(wl, dev, rank, world)
+        w = qat_workload(wl, dev, rank, world, args.backend)
 
     def barrier():
         if world > 1:
@@ -508,8 +548,9 @@ def main() -> None:
     per_step_s = ms_max / 1e3 / args.steps
     if w["bound"] == "hbm":
         achieved, peak, punit = w["units_per_step"] / per_step_s, peaks["hbm_gbs"], "GB/s"
-    elif wl == "fp4_gemm":
-        achieved, peak, punit = w["units_per_step"] / per_step_s, peaks["bf16_tflops"], "TFLOP/s"
+    elif wl == "fp4_gemm":  # the GEMM kernel alone, A pre-quantized
+        kernel_s = time_kernel(w["kernel_step"], args.steps, dev) / 1e3
+        achieved, peak, punit = w["units_per_step"] / kernel_s, 4 * peaks["bf16_tflops"], "TFLOP/s"
     else:
         achieved = w["units_per_step"] * w["flops_per_unit"] / per_step_s / 1e12
         peak, punit = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]), "TFLOP/s"
@@ -528,8 +569,7 @@ def main() -> None:
         "clocks": clocks,
     }
     if wl == "fp4_gemm":
-        line["roofline"]["peak_note"] = ("denominator = measured cuBLAS bf16 peak (no measured FP4 peak; "
-                                         "nominal dense FP4 is 9 PFLOP/s)")
+        line["roofline"]["peak_note"] = FP4_PEAK_NOTE
     if wl.startswith("qat"):
         line["roofline"]["peak_note"] = "model FLOPs (6P + 12 L d s per token) vs measured sustained bf16 peak"
     if world == 1 and wl.startswith("qat") and not args.no_components:
@@ -537,8 +577,7 @@ def main() -> None:
             "nvfp4_quant": measure_component("nvfp4_quant", dev, 200, 10, peaks),
             "fp4_gemm": measure_component("fp4_gemm", dev, 20, 5, peaks),
         }
-        line["components"]["fp4_gemm"]["roofline"]["peak_note"] = (
-            "denominator = measured cuBLAS bf16 peak (no measured FP4 peak; nominal dense FP4 is 9 PFLOP/s)")
+        line["components"]["fp4_gemm"]["roofline"]["peak_note"] = FP4_PEAK_NOTE
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
