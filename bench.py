@@ -68,6 +68,8 @@ def parse_args():
     ap.add_argument("--no-components", action="store_true",
                     help="skip the N=1 component measurements (quantize GB/s, GEMM TFLOP/s)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--torch-profile", default="", metavar="PATH",
+                    help="after the timed region, profile 2 more steps (CUDA kernels) and write the table to PATH")
     ap.add_argument("--backend", default="nvfp4", choices=["nvfp4", "nvfp4_qbwd", "mxfp4", "mxfp8"],
                     help="QAT workloads: QLinear backend (nvfp4 = cdl's numerics: bf16 backward)")
     ap.add_argument("--spinup-s", type=float, default=1.0, help="untimed clock ramp before warm-up")
@@ -511,6 +513,15 @@ def main() -> None:
     ms = e0.elapsed_time(e1)
     clocks = sampler.stop()
     del keep, run
+    if args.torch_profile and world == 1:  # kernel breakdown, outside the timed region
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for i in range(2):
+                w["step"](i)
+            torch.cuda.synchronize()
+        with open(args.torch_profile, "w") as f:
+            f.write(prof.key_averages().table(sort_by="self_cuda_time_total", row_limit=40, max_name_column_width=90))
     ms_t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)

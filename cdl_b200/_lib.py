@@ -36,7 +36,7 @@ _I64 = ctypes.c_int64
 _I = ctypes.c_int
 _SZ = ctypes.c_size_t
 
-# name -> (restype, argtypes); every symbol declared in include/cdlb200.h
+# name -> (restype, argtypes); every symbol declared in include/*.h
 SIGNATURES: dict[str, tuple] = {
     "cdlb200_status_string": (ctypes.c_char_p, [_I]),
     "cdlb200_version": (_I, []),
@@ -50,6 +50,13 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_swizzle_scales": (_I, [_P, _I64, _I64, _P, _P]),
     "cdlb200_mm_fp4": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _P, _I64, _P, _P]),
     "cdlb200_mm_mxfp8": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _I64, _P, _P]),
+    # include/cdlb200_step.h
+    "cdlb200_rmsnorm_fwd": (_I, [_P, _P, _I64, _I64, ctypes.c_float, _P, _P, _P]),
+    "cdlb200_rmsnorm_bwd_workspace_bytes": (_I64, [_I64, _I64]),
+    "cdlb200_rmsnorm_bwd": (_I, [_P, _P, _P, _P, _I64, _I64, _P, _P, _P, _I64, _P]),
+    "cdlb200_rope": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _P, _P]),
+    "cdlb200_swiglu_fwd": (_I, [_P, _P, _I64, _P, _P]),
+    "cdlb200_swiglu_bwd": (_I, [_P, _P, _P, _I64, _P, _P, _P]),
 }
 
 

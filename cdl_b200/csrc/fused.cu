@@ -1,0 +1,355 @@
+// fused.cu -- the elementwise parts of the SmolLM2 (Llama) QAT step, one
+// memory pass each, following the rounding steps of the eager reference
+// modules so that the results stay within bf16 rounding of them:
+//
+//   RMSNorm   y = bf16(w * bf16(x * rsqrt(mean(x^2) + eps)))        (x -> fp32 first)
+//   RoPE      out = bf16(bf16(q * cos) + bf16(rot(q) * sin)),  rot(q) = (-q[D/2:], q[:D/2])
+//   SwiGLU    h = bf16(bf16(silu(g)) * u)
+//
+// and their backward passes (the gradients autograd forms for those modules,
+// with fp32 intermediates).  All tensors are bf16, row-major, 16-byte aligned
+// rows; each thread moves 8 values (16 bytes) at a time.
+#include "common.cuh"
+
+namespace cdlb200 {
+namespace {
+
+__device__ __forceinline__ float bf_lo(uint32_t w) { return u2f(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return u2f(w & 0xffff0000u); }
+__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+__device__ __forceinline__ float rbf(float v) {  // round to bf16 and back
+    return u2f(pack_bf2(v, 0.f) << 16);
+}
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+    f[0] = bf_lo(v.x), f[1] = bf_hi(v.x), f[2] = bf_lo(v.y), f[3] = bf_hi(v.y);
+    f[4] = bf_lo(v.z), f[5] = bf_hi(v.z), f[6] = bf_lo(v.w), f[7] = bf_hi(v.w);
+}
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+    return make_uint4(pack_bf2(f[0], f[1]), pack_bf2(f[2], f[3]), pack_bf2(f[4], f[5]), pack_bf2(f[6], f[7]));
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm: one warp per row; lane l owns the 8-value vectors l, l + 32, ...
+// (VPL vectors at most, d = 8 * nvec).
+// ---------------------------------------------------------------------------
+template <int VPL>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const uint4* __restrict__ x, const uint4* __restrict__ w,
+                                                          int64_t rows, int nvec, float eps, uint4* __restrict__ y,
+                                                          float* __restrict__ rstd) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+        uint4 v[VPL];
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) {
+            const int c = lane + 32 * j;
+            v[j] = c < nvec ? x[r * nvec + c] : make_uint4(0u, 0u, 0u, 0u);
+            float f[8];
+            unpack8(v[j], f);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
+        }
+        ss = warp_sum(ss);
+        const float rs = rsqrtf(ss / (float)(8 * nvec) + eps);
+        if (lane == 0) rstd[r] = rs;
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) {
+            const int c = lane + 32 * j;
+            if (c >= nvec) continue;
+            float f[8], g[8];
+            unpack8(v[j], f);
+            unpack8(w[c], g);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) f[i] = g[i] * rbf(f[i] * rs);
+            y[r * nvec + c] = pack8(f);
+        }
+    }
+}
+
+// dx = bf16(rs * g1 - x * rs^3 * sum(g1 * x) / d) with g1 = bf16(dy * w);
+// dw partial sums (fp32, one row of `part` per CTA) of dy * bf16(x * rs).
+template <int VPL>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const uint4* __restrict__ dy, const uint4* __restrict__ x,
+                                                          const uint4* __restrict__ w, const float* __restrict__ rstd,
+                                                          int64_t rows, int nvec, uint4* __restrict__ dx,
+                                                          float* __restrict__ part) {
+    extern __shared__ float dw_s[];  // [8 * nvec]
+    const int lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < 8 * nvec; i += blockDim.x) dw_s[i] = 0.f;
+    __syncthreads();
+    float acc[VPL][8];
+#pragma unroll
+    for (int j = 0; j < VPL; ++j)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[j][i] = 0.f;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const float inv_d = 1.0f / (float)(8 * nvec);
+    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+        const float rs = rstd[r];
+        uint4 xv[VPL], dv[VPL];  // the row stays in registers as bf16; fp32 values are recomputed
+        float dot = 0.f;
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) {
+            const int c = lane + 32 * j;
+            xv[j] = c < nvec ? x[r * nvec + c] : make_uint4(0u, 0u, 0u, 0u);
+            dv[j] = c < nvec ? dy[r * nvec + c] : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) {
+            const int c = lane + 32 * j;
+            if (c >= nvec) continue;
+            float xf[8], d8[8], w8[8];
+            unpack8(xv[j], xf);
+            unpack8(dv[j], d8);
+            unpack8(w[c], w8);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                dot = fmaf(rbf(d8[i] * w8[i]), xf[i], dot);
+                acc[j][i] = fmaf(d8[i], rbf(xf[i] * rs), acc[j][i]);
+            }
+        }
+        dot = warp_sum(dot);
+        const float k = rs * rs * rs * dot * inv_d;
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) {
+            const int c = lane + 32 * j;
+            if (c >= nvec) continue;
+            float xf[8], d8[8], w8[8], o[8];
+            unpack8(xv[j], xf);
+            unpack8(dv[j], d8);
+            unpack8(w[c], w8);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = rs * rbf(d8[i] * w8[i]) - xf[i] * k;
+            dx[r * nvec + c] = pack8(o);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+        const int c = lane + 32 * j;
+        if (c >= nvec) continue;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) atomicAdd(&dw_s[8 * c + i], acc[j][i]);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 8 * nvec; i += blockDim.x) part[(int64_t)blockIdx.x * 8 * nvec + i] = dw_s[i];
+}
+
+// dw[i] = bf16(sum over the CTA partials): a CTA per 32 columns, its 8 warps
+// splitting the partials.
+__global__ void __launch_bounds__(256) colsum_kernel(const float* __restrict__ part, int nparts, int d,
+                                                     uint16_t* __restrict__ dw) {
+    __shared__ float red[8][33];
+    const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+    const int i = blockIdx.x * 32 + lane;
+    float s = 0.f;
+    if (i < d)
+        for (int p = wp; p < nparts; p += 8) s += part[(int64_t)p * d + i];
+    red[wp][lane] = s;
+    __syncthreads();
+    if (wp == 0) {
+        float t = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) t += red[k][lane];
+        if (i < d) dw[i] = (uint16_t)(pack_bf2(t, 0.f) & 0xffffu);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// RoPE on x[tokens, heads, D] (D = 8 * 2 * halfv), cos/sin[cos_tokens, D],
+// token t using row t % cos_tokens (a batch sharing one position table).  One
+// thread per (token, head, 8-value vector of the first half) handles that
+// vector and its partner in the second half.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rope_kernel(const uint4* __restrict__ x, const uint4* __restrict__ cosv,
+                                                   const uint4* __restrict__ sinv, int64_t tokens, int heads,
+                                                   int halfv, int64_t cos_tokens, int backward,
+                                                   uint4* __restrict__ out) {
+    const int64_t total = tokens * heads * halfv;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int v = (int)(t % halfv);
+        const int64_t th = t / halfv, tok = (th / heads) % cos_tokens;  // cos/sin repeat every cos_tokens
+        const int64_t base = th * 2 * halfv;
+        float a[8], b[8], c1[8], c2[8], s1[8], s2[8], o1[8], o2[8];
+        unpack8(x[base + v], a);
+        unpack8(x[base + halfv + v], b);
+        unpack8(cosv[tok * 2 * halfv + v], c1);
+        unpack8(cosv[tok * 2 * halfv + halfv + v], c2);
+        unpack8(sinv[tok * 2 * halfv + v], s1);
+        unpack8(sinv[tok * 2 * halfv + halfv + v], s2);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (!backward) {  // (x*cos) + (rot(x)*sin), rot(x) = (-b, a)
+                o1[i] = rbf(a[i] * c1[i]) - rbf(b[i] * s1[i]);
+                o2[i] = rbf(b[i] * c2[i]) + rbf(a[i] * s2[i]);
+            } else {  // g*cos + rot^T(g*sin), rot^T(u) = (u2, -u1)
+                o1[i] = rbf(a[i] * c1[i]) + rbf(b[i] * s2[i]);
+                o2[i] = rbf(b[i] * c2[i]) - rbf(a[i] * s1[i]);
+            }
+        }
+        out[base + v] = pack8(o1);
+        out[base + halfv + v] = pack8(o2);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// SwiGLU: h = bf16(bf16(silu(g)) * u); backward with s = sigmoid(g):
+//   dsilu = bf16(dh * u), du = bf16(dh * bf16(silu(g))),
+//   dg = bf16(dsilu * s * (1 + g * (1 - s)))
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float sigmoid_f(float g) { return 1.0f / (1.0f + expf(-g)); }
+
+__global__ void __launch_bounds__(256) swiglu_fwd_kernel(const uint4* __restrict__ g, const uint4* __restrict__ u,
+                                                         int64_t nvec, uint4* __restrict__ h) {
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < nvec; t += (int64_t)gridDim.x * blockDim.x) {
+        float a[8], b[8];
+        unpack8(g[t], a);
+        unpack8(u[t], b);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a[i] = rbf(a[i] * sigmoid_f(a[i])) * b[i];
+        h[t] = pack8(a);
+    }
+}
+
+__global__ void __launch_bounds__(256) swiglu_bwd_kernel(const uint4* __restrict__ dh, const uint4* __restrict__ g,
+                                                         const uint4* __restrict__ u, int64_t nvec,
+                                                         uint4* __restrict__ dg, uint4* __restrict__ du) {
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < nvec; t += (int64_t)gridDim.x * blockDim.x) {
+        float d[8], a[8], b[8], og[8], ou[8];
+        unpack8(dh[t], d);
+        unpack8(g[t], a);
+        unpack8(u[t], b);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float s = sigmoid_f(a[i]);
+            const float ds = rbf(d[i] * b[i]);
+            ou[i] = d[i] * rbf(a[i] * s);
+            og[i] = ds * (s * (1.0f + a[i] * (1.0f - s)));
+        }
+        dg[t] = pack8(og);
+        du[t] = pack8(ou);
+    }
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int grid_for(int64_t items, int per_block) {
+    const int64_t cap = (int64_t)num_sms() * 8;
+    const int64_t g = (items + per_block - 1) / per_block;
+    return (int)(g < 1 ? 1 : (g < cap ? g : cap));
+}
+
+}  // namespace
+}  // namespace cdlb200
+
+using namespace cdlb200;
+
+extern "C" int cdlb200_rmsnorm_fwd(const void* x, const void* w, int64_t rows, int64_t d, float eps, void* y,
+                                   float* rstd, void* stream) {
+    if (rows < 0 || d <= 0 || (d % 8) != 0 || d > 8 * 32 * 8) return CDLB200_ERR_INVALID_ARG;
+    if (rows == 0) return CDLB200_OK;
+    if (!x || !w || !y || !rstd) return CDLB200_ERR_INVALID_ARG;
+    if (!al16(x) || !al16(w) || !al16(y)) return CDLB200_ERR_ALIGNMENT;
+    const int nvec = (int)(d / 8), vpl = (nvec + 31) / 32;
+    const int grid = grid_for(rows, 8);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    auto args = [&](auto kern) {
+        kern<<<grid, 256, 0, st>>>(static_cast<const uint4*>(x), static_cast<const uint4*>(w), rows, nvec, eps,
+                                   static_cast<uint4*>(y), rstd);
+    };
+    if (vpl <= 1) args(rmsnorm_fwd_kernel<1>);
+    else if (vpl <= 2) args(rmsnorm_fwd_kernel<2>);
+    else if (vpl <= 4) args(rmsnorm_fwd_kernel<4>);
+    else args(rmsnorm_fwd_kernel<8>);
+    CDLB200_CHECK_LAUNCH();
+    return CDLB200_OK;
+}
+
+// the backward runs one persistent CTA per SM (each accumulates its rows' dw
+// in registers, then once into shared memory and one partial row)
+static int bwd_grid(int64_t rows) {
+    const int64_t g = (rows + 7) / 8, cap = num_sms();
+    return (int)(g < 1 ? 1 : (g < cap ? g : cap));
+}
+
+extern "C" int64_t cdlb200_rmsnorm_bwd_workspace_bytes(int64_t rows, int64_t d) {
+    if (rows <= 0 || d <= 0) return 0;
+    return (int64_t)bwd_grid(rows) * d * (int64_t)sizeof(float);
+}
+
+extern "C" int cdlb200_rmsnorm_bwd(const void* dy, const void* x, const void* w, const float* rstd, int64_t rows,
+                                   int64_t d, void* dx, void* dw, void* workspace, int64_t workspace_bytes,
+                                   void* stream) {
+    if (rows < 0 || d <= 0 || (d % 8) != 0 || d > 8 * 32 * 8) return CDLB200_ERR_INVALID_ARG;
+    if (rows == 0) return CDLB200_OK;
+    if (!dy || !x || !w || !rstd || !dx || !dw || !workspace) return CDLB200_ERR_INVALID_ARG;
+    if (!al16(dy) || !al16(x) || !al16(w) || !al16(dx)) return CDLB200_ERR_ALIGNMENT;
+    if (workspace_bytes < cdlb200_rmsnorm_bwd_workspace_bytes(rows, d)) return CDLB200_ERR_WORKSPACE;
+    const int nvec = (int)(d / 8), vpl = (nvec + 31) / 32;
+    const int grid = bwd_grid(rows);
+    const size_t smem = (size_t)d * sizeof(float);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float* part = static_cast<float*>(workspace);
+    auto args = [&](auto kern) {
+        kern<<<grid, 256, smem, st>>>(static_cast<const uint4*>(dy), static_cast<const uint4*>(x),
+                                      static_cast<const uint4*>(w), rstd, rows, nvec, static_cast<uint4*>(dx), part);
+    };
+    if (vpl <= 1) args(rmsnorm_bwd_kernel<1>);
+    else if (vpl <= 2) args(rmsnorm_bwd_kernel<2>);
+    else if (vpl <= 4) args(rmsnorm_bwd_kernel<4>);
+    else args(rmsnorm_bwd_kernel<8>);
+    CDLB200_CHECK_LAUNCH();
+    colsum_kernel<<<(unsigned)((d + 31) / 32), 256, 0, st>>>(part, grid, (int)d, static_cast<uint16_t*>(dw));
+    CDLB200_CHECK_LAUNCH();
+    return CDLB200_OK;
+}
+
+extern "C" int cdlb200_rope(const void* x, const void* cos, const void* sin, int64_t tokens, int64_t heads,
+                            int64_t head_dim, int64_t cos_tokens, int backward, void* out, void* stream) {
+    if (tokens < 0 || heads <= 0 || head_dim <= 0 || (head_dim % 16) != 0 || (backward != 0 && backward != 1) ||
+        cos_tokens <= 0)
+        return CDLB200_ERR_INVALID_ARG;
+    if (tokens == 0) return CDLB200_OK;
+    if (!x || !cos || !sin || !out) return CDLB200_ERR_INVALID_ARG;
+    if (!al16(x) || !al16(cos) || !al16(sin) || !al16(out)) return CDLB200_ERR_ALIGNMENT;
+    const int halfv = (int)(head_dim / 16);
+    const int64_t items = tokens * heads * halfv;
+    rope_kernel<<<grid_for(items, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint4*>(x), static_cast<const uint4*>(cos), static_cast<const uint4*>(sin), tokens,
+        (int)heads, halfv, cos_tokens, backward, static_cast<uint4*>(out));
+    CDLB200_CHECK_LAUNCH();
+    return CDLB200_OK;
+}
+
+extern "C" int cdlb200_swiglu_fwd(const void* g, const void* u, int64_t n, void* h, void* stream) {
+    if (n < 0 || (n % 8) != 0) return CDLB200_ERR_INVALID_ARG;
+    if (n == 0) return CDLB200_OK;
+    if (!g || !u || !h) return CDLB200_ERR_INVALID_ARG;
+    if (!al16(g) || !al16(u) || !al16(h)) return CDLB200_ERR_ALIGNMENT;
+    swiglu_fwd_kernel<<<grid_for(n / 8, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint4*>(g), static_cast<const uint4*>(u), n / 8, static_cast<uint4*>(h));
+    CDLB200_CHECK_LAUNCH();
+    return CDLB200_OK;
+}
+
+extern "C" int cdlb200_swiglu_bwd(const void* dh, const void* g, const void* u, int64_t n, void* dg, void* du,
+                                  void* stream) {
+    if (n < 0 || (n % 8) != 0) return CDLB200_ERR_INVALID_ARG;
+    if (n == 0) return CDLB200_OK;
+    if (!dh || !g || !u || !dg || !du) return CDLB200_ERR_INVALID_ARG;
+    if (!al16(dh) || !al16(g) || !al16(u) || !al16(dg) || !al16(du)) return CDLB200_ERR_ALIGNMENT;
+    swiglu_bwd_kernel<<<grid_for(n / 8, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint4*>(dh), static_cast<const uint4*>(g), static_cast<const uint4*>(u), n / 8,
+        static_cast<uint4*>(dg), static_cast<uint4*>(du));
+    CDLB200_CHECK_LAUNCH();
+    return CDLB200_OK;
+}

@@ -1,0 +1,143 @@
+"""Fused RMSNorm, rotary embedding and SwiGLU for the Llama decoder of the
+QAT step (``include/cdlb200_step.h``).
+
+cdl trains SmolLM2 as a Hugging Face ``LlamaForCausalLM`` (smollm2.py), whose
+``LlamaRMSNorm``, ``apply_rotary_pos_emb`` and ``LlamaMLP`` run as chains of
+eager elementwise kernels.  ``patch_llama(model)`` swaps them for one CUDA
+pass each (forward and backward), keeping the rounding steps of the eager
+modules.  Tensors that are not bf16 on a CUDA device go through the original
+Hugging Face code.
+"""
+
+from __future__ import annotations
+
+import types
+
+import torch
+
+from cdl_b200 import _lib
+
+
+def _cuda_bf16(*ts: torch.Tensor) -> bool:
+    return all(t.is_cuda and t.dtype == torch.bfloat16 for t in ts)
+
+
+class RMSNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+        d = x.shape[-1]
+        x2 = x.reshape(-1, d).contiguous()
+        y = torch.empty_like(x2)
+        rstd = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device)
+        _lib.call("cdlb200_rmsnorm_fwd", _lib.ptr(x2), _lib.ptr(w), x2.shape[0], d, float(eps), _lib.ptr(y),
+                  _lib.ptr(rstd), _lib.stream(x.device))
+        ctx.save_for_backward(x2, w, rstd)
+        ctx.shape = x.shape
+        return y.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, dy: torch.Tensor):
+        x2, w, rstd = ctx.saved_tensors
+        rows, d = x2.shape
+        dy2 = dy.reshape(rows, d).contiguous()
+        dx = torch.empty_like(x2)
+        dw = torch.empty_like(w)
+        nbytes = int(_lib.lib().cdlb200_rmsnorm_bwd_workspace_bytes(rows, d))
+        ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=x2.device)
+        _lib.call("cdlb200_rmsnorm_bwd", _lib.ptr(dy2), _lib.ptr(x2), _lib.ptr(w), _lib.ptr(rstd), rows, d,
+                  _lib.ptr(dx), _lib.ptr(dw), _lib.ptr(ws), ws.numel(), _lib.stream(x2.device))
+        return dx.view(ctx.shape), dw, None
+
+
+class RopeFn(torch.autograd.Function):
+    """``x * cos + rotate_half(x) * sin`` on ``x[B, H, S, D]`` (a transposed
+    view of the ``[B, S, H, D]`` projection output), ``cos/sin[Bc, S, D]``
+    with ``Bc`` 1 or B."""
+
+    @staticmethod
+    def _run(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, backward: int) -> torch.Tensor:
+        xt = x.transpose(1, 2)
+        if not xt.is_contiguous():
+            xt = xt.contiguous()
+        b, s, h, d = xt.shape
+        out = torch.empty_like(xt)
+        _lib.call("cdlb200_rope", _lib.ptr(xt), _lib.ptr(cos), _lib.ptr(sin), b * s, h, d, cos.shape[0] * s,
+                  backward, _lib.ptr(out), _lib.stream(x.device))
+        return out.transpose(1, 2)
+
+    @staticmethod
+    def forward(ctx, x, cos, sin):
+        ctx.save_for_backward(cos, sin)
+        return RopeFn._run(x, cos, sin, 0)
+
+    @staticmethod
+    def backward(ctx, g):
+        cos, sin = ctx.saved_tensors
+        return RopeFn._run(g, cos, sin, 1), None, None
+
+
+class SwiGLUFn(torch.autograd.Function):
+    """``silu(g) * u`` with both rounded to bf16, as ``LlamaMLP`` computes it."""
+
+    @staticmethod
+    def forward(ctx, g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+        g, u = g.contiguous(), u.contiguous()
+        h = torch.empty_like(g)
+        _lib.call("cdlb200_swiglu_fwd", _lib.ptr(g), _lib.ptr(u), g.numel(), _lib.ptr(h), _lib.stream(g.device))
+        ctx.save_for_backward(g, u)
+        return h
+
+    @staticmethod
+    def backward(ctx, dh: torch.Tensor):
+        g, u = ctx.saved_tensors
+        dh = dh.contiguous()
+        dg, du = torch.empty_like(g), torch.empty_like(u)
+        _lib.call("cdlb200_swiglu_bwd", _lib.ptr(dh), _lib.ptr(g), _lib.ptr(u), g.numel(), _lib.ptr(dg), _lib.ptr(du),
+                  _lib.stream(g.device))
+        return dg, du
+
+
+def _rmsnorm_forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
+    d = hidden_states.shape[-1]
+    if _cuda_bf16(hidden_states, self.weight) and d % 8 == 0 and d <= 2048:
+        return RMSNormFn.apply(hidden_states, self.weight, self.variance_epsilon)
+    return self._cdlb200_eager_forward(hidden_states)
+
+
+def _mlp_forward(self, x: torch.Tensor) -> torch.Tensor:
+    g, u = self.gate_proj(x), self.up_proj(x)
+    if _cuda_bf16(g, u) and g.numel() % 8 == 0 and self.config.hidden_act == "silu":
+        return self.down_proj(SwiGLUFn.apply(g, u))
+    return self.down_proj(self.act_fn(g) * u)
+
+
+_EAGER_ROPE = None
+
+
+def _apply_rotary_pos_emb(q, k, cos, sin, unsqueeze_dim=1):
+    if (unsqueeze_dim == 1 and _cuda_bf16(q, k, cos, sin) and q.shape[-1] % 16 == 0 and cos.dim() == 3
+            and cos.is_contiguous() and sin.is_contiguous() and cos.shape[0] in (1, q.shape[0])):
+        return RopeFn.apply(q, cos, sin), RopeFn.apply(k, cos, sin)
+    return _EAGER_ROPE(q, k, cos, sin, unsqueeze_dim)
+
+
+def patch_llama(model: torch.nn.Module) -> int:
+    """Route the RMSNorm, rotary and SwiGLU parts of a transformers Llama model
+    through the fused kernels; returns the number of modules patched."""
+    global _EAGER_ROPE
+    from transformers.models.llama import modeling_llama as ml
+
+    if _EAGER_ROPE is None:
+        _EAGER_ROPE = ml.apply_rotary_pos_emb
+        ml.apply_rotary_pos_emb = _apply_rotary_pos_emb
+    count = 0
+    for m in model.modules():
+        if isinstance(m, ml.LlamaRMSNorm) and not hasattr(m, "_cdlb200_eager_forward"):
+            m._cdlb200_eager_forward = m.forward
+            m.forward = types.MethodType(_rmsnorm_forward, m)
+            count += 1
+        elif isinstance(m, ml.LlamaMLP) and not getattr(m, "_cdlb200_fused", False):
+            m.forward = types.MethodType(_mlp_forward, m)
+            m._cdlb200_fused = True
+            count += 1
+    return count

@@ -59,7 +59,9 @@ SPECS = {
 }
 
 
-def build_model(spec: ModelSpec, device: torch.device, seed: int = 0) -> nn.Module:
+def build_model(spec: ModelSpec, device: torch.device, seed: int = 0, fused: bool | None = None) -> nn.Module:
+    """Random-init Llama of ``spec`` in bf16.  ``fused`` (default: on CUDA)
+    routes its RMSNorm / rotary / SwiGLU through the fused kernels."""
     from transformers import LlamaConfig, LlamaForCausalLM
 
     cfg = LlamaConfig(
@@ -73,7 +75,12 @@ def build_model(spec: ModelSpec, device: torch.device, seed: int = 0) -> nn.Modu
     torch.manual_seed(seed)
     with torch.device(device):
         model = LlamaForCausalLM(cfg)
-    return model.to(dtype=torch.bfloat16)
+    model = model.to(dtype=torch.bfloat16)
+    if fused if fused is not None else device.type == "cuda":
+        from cdl_b200.model.components.fused import patch_llama
+
+        patch_llama(model)
+    return model
 
 
 def apply_quant(model: nn.Module, backend: str = "nvfp4", simulation: str | None = None) -> int:
@@ -169,10 +176,11 @@ class QatStep:
     """One QAT training step: forward, loss, backward (+ DP all-reduce), clip, AdamW."""
 
     def __init__(self, spec: ModelSpec, device: torch.device, backend: str = "nvfp4", lr: float = 3e-4,
-                 grad_clip: float = 1.0, seed: int = 0, ddp: bool = False, bucket_mb: int = 64):
+                 grad_clip: float = 1.0, seed: int = 0, ddp: bool = False, bucket_mb: int = 64,
+                 fused: bool | None = None):
         self.spec = spec
         self.device = device
-        self.model = build_model(spec, device, seed)
+        self.model = build_model(spec, device, seed, fused)
         self.n_quant = apply_quant(self.model, backend)
         self.model.train()
         params = [p for p in self.model.parameters() if p.requires_grad]
