@@ -26,7 +26,8 @@ from cdl_b200.api.quant import QTensor
 from cdl_b200.core.kernel.dequant import mxfp4_dequant, mxfp8_dequant, nvfp4_dequant
 from cdl_b200.core.kernel.quant import mxfp4_quant, mxfp8_quant, nvfp4_quant
 from cdl_b200.core.mm.swizzle import expand_rows, pad_k, pad_n, swizzle_scale_factors
-from cdl_b200.model.wrapper.ops import mm_fp4, mm_mxfp8
+from cdl_b200.model.wrapper.ops import mm_fp4_direct as mm_fp4
+from cdl_b200.model.wrapper.ops import mm_mxfp8_direct as mm_mxfp8
 
 _DEQ = {"nvfp4": nvfp4_dequant, "mxfp4": mxfp4_dequant, "mxfp8": mxfp8_dequant}
 _QUANT = {"nvfp4": nvfp4_quant, "mxfp4": mxfp4_quant, "mxfp8": mxfp8_quant}

@@ -35,8 +35,7 @@ def _flat(t: torch.Tensor) -> torch.Tensor:
     return t.contiguous().view(torch.uint8)
 
 
-@torch.library.custom_op("cdl_b200::mm_fp4", mutates_args=())
-def mm_fp4(
+def mm_fp4_direct(
     a: torch.Tensor,
     b: torch.Tensor,
     a_scale: torch.Tensor,
@@ -45,6 +44,7 @@ def mm_fp4(
     block_size: int,
     use_nvfp4: bool,
 ) -> torch.Tensor:
+    """``mm_fp4`` without the operator dispatch (what the QLinear backends call)."""
     dev = _lib.require_cuda(a, b, a_scale, b_scale, alpha)
     a = a.contiguous().view(torch.uint8)
     brows = _storage_rows(b).view(torch.uint8)
@@ -61,13 +61,26 @@ def mm_fp4(
     return out
 
 
+@torch.library.custom_op("cdl_b200::mm_fp4", mutates_args=())
+def mm_fp4(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    a_scale: torch.Tensor,
+    b_scale: torch.Tensor,
+    alpha: torch.Tensor,
+    block_size: int,
+    use_nvfp4: bool,
+) -> torch.Tensor:
+    return mm_fp4_direct(a, b, a_scale, b_scale, alpha, block_size, use_nvfp4)
+
+
 @mm_fp4.register_fake
 def _(a, b, a_scale, b_scale, alpha, block_size, use_nvfp4):
     return torch.empty(a.shape[0], b.shape[1], dtype=torch.bfloat16, device=a.device)
 
 
-@torch.library.custom_op("cdl_b200::mm_mxfp8", mutates_args=())
-def mm_mxfp8(a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor, b_scale: torch.Tensor) -> torch.Tensor:
+def mm_mxfp8_direct(a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor, b_scale: torch.Tensor) -> torch.Tensor:
+    """``mm_mxfp8`` without the operator dispatch."""
     dev = _lib.require_cuda(a, b, a_scale, b_scale)
     a = a.contiguous().view(torch.uint8)
     brows = _storage_rows(b).view(torch.uint8)
@@ -81,6 +94,11 @@ def mm_mxfp8(a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor, b_scale: t
         None, m, n, k, _lib.ptr(out), n, None, _lib.stream(dev),
     )
     return out
+
+
+@torch.library.custom_op("cdl_b200::mm_mxfp8", mutates_args=())
+def mm_mxfp8(a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor, b_scale: torch.Tensor) -> torch.Tensor:
+    return mm_mxfp8_direct(a, b, a_scale, b_scale)
 
 
 @mm_mxfp8.register_fake
