@@ -59,6 +59,22 @@ SPECS = {
 }
 
 
+_CAUSAL_SDPA = "cdl_b200_causal_sdpa"
+
+
+def _causal_attention() -> str:
+    """transformers' SDPA attention registered under a name that has no mask
+    builder: the model then passes no mask and SDPA runs with is_causal=True,
+    which is the attention of independent, unpadded sequences -- the only
+    inputs of this step.  It skips the packed-sequence probe of the mask
+    builder, a device-to-host read on every forward."""
+    from transformers import AttentionInterface
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+
+    AttentionInterface.register(_CAUSAL_SDPA, sdpa_attention_forward)
+    return _CAUSAL_SDPA
+
+
 def build_model(spec: ModelSpec, device: torch.device, seed: int = 0, fused: bool | None = None) -> nn.Module:
     """Random-init Llama of ``spec`` in bf16.  ``fused`` (default: on CUDA)
     routes its RMSNorm / rotary / SwiGLU through the fused kernels."""
@@ -71,7 +87,7 @@ def build_model(spec: ModelSpec, device: torch.device, seed: int = 0, fused: boo
         rms_norm_eps=1e-5, tie_word_embeddings=spec.tied, initializer_range=0.02, hidden_act="silu",
         attention_bias=False, mlp_bias=False, use_cache=False,
     )
-    cfg._attn_implementation = "sdpa"
+    cfg._attn_implementation = _causal_attention()
     torch.manual_seed(seed)
     with torch.device(device):
         model = LlamaForCausalLM(cfg)
@@ -177,7 +193,7 @@ class QatStep:
 
     def __init__(self, spec: ModelSpec, device: torch.device, backend: str = "nvfp4", lr: float = 3e-4,
                  grad_clip: float = 1.0, seed: int = 0, ddp: bool = False, bucket_mb: int = 64,
-                 fused: bool | None = None):
+                 fused: bool | None = None, graph: bool = False):
         self.spec = spec
         self.device = device
         self.model = build_model(spec, device, seed, fused)
@@ -187,10 +203,12 @@ class QatStep:
         self.params = params
         decay = [p for p in params if p.ndim > 1]
         no_decay = [p for p in params if p.ndim <= 1]
-        fused = device.type == "cuda"
+        on_cuda = device.type == "cuda"
         self.opt = torch.optim.AdamW(
             [{"params": decay, "weight_decay": 0.0}, {"params": no_decay, "weight_decay": 0.0}],
-            lr=lr, betas=(0.9, 0.95), fused=fused, foreach=not fused)
+            lr=lr, betas=(0.9, 0.95), fused=on_cuda, foreach=not on_cuda, capturable=graph and on_cuda)
+        self.graph_mode = graph and on_cuda
+        self._graph = None
         self.grad_clip = grad_clip
         self.net = LossModule(self.model)
         if ddp:
@@ -199,13 +217,39 @@ class QatStep:
             self.net = DDP(self.net, device_ids=[device.index] if device.type == "cuda" else None,
                            bucket_cap_mb=bucket_mb, gradient_as_bucket_view=True, static_graph=True)
 
-    def step(self, input_ids: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    def _eager_step(self, input_ids: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         loss = self.net(input_ids)
         loss.backward()
         gnorm = torch.nn.utils.clip_grad_norm_(self.params, self.grad_clip, foreach=True)
         self.opt.step()
         self.opt.zero_grad(set_to_none=True)
         return loss.detach(), gnorm.detach()
+
+    def step(self, input_ids: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """One training step.  In graph mode the first call runs warm-up steps
+        on a side stream and captures the whole step (forward, backward,
+        clipping, AdamW) in a CUDA graph; every call then copies the tokens
+        into the graph's input buffer and replays it.  The returned loss and
+        gradient norm are the graph's output buffers."""
+        if not self.graph_mode:
+            return self._eager_step(input_ids)
+        if self._graph is None:
+            self._capture(input_ids)
+        self._static_ids.copy_(input_ids, non_blocking=True)
+        self._graph.replay()
+        return self._static_out
+
+    def _capture(self, input_ids: torch.Tensor, warmup: int = 3) -> None:
+        self._static_ids = input_ids.detach().clone()
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self._eager_step(self._static_ids)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        self._graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self._graph):
+            self._static_out = self._eager_step(self._static_ids)
 
 
 def random_tokens(batch: int, seq: int, vocab: int, seed: int, device: torch.device) -> torch.Tensor:
