@@ -347,7 +347,8 @@ def qat_workload(name, dev, rank, world, backend="nvfp4"):
         "step": lambda i: step.step(pool[i % len(pool)]), "e2e_step": e2e_step, "graph": False,
         "units_per_step": batch * seq, "unit": "tokens/s", "metric": "SmolLM2 NVFP4 QAT tokens/s",
         "dtype": ("nvfp4 fwd/dgrad/wgrad GEMMs (e2m1/ue4m3)" if qbwd else
-                  "nvfp4 fwd GEMMs (e2m1/ue4m3), bf16 dgrad/wgrad as cdl") + ", bf16 params + fused AdamW",
+                  "nvfp4 fwd GEMMs (e2m1/ue4m3), bf16 dgrad/wgrad as cdl") + ", bf16 params, clip + AdamW "
+                 f"({step.optimizer})",
         "config": {"workload": f"{name} {'C4' if name == 'qat_135m' else 'C5'} {spec.name} QAT step, "
                                f"{batch}x{seq} tokens per rank, AdamW lr 3e-4, backend {backend}",
                    "backend": backend,
@@ -357,8 +358,10 @@ def qat_workload(name, dev, rank, world, backend="nvfp4"):
         "flops_per_unit": qat.flops_per_token(spec, seq), "kernel": "full QAT step",
         # per QLinear: quantize x and w, swizzle both scale sets, GEMM (5); backward: dequantize w and x
         # (2), or with the quantized backward quantize g, g^T, w^T, x^T (1 + 3 x amax + transpose) and
-        # two GEMMs (9)
-        "launches_per_step": (14 if qbwd else 7) * step.n_quant,
+        # two GEMMs (9).  Per decoder layer: RMSNorm fwd x2, bwd x2 (+ column sum) = 6, RoPE 4, SwiGLU 2;
+        # the final norm 3; clip + AdamW 3.
+        "launches_per_step": ((14 if qbwd else 7) * step.n_quant + 12 * spec.layers + 3
+                              + (3 if step.optimizer == "fused" else 0)),
     }
 
 

@@ -35,6 +35,8 @@ _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _I = ctypes.c_int
 _SZ = ctypes.c_size_t
+_F = ctypes.c_float
+_D = ctypes.c_double
 
 # name -> (restype, argtypes); every symbol declared in include/*.h
 SIGNATURES: dict[str, tuple] = {
@@ -46,6 +48,7 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_mxfp4_quant": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P]),
     "cdlb200_mxfp8_quant": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P]),
     "cdlb200_fp4_dequant": (_I, [_P, _P, _P, _I64, _I64, _I, _I, _P, _P]),
+    "cdlb200_fp4_dequant_swizzled": (_I, [_P, _P, _P, _I64, _I64, _I, _I, _P, _P]),
     "cdlb200_mxfp8_dequant": (_I, [_P, _P, _P, _I64, _I64, _P, _P]),
     "cdlb200_swizzle_scales": (_I, [_P, _I64, _I64, _P, _P]),
     "cdlb200_mm_fp4": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _P, _I64, _P, _P]),
@@ -57,7 +60,16 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_rope": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _P, _P]),
     "cdlb200_swiglu_fwd": (_I, [_P, _P, _I64, _P, _P]),
     "cdlb200_swiglu_bwd": (_I, [_P, _P, _P, _I64, _P, _P, _P]),
+    "cdlb200_cross_entropy": (_I, [_P, _P, _I64, _I64, _F, _P, _P]),
+    "cdlb200_clip_adamw_workspace_bytes": (_I64, [_P, _I]),
+    "cdlb200_clip_adamw": (_I, [_P, _I, _D, _D, _D, _D, _D, _D, _P, _I64, _P, _P]),
 }
+
+
+class AdamwTensor(ctypes.Structure):
+    """``cdlb200_adamw_tensor`` (include/cdlb200_step.h)."""
+
+    _fields_ = [("param", _P), ("grad", _P), ("exp_avg", _P), ("exp_avg_sq", _P), ("numel", _I64)]
 
 
 class CdlB200Error(RuntimeError):

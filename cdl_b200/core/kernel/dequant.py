@@ -13,7 +13,7 @@ import torch
 from cdl_b200 import _lib
 
 
-def _fp4_dequant(packed, scale, alpha, group_size: int, scale_is_e8m0: bool) -> torch.Tensor:
+def _fp4_dequant(packed, scale, alpha, group_size: int, scale_is_e8m0: bool, swizzled: bool = False) -> torch.Tensor:
     dev = _lib.require_cuda(packed, scale, alpha)
     rows, half_k = packed.shape
     k = half_k * 2
@@ -24,18 +24,21 @@ def _fp4_dequant(packed, scale, alpha, group_size: int, scale_is_e8m0: bool) -> 
     scale = scale.contiguous()
     alpha = alpha.reshape(-1).float().contiguous()
     _lib.call(
-        "cdlb200_fp4_dequant", _lib.ptr(packed), _lib.ptr(scale), _lib.ptr(alpha), rows, k,
-        group_size, int(scale_is_e8m0), _lib.ptr(out), _lib.stream(dev),
+        "cdlb200_fp4_dequant_swizzled" if swizzled else "cdlb200_fp4_dequant", _lib.ptr(packed), _lib.ptr(scale),
+        _lib.ptr(alpha), rows, k, group_size, int(scale_is_e8m0), _lib.ptr(out), _lib.stream(dev),
     )
     return out
 
 
-def nvfp4_dequant(packed: torch.Tensor, scale: torch.Tensor, alpha: torch.Tensor, block_k: int = 1024) -> torch.Tensor:
-    return _fp4_dequant(packed, scale, alpha, 16, False)
+def nvfp4_dequant(packed: torch.Tensor, scale: torch.Tensor, alpha: torch.Tensor, block_k: int = 1024, *,
+                  swizzled: bool = False) -> torch.Tensor:
+    """``swizzled=True``: ``scale`` is in the 128x4 GEMM layout (a B200 extension)."""
+    return _fp4_dequant(packed, scale, alpha, 16, False, swizzled)
 
 
-def mxfp4_dequant(packed: torch.Tensor, scale: torch.Tensor, alpha: torch.Tensor, block_k: int = 1024) -> torch.Tensor:
-    return _fp4_dequant(packed, scale, alpha, 32, True)
+def mxfp4_dequant(packed: torch.Tensor, scale: torch.Tensor, alpha: torch.Tensor, block_k: int = 1024, *,
+                  swizzled: bool = False) -> torch.Tensor:
+    return _fp4_dequant(packed, scale, alpha, 32, True, swizzled)
 
 
 def mxfp8_dequant(

@@ -20,6 +20,8 @@ flow to the unquantized proxies):
 
 from __future__ import annotations
 
+import weakref
+
 import torch
 
 from cdl_b200.api.quant import QTensor
@@ -53,10 +55,28 @@ def _quantized_grads(fmt: str, g: torch.Tensor, x: torch.Tensor | None, w: torch
     return dx, dw
 
 
+# dequantized activations of recent backward calls, most recent first: the
+# linears that share an input (q/k/v, gate/up) share its codes tensor, so its
+# backward dequantize runs once
+_DEQUANTIZED: list = []
+
+
+def _dequant_activation(deq, codes, scales, alpha, kw):
+    key = (codes.data_ptr(), codes._version, scales.data_ptr(), bool(kw))
+    for ref, k, out in _DEQUANTIZED:
+        if k == key and ref() is codes:
+            return out
+    out = deq(codes, scales, alpha, **kw)
+    _DEQUANTIZED.insert(0, (weakref.ref(codes), key, out))
+    del _DEQUANTIZED[2:]
+    return out
+
+
 class BlockScaledMatMul(torch.autograd.Function):
     @staticmethod
     def forward(ctx, fmt: str, x: QTensor, x_proxy, w: QTensor, w_proxy, quantized_backward: bool = False):
         ctx.fmt = fmt
+        ctx.swizzled = False
         # the quantized backward needs every GEMM dimension to be a multiple of 32
         ctx.qbwd = bool(quantized_backward) and x_proxy is not None and w_proxy is not None and all(
             d % 32 == 0 for d in (*x_proxy.shape, w_proxy.shape[0]))
@@ -64,6 +84,17 @@ class BlockScaledMatMul(torch.autograd.Function):
             ctx.proxies = (x_proxy.reshape(-1, x_proxy.shape[-1]), w_proxy)
         ctx.x_k = x_proxy.shape[-1] if x_proxy is not None else None
         ctx.w_k = w_proxy.shape[-1] if w_proxy is not None else None
+        if (fmt != "mxfp8" and hasattr(x, "encode_swizzled") and hasattr(w, "encode_swizzled")
+                and x.k == w.k and x.k % 32 == 0 and w.theta.shape[0] % 8 == 0):
+            # codes and GEMM-layout scales from one quantize launch per operand;
+            # the backward dequantizes from the same swizzled scales
+            x_theta, x_q, x_alpha = x.encode_swizzled(fmt)
+            w_theta, w_q, w_alpha = w.encode_swizzled(fmt)
+            if not ctx.qbwd:
+                ctx.swizzled = True
+                ctx.save_for_backward(x_theta, x_q, x_alpha, w_theta, w_q, w_alpha)
+            return mm_fp4(x_theta, w_theta.T, x_q, w_q.T, x_alpha * w_alpha, 16 if fmt == "nvfp4" else 32,
+                          fmt == "nvfp4")
         x_theta, x_q, x_alpha = getattr(x, fmt)()
         w_theta, w_q, w_alpha = getattr(w, fmt)()
         x_theta = x_theta.reshape(-1, x_theta.shape[-1])
@@ -103,10 +134,11 @@ class BlockScaledMatMul(torch.autograd.Function):
         if ctx.fmt == "mxfp8":
             x_theta = x_theta.view(torch.float8_e4m3fn)
             w_theta = w_theta.view(torch.float8_e4m3fn)
+        kw = {"swizzled": True} if ctx.swizzled else {}
         if ctx.x_k is not None:
-            dx = grad_output @ deq(w_theta, w_q, w_alpha)[:, : ctx.x_k]
+            dx = grad_output @ deq(w_theta, w_q, w_alpha, **kw)[:, : ctx.x_k]
         if ctx.w_k is not None:
-            dw = grad_output.T @ deq(x_theta, x_q, x_alpha)[:, : ctx.w_k]
+            dw = grad_output.T @ _dequant_activation(deq, x_theta, x_q, x_alpha, kw)[:, : ctx.w_k]
         return None, None, dx, None, dw, None
 
 

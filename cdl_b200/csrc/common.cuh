@@ -122,6 +122,21 @@ __host__ __device__ __forceinline__ int64_t swizzle_offset(int64_t r, int64_t c,
     return (((r >> 7) * c4 + (c >> 2)) * 32 + (r & 31)) * 16 + ((r >> 5) & 3) * 4 + (c & 3);
 }
 
+// Quotient by a divisor fixed for a launch, for numerators below 2^31, by
+// one multiply-high (Granlund & Montgomery, "Division by invariant integers
+// using multiplication", PLDI 1994): with l = ceil(log2 d) and
+// m = floor(2^32 (2^l - d) / d) + 1, n / d = (mulhi(m, n) + n) >> l.
+struct FastDiv {
+    uint32_t d, m, l;
+    FastDiv() : d(1), m(1), l(0) {}
+    explicit FastDiv(uint32_t div) : d(div < 1 ? 1 : div) {
+        l = 0;
+        while ((1ull << l) < d) ++l;
+        m = (uint32_t)(((1ull << 32) * ((1ull << l) - d)) / d + 1);
+    }
+    __device__ __forceinline__ uint32_t div(uint32_t n) const { return (__umulhi(m, n) + n) >> l; }
+};
+
 // Streaming 16-byte global load that does not allocate in L1.
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
     uint4 v;

@@ -72,6 +72,92 @@ __global__ void fp4_dequant_generic_kernel(const uint8_t* __restrict__ packed,
     }
 }
 
+// Eight e2m1 codes (one 32-bit word, element 2j in the low nibble of byte j)
+// -> four f16x2 by the hardware converter (every e2m1 value is exact in f16).
+__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t (&h)[4]) {
+    asm("{\n"
+        ".reg .b8 b0, b1, b2, b3;\n"
+        "mov.b32 {b0, b1, b2, b3}, %4;\n"
+        "cvt.rn.f16x2.e2m1x2 %0, b0;\n"
+        "cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+        "cvt.rn.f16x2.e2m1x2 %2, b2;\n"
+        "cvt.rn.f16x2.e2m1x2 %3, b3;\n"
+        "}"
+        : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+        : "r"(w));
+}
+
+__device__ __forceinline__ void f16x2_to_f32(uint32_t h, float& lo, float& hi) {
+    asm("{\n"
+        ".reg .f16 a, b;\n"
+        "mov.b32 {a, b}, %2;\n"
+        "cvt.f32.f16 %0, a;\n"
+        "cvt.f32.f16 %1, b;\n"
+        "}"
+        : "=f"(lo), "=f"(hi)
+        : "r"(h));
+}
+
+// FP4 dequantize, 32 elements (16 code bytes) per thread and step with two
+// steps in flight; scales read from the linear [rows, k/BLOCK] layout or, with
+// SWZ, from the 128x4 tiled layout the GEMM consumes (block b of the flat
+// array sits at row b / nb, column b % nb).
+template <int BLOCK, bool E8M0, bool SWZ>
+__global__ void __launch_bounds__(256) fp4_dequant32_kernel(const uint4* __restrict__ packed,
+                                                            const uint8_t* __restrict__ scale,
+                                                            const float* __restrict__ alpha_p, int64_t n32,
+                                                            FastDiv nb, uint32_t c4, uint4* __restrict__ out) {
+    constexpr int kU = 2, kSb = 32 / BLOCK;
+    const float alpha = *alpha_p;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t0 < n32; t0 += kU * stride) {
+        uint4 p[kU];
+        uint32_t sb[kU][kSb];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int64_t t = t0 + u * stride;
+            if (t < n32) {
+                p[u] = ldg_stream(packed + t);
+#pragma unroll
+                for (int j = 0; j < kSb; ++j) {
+                    const int64_t b = t * kSb + j;
+                    int64_t off = b;
+                    if (SWZ) {
+                        const uint32_t r = nb.div((uint32_t)b);
+                        off = swizzle_offset(r, (int64_t)((uint32_t)b - r * nb.d), c4);
+                    }
+                    sb[u][j] = __ldg(scale + off);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int64_t t = t0 + u * stride;
+            if (t >= n32) continue;
+            const uint32_t words[4] = {p[u].x, p[u].y, p[u].z, p[u].w};
+            uint32_t o[16];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t b = sb[u][(i * 8) / BLOCK];
+                const float sc = E8M0 ? e8m0_to_f32(b) : e4m3_to_f32(b);
+                uint32_t h[4];
+                e2m1x8_to_f16x2(words[i], h);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float lo, hi;
+                    f16x2_to_f32(h[j], lo, hi);
+                    o[4 * i + j] = pack_bf16x2(__fmul_rn(__fmul_rn(lo, sc), alpha), __fmul_rn(__fmul_rn(hi, sc), alpha));
+                }
+            }
+            uint4* dst = out + 4 * t;
+            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+            dst[2] = make_uint4(o[8], o[9], o[10], o[11]);
+            dst[3] = make_uint4(o[12], o[13], o[14], o[15]);
+        }
+    }
+}
+
 template <bool HAS_ALPHA>
 __global__ void __launch_bounds__(256) mxfp8_dequant_flat_kernel(const uint4* __restrict__ packed,
                                                                  const uint8_t* __restrict__ scale,
@@ -140,14 +226,44 @@ unsigned grid_for(int64_t work, int per_cta) {
 
 using namespace cdlb200;
 
-extern "C" int cdlb200_fp4_dequant(const void* packed, const void* scale, const float* alpha,
-                                   int64_t rows, int64_t k, int block, int scale_is_e8m0, void* out,
-                                   void* stream) {
+namespace {
+
+int fp4_dequant_impl(const void* packed, const void* scale, const float* alpha, int64_t rows, int64_t k, int block,
+                     int scale_is_e8m0, bool swizzled, void* out, cudaStream_t st) {
     if (rows < 0 || k < 0 || (block != 16 && block != 32)) return CDLB200_ERR_INVALID_ARG;
     if (rows == 0 || k == 0) return CDLB200_OK;
     if (!packed || !scale || !alpha || !out || (k % block) != 0) return CDLB200_ERR_INVALID_ARG;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int64_t n = rows * k;
+    const int64_t nblocks = n / block;
+    const bool vec = aligned(packed, 16) && aligned(out, 16) && (n % 32) == 0 && nblocks < (1ll << 31);
+    if (swizzled && (!vec || (k % 32) != 0)) return CDLB200_ERR_ALIGNMENT;
+    if (vec) {
+        const int64_t n32 = n / 32;
+        const FastDiv nb((uint32_t)(k / block));
+        const uint32_t c4 = (uint32_t)((k / block + 3) / 4);
+        const unsigned grid = grid_for(n32, 512);
+#define CDLB200_FP4_DQ32(BLK, E8)                                                                            \
+    if (swizzled)                                                                                            \
+        fp4_dequant32_kernel<BLK, E8, true><<<grid, 256, 0, st>>>(                                           \
+            static_cast<const uint4*>(packed), static_cast<const uint8_t*>(scale), alpha, n32, nb, c4,       \
+            static_cast<uint4*>(out));                                                                       \
+    else                                                                                                     \
+        fp4_dequant32_kernel<BLK, E8, false><<<grid, 256, 0, st>>>(                                          \
+            static_cast<const uint4*>(packed), static_cast<const uint8_t*>(scale), alpha, n32, nb, c4,       \
+            static_cast<uint4*>(out));
+        if (block == 16 && !scale_is_e8m0) {
+            CDLB200_FP4_DQ32(16, false)
+        } else if (block == 16) {
+            CDLB200_FP4_DQ32(16, true)
+        } else if (!scale_is_e8m0) {
+            CDLB200_FP4_DQ32(32, false)
+        } else {
+            CDLB200_FP4_DQ32(32, true)
+        }
+#undef CDLB200_FP4_DQ32
+        CDLB200_CHECK_LAUNCH();
+        return CDLB200_OK;
+    }
     const bool flat = aligned(packed, 8) && aligned(out, 16);
 #define CDLB200_FP4_DQ(BLK, E8)                                                                   \
     if (flat)                                                                                     \
@@ -170,6 +286,22 @@ extern "C" int cdlb200_fp4_dequant(const void* packed, const void* scale, const 
 #undef CDLB200_FP4_DQ
     CDLB200_CHECK_LAUNCH();
     return CDLB200_OK;
+}
+
+}  // namespace
+
+extern "C" int cdlb200_fp4_dequant(const void* packed, const void* scale, const float* alpha,
+                                   int64_t rows, int64_t k, int block, int scale_is_e8m0, void* out,
+                                   void* stream) {
+    return fp4_dequant_impl(packed, scale, alpha, rows, k, block, scale_is_e8m0, false, out,
+                            static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cdlb200_fp4_dequant_swizzled(const void* packed, const void* scale, const float* alpha,
+                                            int64_t rows, int64_t k, int block, int scale_is_e8m0, void* out,
+                                            void* stream) {
+    return fp4_dequant_impl(packed, scale, alpha, rows, k, block, scale_is_e8m0, true, out,
+                            static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int cdlb200_mxfp8_dequant(const void* packed, const void* scale, const float* alpha,

@@ -240,6 +240,80 @@ __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const uint4* __restrict
     }
 }
 
+// ---------------------------------------------------------------------------
+// Cross entropy over bf16 logits, one CTA per row, three passes over the row
+// (the second and third come from L2):
+//   m = max x,  lse = log(sum exp(x - m)) + m,  loss = lse - x[t],
+//   x <- bf16((exp(x - lse) - [j == t]) * scale)  (in place; scale = 1/n gives
+//                                                  d(sum loss / n)/dx, as torch's
+//                                                  division by a scalar n does)
+// A target outside [0, vocab) (an ignored position) gives loss 0 and a zero
+// gradient row.
+// ---------------------------------------------------------------------------
+constexpr int kXentThreads = 512;
+
+template <bool MAX>
+__device__ __forceinline__ float block_reduce(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float w = __shfl_xor_sync(0xffffffffu, v, o);
+        v = MAX ? fmaxf(v, w) : v + w;
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();  // red[] is reused by consecutive reductions
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    v = lane < kXentThreads / 32 ? red[lane] : (MAX ? -INFINITY : 0.0f);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float w = __shfl_xor_sync(0xffffffffu, v, o);
+        v = MAX ? fmaxf(v, w) : v + w;
+    }
+    return v;
+}
+
+__global__ void __launch_bounds__(kXentThreads) xent_kernel(uint4* __restrict__ logits,
+                                                            const int64_t* __restrict__ targets, int64_t vocab,
+                                                            float scale, float* __restrict__ loss) {
+    __shared__ float red[32];
+    const int64_t row = blockIdx.x;
+    const int nv = (int)(vocab / 8);
+    uint4* x = logits + row * nv;
+    const int64_t t = targets[row];
+    const bool valid = t >= 0 && t < vocab;
+    const float xt = valid ? bf_lo((uint32_t)reinterpret_cast<const uint16_t*>(x)[t]) : 0.0f;
+
+    float m = -INFINITY;
+    for (int i = threadIdx.x; i < nv; i += kXentThreads) {
+        float f[8];
+        unpack8(x[i], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) m = fmaxf(m, f[j]);
+    }
+    m = block_reduce<true>(m, red);
+    const float mu = isinf(m) ? 0.0f : m;  // as torch.logsumexp: an infinite max is not subtracted
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < nv; i += kXentThreads) {
+        float f[8];
+        unpack8(x[i], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += expf(f[j] - mu);
+    }
+    s = block_reduce<false>(s, red);
+    const float lse = logf(s) + mu;
+    if (threadIdx.x == 0) loss[row] = valid ? lse - xt : 0.0f;
+    for (int i = threadIdx.x; i < nv; i += kXentThreads) {
+        float f[8];
+        unpack8(x[i], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float p = valid ? expf(f[j] - lse) - (8 * (int64_t)i + j == t ? 1.0f : 0.0f) : 0.0f;
+            f[j] = __fmul_rn(p, scale);
+        }
+        x[i] = pack8(f);
+    }
+}
+
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int grid_for(int64_t items, int per_block) {
@@ -350,6 +424,19 @@ extern "C" int cdlb200_swiglu_bwd(const void* dh, const void* g, const void* u, 
     swiglu_bwd_kernel<<<grid_for(n / 8, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint4*>(dh), static_cast<const uint4*>(g), static_cast<const uint4*>(u), n / 8,
         static_cast<uint4*>(dg), static_cast<uint4*>(du));
+    CDLB200_CHECK_LAUNCH();
+    return CDLB200_OK;
+}
+
+extern "C" int cdlb200_cross_entropy(void* logits, const int64_t* targets, int64_t rows, int64_t vocab,
+                                     float scale, float* loss, void* stream) {
+    if (rows < 0 || vocab <= 0 || (vocab % 8) != 0) return CDLB200_ERR_INVALID_ARG;
+    if (rows == 0) return CDLB200_OK;
+    if (!logits || !targets || !loss) return CDLB200_ERR_INVALID_ARG;
+    if (!al16(logits)) return CDLB200_ERR_ALIGNMENT;
+    if (rows > 0x7fffffffLL) return CDLB200_ERR_INVALID_ARG;
+    xent_kernel<<<(unsigned)rows, kXentThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<uint4*>(logits), targets, vocab, scale, loss);
     CDLB200_CHECK_LAUNCH();
     return CDLB200_OK;
 }

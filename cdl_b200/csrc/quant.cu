@@ -339,7 +339,7 @@ __global__ void empty_alpha_kernel(float* gmax_out, float* alpha_out) {
 template <int FMT, bool SWZ, int U>
 __global__ void __launch_bounds__(256) quant_flat_kernel(const uint4* __restrict__ x, int64_t nvec,
                                                          uint8_t* __restrict__ packed,
-                                                         uint8_t* __restrict__ scale, int64_t nb,
+                                                         uint8_t* __restrict__ scale, FastDiv nb,
                                                          int64_t c4, const float* __restrict__ gmax_p,
                                                          const float* __restrict__ alpha_p) {
     constexpr int B = FmtTraits<FMT>::kBlock;
@@ -379,7 +379,10 @@ __global__ void __launch_bounds__(256) quant_flat_kernel(const uint4* __restrict
                 if ((lane & (VPB - 1)) == 0) {
                     const int64_t blk = v / VPB;
                     int64_t off = blk;
-                    if constexpr (SWZ) off = swizzle_offset(blk / nb, blk % nb, c4);
+                    if constexpr (SWZ) {  // the host guarantees < 2^31 blocks with SWZ
+                        const uint32_t r = nb.div((uint32_t)blk);
+                        off = swizzle_offset(r, (int64_t)((uint32_t)blk - r * nb.d), c4);
+                    }
                     scale[off] = (uint8_t)bc.byte;
                 }
             }
@@ -393,7 +396,7 @@ __global__ void __launch_bounds__(256) quant_flat_kernel(const uint4* __restrict
 template <bool SWZ, int U>
 __global__ void __launch_bounds__(256) nvfp4_flat_kernel(const uint4* __restrict__ x, int64_t nblk,
                                                          uint2* __restrict__ packed,
-                                                         uint8_t* __restrict__ scale, int64_t nb,
+                                                         uint8_t* __restrict__ scale, FastDiv nb,
                                                          int64_t c4, const float* __restrict__ gmax_p,
                                                          const float* __restrict__ alpha_p) {
     const Nvfp4Tensor g = nvfp4_tensor(gmax_p, alpha_p);
@@ -416,7 +419,10 @@ __global__ void __launch_bounds__(256) nvfp4_flat_kernel(const uint4* __restrict
                 const uint32_t byte = nvfp4_block16(w0[u], w1[u], max(amax8(w0[u]), amax8(w1[u])), g, out);
                 packed[b] = out;
                 int64_t off = b;
-                if constexpr (SWZ) off = swizzle_offset(b / nb, b % nb, c4);
+                if constexpr (SWZ) {  // the host guarantees < 2^31 blocks with SWZ
+                    const uint32_t r = nb.div((uint32_t)b);
+                    off = swizzle_offset(r, (int64_t)((uint32_t)b - r * nb.d), c4);
+                }
                 scale[off] = (uint8_t)byte;
             }
         }
@@ -573,7 +579,7 @@ __device__ __forceinline__ uint2 encode_block(const uint4& a0, const uint4& a1, 
 template <bool SWZ>
 __global__ void __launch_bounds__(kFusedThreads, 2) nvfp4_fused_kernel(
     const uint4* __restrict__ x, int64_t nblk, uint2* __restrict__ packed, uint8_t* __restrict__ scale,
-    int64_t nb, int64_t c4, uint8_t* __restrict__ ws, float* __restrict__ gmax_out,
+    FastDiv nb, int64_t c4, uint8_t* __restrict__ ws, float* __restrict__ gmax_out,
     float* __restrict__ alpha_out) {
     __shared__ uint32_t red[kFusedThreads / 32];
     __shared__ ScaleEntry table[128];
@@ -683,7 +689,12 @@ __global__ void __launch_bounds__(kFusedThreads, 2) nvfp4_fused_kernel(
             const uint32_t byte = nvfp4_scale_byte(mag, t);
             const int64_t b = bs[u];
             packed[b] = encode_block(v[2 * u], v[2 * u + 1], byte, table[byte], mode);
-            scale[SWZ ? swizzle_offset(b / nb, b % nb, c4) : b] = (uint8_t)byte;
+            int64_t off = b;
+            if constexpr (SWZ) {  // with SWZ the host guarantees nblk < 2^31
+                const uint32_t r = nb.div((uint32_t)b);
+                off = swizzle_offset(r, (int64_t)((uint32_t)b - r * nb.d), c4);
+            }
+            scale[off] = (uint8_t)byte;
         }
     }
 
@@ -880,8 +891,11 @@ int launch_encode(const void* x, int64_t rows, int64_t k, int64_t ldx, int trans
     const int64_t c4 = (nb + 3) / 4;
     const int64_t pstride = FmtTraits<FMT>::kFp4 ? nb * B / 2 : nb * B;
     const int sms = num_sms();
+    // the flat kernels locate a swizzled scale with 32-bit block indices
     const bool flat = !transpose && ldx == k && (k % B) == 0 && aligned(x, 16) &&
-                      aligned(packed, (FmtTraits<FMT>::kFp4 && FMT != kNVFP4) ? 4 : 8);
+                      aligned(packed, (FmtTraits<FMT>::kFp4 && FMT != kNVFP4) ? 4 : 8) &&
+                      (!SWZ || rows * nb < (1ll << 31));
+    const FastDiv nbd((uint32_t)(nb < (1ll << 31) ? nb : 1));
     if (flat && FMT == kNVFP4) {
         constexpr int U = 2;
         const int64_t nblk = rows * k / 16;
@@ -889,7 +903,7 @@ int launch_encode(const void* x, int64_t rows, int64_t k, int64_t ldx, int trans
         grid = grid < (int64_t)sms * 8 ? grid : (int64_t)sms * 8;
         nvfp4_flat_kernel<SWZ, U><<<(unsigned)grid, 256, 0, st>>>(
             reinterpret_cast<const uint4*>(x), nblk, static_cast<uint2*>(packed),
-            static_cast<uint8_t*>(scale), nb, c4, gmax, alpha);
+            static_cast<uint8_t*>(scale), nbd, c4, gmax, alpha);
     } else if (flat) {
         constexpr int U = 4;
         const int64_t nvec = rows * k / 8;
@@ -897,7 +911,7 @@ int launch_encode(const void* x, int64_t rows, int64_t k, int64_t ldx, int trans
         grid = grid < (int64_t)sms * 8 ? grid : (int64_t)sms * 8;
         quant_flat_kernel<FMT, SWZ, U><<<(unsigned)grid, 256, 0, st>>>(
             reinterpret_cast<const uint4*>(x), nvec, static_cast<uint8_t*>(packed),
-            static_cast<uint8_t*>(scale), nb, c4, gmax, alpha);
+            static_cast<uint8_t*>(scale), nbd, c4, gmax, alpha);
     } else if (transpose) {
         const int64_t tiles = ((k + kTrCols - 1) / kTrCols) * ((rows + TrTile<FMT>::kRows - 1) / TrTile<FMT>::kRows);
         int64_t grid = tiles < (int64_t)sms * 4 ? tiles : (int64_t)sms * 4;
@@ -988,6 +1002,8 @@ int launch_fused_impl(const void* x, int64_t rows, int64_t k, void* packed, void
     if (grid > kMaxAmaxGrid) grid = kMaxAmaxGrid;
     if (grid > nchunk) grid = nchunk;
     const int64_t nb = k / 16, c4 = (nb + 3) / 4;
+    if (SWZ && nblk >= (1ll << 31)) return CDLB200_ERR_INVALID_ARG;
+    const FastDiv nbd((uint32_t)(nb < (1ll << 31) ? nb : 1));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(kFusedThreads);
@@ -1000,7 +1016,7 @@ int launch_fused_impl(const void* x, int64_t rows, int64_t k, void* packed, void
     cfg.numAttrs = 1;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, nvfp4_fused_kernel<SWZ>, reinterpret_cast<const uint4*>(x),
                                              nblk, static_cast<uint2*>(packed), static_cast<uint8_t*>(scale),
-                                             nb, c4, ws, gmax, alpha);
+                                             nbd, c4, ws, gmax, alpha);
     if (e != cudaSuccess) {
         (void)cudaGetLastError();
         return CDLB200_ERR_LAUNCH;

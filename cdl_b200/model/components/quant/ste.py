@@ -9,6 +9,7 @@ straight through (identity, no clipping mask); ``dequantize()`` serves the
 
 from __future__ import annotations
 
+import weakref
 from dataclasses import dataclass
 from typing import Literal
 
@@ -19,6 +20,11 @@ from cdl_b200.core.kernel.dequant import mxfp4_dequant, mxfp8_dequant, nvfp4_deq
 from cdl_b200.core.kernel.quant import mxfp4_quant, mxfp8_quant, nvfp4_quant
 
 Simulation = Literal["nvfp4", "mxfp4", "mxfp8"]
+
+# recent activation encodings, most recent first: (weakref to the storage
+# owner, (format, view, version), (codes, scales, alpha))
+_ENCODED: list = []
+_ENCODED_MAX = 4
 
 
 @dataclass
@@ -49,6 +55,32 @@ class SteTensor(QTensor):
 
     def mxfp8(self):
         return self._encode(mxfp8_quant)
+
+    def encode_swizzled(self, fmt: Simulation):
+        """``(codes, scales, alpha)`` of ``theta`` flattened to 2-D, with the
+        scales already in the 128x4 layout of the block-scaled GEMM (one
+        quantize launch, no separate swizzle).  Same codes and scale bytes as
+        ``nvfp4()`` / ``mxfp4()`` / ``mxfp8()``.
+
+        An activation read by several linears (q/k/v, gate/up) is encoded
+        once: the result is kept for the tensor it came from while that tensor
+        is alive and unmodified (same storage owner, view and version)."""
+        fn = {"nvfp4": nvfp4_quant, "mxfp4": mxfp4_quant, "mxfp8": mxfp8_quant}[fmt]
+        theta = self.theta.reshape(-1, self.k)
+        owner = theta._base if theta._base is not None else theta
+        # parameters are excluded: optimizers may update them without a version bump
+        cacheable = not (owner.is_leaf and owner.requires_grad)
+        if cacheable:
+            key = (fmt, theta.data_ptr(), tuple(theta.shape), theta.stride(), theta.dtype, theta._version)
+            for ref, k, res in _ENCODED:
+                if k == key and ref() is owner:
+                    return res
+        with torch.no_grad():
+            res = fn(theta, swizzled=True)
+        if cacheable:
+            _ENCODED.insert(0, (weakref.ref(owner), key, res))
+            del _ENCODED[_ENCODED_MAX:]
+        return res
 
     def dequantize(self) -> torch.Tensor:
         if self.simulation is None:

@@ -9,7 +9,8 @@ is next-token cross entropy through the unquantized LM head, computed the way
 cdl's Liger fused linear cross entropy does it (chunks of tokens; the logits
 are never materialised for the whole batch, and the gradients of the hidden
 states and of the head weight are formed in the same pass); the optimizer is
-AdamW (betas 0.9/0.95, fused on CUDA) with gradient-norm clipping at 1.0.
+AdamW (betas 0.9/0.95) with gradient-norm clipping at 1.0, on CUDA both in
+three launches of ``cdlb200_clip_adamw`` (``train/optim.py``).
 
 Models are built from the BASELINE configurations with random init (std
 0.02) -- no checkpoint is loaded -- and trained on uniform random tokens.
@@ -25,10 +26,12 @@ from __future__ import annotations
 import math
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 import torch.nn.functional as F
 from torch import nn
 
+from cdl_b200 import _lib
 from cdl_b200.model.components.linear import QLinear
 from cdl_b200.model.components.quant.ste import SteQuant
 
@@ -125,30 +128,46 @@ def apply_quant(model: nn.Module, backend: str = "nvfp4", simulation: str | None
 class LinearCrossEntropy(torch.autograd.Function):
     """Mean cross entropy of ``h @ w^T`` against ``targets``, ``chunk`` tokens
     at a time (the algorithm of Liger's fused linear cross entropy, which cdl
-    uses for its LM head, smollm2.py:667-677).  Per chunk: fp32 logits, the
-    log-sum-exp and the loss, then ``d loss / d logits = (softmax - onehot) / n``
-    in the hidden dtype, ``grad_h = dl @ w`` and ``grad_w += dl^T @ h``.  The
-    backward only scales the stored gradients."""
+    uses for its LM head, smollm2.py:667-677).  Per chunk: logits in the
+    hidden dtype, their fp32 log-sum-exp and the loss, then
+    ``d loss / d logits = (softmax - onehot) / n`` in the hidden dtype,
+    ``grad_h = dl @ w`` and ``grad_w += dl^T @ h``.  The backward only scales
+    the stored gradients."""
 
     @staticmethod
     def forward(ctx, h: torch.Tensor, w: torch.Tensor, targets: torch.Tensor, chunk: int) -> torch.Tensor:
         n = h.shape[0]
         grad_h = torch.empty_like(h) if ctx.needs_input_grad[0] else None
         grad_w = torch.zeros_like(w) if ctx.needs_input_grad[1] else None
-        total = torch.zeros((), dtype=torch.float32, device=h.device)
+        # on the GPU one kernel per chunk (cdlb200_cross_entropy) turns the
+        # bf16 logits into per-row losses and, in place, the bf16 gradient
+        kernel = h.is_cuda and h.dtype == torch.bfloat16 and w.shape[0] % 8 == 0
+        if kernel:
+            targets = targets.to(torch.int64).contiguous()
+            rows_loss = torch.empty(n, dtype=torch.float32, device=h.device)
+            inv_n = float(np.float32(1.0) / np.float32(n))
+        else:
+            total = torch.zeros((), dtype=torch.float32, device=h.device)
         for s in range(0, n, chunk):
             hc, tc = h[s:s + chunk], targets[s:s + chunk]
-            logits = (hc @ w.t()).float()
-            lse = torch.logsumexp(logits, dim=1)
-            total += (lse - logits.gather(1, tc[:, None])[:, 0]).sum()
-            p = logits.sub_(lse[:, None]).exp_()
-            p[torch.arange(p.shape[0], device=p.device), tc] -= 1.0
-            dl = p.div_(n).to(h.dtype)
+            if kernel:
+                dl = hc @ w.t()
+                _lib.call("cdlb200_cross_entropy", _lib.ptr(dl), _lib.ptr(tc), dl.shape[0], dl.shape[1], inv_n,
+                          _lib.ptr(rows_loss) + 4 * s, _lib.stream(h.device))
+            else:
+                logits = (hc @ w.t()).float()
+                lse = torch.logsumexp(logits, dim=1)
+                total += (lse - logits.gather(1, tc[:, None])[:, 0]).sum()
+                p = logits.sub_(lse[:, None]).exp_()
+                p[torch.arange(p.shape[0], device=p.device), tc] -= 1.0
+                dl = p.div_(n).to(h.dtype)
             if grad_h is not None:
                 torch.mm(dl, w, out=grad_h[s:s + chunk])
             if grad_w is not None:
                 grad_w.addmm_(dl.t(), hc)
         ctx.save_for_backward(grad_h, grad_w)
+        if kernel:
+            total = rows_loss.sum()
         return total / n
 
     @staticmethod
@@ -193,7 +212,7 @@ class QatStep:
 
     def __init__(self, spec: ModelSpec, device: torch.device, backend: str = "nvfp4", lr: float = 3e-4,
                  grad_clip: float = 1.0, seed: int = 0, ddp: bool = False, bucket_mb: int = 64,
-                 fused: bool | None = None, graph: bool = False):
+                 fused: bool | None = None, graph: bool = False, optimizer: str | None = None):
         self.spec = spec
         self.device = device
         self.model = build_model(spec, device, seed, fused)
@@ -204,9 +223,19 @@ class QatStep:
         decay = [p for p in params if p.ndim > 1]
         no_decay = [p for p in params if p.ndim <= 1]
         on_cuda = device.type == "cuda"
-        self.opt = torch.optim.AdamW(
-            [{"params": decay, "weight_decay": 0.0}, {"params": no_decay, "weight_decay": 0.0}],
-            lr=lr, betas=(0.9, 0.95), fused=on_cuda, foreach=not on_cuda, capturable=graph and on_cuda)
+        # "fused": clip + AdamW through cdlb200_clip_adamw (CUDA); "torch":
+        # clip_grad_norm_ + torch.optim.AdamW (fused kernels on CUDA)
+        self.optimizer = optimizer or ("fused" if on_cuda else "torch")
+        if self.optimizer == "fused":
+            from cdl_b200.train.optim import ClipAdamW
+
+            self.opt = ClipAdamW(params, lr=lr, betas=(0.9, 0.95), weight_decay=0.0, max_norm=grad_clip)
+        elif self.optimizer == "torch":
+            self.opt = torch.optim.AdamW(
+                [{"params": decay, "weight_decay": 0.0}, {"params": no_decay, "weight_decay": 0.0}],
+                lr=lr, betas=(0.9, 0.95), fused=on_cuda, foreach=not on_cuda, capturable=graph and on_cuda)
+        else:
+            raise ValueError(f"unknown optimizer {optimizer!r}")
         self.graph_mode = graph and on_cuda
         self._graph = None
         self.grad_clip = grad_clip
@@ -220,8 +249,11 @@ class QatStep:
     def _eager_step(self, input_ids: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         loss = self.net(input_ids)
         loss.backward()
-        gnorm = torch.nn.utils.clip_grad_norm_(self.params, self.grad_clip, foreach=True)
-        self.opt.step()
+        if self.optimizer == "fused":
+            gnorm = self.opt.step()
+        else:
+            gnorm = torch.nn.utils.clip_grad_norm_(self.params, self.grad_clip, foreach=True)
+            self.opt.step()
         self.opt.zero_grad(set_to_none=True)
         return loss.detach(), gnorm.detach()
 

@@ -119,6 +119,17 @@ int cdlb200_fp4_dequant(const void* packed, const void* scale, const float* alph
                         int64_t k, int block, int scale_is_e8m0, void* out, void* stream);
 
 /*
+ * FP4 dequantize with the scales in the 128x4 tiled layout the block-scaled
+ * GEMM reads ([ceil(rows/128)*128, ceil(k/block/4)*4], as written by the
+ * quantizers with CDLB200_SCALE_SWIZZLED), so that a linear layer can keep one
+ * scale copy for its forward GEMM and its backward dequantize.  Same result
+ * as cdlb200_fp4_dequant on the linear scales.  k % 32 == 0, packed and out
+ * 16-byte aligned (else CDLB200_ERR_ALIGNMENT).
+ */
+int cdlb200_fp4_dequant_swizzled(const void* packed, const void* scale, const float* alpha, int64_t rows,
+                                 int64_t k, int block, int scale_is_e8m0, void* out, void* stream);
+
+/*
  * MXFP8 dequantize: out = bf16(e4m3 * e8m0 [* alpha]).
  * Replaces cdl/core/kernel/dequant.py:121-143 `mxfp8_dequant` / the Triton
  * `_mxfp8_dequant_kernel` (dequant.py:50-72).  alpha may be NULL (None).

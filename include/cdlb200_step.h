@@ -43,6 +43,47 @@ int cdlb200_swiglu_fwd(const void* g, const void* u, int64_t n, void* h, void* s
 /* dg, du of the SwiGLU product above, given dh. */
 int cdlb200_swiglu_bwd(const void* dh, const void* g, const void* u, int64_t n, void* dg, void* du, void* stream);
 
+/* Cross entropy of bf16 logits[rows, vocab] (contiguous, vocab % 8 == 0)
+ * against int64 targets[rows], the per-chunk step of the reference's fused
+ * linear cross entropy (Liger, used by cdl smollm2.py for the LM head):
+ *   lse = log(sum exp(x - max x)) + max x (fp32),  loss[r] = lse - x[r, t_r],
+ *   logits <- bf16((exp(x - lse) - onehot(t_r)) * scale)   (in place),
+ * with scale = 1/n the gradient of sum(loss) / n (torch divides a tensor by a
+ * scalar n as a multiply by the fp32 reciprocal).  A target outside
+ * [0, vocab) gives loss 0 and a zero gradient row. */
+int cdlb200_cross_entropy(void* logits, const int64_t* targets, int64_t rows, int64_t vocab, float scale,
+                          float* loss, void* stream);
+
+/* One parameter tensor of the optimizer below: param, its gradient and the
+ * two AdamW moments, all bf16, contiguous, 16-byte aligned, numel % 8 == 0. */
+typedef struct {
+    void* param;
+    const void* grad;
+    void* exp_avg;
+    void* exp_avg_sq;
+    int64_t numel;
+} cdlb200_adamw_tensor;
+
+/* Device workspace (bytes) cdlb200_clip_adamw needs for these tensors. */
+int64_t cdlb200_clip_adamw_workspace_bytes(const cdlb200_adamw_tensor* tensors, int count);
+
+/* Gradient clipping and one AdamW step over all tensors, as the reference's
+ * training step runs them (cdl smollm2.py: torch.nn.utils.clip_grad_norm_
+ * then torch.optim.AdamW):
+ *   norm_i = bf16(||grad_i||_2), norm = bf16(sqrt(sum norm_i^2)),
+ *   coef   = min(bf16(bf16(1 / bf16(norm + 1e-6)) * max_norm), 1),  g = bf16(grad * coef),
+ *   step  += 1, p -= lr*wd*p, m = b1 m + (1-b1) g, v = b2 v + (1-b2) g^2,
+ *   p -= lr/(1-b1^step) * m / (sqrt(v)/sqrt(1-b2^step) + eps),
+ * with fp32 element arithmetic (bias corrections in double), p/m/v stored
+ * back as bf16; max_norm <= 0 disables
+ * the clip (coef = 1).  The step counter lives in the workspace, which must
+ * be zero-filled before the first step and kept between steps.  grad_norm
+ * (device fp32, optional) receives norm.  Three kernel launches per 512
+ * tensors, no host synchronization. */
+int cdlb200_clip_adamw(const cdlb200_adamw_tensor* tensors, int count, double max_norm, double lr,
+                       double beta1, double beta2, double eps, double weight_decay, void* workspace,
+                       int64_t workspace_bytes, float* grad_norm, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

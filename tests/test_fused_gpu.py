@@ -105,3 +105,62 @@ def test_qat_step_with_fused_modules_tracks_eager():
                          for i in range(20)]
     for a, b in zip(curves[True], curves[False]):
         assert abs(a - b) / b < 5e-3, (a, b)
+
+
+@pytest.mark.parametrize("rows,vocab", [(64, 49152), (37, 1000), (5, 8)])
+def test_cross_entropy_kernel_matches_torch(rows, vocab):
+    """cdlb200_cross_entropy against the torch chunk step it replaces: fp32
+    log-sum-exp of the bf16 logits, per-row loss, bf16 (softmax - onehot) / n.
+    Row 1 carries an ignored target (-100): zero loss and zero gradient."""
+    import numpy as np
+
+    from cdl_b200 import _lib
+
+    gen = torch.Generator("cuda").manual_seed(rows + vocab)
+    logits = (torch.randn(rows, vocab, device="cuda", generator=gen) * 3).bfloat16()
+    targets = torch.randint(0, vocab, (rows,), device="cuda", generator=gen)
+    if rows > 1:
+        targets[1] = -100
+    n = 4 * rows + 3
+    ref = logits.float()
+    lse = torch.logsumexp(ref, dim=1)
+    valid = targets >= 0
+    safe_t = targets.clamp_min(0)
+    ref_loss = torch.where(valid, lse - ref.gather(1, safe_t[:, None])[:, 0], torch.zeros_like(lse))
+    p = (ref - lse[:, None]).exp()
+    p[torch.arange(rows, device="cuda")[valid], targets[valid]] -= 1.0
+    p[~valid] = 0.0
+    ref_grad = p.div_(n).bfloat16()
+
+    out = logits.clone()
+    loss = torch.empty(rows, dtype=torch.float32, device="cuda")
+    _lib.call("cdlb200_cross_entropy", _lib.ptr(out), _lib.ptr(targets), rows, vocab,
+              float(np.float32(1.0) / np.float32(n)), _lib.ptr(loss), _lib.stream(out.device))
+    torch.cuda.synchronize()
+    assert torch.allclose(loss, ref_loss, rtol=1e-5, atol=1e-5)
+    assert _max_ulp(out, ref_grad) <= 1
+    differ = float((out != ref_grad).float().mean())
+    print("cross entropy: elements differing by one bf16 step", differ)
+    assert differ < 1e-3
+    if rows > 1:
+        assert float(out[1].float().abs().max()) == 0.0 and float(loss[1]) == 0.0
+
+
+def test_linear_cross_entropy_matches_plain_loss():
+    """Chunked LinearCrossEntropy (kernel per chunk) against plain fp32-logit
+    cross entropy with autograd: loss and both gradients."""
+    from cdl_b200.train.qat import LinearCrossEntropy
+
+    gen = torch.Generator("cuda").manual_seed(7)
+    n, d, v = 3000, 256, 4096
+    h = (torch.randn(n, d, device="cuda", generator=gen)).bfloat16().requires_grad_()
+    w = (torch.randn(v, d, device="cuda", generator=gen) * 0.05).bfloat16().requires_grad_()
+    t = torch.randint(0, v, (n,), device="cuda", generator=gen)
+    loss = LinearCrossEntropy.apply(h, w, t, 1024)
+    loss.backward()
+    h2, w2 = h.detach().clone().requires_grad_(), w.detach().clone().requires_grad_()
+    ref = torch.nn.functional.cross_entropy((h2 @ w2.t()).float(), t)
+    ref.backward()
+    assert abs(float(loss.detach()) - float(ref.detach())) < 1e-4 * float(ref.detach())
+    assert _rel(h.grad, h2.grad) < 1e-2
+    assert _rel(w.grad, w2.grad) < 1e-2

@@ -1,0 +1,121 @@
+"""ClipAdamW (cdlb200_clip_adamw) against torch's clip_grad_norm_ +
+AdamW(fused=True) on bf16 tensors, the pair the reference's step runs."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+SIZES = [8, 24, 2048, 16384, 16392, 100000, 256 * 1024, 2048 * 2048 + 8]
+
+
+def _ulp_diff(a, b):
+    """|a - b| in units of the bf16 spacing at max(|a|, |b|)."""
+    a, b = a.float(), b.float()
+    mag = torch.maximum(a.abs(), b.abs()).clamp_min(1e-30)
+    ulp = torch.exp2(torch.floor(torch.log2(mag)) - 7)
+    return ((a - b).abs() / ulp)
+
+
+@pytest.mark.parametrize("grad_scale", [1e-4, 1.0])  # clip inactive / active
+def test_clip_adamw_matches_torch(grad_scale):
+    from cdl_b200.train.optim import ClipAdamW
+
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(0)
+    init = [(torch.randn(n, device=dev, generator=gen) * 0.02).to(torch.bfloat16) for n in SIZES]
+    ours = [t.clone().requires_grad_() for t in init]
+    ref = [t.clone().requires_grad_() for t in init]
+    opt = ClipAdamW(ours, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, max_norm=1.0)
+    topt = torch.optim.AdamW(ref, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, fused=True)
+    for step in range(4):
+        grads = [(torch.randn(n, device=dev, generator=gen) * grad_scale).to(torch.bfloat16) for n in SIZES]
+        for p, q, g in zip(ours, ref, grads):
+            p.grad, q.grad = g.clone(), g.clone()
+        norm = opt.step()
+        tnorm = torch.nn.utils.clip_grad_norm_(ref, 1.0, foreach=True)
+        topt.step()
+        opt.zero_grad()
+        topt.zero_grad()
+        assert abs(float(norm) - float(tnorm)) <= float(tnorm) * 2 ** -7, (step, float(norm), float(tnorm))
+        for name, mine, theirs in (("param", ours, ref),
+                                   ("exp_avg", opt.exp_avg, [topt.state[q]["exp_avg"] for q in ref]),
+                                   ("exp_avg_sq", opt.exp_avg_sq, [topt.state[q]["exp_avg_sq"] for q in ref])):
+            d = torch.cat([_ulp_diff(a.detach(), b.detach()) for a, b in zip(mine, theirs)])
+            frac = float((d > 0).float().mean())
+            print(step, name, "max ulp", float(d.max()), "differing", frac)
+            assert frac < 0.02, (step, name)
+            if name == "param":
+                # a moment one ulp apart moves the update by a fraction of
+                # lr, which for a parameter near zero is many of its ulps
+                a = torch.cat([x.detach().float() for x in mine])
+                b = torch.cat([x.detach().float() for x in theirs])
+                ulp = torch.exp2(torch.floor(torch.log2(torch.maximum(a.abs(), b.abs()).clamp_min(1e-30))) - 7)
+                assert bool(((a - b).abs() <= 2 * ulp + 0.05 * 3e-4).all()), (step, name)
+            else:
+                # per step the moments round within one ulp of torch's; they
+                # are recurrences, so a one-ulp difference of an earlier step
+                # carries over, which for a first moment that has cancelled to
+                # near zero is many of its ulps: bound it by the tensor's scale
+                for x, y in zip(mine, theirs):
+                    x, y = x.detach().float(), y.detach().float()
+                    ulp = torch.exp2(torch.floor(torch.log2(torch.maximum(x.abs(), y.abs()).clamp_min(1e-30))) - 7)
+                    tol = 2 * ulp + 2 ** -7 * float(y.abs().max())
+                    assert bool(((x - y).abs() <= tol).all()), (step, name)
+    assert opt.steps_done == 4
+
+
+def test_clip_adamw_deterministic_and_capturable():
+    """Two runs give identical bits; the same step captured in a CUDA graph
+    and replayed gives identical bits too."""
+    from cdl_b200.train.optim import ClipAdamW
+
+    dev = torch.device("cuda")
+
+    def run(graph):
+        gen = torch.Generator(device=dev).manual_seed(1)
+        ps = [(torch.randn(n, device=dev, generator=gen) * 0.02).to(torch.bfloat16).requires_grad_() for n in SIZES]
+        gs = [torch.randn(n, device=dev, generator=gen).to(torch.bfloat16) for n in SIZES]
+        opt = ClipAdamW(ps, lr=1e-3, betas=(0.9, 0.95), max_norm=1.0)
+        for p, g in zip(ps, gs):
+            p.grad = g
+        if graph:
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                opt.step()
+            torch.cuda.current_stream().wait_stream(s)
+            cg = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(cg):
+                out = opt.step()
+            for _ in range(3):
+                cg.replay()
+        else:
+            for _ in range(4):
+                out = opt.step()
+        torch.cuda.synchronize()
+        return [p.detach().clone() for p in ps], float(out)
+
+    a, na = run(False)
+    b, nb = run(False)
+    c, nc = run(True)
+    assert na == nb == nc
+    for x, y, z in zip(a, b, c):
+        assert torch.equal(x, y) and torch.equal(x, z)
+
+
+def test_qat_step_fused_optimizer_vs_torch():
+    """The QAT step with ClipAdamW follows the loss curve of the step with
+    torch's clip + AdamW."""
+    from cdl_b200.train import qat
+
+    spec = qat.SPECS["tiny"]
+    dev = torch.device("cuda")
+    curves = {}
+    for optimizer in ("fused", "torch"):
+        step = qat.QatStep(spec, dev, backend="nvfp4", lr=3e-4, seed=0, optimizer=optimizer)
+        curves[optimizer] = [float(step.step(qat.random_tokens(8, 256, spec.vocab, seed=300 + i, device=dev))[0])
+                             for i in range(20)]
+    worst = max(abs(a - b) / b for a, b in zip(curves["fused"], curves["torch"]))
+    print("max relative loss difference, fused vs torch optimizer:", worst)
+    assert worst < 5e-3

@@ -135,3 +135,24 @@ def test_loss_curve_quantized_backward():
     worst = max(abs(a - b) / b for a, b in zip(curves["nvfp4_qbwd"], curves["nvfp4"]))
     print("max relative loss difference, quantized vs bf16 backward:", worst)
     assert worst < 2e-2
+
+
+
+def test_graph_step_matches_eager():
+    """The CUDA-graph step (three warm-up steps and the capture on the first
+    batch, then replays with fresh tokens copied into the static input) follows
+    the loss curve of the eager step on the same sequence of batches."""
+    from cdl_b200.train import qat
+
+    spec = qat.SPECS["tiny"]
+    dev = torch.device("cuda")
+    batches = [qat.random_tokens(8, 256, spec.vocab, seed=200 + i, device=dev) for i in range(12)]
+    graph = qat.QatStep(spec, dev, backend="nvfp4", lr=3e-4, seed=0, graph=True)
+    got = [float(graph.step(b)[0]) for b in batches]
+    eager = qat.QatStep(spec, dev, backend="nvfp4", lr=3e-4, seed=0)
+    for _ in range(3):
+        eager.step(batches[0])
+    ref = [float(eager.step(b)[0]) for b in batches]
+    print("graph:", got[:4], "eager:", ref[:4])
+    worst = max(abs(a - b) / b for a, b in zip(got, ref))
+    assert worst < 5e-3

@@ -214,3 +214,22 @@ def test_nvfp4_many_global_scales_vs_oracle():
         np.testing.assert_array_equal(_np(scale), os_, err_msg=f"scale 2^{e}*{mnt}")
         np.testing.assert_array_equal(_np(packed), op, err_msg=f"scale 2^{e}*{mnt}")
         assert alpha.cpu().numpy().view(np.uint32)[0] == oa.view(np.uint32)[0]
+
+
+@pytest.mark.parametrize("fmt", [oracle.NVFP4, oracle.MXFP4])
+@pytest.mark.parametrize("shape", [(128, 512), (257, 1024), (1000, 4128), (3, 96), (130, 160)])
+def test_fp4_dequant_vs_oracle_linear_and_swizzled(fmt, shape):
+    """The vectorized FP4 dequantize (32 elements per thread) on linear and on
+    swizzled (GEMM-layout) scales: bit-identical to the oracle's dequantize."""
+    x = workloads.c2_mx(*shape, seed=shape[0] + shape[1] + 31 * fmt)
+    xb = _bits(x)
+    op, os_, oa = oracle.quant(xb, fmt)
+    want = oracle.dequant(op, os_, fmt, oa if fmt == oracle.NVFP4 else 1.0)
+    packed, scale, alpha = _q()[fmt](x.cuda())
+    if fmt == oracle.MXFP4:
+        alpha = torch.ones(1, device="cuda")
+    out = _dq()[fmt](packed, scale, alpha)
+    np.testing.assert_array_equal(_bits(out), want)
+    p2, s2, a2 = _q()[fmt](x.cuda(), swizzled=True)
+    out2 = _dq()[fmt](p2, s2, alpha if fmt == oracle.MXFP4 else a2, swizzled=True)
+    np.testing.assert_array_equal(_bits(out2), want)
