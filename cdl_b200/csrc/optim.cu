@@ -12,8 +12,9 @@
 //             reduction), rounded to bf16 as torch's per-tensor norms are, the
 //             total norm, the clip coefficient and the bias corrections of the
 //             next step, all into a scalar block in the workspace
-//   adamw     g = bf16(grad * coef), then the AdamW update in fp32, p/m/v
-//             written back as bf16
+//   adamw     g = bf16(grad * coef), then torch's foreach AdamW sequence
+//             per element (every step rounded to bf16 as the list
+//             operations store it), p/m/v written back
 //
 // The tensor table (pointers, sizes, chunk offsets) travels in the kernel
 // parameter block, so a launch needs no host-to-device copy and the sequence
@@ -44,8 +45,8 @@ struct OptScalars {
     float sumsq;      // running sum of the squared bf16 per-tensor norms
     float norm;       // bf16(total norm)
     float coef;       // clip coefficient
-    float step_size;  // lr / (1 - beta1^step)
-    float inv_bc2s;   // 1 / sqrt(1 - beta2^step)
+    float step_size;  // -lr / (1 - beta1^step), rounded to fp32
+    float bc2s;       // sqrt(1 - beta2^step), rounded to fp32
     float pad[2];
 };
 constexpr int64_t kScalarBytes = 64;
@@ -145,35 +146,46 @@ __global__ void __launch_bounds__(1024) finalize_kernel(const __grid_constant__ 
     sc->step = step;
     sc->norm = norm;
     sc->coef = coef;
-    sc->step_size = (float)(lr / bc1);
-    sc->inv_bc2s = (float)(1.0 / sqrt(bc2));
+    sc->step_size = (float)(-(lr / bc1));
+    sc->bc2s = (float)sqrt(bc2);
     if (grad_norm) *grad_norm = norm;
 }
 
-// Hyper-parameters as the update uses them: fp32 copies of the double
-// values the caller passed (1 - beta computed in double first).
+// The update follows, per element and in order, the foreach AdamW torch runs
+// for bf16 parameters on CUDA (torch.optim.AdamW's default, which cdl's
+// training script uses): every list operation computes in fp32 with its
+// scalar in fp32 and stores bf16.
+//   p = bf16(p * (1 - lr*wd))                     _foreach_mul_
+//   m = bf16(m + w1 * (g - m))                    _foreach_lerp_ (w1 = 1 - b1 < 0.5)
+//   v = bf16(v * b2);  v = bf16(v + c2 * (g*g))   _foreach_mul_, _foreach_addcmul_
+//   s = bf16(sqrt(v)); s = bf16(s / bc2s); s = bf16(s + eps)
+//   p = bf16(p + step * (m / s))                  _foreach_addcdiv_ (step < 0)
+// with the fused multiply-adds the compiled list kernels use.
 struct AdamConst {
-    float b1, c1, b2, c2, eps, lr_wd;
+    float w1, b2, c2, eps, wd_scale;
+    int decay;
 };
 
 __device__ __forceinline__ void adamw8(uint4& p, const uint4& gr, uint4& m, uint4& v, float coef,
-                                       const AdamConst& k, float step_size, float inv_bc2s) {
+                                       const AdamConst& k, float step, float bc2s) {
     const uint32_t pw[4] = {p.x, p.y, p.z, p.w}, gw[4] = {gr.x, gr.y, gr.z, gr.w};
     const uint32_t mw[4] = {m.x, m.y, m.z, m.w}, vw[4] = {v.x, v.y, v.z, v.w};
     uint32_t po[4], mo[4], vo[4];
-    const float b1 = k.b1, b2 = k.b2, c1 = k.c1, c2 = k.c2, eps = k.eps, lr_wd = k.lr_wd;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         float pf[2] = {bf16lo(pw[j]), bf16hi(pw[j])}, gf[2] = {bf16lo(gw[j]), bf16hi(gw[j])};
         float mf[2] = {bf16lo(mw[j]), bf16hi(mw[j])}, vf[2] = {bf16lo(vw[j]), bf16hi(vw[j])};
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const float gg = bf_round(__fmul_rn(gf[h], coef));  // the clipped gradient, stored as bf16 by torch
-            mf[h] = __fmaf_rn(b1, mf[h], __fmul_rn(c1, gg));
-            vf[h] = __fmaf_rn(b2, vf[h], __fmul_rn(__fmul_rn(c2, gg), gg));
-            pf[h] = __fmaf_rn(-lr_wd, pf[h], pf[h]);
-            const float denom = __fmaf_rn(sqrtf(vf[h]), inv_bc2s, eps);
-            pf[h] = __fmaf_rn(-__fmul_rn(step_size, mf[h]), __frcp_rn(denom), pf[h]);
+            const float g = bf_round(__fmul_rn(gf[h], coef));  // clip: _foreach_mul_(grads, coef)
+            if (k.decay) pf[h] = bf_round(__fmul_rn(pf[h], k.wd_scale));
+            mf[h] = bf_round(__fmaf_rn(k.w1, __fsub_rn(g, mf[h]), mf[h]));
+            vf[h] = bf_round(__fmul_rn(vf[h], k.b2));
+            vf[h] = bf_round(__fmaf_rn(k.c2, __fmul_rn(g, g), vf[h]));
+            float sq = bf_round(__fsqrt_rn(vf[h]));
+            sq = bf_round(__fdiv_rn(sq, bc2s));
+            sq = bf_round(__fadd_rn(sq, k.eps));
+            pf[h] = bf_round(__fmaf_rn(step, __fdiv_rn(mf[h], sq), pf[h]));
         }
         po[j] = pack2(pf[0], pf[1]);
         mo[j] = pack2(mf[0], mf[1]);
@@ -186,7 +198,7 @@ __device__ __forceinline__ void adamw8(uint4& p, const uint4& gr, uint4& m, uint
 
 __global__ void __launch_bounds__(kOptThreads) adamw_kernel(const __grid_constant__ OptGroup g,
                                                             const OptScalars* __restrict__ sc, AdamConst k) {
-    const float coef = sc->coef, step_size = sc->step_size, inv_bc2s = sc->inv_bc2s;
+    const float coef = sc->coef, step_size = sc->step_size, bc2s = sc->bc2s;
     const int tid = threadIdx.x;
     constexpr int kU = 2;  // 8-element groups per thread in flight (4 loads each)
     for (int64_t c = g.chunk0[0] + blockIdx.x; c < g.chunk0[g.count]; c += gridDim.x) {
@@ -215,7 +227,7 @@ __global__ void __launch_bounds__(kOptThreads) adamw_kernel(const __grid_constan
             for (int u = 0; u < kU; ++u) {
                 const int i = i0 + u * kOptThreads + tid;
                 if (i < nv) {
-                    adamw8(p[u], gr[u], m[u], v[u], coef, k, step_size, inv_bc2s);
+                    adamw8(p[u], gr[u], m[u], v[u], coef, k, step_size, bc2s);
                     pp[i] = p[u];
                     mp[i] = m[u];
                     vp[i] = v[u];
@@ -289,12 +301,12 @@ extern "C" int cdlb200_clip_adamw(const cdlb200_adamw_tensor* tensors, int count
         CDLB200_CHECK_LAUNCH();
     }
     AdamConst kc;
-    kc.b1 = (float)beta1;
-    kc.c1 = (float)(1.0 - beta1);
+    kc.w1 = (float)(1.0 - beta1);
     kc.b2 = (float)beta2;
     kc.c2 = (float)(1.0 - beta2);
     kc.eps = (float)eps;
-    kc.lr_wd = (float)(lr * weight_decay);
+    kc.wd_scale = (float)(1.0 - lr * weight_decay);
+    kc.decay = weight_decay != 0.0;
     for (int k = 0; k < ng; ++k) {
         const int64_t n = groups[k].chunk0[groups[k].count] - groups[k].chunk0[0];
         adamw_kernel<<<(int)(n < cap ? n : cap), kOptThreads, 0, st>>>(groups[k], sc, kc);

@@ -553,14 +553,19 @@ __device__ __forceinline__ uint32_t search8(const uint4& w, const uint32_t* tt) 
 constexpr int kFusedThreads = 512;  // threads of the fused NVFP4 kernel (two CTAs per SM)
 constexpr int kChunkBlocks = kFusedThreads;  // one block per thread per chunk (16 KiB)
 constexpr int kAmaxChunks = 16;  // chunks whose per-block amax phase 1 keeps for phase 2
+constexpr int kMaxSearchEntries = 8;  // more kSearch table entries than this: search every block
 
-__device__ __forceinline__ uint2 encode_block(const uint4& a0, const uint4& a1, uint32_t byte,
-                                              const ScaleEntry& e, int mode) {
+// Codes of one block with the table entry of its scale byte: the hardware
+// converter for a kCvt entry, else the exact search (kSearch, or every entry
+// when `all_search`), or the literal divide (kDivide).
+__device__ __forceinline__ uint2 encode_block(const uint4& a0, const uint4& a1, const ScaleEntry& e,
+                                              bool all_search) {
     uint2 out;
-    if (mode == 0) {
+    const uint32_t kind = e.kind;
+    if (kind == kCvt && !all_search) {
         out.x = cvt8_scaled(a0, e.c);
         out.y = cvt8_scaled(a1, e.c);
-    } else if (mode == 2 || e.kind != kDivide) {
+    } else if (kind != kDivide) {
         uint32_t tt[7];
 #pragma unroll
         for (int j = 0; j < 7; ++j) tt[j] = e.tt[j];
@@ -583,6 +588,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2) nvfp4_fused_kernel(
     float* __restrict__ alpha_out) {
     __shared__ uint32_t red[kFusedThreads / 32];
     __shared__ ScaleEntry table[128];
+    __shared__ float ctab[128];  // the cvt multiplier of a kCvt entry, else -1: one 4-byte lookup per block
     __shared__ float s_gmax;
     __shared__ int s_mode;
     __shared__ uint16_t amax_s[kAmaxChunks * kChunkBlocks];
@@ -657,44 +663,49 @@ __global__ void __launch_bounds__(kFusedThreads, 2) nvfp4_fused_kernel(
         const ScaleEntry e = make_scale_entry(byte < 1 ? 1u : (byte > 126 ? 126u : byte), t.alpha, tid & 3);
         if ((tid & 3) == 0 && byte >= 1 && byte <= 126) {
             table[byte] = e;
-            // mode bits: 2 = some kSearch, 4 = some kDivide
-            const int bit = e.kind == kSearch ? 2 : (e.kind == kDivide ? 4 : 0);
-            if (bit) atomicOr(&s_mode, bit);
+            ctab[byte] = e.kind == kCvt ? e.c : -1.0f;
+            if (e.kind == kSearch) atomicAdd(&s_mode, 1);  // count of search entries
         }
     }
     __syncthreads();
-    // 0: cvt; 2: packed search; 3: search + divide
-    const int mode = s_mode == 0 ? 0 : (s_mode < 4 ? 2 : 3);
+    // A few kSearch entries: each block follows its own entry (the warps that
+    // meet one diverge); many: every block takes the search, uniformly.
+    const bool all_search = s_mode > kMaxSearchEntries;
 
-    // ---- phase 2: encode own chunks, last-streamed first (they come from L2)
-    for (int q1 = nmine - 1; q1 >= 0; q1 -= 2) {
-        uint4 v[4];
-        int64_t bs[2];
-        bool ok[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            bs[u] = blk(q1 - u);
-            ok[u] = q1 - u >= 0 && bs[u] < nblk;
-            if (ok[u]) {
-                v[2 * u] = ldg_stream(x + 2 * bs[u]);
-                v[2 * u + 1] = ldg_stream(x + 2 * bs[u] + 1);
-            }
+    // ---- phase 2: encode own chunks, last-streamed first (they come from
+    //      L2), the next block's loads in flight while one is encoded
+    {
+        int q = nmine - 1;
+        int64_t b = q >= 0 ? blk(q) : nblk;
+        uint4 a0 = make_uint4(0u, 0u, 0u, 0u), a1 = a0;
+        if (b < nblk) {
+            a0 = ldg_stream(x + 2 * b);
+            a1 = ldg_stream(x + 2 * b + 1);
         }
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            if (!ok[u]) continue;
-            const int q = q1 - u;
-            const uint32_t mag = q < kAmaxChunks ? (uint32_t)amax_s[q * kChunkBlocks + tid]
-                                                 : max(amax8(v[2 * u]), amax8(v[2 * u + 1]));
-            const uint32_t byte = nvfp4_scale_byte(mag, t);
-            const int64_t b = bs[u];
-            packed[b] = encode_block(v[2 * u], v[2 * u + 1], byte, table[byte], mode);
-            int64_t off = b;
-            if constexpr (SWZ) {  // with SWZ the host guarantees nblk < 2^31
-                const uint32_t r = nb.div((uint32_t)b);
-                off = swizzle_offset(r, (int64_t)((uint32_t)b - r * nb.d), c4);
+        for (; q >= 0; --q) {
+            const int64_t bn = q >= 1 ? blk(q - 1) : nblk;
+            uint4 n0 = make_uint4(0u, 0u, 0u, 0u), n1 = n0;
+            if (bn < nblk) {
+                n0 = ldg_stream(x + 2 * bn);
+                n1 = ldg_stream(x + 2 * bn + 1);
             }
-            scale[off] = (uint8_t)byte;
+            if (b < nblk) {
+                const uint32_t mag = q < kAmaxChunks ? (uint32_t)amax_s[q * kChunkBlocks + tid]
+                                                     : max(amax8(a0), amax8(a1));
+                const uint32_t byte = nvfp4_scale_byte(mag, t);
+                const float c = all_search ? -1.0f : ctab[byte];
+                packed[b] = c > 0.0f ? make_uint2(cvt8_scaled(a0, c), cvt8_scaled(a1, c))
+                                     : encode_block(a0, a1, table[byte], all_search);
+                int64_t off = b;
+                if constexpr (SWZ) {  // with SWZ the host guarantees nblk < 2^31
+                    const uint32_t r = nb.div((uint32_t)b);
+                    off = swizzle_offset(r, (int64_t)((uint32_t)b - r * nb.d), c4);
+                }
+                scale[off] = (uint8_t)byte;
+            }
+            a0 = n0;
+            a1 = n1;
+            b = bn;
         }
     }
 

@@ -224,7 +224,8 @@ class QatStep:
         no_decay = [p for p in params if p.ndim <= 1]
         on_cuda = device.type == "cuda"
         # "fused": clip + AdamW through cdlb200_clip_adamw (CUDA); "torch":
-        # clip_grad_norm_ + torch.optim.AdamW (fused kernels on CUDA)
+        # clip_grad_norm_ + torch.optim.AdamW with its default (foreach)
+        # implementation, as cdl constructs it
         self.optimizer = optimizer or ("fused" if on_cuda else "torch")
         if self.optimizer == "fused":
             from cdl_b200.train.optim import ClipAdamW
@@ -233,7 +234,7 @@ class QatStep:
         elif self.optimizer == "torch":
             self.opt = torch.optim.AdamW(
                 [{"params": decay, "weight_decay": 0.0}, {"params": no_decay, "weight_decay": 0.0}],
-                lr=lr, betas=(0.9, 0.95), fused=on_cuda, foreach=not on_cuda, capturable=graph and on_cuda)
+                lr=lr, betas=(0.9, 0.95), capturable=graph and on_cuda)
         else:
             raise ValueError(f"unknown optimizer {optimizer!r}")
         self.graph_mode = graph and on_cuda

@@ -69,17 +69,18 @@ int64_t cdlb200_clip_adamw_workspace_bytes(const cdlb200_adamw_tensor* tensors, 
 
 /* Gradient clipping and one AdamW step over all tensors, as the reference's
  * training step runs them (cdl smollm2.py: torch.nn.utils.clip_grad_norm_
- * then torch.optim.AdamW):
+ * then torch.optim.AdamW with its default foreach implementation):
  *   norm_i = bf16(||grad_i||_2), norm = bf16(sqrt(sum norm_i^2)),
  *   coef   = min(bf16(bf16(1 / bf16(norm + 1e-6)) * max_norm), 1),  g = bf16(grad * coef),
- *   step  += 1, p -= lr*wd*p, m = b1 m + (1-b1) g, v = b2 v + (1-b2) g^2,
- *   p -= lr/(1-b1^step) * m / (sqrt(v)/sqrt(1-b2^step) + eps),
- * with fp32 element arithmetic (bias corrections in double), p/m/v stored
- * back as bf16; max_norm <= 0 disables
- * the clip (coef = 1).  The step counter lives in the workspace, which must
- * be zero-filled before the first step and kept between steps.  grad_norm
- * (device fp32, optional) receives norm.  Three kernel launches per 512
- * tensors, no host synchronization. */
+ *   step  += 1,  p = bf16(p * (1 - lr*wd)),  m = bf16(lerp(m, g, 1 - b1)),
+ *   v = bf16(bf16(v * b2) + (1 - b2) * g*g),
+ *   s = bf16(bf16(bf16(sqrt(v)) / sqrt(1 - b2^step)) + eps),
+ *   p = bf16(p - lr/(1 - b1^step) * (m / s)),
+ * each operation in fp32 with fp32 scalars, as torch's list kernels compute
+ * it; max_norm <= 0 disables the clip (coef = 1).  The step counter lives in
+ * the workspace, which must be zero-filled before the first step and kept
+ * between steps.  grad_norm (device fp32, optional) receives norm.  Three
+ * kernel launches per 512 tensors, no host synchronization. */
 int cdlb200_clip_adamw(const cdlb200_adamw_tensor* tensors, int count, double max_norm, double lr,
                        double beta1, double beta2, double eps, double weight_decay, void* workspace,
                        int64_t workspace_bytes, float* grad_norm, void* stream);

@@ -17,8 +17,12 @@ def _ulp_diff(a, b):
     return ((a - b).abs() / ulp)
 
 
+@pytest.mark.parametrize("weight_decay", [0.0, 0.1])
 @pytest.mark.parametrize("grad_scale", [1e-4, 1.0])  # clip inactive / active
-def test_clip_adamw_matches_torch(grad_scale):
+def test_clip_adamw_matches_torch(grad_scale, weight_decay):
+    """Bit-level parity with the reference's optimizer: clip_grad_norm_
+    (foreach) then torch.optim.AdamW with its default foreach implementation
+    (what cdl's training script constructs), on bf16 tensors over four steps."""
     from cdl_b200.train.optim import ClipAdamW
 
     dev = torch.device("cuda")
@@ -26,8 +30,8 @@ def test_clip_adamw_matches_torch(grad_scale):
     init = [(torch.randn(n, device=dev, generator=gen) * 0.02).to(torch.bfloat16) for n in SIZES]
     ours = [t.clone().requires_grad_() for t in init]
     ref = [t.clone().requires_grad_() for t in init]
-    opt = ClipAdamW(ours, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, max_norm=1.0)
-    topt = torch.optim.AdamW(ref, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, fused=True)
+    opt = ClipAdamW(ours, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=weight_decay, max_norm=1.0)
+    topt = torch.optim.AdamW(ref, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=weight_decay, foreach=True)
     for step in range(4):
         grads = [(torch.randn(n, device=dev, generator=gen) * grad_scale).to(torch.bfloat16) for n in SIZES]
         for p, q, g in zip(ours, ref, grads):
@@ -41,27 +45,15 @@ def test_clip_adamw_matches_torch(grad_scale):
         for name, mine, theirs in (("param", ours, ref),
                                    ("exp_avg", opt.exp_avg, [topt.state[q]["exp_avg"] for q in ref]),
                                    ("exp_avg_sq", opt.exp_avg_sq, [topt.state[q]["exp_avg_sq"] for q in ref])):
-            d = torch.cat([_ulp_diff(a.detach(), b.detach()) for a, b in zip(mine, theirs)])
-            frac = float((d > 0).float().mean())
-            print(step, name, "max ulp", float(d.max()), "differing", frac)
-            assert frac < 0.02, (step, name)
-            if name == "param":
-                # a moment one ulp apart moves the update by a fraction of
-                # lr, which for a parameter near zero is many of its ulps
-                a = torch.cat([x.detach().float() for x in mine])
-                b = torch.cat([x.detach().float() for x in theirs])
-                ulp = torch.exp2(torch.floor(torch.log2(torch.maximum(a.abs(), b.abs()).clamp_min(1e-30))) - 7)
-                assert bool(((a - b).abs() <= 2 * ulp + 0.05 * 3e-4).all()), (step, name)
-            else:
-                # per step the moments round within one ulp of torch's; they
-                # are recurrences, so a one-ulp difference of an earlier step
-                # carries over, which for a first moment that has cancelled to
-                # near zero is many of its ulps: bound it by the tensor's scale
-                for x, y in zip(mine, theirs):
-                    x, y = x.detach().float(), y.detach().float()
-                    ulp = torch.exp2(torch.floor(torch.log2(torch.maximum(x.abs(), y.abs()).clamp_min(1e-30))) - 7)
-                    tol = 2 * ulp + 2 ** -7 * float(y.abs().max())
-                    assert bool(((x - y).abs() <= tol).all()), (step, name)
+            a = torch.cat([x.detach().reshape(-1) for x in mine])
+            b = torch.cat([x.detach().reshape(-1) for x in theirs])
+            frac = float((a != b).float().mean())
+            d = _ulp_diff(a, b)
+            print(step, name, "elements differing", frac, "max ulp", float(d.max()))
+            # identical up to the last bit of a host-side scalar (pow / sqrt
+            # of the bias corrections), which moves a handful of roundings
+            assert frac < 1e-4, (step, name)
+            assert float(d.max()) <= 1.0, (step, name)
     assert opt.steps_done == 4
 
 
