@@ -63,13 +63,21 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_cross_entropy": (_I, [_P, _P, _I64, _I64, _F, _P, _P]),
     "cdlb200_clip_adamw_workspace_bytes": (_I64, [_P, _I]),
     "cdlb200_clip_adamw": (_I, [_P, _I, _D, _D, _D, _D, _D, _D, _P, _I64, _P, _P]),
+    "cdlb200_nvfp4_encode_multi": (_I, [_P, _I, _P]),
 }
 
 
 class AdamwTensor(ctypes.Structure):
     """``cdlb200_adamw_tensor`` (include/cdlb200_step.h)."""
 
-    _fields_ = [("param", _P), ("grad", _P), ("exp_avg", _P), ("exp_avg_sq", _P), ("numel", _I64)]
+    _fields_ = [("param", _P), ("grad", _P), ("exp_avg", _P), ("exp_avg_sq", _P), ("numel", _I64), ("amax", _P)]
+
+
+class Nvfp4EncodeTensor(ctypes.Structure):
+    """``cdlb200_nvfp4_encode_tensor`` (include/cdlb200_step.h)."""
+
+    _fields_ = [("x", _P), ("rows", _I64), ("k", _I64), ("amax", _P), ("packed", _P), ("scale", _P),
+                ("alpha", _P), ("deq", _P)]
 
 
 class CdlB200Error(RuntimeError):

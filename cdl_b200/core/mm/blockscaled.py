@@ -92,7 +92,13 @@ class BlockScaledMatMul(torch.autograd.Function):
             w_theta, w_q, w_alpha = w.encode_swizzled(fmt)
             if not ctx.qbwd:
                 ctx.swizzled = True
-                ctx.save_for_backward(x_theta, x_q, x_alpha, w_theta, w_q, w_alpha)
+                # the weight's dequantized copy, when its encoder keeps one
+                w_deq = w.cached_dequant(fmt) if hasattr(w, "cached_dequant") else None
+                ctx.w_deq = w_deq is not None
+                if ctx.w_deq:
+                    ctx.save_for_backward(x_theta, x_q, x_alpha, w_deq)
+                else:
+                    ctx.save_for_backward(x_theta, x_q, x_alpha, w_theta, w_q, w_alpha)
             return mm_fp4(x_theta, w_theta.T, x_q, w_q.T, x_alpha * w_alpha, 16 if fmt == "nvfp4" else 32,
                           fmt == "nvfp4")
         x_theta, x_q, x_alpha = getattr(x, fmt)()
@@ -127,6 +133,14 @@ class BlockScaledMatMul(torch.autograd.Function):
             x_src, w_src = ctx.proxies
             dx, dw = _quantized_grads(ctx.fmt, grad_output, x_src if ctx.w_k is not None else None,
                                       w_src if ctx.x_k is not None else None)
+            return None, None, dx, None, dw, None
+        if getattr(ctx, "w_deq", False):
+            x_theta, x_q, x_alpha, w_deq = ctx.saved_tensors
+            dx = grad_output @ w_deq[:, : ctx.x_k] if ctx.x_k is not None else None
+            dw = None
+            if ctx.w_k is not None:
+                dw = grad_output.T @ _dequant_activation(_DEQ[ctx.fmt], x_theta, x_q, x_alpha,
+                                                         {"swizzled": True})[:, : ctx.w_k]
             return None, None, dx, None, dw, None
         x_theta, x_q, x_alpha, w_theta, w_q, w_alpha = ctx.saved_tensors
         deq = _DEQ[ctx.fmt]

@@ -72,32 +72,6 @@ __global__ void fp4_dequant_generic_kernel(const uint8_t* __restrict__ packed,
     }
 }
 
-// Eight e2m1 codes (one 32-bit word, element 2j in the low nibble of byte j)
-// -> four f16x2 by the hardware converter (every e2m1 value is exact in f16).
-__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t (&h)[4]) {
-    asm("{\n"
-        ".reg .b8 b0, b1, b2, b3;\n"
-        "mov.b32 {b0, b1, b2, b3}, %4;\n"
-        "cvt.rn.f16x2.e2m1x2 %0, b0;\n"
-        "cvt.rn.f16x2.e2m1x2 %1, b1;\n"
-        "cvt.rn.f16x2.e2m1x2 %2, b2;\n"
-        "cvt.rn.f16x2.e2m1x2 %3, b3;\n"
-        "}"
-        : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
-        : "r"(w));
-}
-
-__device__ __forceinline__ void f16x2_to_f32(uint32_t h, float& lo, float& hi) {
-    asm("{\n"
-        ".reg .f16 a, b;\n"
-        "mov.b32 {a, b}, %2;\n"
-        "cvt.f32.f16 %0, a;\n"
-        "cvt.f32.f16 %1, b;\n"
-        "}"
-        : "=f"(lo), "=f"(hi)
-        : "r"(h));
-}
-
 // FP4 dequantize, 32 elements (16 code bytes) per thread and step with two
 // steps in flight; scales read from the linear [rows, k/BLOCK] layout or, with
 // SWZ, from the 128x4 tiled layout the GEMM consumes (block b of the flat

@@ -118,6 +118,9 @@ __global__ void __launch_bounds__(1024) finalize_kernel(const __grid_constant__ 
                                                         double beta2, float* grad_norm) {
     __shared__ float nrm[kOptGroup];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // the update kernel folds each tensor's new max|param| into its amax word
+    for (int ti = threadIdx.x; ti < g.count; ti += blockDim.x)
+        if (g.t[ti].amax) *g.t[ti].amax = 0u;
     for (int ti = warp; ti < g.count; ti += 32) {
         float s = 0.f;
         for (int64_t c = g.chunk0[ti] + lane; c < g.chunk0[ti + 1]; c += 32) s += partial[c];
@@ -211,6 +214,7 @@ __global__ void __launch_bounds__(kOptThreads) adamw_kernel(const __grid_constan
         const uint4* gp = static_cast<const uint4*>(t.grad) + base / 8;
         uint4* mp = static_cast<uint4*>(t.exp_avg) + base / 8;
         uint4* vp = static_cast<uint4*>(t.exp_avg_sq) + base / 8;
+        uint32_t amax = 0;  // max |new param| over this thread's values, as bf16 magnitude bits
         for (int i0 = 0; i0 < nv; i0 += kU * kOptThreads) {
             uint4 p[kU], gr[kU], m[kU], v[kU];
 #pragma unroll
@@ -231,8 +235,19 @@ __global__ void __launch_bounds__(kOptThreads) adamw_kernel(const __grid_constan
                     pp[i] = p[u];
                     mp[i] = m[u];
                     vp[i] = v[u];
+                    if (t.amax) {
+                        uint32_t a, b;
+                        asm("max.u16x2 %0, %1, %2;" : "=r"(a) : "r"(p[u].x & 0x7fff7fffu), "r"(p[u].y & 0x7fff7fffu));
+                        asm("max.u16x2 %0, %1, %2;" : "=r"(b) : "r"(p[u].z & 0x7fff7fffu), "r"(p[u].w & 0x7fff7fffu));
+                        asm("max.u16x2 %0, %1, %2;" : "=r"(a) : "r"(a), "r"(b));
+                        amax = max(amax, max(a & 0xffffu, a >> 16));
+                    }
                 }
             }
+        }
+        if (t.amax) {  // uniform per CTA: one reduction per warp
+            amax = __reduce_max_sync(0xffffffffu, amax);
+            if ((tid & 31) == 0) atomicMax(t.amax, amax);
         }
     }
 }

@@ -41,6 +41,9 @@
 // >= 2^-14 away from it; one Markstein correction of RN(p * RN(1/gmax))
 // (exact when the quotient is representable, within 2 ulp otherwise) gives
 // the same byte as the IEEE divide.
+#include <vector>
+
+#include "cdlb200_step.h"
 #include "common.cuh"
 
 namespace cdlb200 {
@@ -718,6 +721,102 @@ __global__ void __launch_bounds__(kFusedThreads, 2) nvfp4_fused_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// Multi-tensor NVFP4 encode with a known global amax (the weights of the QAT
+// step, right after the optimizer wrote them): one pass over all tensors,
+// work chunks of 512 blocks dealt over the grid, each block encoded exactly
+// by nvfp4_block16 (no per-tensor table: consecutive chunks of a CTA belong
+// to different tensors), scales written in the GEMM layout, and optionally
+// the dequantized copy for the bf16 backward in the same pass.
+// ---------------------------------------------------------------------------
+constexpr int kEncThreads = 256;
+constexpr int kEncChunkBlocks = 2 * kEncThreads;  // 16-element blocks per work chunk
+constexpr int kEncGroup = 256;                    // tensors per launch (table in the parameter block)
+
+struct EncGroup {
+    int count, pad;
+    int64_t chunk0[kEncGroup + 1];  // global chunk index of each tensor's first chunk
+    FastDiv nb[kEncGroup];          // k / 16 per tensor
+    cdlb200_nvfp4_encode_tensor t[kEncGroup];
+};
+
+__device__ __forceinline__ int enc_tensor_of(const EncGroup& g, int64_t c) {
+    int lo = 0, hi = g.count - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (g.chunk0[mid] <= c) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+// bf16((e2m1 * scale) * alpha) of the 8 codes in one word -> one uint4
+__device__ __forceinline__ uint4 dequant8(uint32_t codes, float sc, float alpha) {
+    uint32_t h[4], o[4];
+    e2m1x8_to_f16x2(codes, h);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        float lo, hi;
+        f16x2_to_f32(h[j], lo, hi);
+        o[j] = bf16x2_rn(__fmul_rn(__fmul_rn(lo, sc), alpha), __fmul_rn(__fmul_rn(hi, sc), alpha));
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__global__ void __launch_bounds__(kEncThreads) nvfp4_encode_multi_kernel(const __grid_constant__ EncGroup g) {
+    const int tid = threadIdx.x;
+    for (int64_t c = g.chunk0[0] + blockIdx.x; c < g.chunk0[g.count]; c += gridDim.x) {
+        const int ti = enc_tensor_of(g, c);
+        const cdlb200_nvfp4_encode_tensor& T = g.t[ti];
+        const FastDiv nb = g.nb[ti];
+        const int64_t nblk = T.rows * (int64_t)nb.d;
+        const int64_t c4 = (nb.d + 3) / 4;
+        // the tensor's global scale, as the fused quantizer derives it from its amax
+        const uint32_t gm = *T.amax;
+        Nvfp4Tensor tn;
+        tn.gmax = gm > 0x7f80u ? u2f(0x7fc00000u) : fmaxf(u2f(gm << 16), 1.1754943508222875e-38f);
+        tn.alpha = __fdiv_rn(tn.gmax, 2688.0f);
+        tn.markstein = tn.gmax >= 0x1p-100f && tn.gmax <= 1.0e35f;
+        tn.yg = tn.markstein ? __frcp_rn(tn.gmax) : 0.0f;
+        if (c == g.chunk0[ti] && tid == 0) *T.alpha = tn.alpha;
+        const int64_t base = (c - g.chunk0[ti]) * kEncChunkBlocks;
+        const uint4* x = static_cast<const uint4*>(T.x);
+        uint4 w[4];
+        int64_t b[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            b[j] = base + j * kEncThreads + tid;
+            if (b[j] < nblk) {
+                w[2 * j] = ldg_stream(x + 2 * b[j]);
+                w[2 * j + 1] = ldg_stream(x + 2 * b[j] + 1);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            if (b[j] >= nblk) continue;
+            uint2 out;
+            const uint32_t byte = nvfp4_block16(w[2 * j], w[2 * j + 1], max(amax8(w[2 * j]), amax8(w[2 * j + 1])),
+                                                tn, out);
+            static_cast<uint2*>(T.packed)[b[j]] = out;
+            const uint32_t r = nb.div((uint32_t)b[j]);
+            static_cast<uint8_t*>(T.scale)[swizzle_offset(r, (int64_t)((uint32_t)b[j] - r * nb.d), c4)] =
+                (uint8_t)byte;
+            if (T.deq) {
+                const float sc = e4m3_to_f32(byte);
+                uint4* d = static_cast<uint4*>(T.deq) + 2 * b[j];
+                d[0] = dequant8(out.x, sc, tn.alpha);
+                d[1] = dequant8(out.y, sc, tn.alpha);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // general path: any leading dimension, ragged k, transposed (dim-0) blocks.
 // One thread per (output row r, block b); element (r, c) is x[r*sr + c*sc].
 // Threads are ordered r-fastest so a transposed input is read coalesced.
@@ -1107,4 +1206,44 @@ extern "C" int cdlb200_mxfp8_quant(const void* x, int64_t rows, int64_t k, int64
     if ((rc = device_ok()) != CDLB200_OK) return rc;
     return quant_entry<kMXFP8>(x, rows, k, ldx, transpose, packed, scale, scale_layout, nullptr,
                                nullptr, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cdlb200_nvfp4_encode_multi(const cdlb200_nvfp4_encode_tensor* tensors, int count, void* stream) {
+    if (count < 0 || (count > 0 && !tensors)) return CDLB200_ERR_INVALID_ARG;
+    for (int i = 0; i < count; ++i) {
+        const cdlb200_nvfp4_encode_tensor& t = tensors[i];
+        if (t.rows < 0 || t.k < 0 || (t.k % 16) != 0) return CDLB200_ERR_INVALID_ARG;
+        if (t.rows == 0 || t.k == 0) continue;
+        if (!t.x || !t.amax || !t.packed || !t.scale || !t.alpha) return CDLB200_ERR_INVALID_ARG;
+        if ((t.rows % 128) != 0 || ((t.k / 16) % 4) != 0 || t.rows * (t.k / 16) >= (1ll << 31))
+            return CDLB200_ERR_INVALID_ARG;
+        if (!aligned(t.x, 16) || !aligned(t.packed, 8) || (t.deq && !aligned(t.deq, 16))) return CDLB200_ERR_ALIGNMENT;
+    }
+    int rc;
+    if ((rc = device_ok()) != CDLB200_OK) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    std::vector<EncGroup> groups;
+    int64_t chunk = 0;
+    for (int i = 0; i < count; ++i) {
+        const cdlb200_nvfp4_encode_tensor& t = tensors[i];
+        if (t.rows == 0 || t.k == 0) continue;
+        if (groups.empty() || groups.back().count == kEncGroup) {
+            groups.emplace_back();
+            groups.back().count = 0;
+            groups.back().pad = 0;
+        }
+        EncGroup& g = groups.back();
+        g.t[g.count] = t;
+        g.nb[g.count] = FastDiv((uint32_t)(t.k / 16));
+        g.chunk0[g.count] = chunk;
+        chunk += (t.rows * (t.k / 16) + kEncChunkBlocks - 1) / kEncChunkBlocks;
+        g.chunk0[++g.count] = chunk;
+    }
+    const int64_t cap = (int64_t)num_sms() * 8;
+    for (const EncGroup& g : groups) {
+        const int64_t n = g.chunk0[g.count] - g.chunk0[0];
+        nvfp4_encode_multi_kernel<<<(unsigned)(n < cap ? n : cap), kEncThreads, 0, st>>>(g);
+        CDLB200_CHECK_LAUNCH();
+    }
+    return CDLB200_OK;
 }

@@ -25,6 +25,8 @@ Simulation = Literal["nvfp4", "mxfp4", "mxfp8"]
 # owner, (format, view, version), (codes, scales, alpha))
 _ENCODED: list = []
 _ENCODED_MAX = 4
+# attribute the optimizer's weight encoder sets on a weight (train/optim.py)
+_ENCODED_ATTR = "_cdlb200_nvfp4"
 
 
 @dataclass
@@ -66,6 +68,9 @@ class SteTensor(QTensor):
         once: the result is kept for the tensor it came from while that tensor
         is alive and unmodified (same storage owner, view and version)."""
         fn = {"nvfp4": nvfp4_quant, "mxfp4": mxfp4_quant, "mxfp8": mxfp8_quant}[fmt]
+        enc = self._weight_encoding(fmt)
+        if enc is not None:  # written by the optimizer step that produced this weight
+            return enc[1], enc[2], enc[3]
         theta = self.theta.reshape(-1, self.k)
         owner = theta._base if theta._base is not None else theta
         # parameters are excluded: optimizers may update them without a version bump
@@ -81,6 +86,19 @@ class SteTensor(QTensor):
             _ENCODED.insert(0, (weakref.ref(owner), key, res))
             del _ENCODED[_ENCODED_MAX:]
         return res
+
+    def _weight_encoding(self, fmt: Simulation):
+        """The optimizer's NVFP4 encoding of this (weight) tensor, if it is
+        current: (version, codes, scales, alpha, dequantized)."""
+        enc = getattr(self.theta, _ENCODED_ATTR, None)
+        if fmt != "nvfp4" or enc is None or enc[0] != self.theta._version or self.theta.dim() != 2:
+            return None
+        return enc
+
+    def cached_dequant(self, fmt: Simulation) -> torch.Tensor | None:
+        """bf16 ``deq(Q(theta))`` kept with the optimizer's encoding, else None."""
+        enc = self._weight_encoding(fmt)
+        return None if enc is None else enc[4]
 
     def dequantize(self) -> torch.Tensor:
         if self.simulation is None:

@@ -17,8 +17,12 @@ import ctypes
 from typing import Iterable
 
 import torch
+from torch.autograd.graph import increment_version
 
 from cdl_b200 import _lib
+
+# attribute of an encoded weight: (version, packed, scales, alpha, dequantized)
+ENCODED_ATTR = "_cdlb200_nvfp4"
 
 
 class ClipAdamW:
@@ -30,7 +34,8 @@ class ClipAdamW:
     skipped, as torch does."""
 
     def __init__(self, params: Iterable[torch.Tensor], lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.999),
-                 eps: float = 1e-8, weight_decay: float = 0.0, max_norm: float = 1.0):
+                 eps: float = 1e-8, weight_decay: float = 0.0, max_norm: float = 1.0,
+                 encode: Iterable[torch.Tensor] = ()):
         self.params = [p for p in params if p.requires_grad]
         if not self.params:
             raise ValueError("ClipAdamW: no parameters")
@@ -53,6 +58,7 @@ class ClipAdamW:
         self._ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
         self._norm = torch.zeros((), dtype=torch.float32, device=dev)
         self.device = dev
+        self._encoder = WeightEncoder(self, list(encode)) if encode else None
 
     @torch.no_grad()
     def step(self) -> torch.Tensor:
@@ -69,6 +75,11 @@ class ClipAdamW:
         _lib.call("cdlb200_clip_adamw", ctypes.addressof(tab), len(self.params), float(self.max_norm),
                   float(self.lr), float(b1), float(b2), float(self.eps), float(self.weight_decay),
                   _lib.ptr(self._ws), self._ws.numel(), _lib.ptr(self._norm), _lib.stream(self.device))
+        # the kernels wrote the parameters in place: advance their version
+        # counters as a torch in-place update would
+        increment_version([p for i, p in enumerate(self.params) if tab[i].numel])
+        if self._encoder is not None:
+            self._encoder.refresh()
         return self._norm.clone()
 
     def zero_grad(self, set_to_none: bool = True) -> None:
@@ -82,3 +93,61 @@ class ClipAdamW:
     def steps_done(self) -> int:
         """Completed steps (reads the device counter: synchronizes)."""
         return int(self._ws[:4].view(torch.float32).item())
+
+
+class WeightEncoder:
+    """NVFP4 encodings of the quantized linears' weights, refreshed by the
+    optimizer step that changed them.
+
+    cdl quantizes every weight in each forward and dequantizes it again for
+    the bf16 dgrad GEMM of the backward (core/mm/nvfp4.py).  The weights only
+    change in the optimizer step, so here the update kernel also folds each
+    weight's new max|w| into an amax word, and right after it one launch of
+    ``cdlb200_nvfp4_encode_multi`` writes, for every weight, the codes, the
+    GEMM-layout scales, alpha and the dequantized copy -- the same values the
+    per-layer quantize and dequantize would produce.  Each weight carries them
+    as ``ENCODED_ATTR`` together with its version; the linear layer uses them
+    while the version matches (see ``SteTensor``), else it quantizes as usual.
+    Weights that do not fit the encoder's layout (rows % 128, (k/16) % 4) are
+    left to the per-layer path."""
+
+    def __init__(self, opt: ClipAdamW, weights: list[torch.Tensor]):
+        index = {id(p): i for i, p in enumerate(opt.params)}
+        self.opt = opt
+        self.weights = [w for w in weights if id(w) in index and w.dim() == 2 and w.shape[0] % 128 == 0
+                        and w.shape[1] % 64 == 0]
+        dev = opt.device
+        n = len(self.weights)
+        self.amax = torch.zeros(max(n, 1), dtype=torch.int32, device=dev)
+        self.table = (_lib.Nvfp4EncodeTensor * max(n, 1))()
+        self.buffers = []
+        for j, w in enumerate(self.weights):
+            rows, k = w.shape
+            packed = torch.empty(rows, k // 2, dtype=torch.uint8, device=dev)
+            scale = torch.empty(rows, k // 16, dtype=torch.uint8, device=dev)
+            alpha = torch.empty(1, dtype=torch.float32, device=dev)
+            deq = torch.empty(rows, k, dtype=torch.bfloat16, device=dev)
+            amax_ptr = self.amax.data_ptr() + 4 * j
+            t = self.table[j]
+            t.x, t.rows, t.k, t.amax = w.data_ptr(), rows, k, amax_ptr
+            t.packed, t.scale, t.alpha, t.deq = packed.data_ptr(), scale.data_ptr(), alpha.data_ptr(), deq.data_ptr()
+            opt._table[index[id(w)]].amax = amax_ptr
+            self.buffers.append((packed, scale, alpha, deq))
+
+    def refresh(self) -> None:
+        """Encode the weights the last update wrote (those that had a grad)."""
+        opt = self.opt
+        live = []
+        for j, w in enumerate(self.weights):
+            if w.grad is None:  # not updated this step: keep (or lack) its encoding
+                self.table[j].rows = 0
+            else:
+                self.table[j].rows = w.shape[0]
+                live.append(j)
+        if not live:
+            return
+        _lib.call("cdlb200_nvfp4_encode_multi", ctypes.addressof(self.table), len(self.weights),
+                  _lib.stream(opt.device))
+        for j in live:
+            w = self.weights[j]
+            setattr(w, ENCODED_ATTR, (w._version, *self.buffers[j]))

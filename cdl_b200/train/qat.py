@@ -230,7 +230,10 @@ class QatStep:
         if self.optimizer == "fused":
             from cdl_b200.train.optim import ClipAdamW
 
-            self.opt = ClipAdamW(params, lr=lr, betas=(0.9, 0.95), weight_decay=0.0, max_norm=grad_clip)
+            # the QLinear weights of the nvfp4 backend are re-encoded by the step that updates them
+            encode = [m.weight for m in self.model.modules() if isinstance(m, QLinear) and m.backend == "nvfp4"]
+            self.opt = ClipAdamW(params, lr=lr, betas=(0.9, 0.95), weight_decay=0.0, max_norm=grad_clip,
+                                 encode=encode)
         elif self.optimizer == "torch":
             self.opt = torch.optim.AdamW(
                 [{"params": decay, "weight_decay": 0.0}, {"params": no_decay, "weight_decay": 0.0}],

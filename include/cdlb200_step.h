@@ -62,6 +62,10 @@ typedef struct {
     void* exp_avg;
     void* exp_avg_sq;
     int64_t numel;
+    /* optional (NULL: none): receives the bf16 magnitude bits of max|param|
+     * after the update, the global amax an NVFP4 encode of the new weights
+     * needs (cdlb200_nvfp4_encode_multi) */
+    uint32_t* amax;
 } cdlb200_adamw_tensor;
 
 /* Device workspace (bytes) cdlb200_clip_adamw needs for these tensors. */
@@ -84,6 +88,26 @@ int64_t cdlb200_clip_adamw_workspace_bytes(const cdlb200_adamw_tensor* tensors, 
 int cdlb200_clip_adamw(const cdlb200_adamw_tensor* tensors, int count, double max_norm, double lr,
                        double beta1, double beta2, double eps, double weight_decay, void* workspace,
                        int64_t workspace_bytes, float* grad_norm, void* stream);
+
+/* One tensor of the multi-tensor NVFP4 encoder below. */
+typedef struct {
+    const void* x;         /* bf16 [rows, k], contiguous, 16-byte aligned */
+    int64_t rows, k;       /* k % 16 == 0; rows % 128 == 0 and (k/16) % 4 == 0 (swizzled scales need no padding) */
+    const uint32_t* amax;  /* bf16 magnitude bits of max|x| (as cdlb200_clip_adamw writes them) */
+    void* packed;          /* uint8 [rows, k/2]: e2m1 codes, element 2j in the low nibble */
+    void* scale;           /* uint8 [rows, k/16] in the 128x4 GEMM layout */
+    float* alpha;          /* fp32 [1]: gmax / 2688 */
+    void* deq;             /* optional bf16 [rows, k]: bf16((e2m1 * scale) * alpha), the backward operand */
+} cdlb200_nvfp4_encode_tensor;
+
+/* NVFP4 quantize of many tensors whose global amax is already known (the
+ * weights of a QAT step, right after the optimizer wrote them and their
+ * amax): the same codes, scale bytes and alpha as cdlb200_nvfp4_quant with
+ * CDLB200_SCALE_SWIZZLED, plus the dequantized copy the bf16 backward GEMMs
+ * read, for all tensors in one pass (one launch per 256 tensors).  Replaces,
+ * per QLinear, the weight quantize of the forward (cdl core/mm/nvfp4.py) and
+ * the weight dequantize of the backward (dequant.py:103-109). */
+int cdlb200_nvfp4_encode_multi(const cdlb200_nvfp4_encode_tensor* tensors, int count, void* stream);
 
 #ifdef __cplusplus
 }

@@ -111,3 +111,68 @@ def test_qat_step_fused_optimizer_vs_torch():
     worst = max(abs(a - b) / b for a, b in zip(curves["fused"], curves["torch"]))
     print("max relative loss difference, fused vs torch optimizer:", worst)
     assert worst < 5e-3
+
+
+def _amax_bits(x):
+    return int((x.view(torch.int16).int() & 0x7FFF).max())
+
+
+def test_encode_multi_matches_per_tensor_quantize():
+    """cdlb200_nvfp4_encode_multi (amax given) against the per-tensor NVFP4
+    quantizer with swizzled scales, and its dequantized copy against the
+    dequantizer: bit-identical, for several shapes in one launch."""
+    import ctypes
+
+    from cdl_b200 import _lib
+    from cdl_b200.core.kernel.dequant import nvfp4_dequant
+    from cdl_b200.core.kernel.quant import nvfp4_quant
+
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(5)
+    shapes = [(128, 64), (256, 512), (2048, 2048), (384, 1088)]
+    xs = [(torch.randn(r, k, device=dev, generator=gen) * (0.01 + i)).bfloat16() for i, (r, k) in enumerate(shapes)]
+    xs[1][3, 7] = 0.0
+    amax = torch.tensor([_amax_bits(x) for x in xs], dtype=torch.int32, device=dev)
+    tab = (_lib.Nvfp4EncodeTensor * len(xs))()
+    outs = []
+    for i, x in enumerate(xs):
+        r, k = x.shape
+        o = (torch.empty(r, k // 2, dtype=torch.uint8, device=dev), torch.empty(r, k // 16, dtype=torch.uint8, device=dev),
+             torch.empty(1, device=dev), torch.empty(r, k, dtype=torch.bfloat16, device=dev))
+        outs.append(o)
+        t = tab[i]
+        t.x, t.rows, t.k, t.amax = x.data_ptr(), r, k, amax.data_ptr() + 4 * i
+        t.packed, t.scale, t.alpha, t.deq = (v.data_ptr() for v in o)
+    _lib.call("cdlb200_nvfp4_encode_multi", ctypes.addressof(tab), len(xs), _lib.stream(dev))
+    for x, (p, s, a, d) in zip(xs, outs):
+        rp, rs, ra = nvfp4_quant(x, swizzled=True)
+        assert torch.equal(p, rp) and torch.equal(s, rs) and torch.equal(a.reshape(-1), ra.reshape(-1))
+        assert torch.equal(d, nvfp4_dequant(rp, rs, ra, swizzled=True))
+
+
+def test_optimizer_weight_encoding_is_current():
+    """After ClipAdamW.step the encoded weights equal a fresh quantize of the
+    updated weights, and a weight modified afterwards falls back (its version
+    moved on)."""
+    from cdl_b200.core.kernel.quant import nvfp4_quant
+    from cdl_b200.train.optim import ENCODED_ATTR, ClipAdamW
+
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(6)
+    ws = [(torch.randn(r, k, device=dev, generator=gen) * 0.02).bfloat16().requires_grad_()
+          for r, k in [(256, 256), (512, 128), (128, 1024)]]
+    bias = torch.zeros(64, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    opt = ClipAdamW(ws + [bias], lr=1e-2, betas=(0.9, 0.95), encode=ws)
+    for step in range(3):
+        for w in ws + [bias]:
+            w.grad = torch.randn(w.shape, device=dev, generator=gen).bfloat16()
+        opt.step()
+        opt.zero_grad()
+        for w in ws:
+            ver, p, s, a, d = getattr(w, ENCODED_ATTR)
+            assert ver == w._version
+            rp, rs, ra = nvfp4_quant(w.detach(), swizzled=True)
+            assert torch.equal(p, rp) and torch.equal(s, rs) and torch.equal(a.reshape(-1), ra.reshape(-1))
+    with torch.no_grad():
+        ws[0].mul_(2)
+    assert getattr(ws[0], ENCODED_ATTR)[0] != ws[0]._version
