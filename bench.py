@@ -356,12 +356,8 @@ def qat_workload(name, dev, rank, world, backend="nvfp4"):
                    "parallelism": f"dp{world}" if world > 1 else "single", "l2": "activations >> L2"},
         "h2d": host_ids.numel() * 8, "d2h": 4, "bound": "tensor",
         "flops_per_unit": qat.flops_per_token(spec, seq), "kernel": "full QAT step",
-        # per QLinear: quantize x and w, swizzle both scale sets, GEMM (5); backward: dequantize w and x
-        # (2), or with the quantized backward quantize g, g^T, w^T, x^T (1 + 3 x amax + transpose) and
-        # two GEMMs (9).  Per decoder layer: RMSNorm fwd x2, bwd x2 (+ column sum) = 6, RoPE 4, SwiGLU 2;
-        # the final norm 3; clip + AdamW 3.
-        "launches_per_step": ((14 if qbwd else 7) * step.n_quant + 12 * spec.layers + 3
-                              + (3 if step.optimizer == "fused" else 0)),
+        # eager steps: the library counts its kernel launches as they are issued
+        "launches_per_step": None, "count_launches": True,
     }
 
 
@@ -508,11 +504,15 @@ def main() -> None:
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    from cdl_b200 import _lib as _cdl_lib
+
+    launches0 = _cdl_lib.launches
     e0.record()
     run()
     e1.record()
     torch.cuda.synchronize()
     barrier()
+    counted_launches = _cdl_lib.launches - launches0
     ms = e0.elapsed_time(e1)
     clocks = sampler.stop()
     del keep, run
@@ -579,7 +579,8 @@ def main() -> None:
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_value, 3), "unit": w["unit"], "h2d_bytes_per_step": w["h2d"],
                 "d2h_bytes_per_step": w["d2h"]},
-        "gpu_launches": (w["launches_per_step"] * args.steps) if w["launches_per_step"] else None,
+        "gpu_launches": (counted_launches if w.get("count_launches")
+                         else (w["launches_per_step"] * args.steps) if w["launches_per_step"] else None),
         "clocks": clocks,
     }
     if wl == "fp4_gemm":

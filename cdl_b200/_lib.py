@@ -54,11 +54,11 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_mm_fp4": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _P, _I64, _P, _P]),
     "cdlb200_mm_mxfp8": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _I64, _P, _P]),
     # include/cdlb200_step.h
-    "cdlb200_rmsnorm_fwd": (_I, [_P, _P, _I64, _I64, ctypes.c_float, _P, _P, _P]),
+    "cdlb200_rmsnorm_fwd": (_I, [_P, _P, _I64, _I64, ctypes.c_float, _P, _P, _P, _P]),
     "cdlb200_rmsnorm_bwd_workspace_bytes": (_I64, [_I64, _I64]),
     "cdlb200_rmsnorm_bwd": (_I, [_P, _P, _P, _P, _I64, _I64, _P, _P, _P, _I64, _P]),
     "cdlb200_rope": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _P, _P]),
-    "cdlb200_swiglu_fwd": (_I, [_P, _P, _I64, _P, _P]),
+    "cdlb200_swiglu_fwd": (_I, [_P, _P, _I64, _P, _P, _P]),
     "cdlb200_swiglu_bwd": (_I, [_P, _P, _P, _I64, _P, _P, _P]),
     "cdlb200_cross_entropy": (_I, [_P, _P, _I64, _I64, _F, _P, _P]),
     "cdlb200_clip_adamw_workspace_bytes": (_I64, [_P, _I]),
@@ -109,7 +109,15 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
+# kernels one call of an entry point launches (default 1); `launches` counts
+# them over the process, so a benchmark can report how many ran
+KERNELS_PER_CALL = {"cdlb200_rmsnorm_bwd": 2, "cdlb200_clip_adamw": 3}
+launches = 0
+
+
 def call(name: str, *args) -> None:
+    global launches
+    launches += KERNELS_PER_CALL.get(name, 1)
     status = getattr(lib(), name)(*args)
     if status != OK:
         msg = lib().cdlb200_status_string(status).decode()

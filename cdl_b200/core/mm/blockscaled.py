@@ -92,13 +92,13 @@ class BlockScaledMatMul(torch.autograd.Function):
             w_theta, w_q, w_alpha = w.encode_swizzled(fmt)
             if not ctx.qbwd:
                 ctx.swizzled = True
-                # the weight's dequantized copy, when its encoder keeps one
+                # dequantized copies formed with the encodings, where there are
+                # some, replace the backward's dequantize
+                x_deq = x.cached_dequant(fmt) if hasattr(x, "cached_dequant") else None
                 w_deq = w.cached_dequant(fmt) if hasattr(w, "cached_dequant") else None
-                ctx.w_deq = w_deq is not None
-                if ctx.w_deq:
-                    ctx.save_for_backward(x_theta, x_q, x_alpha, w_deq)
-                else:
-                    ctx.save_for_backward(x_theta, x_q, x_alpha, w_theta, w_q, w_alpha)
+                ctx.x_deq, ctx.w_deq = x_deq is not None, w_deq is not None
+                ctx.save_for_backward(*([x_deq] if ctx.x_deq else [x_theta, x_q, x_alpha]),
+                                      *([w_deq] if ctx.w_deq else [w_theta, w_q, w_alpha]))
             return mm_fp4(x_theta, w_theta.T, x_q, w_q.T, x_alpha * w_alpha, 16 if fmt == "nvfp4" else 32,
                           fmt == "nvfp4")
         x_theta, x_q, x_alpha = getattr(x, fmt)()
@@ -134,13 +134,25 @@ class BlockScaledMatMul(torch.autograd.Function):
             dx, dw = _quantized_grads(ctx.fmt, grad_output, x_src if ctx.w_k is not None else None,
                                       w_src if ctx.x_k is not None else None)
             return None, None, dx, None, dw, None
-        if getattr(ctx, "w_deq", False):
-            x_theta, x_q, x_alpha, w_deq = ctx.saved_tensors
-            dx = grad_output @ w_deq[:, : ctx.x_k] if ctx.x_k is not None else None
-            dw = None
+        if ctx.swizzled:
+            saved = list(ctx.saved_tensors)
+            x_deq = saved.pop(0) if ctx.x_deq else None
+            if x_deq is None:
+                x_theta, x_q, x_alpha = saved[:3]
+                saved = saved[3:]
+            w_deq = saved[0] if ctx.w_deq else None
+            if w_deq is None:
+                w_theta, w_q, w_alpha = saved
+            deq = _DEQ[ctx.fmt]
+            dx = dw = None
+            if ctx.x_k is not None:
+                if w_deq is None:
+                    w_deq = deq(w_theta, w_q, w_alpha, swizzled=True)
+                dx = grad_output @ w_deq[:, : ctx.x_k]
             if ctx.w_k is not None:
-                dw = grad_output.T @ _dequant_activation(_DEQ[ctx.fmt], x_theta, x_q, x_alpha,
-                                                         {"swizzled": True})[:, : ctx.w_k]
+                if x_deq is None:
+                    x_deq = _dequant_activation(deq, x_theta, x_q, x_alpha, {"swizzled": True})
+                dw = grad_output.T @ x_deq[:, : ctx.w_k]
             return None, None, dx, None, dw, None
         x_theta, x_q, x_alpha, w_theta, w_q, w_alpha = ctx.saved_tensors
         deq = _DEQ[ctx.fmt]
@@ -148,11 +160,10 @@ class BlockScaledMatMul(torch.autograd.Function):
         if ctx.fmt == "mxfp8":
             x_theta = x_theta.view(torch.float8_e4m3fn)
             w_theta = w_theta.view(torch.float8_e4m3fn)
-        kw = {"swizzled": True} if ctx.swizzled else {}
         if ctx.x_k is not None:
-            dx = grad_output @ deq(w_theta, w_q, w_alpha, **kw)[:, : ctx.x_k]
+            dx = grad_output @ deq(w_theta, w_q, w_alpha)[:, : ctx.x_k]
         if ctx.w_k is not None:
-            dw = grad_output.T @ _dequant_activation(deq, x_theta, x_q, x_alpha, kw)[:, : ctx.w_k]
+            dw = grad_output.T @ _dequant_activation(deq, x_theta, x_q, x_alpha, {})[:, : ctx.w_k]
         return None, None, dx, None, dw, None
 
 

@@ -37,6 +37,27 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+// largest bf16 magnitude (bits) among the 8 values of v
+__device__ __forceinline__ uint32_t mag8(const uint4& v) {
+    uint32_t a, b;
+    asm("max.u16x2 %0, %1, %2;" : "=r"(a) : "r"(v.x & 0x7fff7fffu), "r"(v.y & 0x7fff7fffu));
+    asm("max.u16x2 %0, %1, %2;" : "=r"(b) : "r"(v.z & 0x7fff7fffu), "r"(v.w & 0x7fff7fffu));
+    asm("max.u16x2 %0, %1, %2;" : "=r"(a) : "r"(a), "r"(b));
+    return max(a & 0xffffu, a >> 16);
+}
+
+// Folds each thread's `m` into *amax (one atomic per CTA); all threads call it.
+__device__ __forceinline__ void cta_amax(uint32_t m, uint32_t* amax) {
+    __shared__ uint32_t red[32];
+    m = __reduce_max_sync(0xffffffffu, m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m = max(m, red[w]);
+        atomicMax(amax, m);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // RMSNorm: one warp per row; lane l owns the 8-value vectors l, l + 32, ...
 // (VPL vectors at most, d = 8 * nvec).
@@ -44,8 +65,9 @@ __device__ __forceinline__ float warp_sum(float v) {
 template <int VPL>
 __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const uint4* __restrict__ x, const uint4* __restrict__ w,
                                                           int64_t rows, int nvec, float eps, uint4* __restrict__ y,
-                                                          float* __restrict__ rstd) {
+                                                          float* __restrict__ rstd, uint32_t* __restrict__ amax) {
     const int lane = threadIdx.x & 31;
+    uint32_t am = 0;  // max |y| as bf16 magnitude bits (the NVFP4 global amax of the output)
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
         uint4 v[VPL];
@@ -71,9 +93,12 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const uint4* __restric
             unpack8(w[c], g);
 #pragma unroll
             for (int i = 0; i < 8; ++i) f[i] = g[i] * rbf(f[i] * rs);
-            y[r * nvec + c] = pack8(f);
+            const uint4 o = pack8(f);
+            y[r * nvec + c] = o;
+            am = max(am, mag8(o));
         }
     }
+    if (amax) cta_amax(am, amax);
 }
 
 // dx = bf16(rs * g1 - x * rs^3 * sum(g1 * x) / d) with g1 = bf16(dy * w);
@@ -209,15 +234,19 @@ __global__ void __launch_bounds__(256) rope_kernel(const uint4* __restrict__ x, 
 __device__ __forceinline__ float sigmoid_f(float g) { return 1.0f / (1.0f + expf(-g)); }
 
 __global__ void __launch_bounds__(256) swiglu_fwd_kernel(const uint4* __restrict__ g, const uint4* __restrict__ u,
-                                                         int64_t nvec, uint4* __restrict__ h) {
+                                                         int64_t nvec, uint4* __restrict__ h, uint32_t* __restrict__ amax) {
+    uint32_t am = 0;
     for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < nvec; t += (int64_t)gridDim.x * blockDim.x) {
         float a[8], b[8];
         unpack8(g[t], a);
         unpack8(u[t], b);
 #pragma unroll
         for (int i = 0; i < 8; ++i) a[i] = rbf(a[i] * sigmoid_f(a[i])) * b[i];
-        h[t] = pack8(a);
+        const uint4 o = pack8(a);
+        h[t] = o;
+        am = max(am, mag8(o));
     }
+    if (amax) cta_amax(am, amax);
 }
 
 __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const uint4* __restrict__ dh, const uint4* __restrict__ g,
@@ -328,7 +357,7 @@ int grid_for(int64_t items, int per_block) {
 using namespace cdlb200;
 
 extern "C" int cdlb200_rmsnorm_fwd(const void* x, const void* w, int64_t rows, int64_t d, float eps, void* y,
-                                   float* rstd, void* stream) {
+                                   float* rstd, uint32_t* amax, void* stream) {
     if (rows < 0 || d <= 0 || (d % 8) != 0 || d > 8 * 32 * 8) return CDLB200_ERR_INVALID_ARG;
     if (rows == 0) return CDLB200_OK;
     if (!x || !w || !y || !rstd) return CDLB200_ERR_INVALID_ARG;
@@ -338,7 +367,7 @@ extern "C" int cdlb200_rmsnorm_fwd(const void* x, const void* w, int64_t rows, i
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     auto args = [&](auto kern) {
         kern<<<grid, 256, 0, st>>>(static_cast<const uint4*>(x), static_cast<const uint4*>(w), rows, nvec, eps,
-                                   static_cast<uint4*>(y), rstd);
+                                   static_cast<uint4*>(y), rstd, amax);
     };
     if (vpl <= 1) args(rmsnorm_fwd_kernel<1>);
     else if (vpl <= 2) args(rmsnorm_fwd_kernel<2>);
@@ -404,13 +433,13 @@ extern "C" int cdlb200_rope(const void* x, const void* cos, const void* sin, int
     return CDLB200_OK;
 }
 
-extern "C" int cdlb200_swiglu_fwd(const void* g, const void* u, int64_t n, void* h, void* stream) {
+extern "C" int cdlb200_swiglu_fwd(const void* g, const void* u, int64_t n, void* h, uint32_t* amax, void* stream) {
     if (n < 0 || (n % 8) != 0) return CDLB200_ERR_INVALID_ARG;
     if (n == 0) return CDLB200_OK;
     if (!g || !u || !h) return CDLB200_ERR_INVALID_ARG;
     if (!al16(g) || !al16(u) || !al16(h)) return CDLB200_ERR_ALIGNMENT;
     swiglu_fwd_kernel<<<grid_for(n / 8, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const uint4*>(g), static_cast<const uint4*>(u), n / 8, static_cast<uint4*>(h));
+        static_cast<const uint4*>(g), static_cast<const uint4*>(u), n / 8, static_cast<uint4*>(h), amax);
     CDLB200_CHECK_LAUNCH();
     return CDLB200_OK;
 }

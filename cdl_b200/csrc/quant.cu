@@ -729,7 +729,8 @@ __global__ void __launch_bounds__(kFusedThreads, 2) nvfp4_fused_kernel(
 // the dequantized copy for the bf16 backward in the same pass.
 // ---------------------------------------------------------------------------
 constexpr int kEncThreads = 256;
-constexpr int kEncChunkBlocks = 2 * kEncThreads;  // 16-element blocks per work chunk
+constexpr int kEncPerThread = 4;                              // blocks per thread per chunk, loaded together
+constexpr int kEncChunkBlocks = kEncPerThread * kEncThreads;  // 16-element blocks per work chunk
 constexpr int kEncGroup = 256;                    // tensors per launch (table in the parameter block)
 
 struct EncGroup {
@@ -786,10 +787,10 @@ __global__ void __launch_bounds__(kEncThreads) nvfp4_encode_multi_kernel(const _
         if (c == g.chunk0[ti] && tid == 0) *T.alpha = tn.alpha;
         const int64_t base = (c - g.chunk0[ti]) * kEncChunkBlocks;
         const uint4* x = static_cast<const uint4*>(T.x);
-        uint4 w[4];
-        int64_t b[2];
+        uint4 w[2 * kEncPerThread];
+        int64_t b[kEncPerThread];
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
+        for (int j = 0; j < kEncPerThread; ++j) {
             b[j] = base + j * kEncThreads + tid;
             if (b[j] < nblk) {
                 w[2 * j] = ldg_stream(x + 2 * b[j]);
@@ -797,7 +798,7 @@ __global__ void __launch_bounds__(kEncThreads) nvfp4_encode_multi_kernel(const _
             }
         }
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
+        for (int j = 0; j < kEncPerThread; ++j) {
             if (b[j] >= nblk) continue;
             uint2 out;
             const uint32_t byte = nvfp4_block16(w[2 * j], w[2 * j + 1], max(amax8(w[2 * j]), amax8(w[2 * j + 1])),

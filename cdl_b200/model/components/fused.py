@@ -6,7 +6,9 @@ cdl trains SmolLM2 as a Hugging Face ``LlamaForCausalLM`` (smollm2.py), whose
 eager elementwise kernels.  ``patch_llama(model)`` swaps them for one CUDA
 pass each (forward and backward), keeping the rounding steps of the eager
 modules.  Tensors that are not bf16 on a CUDA device go through the original
-Hugging Face code.
+Hugging Face code.  The RMSNorm and SwiGLU outputs feed quantized linears;
+their kernels also produce the output's global amax (``AMAX_ATTR``), so the
+NVFP4 quantize of those activations is a single encode pass.
 """
 
 from __future__ import annotations
@@ -16,6 +18,15 @@ import types
 import torch
 
 from cdl_b200 import _lib
+
+
+# attribute of a kernel output carrying the NVFP4 global amax formed in its
+# epilogue: (amax word, version of the output when it was written)
+AMAX_ATTR = "_cdlb200_amax"
+
+
+def attach_amax(t: torch.Tensor, amax: torch.Tensor) -> None:
+    setattr(t, AMAX_ATTR, (amax, t._version))
 
 
 def _cuda_bf16(*ts: torch.Tensor) -> bool:
@@ -29,8 +40,10 @@ class RMSNormFn(torch.autograd.Function):
         x2 = x.reshape(-1, d).contiguous()
         y = torch.empty_like(x2)
         rstd = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device)
+        amax = torch.zeros(1, dtype=torch.int32, device=x.device)
         _lib.call("cdlb200_rmsnorm_fwd", _lib.ptr(x2), _lib.ptr(w), x2.shape[0], d, float(eps), _lib.ptr(y),
-                  _lib.ptr(rstd), _lib.stream(x.device))
+                  _lib.ptr(rstd), _lib.ptr(amax), _lib.stream(x.device))
+        attach_amax(y, amax)
         ctx.save_for_backward(x2, w, rstd)
         ctx.shape = x.shape
         return y.view(x.shape)
@@ -83,7 +96,10 @@ class SwiGLUFn(torch.autograd.Function):
     def forward(ctx, g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
         g, u = g.contiguous(), u.contiguous()
         h = torch.empty_like(g)
-        _lib.call("cdlb200_swiglu_fwd", _lib.ptr(g), _lib.ptr(u), g.numel(), _lib.ptr(h), _lib.stream(g.device))
+        amax = torch.zeros(1, dtype=torch.int32, device=g.device)
+        _lib.call("cdlb200_swiglu_fwd", _lib.ptr(g), _lib.ptr(u), g.numel(), _lib.ptr(h), _lib.ptr(amax),
+                  _lib.stream(g.device))
+        attach_amax(h, amax)
         ctx.save_for_backward(g, u)
         return h
 

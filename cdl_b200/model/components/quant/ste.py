@@ -9,11 +9,14 @@ straight through (identity, no clipping mask); ``dequantize()`` serves the
 
 from __future__ import annotations
 
+import ctypes
 import weakref
 from dataclasses import dataclass
 from typing import Literal
 
 import torch
+
+from cdl_b200 import _lib
 
 from cdl_b200.api.quant import QTensor, Quant
 from cdl_b200.core.kernel.dequant import mxfp4_dequant, mxfp8_dequant, nvfp4_dequant
@@ -27,6 +30,31 @@ _ENCODED: list = []
 _ENCODED_MAX = 4
 # attribute the optimizer's weight encoder sets on a weight (train/optim.py)
 _ENCODED_ATTR = "_cdlb200_nvfp4"
+# attribute of an activation whose producing kernel formed its amax
+# (model/components/fused.py)
+_AMAX_ATTR = "_cdlb200_amax"
+
+
+def _lookup(owner: torch.Tensor, key):
+    for ref, k, res in _ENCODED:
+        if k == key and ref() is owner:
+            return res
+    return None
+
+
+def _encode_with_amax(theta: torch.Tensor, amax: torch.Tensor):
+    """NVFP4 (codes, GEMM-layout scales, alpha) and the dequantized copy of a
+    contiguous [rows, k] bf16 tensor whose amax word is given."""
+    rows, k = theta.shape
+    dev = theta.device
+    packed = torch.empty(rows, k // 2, dtype=torch.uint8, device=dev)
+    scale = torch.empty(rows, k // 16, dtype=torch.uint8, device=dev)
+    alpha = torch.empty(1, dtype=torch.float32, device=dev)
+    deq = torch.empty(rows, k, dtype=torch.bfloat16, device=dev)
+    t = _lib.Nvfp4EncodeTensor(theta.data_ptr(), rows, k, amax.data_ptr(), packed.data_ptr(), scale.data_ptr(),
+                               alpha.data_ptr(), deq.data_ptr())
+    _lib.call("cdlb200_nvfp4_encode_multi", ctypes.addressof(t), 1, _lib.stream(dev))
+    return (packed, scale, alpha), deq
 
 
 @dataclass
@@ -77,13 +105,22 @@ class SteTensor(QTensor):
         cacheable = not (owner.is_leaf and owner.requires_grad)
         if cacheable:
             key = (fmt, theta.data_ptr(), tuple(theta.shape), theta.stride(), theta.dtype, theta._version)
-            for ref, k, res in _ENCODED:
-                if k == key and ref() is owner:
-                    return res
+            hit = _lookup(owner, key)
+            if hit is not None:
+                return hit[:3]
+        deq = None
         with torch.no_grad():
-            res = fn(theta, swizzled=True)
+            amax = getattr(owner, _AMAX_ATTR, None)
+            if (fmt == "nvfp4" and amax is not None and amax[1] == owner._version and theta.is_contiguous()
+                    and theta.data_ptr() == owner.data_ptr() and theta.numel() == owner.numel()
+                    and theta.shape[0] % 128 == 0 and self.k % 64 == 0):
+                # the producing kernel formed the amax: encode in one pass, with
+                # the dequantized copy the wgrad GEMM reads
+                res, deq = _encode_with_amax(theta, amax[0])
+            else:
+                res = fn(theta, swizzled=True)
         if cacheable:
-            _ENCODED.insert(0, (weakref.ref(owner), key, res))
+            _ENCODED.insert(0, (weakref.ref(owner), key, (*res, deq)))
             del _ENCODED[_ENCODED_MAX:]
         return res
 
@@ -96,9 +133,17 @@ class SteTensor(QTensor):
         return enc
 
     def cached_dequant(self, fmt: Simulation) -> torch.Tensor | None:
-        """bf16 ``deq(Q(theta))`` kept with the optimizer's encoding, else None."""
+        """bf16 ``deq(Q(theta))`` if one was formed with the encoding (the
+        optimizer's weight encoding, or an activation encoded with its
+        producer's amax), else None.  Call after ``encode_swizzled``."""
         enc = self._weight_encoding(fmt)
-        return None if enc is None else enc[4]
+        if enc is not None:
+            return enc[4]
+        theta = self.theta.reshape(-1, self.k)
+        owner = theta._base if theta._base is not None else theta
+        key = (fmt, theta.data_ptr(), tuple(theta.shape), theta.stride(), theta.dtype, theta._version)
+        hit = _lookup(owner, key)
+        return None if hit is None else hit[3]
 
     def dequantize(self) -> torch.Tensor:
         if self.simulation is None:

@@ -18,9 +18,12 @@ extern "C" {
 #endif
 
 /* y = bf16(w * bf16(x * rsqrt(mean(x^2) + eps))) per row of x[rows, d]
- * (d % 8 == 0, d <= 2048); rstd[rows] (fp32) receives rsqrt(mean(x^2) + eps). */
+ * (d % 8 == 0, d <= 2048); rstd[rows] (fp32) receives rsqrt(mean(x^2) + eps).
+ * amax (optional, zero on entry) receives the bf16 magnitude bits of max|y|:
+ * the global amax the NVFP4 quantize of y needs, formed in the epilogue so
+ * that the quantize skips its own amax pass (cdlb200_nvfp4_encode_multi). */
 int cdlb200_rmsnorm_fwd(const void* x, const void* w, int64_t rows, int64_t d, float eps, void* y, float* rstd,
-                        void* stream);
+                        uint32_t* amax, void* stream);
 
 /* Device scratch (bytes) cdlb200_rmsnorm_bwd needs for rows x d. */
 int64_t cdlb200_rmsnorm_bwd_workspace_bytes(int64_t rows, int64_t d);
@@ -37,8 +40,9 @@ int cdlb200_rmsnorm_bwd(const void* dy, const void* x, const void* w, const floa
 int cdlb200_rope(const void* x, const void* cos, const void* sin, int64_t tokens, int64_t heads, int64_t head_dim,
                  int64_t cos_tokens, int backward, void* out, void* stream);
 
-/* h = bf16(bf16(silu(g)) * u) over n values (n % 8 == 0). */
-int cdlb200_swiglu_fwd(const void* g, const void* u, int64_t n, void* h, void* stream);
+/* h = bf16(bf16(silu(g)) * u) over n values (n % 8 == 0); amax (optional,
+ * zero on entry) receives the bf16 magnitude bits of max|h|. */
+int cdlb200_swiglu_fwd(const void* g, const void* u, int64_t n, void* h, uint32_t* amax, void* stream);
 
 /* dg, du of the SwiGLU product above, given dh. */
 int cdlb200_swiglu_bwd(const void* dh, const void* g, const void* u, int64_t n, void* dg, void* du, void* stream);

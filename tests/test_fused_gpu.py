@@ -164,3 +164,31 @@ def test_linear_cross_entropy_matches_plain_loss():
     assert abs(float(loss.detach()) - float(ref.detach())) < 1e-4 * float(ref.detach())
     assert _rel(h.grad, h2.grad) < 1e-2
     assert _rel(w.grad, w2.grad) < 1e-2
+
+
+def test_epilogue_amax_feeds_single_pass_encode():
+    """RMSNorm and SwiGLU outputs carry their global amax; the NVFP4 encode of
+    such an activation (one pass, with the dequantized copy) equals the
+    two-pass quantizer and the dequantizer bit for bit."""
+    from cdl_b200.core.kernel.dequant import nvfp4_dequant
+    from cdl_b200.core.kernel.quant import nvfp4_quant
+    from cdl_b200.model.components.fused import AMAX_ATTR, RMSNormFn, SwiGLUFn
+    from cdl_b200.model.components.quant.ste import SteTensor
+
+    gen = torch.Generator("cuda").manual_seed(11)
+    x = torch.randn(256, 512, device="cuda", generator=gen).bfloat16()
+    w = (1 + 0.1 * torch.randn(512, device="cuda", generator=gen)).bfloat16()
+    g = torch.randn(384, 1024, device="cuda", generator=gen).bfloat16()
+    u = torch.randn(384, 1024, device="cuda", generator=gen).bfloat16()
+    for out in (RMSNormFn.apply(x, w, 1e-5), SwiGLUFn.apply(g, u)):
+        owner = out._base if out._base is not None else out
+        amax, _ = getattr(owner, AMAX_ATTR)
+        want = int((out.contiguous().view(torch.int16).int() & 0x7FFF).max())
+        assert int(amax.item()) == want
+        st = SteTensor(theta=out.reshape(-1, out.shape[-1]), simulation=None)
+        p, s, a = st.encode_swizzled("nvfp4")
+        d = st.cached_dequant("nvfp4")
+        assert d is not None
+        rp, rs, ra = nvfp4_quant(out.reshape(-1, out.shape[-1]).contiguous(), swizzled=True)
+        assert torch.equal(p, rp) and torch.equal(s, rs) and torch.equal(a.reshape(-1), ra.reshape(-1))
+        assert torch.equal(d, nvfp4_dequant(rp, rs, ra, swizzled=True))
