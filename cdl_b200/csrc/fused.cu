@@ -37,19 +37,21 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-// largest bf16 magnitude (bits) among the 8 values of v
-__device__ __forceinline__ uint32_t mag8(const uint4& v) {
+// running max of bf16 magnitudes, two lanes per word: acc = max(acc, |v|)
+__device__ __forceinline__ uint32_t mag8(uint32_t acc, const uint4& v) {
     uint32_t a, b;
     asm("max.u16x2 %0, %1, %2;" : "=r"(a) : "r"(v.x & 0x7fff7fffu), "r"(v.y & 0x7fff7fffu));
     asm("max.u16x2 %0, %1, %2;" : "=r"(b) : "r"(v.z & 0x7fff7fffu), "r"(v.w & 0x7fff7fffu));
     asm("max.u16x2 %0, %1, %2;" : "=r"(a) : "r"(a), "r"(b));
-    return max(a & 0xffffu, a >> 16);
+    asm("max.u16x2 %0, %1, %2;" : "=r"(acc) : "r"(acc), "r"(a));
+    return acc;
 }
 
-// Folds each thread's `m` into *amax (one atomic per CTA); all threads call it.
-__device__ __forceinline__ void cta_amax(uint32_t m, uint32_t* amax) {
+// Folds each thread's two-lane running max `m2` into *amax (one atomic per
+// CTA); all threads call it.
+__device__ __forceinline__ void cta_amax(uint32_t m2, uint32_t* amax) {
     __shared__ uint32_t red[32];
-    m = __reduce_max_sync(0xffffffffu, m);
+    uint32_t m = __reduce_max_sync(0xffffffffu, max(m2 & 0xffffu, m2 >> 16));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -95,7 +97,7 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const uint4* __restric
             for (int i = 0; i < 8; ++i) f[i] = g[i] * rbf(f[i] * rs);
             const uint4 o = pack8(f);
             y[r * nvec + c] = o;
-            am = max(am, mag8(o));
+            am = mag8(am, o);
         }
     }
     if (amax) cta_amax(am, amax);
@@ -244,7 +246,7 @@ __global__ void __launch_bounds__(256) swiglu_fwd_kernel(const uint4* __restrict
         for (int i = 0; i < 8; ++i) a[i] = rbf(a[i] * sigmoid_f(a[i])) * b[i];
         const uint4 o = pack8(a);
         h[t] = o;
-        am = max(am, mag8(o));
+        am = mag8(am, o);
     }
     if (amax) cta_amax(am, amax);
 }
