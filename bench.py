@@ -55,7 +55,8 @@ QUANT = {
     "mxfp4_quant": ("mxfp4", 16384, 8192, 2.53125, "C2"),
     "mxfp8_quant": ("mxfp8", 16384, 8192, 3.03125, "C2"),
 }
-WORKLOADS = sorted(list(QUANT) + ["fp4_gemm", "qat_135m", "qat_1.7b"])
+WORKLOADS = sorted(list(QUANT) + ["fp4_gemm", "qat_135m", "qat_1.7b", "nvfp4_ecdl"])
+ECDL_TOPK, ECDL_KAPPA = 5, 4.0  # theta_topk default of cdl's training config (smollm2.py:168)
 
 
 def parse_args():
@@ -189,6 +190,62 @@ def cpu_quant_rate(fmt_name, rows, k, bpe, steps, warmup, threads, target_s=None
         n += 1
     dt = time.perf_counter() - t0
     return bpe * rows * k * n / dt / 1e9, f"{n} x {fmt_name} quantize of [{rows},{k}] bf16 ({threads} threads)"
+
+
+def cpu_ecdl_rate(rows, k, threads, target_s=10.0):
+    """The ECDL oracle (numpy restatement) on a bounded row sample of C1."""
+    import numpy as np
+
+    from cdl_b200 import workloads
+    from oracle import ecdl as E
+
+    x = workloads.c1_nvfp4(rows, k, seed=0).float().numpy().reshape(rows, k // 16, 16)
+    sample_rows = 64
+    t0, cnt = time.perf_counter(), 0
+    while cnt < 1 or time.perf_counter() - t0 < target_s:
+        E.forward(E.NVFP4, x[:sample_rows], ECDL_KAPPA, cnt + 1, ECDL_TOPK, E.MODE_NVIDIA)
+        cnt += 1
+    dt = time.perf_counter() - t0
+    return (2.5625 * sample_rows * k * cnt / dt / 1e9,
+            f"{cnt} x NVFP4 ECDL forward (numpy oracle) of {sample_rows}x{k} of C1 (1 thread)")
+
+
+def ecdl_workload(dev, rank):
+    import torch
+
+    from cdl_b200 import workloads
+    from cdl_b200.core.kernel.ecdl import FormatId, ecdl_quant_fwd
+
+    rows, k = QUANT["nvfp4_quant"][1:3]
+    pool_n = max(2, -(-2 * L2_BYTES // (rows * k * 2)))
+    pool = [workloads.c1_nvfp4(rows, k, seed=1000 * rank + i, device=str(dev)).reshape(rows, k // 16, 16)
+            for i in range(pool_n)]
+    kappa = torch.tensor(ECDL_KAPPA, device=dev)
+    seeds = [torch.tensor(i + 1, dtype=torch.int64, device=dev) for i in range(pool_n)]
+    host_in = pool[0].cpu().pin_memory()
+    p0, s0, _ = ecdl_quant_fwd(pool[0], kappa, seeds[0], FormatId.NVFP4, ECDL_TOPK, "nvidia")
+    host_p = torch.empty(p0.shape, dtype=p0.dtype, pin_memory=True)
+    host_s = torch.empty(s0.shape, dtype=s0.dtype, pin_memory=True)
+
+    def e2e_step():
+        p, s_, _ = ecdl_quant_fwd(host_in.to(dev, non_blocking=True), kappa, seeds[0], FormatId.NVFP4, ECDL_TOPK,
+                                  "nvidia")
+        host_p.copy_(p, non_blocking=True)
+        host_s.copy_(s_, non_blocking=True)
+
+    return {
+        "step": lambda i: ecdl_quant_fwd(pool[i % pool_n], kappa, seeds[i % pool_n], FormatId.NVFP4, ECDL_TOPK,
+                                         "nvidia"),
+        "e2e_step": e2e_step, "graph": True,
+        "units_per_step": 2.5625 * rows * k / 1e9, "unit": "GB/s", "metric": "NVFP4 ECDL quant GB/s",
+        "dtype": "bf16->e2m1/e4m3 (stochastic, Philox)",
+        "config": {"workload": f"nvfp4_ecdl C1 [{rows},{k}] bf16 per rank, theta_topk {ECDL_TOPK}, "
+                               f"kappa {ECDL_KAPPA}, nvidia scales",
+                   "l2": f"inputs cycled over {pool_n} tensors (> 2x L2)"},
+        "h2d": host_in.numel() * 2, "d2h": p0.numel() + s0.numel(),
+        "bound": "hbm", "kernel": "ecdl_fwd_kernel (+ ecdl_amax_kernel)",
+        "launches_per_step": 2,
+    }
 
 
 def cpu_gemm_rate(threads, target_s=10.0):
@@ -454,6 +511,9 @@ def main() -> None:
         elif wl == "fp4_gemm":
             val, sample = cpu_gemm_rate(threads, target_s=5.0)
             unit, metric = "TFLOP/s", "FP4 GEMM TFLOPS"
+        elif wl == "nvfp4_ecdl":
+            val, sample = cpu_ecdl_rate(4096, 4096, threads, target_s=5.0)
+            unit, metric = "GB/s", "NVFP4 ECDL quant GB/s"
         else:
             val, sample = cpu_qat_rate("135m" if wl == "qat_135m" else "1.7b", threads, target_s=10.0)
             unit, metric = "tokens/s", "SmolLM2 NVFP4 QAT tokens/s"
@@ -480,6 +540,8 @@ def main() -> None:
         w = quant_workload(wl, dev, rank)
     elif wl == "fp4_gemm":
         w = gemm_workload(dev, rank)
+    elif wl == "nvfp4_ecdl":
+        w = ecdl_workload(dev, rank)
     else:
         w = qat_workload(wl, dev, rank, world, args.backend)
 
@@ -554,6 +616,8 @@ def main() -> None:
             val, sample = cpu_quant_rate(fmt, rows, k, bpe, 3, 1, threads, target_s=10.0)
         elif wl == "fp4_gemm":
             val, sample = cpu_gemm_rate(threads, target_s=10.0)
+        elif wl == "nvfp4_ecdl":
+            val, sample = cpu_ecdl_rate(4096, 4096, threads, target_s=10.0)
         else:
             val, sample = cpu_qat_rate("135m" if wl == "qat_135m" else "1.7b", threads, target_s=10.0)
         cpu = {"value": round(val, 4), "unit": w["unit"], "cores": threads, "kind": "port", "sample": sample}

@@ -61,6 +61,9 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_swiglu_fwd": (_I, [_P, _P, _I64, _P, _P, _P]),
     "cdlb200_swiglu_bwd": (_I, [_P, _P, _P, _I64, _P, _P, _P]),
     "cdlb200_cross_entropy": (_I, [_P, _P, _I64, _I64, _F, _P, _P]),
+    "cdlb200_ecdl_fwd": (_I, [_P, _I, _I64, _I64, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P]),
+    "cdlb200_ecdl_bwd_workspace_bytes": (_I64, [_I64, _I64, _I]),
+    "cdlb200_ecdl_bwd": (_I, [_P, _P, _I, _I64, _I64, _I, _P, _P, _P, _I, _P, _P, _P, _I64, _P]),
     "cdlb200_clip_adamw_workspace_bytes": (_I64, [_P, _I]),
     "cdlb200_clip_adamw": (_I, [_P, _I, _D, _D, _D, _D, _D, _D, _P, _I64, _P, _P]),
     "cdlb200_nvfp4_encode_multi": (_I, [_P, _I, _P]),
@@ -111,7 +114,7 @@ def lib() -> ctypes.CDLL:
 
 # kernels one call of an entry point launches (default 1); `launches` counts
 # them over the process, so a benchmark can report how many ran
-KERNELS_PER_CALL = {"cdlb200_rmsnorm_bwd": 2, "cdlb200_clip_adamw": 3}
+KERNELS_PER_CALL = {"cdlb200_rmsnorm_bwd": 2, "cdlb200_clip_adamw": 3, "cdlb200_ecdl_fwd": 2, "cdlb200_ecdl_bwd": 2}
 launches = 0
 
 

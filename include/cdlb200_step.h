@@ -113,6 +113,33 @@ typedef struct {
  * the weight dequantize of the backward (dequant.py:103-109). */
 int cdlb200_nvfp4_encode_multi(const cdlb200_nvfp4_encode_tensor* tensors, int count, void* stream);
 
+/* ECDL stochastic quantizer (cdl/core/kernel/ecdl: launch.py launch_ecdl_fwd /
+ * launch_ecdl_bwd, kernel.py _ecdl_fwd / _ecdl_bwd).  theta is bf16 (theta_f32
+ * = 0) or fp32, [rows, nb * block] with block 16 (NVFP4) or 32 (MXFP4 /
+ * MXFP8).  Forward: per block a scale (nvidia mode: UE4M3 index from
+ * block amax * 448 / global amax, alpha = global amax / 2688; OCP mode: E8M0
+ * from the block exponent, alpha = 1), then for every element a level index
+ * sampled from the top-k window around x / s with weights
+ * exp(-kappa (c - t)^2) and the uniform number of Triton's
+ * tl.rand(seed, flat index) (Philox4x32-10).  packed: FP4 codes (two per
+ * byte, element 2j low) or e4m3 bytes; scale: [rows, nb] bytes (index + 1
+ * for UE4M3).  kappa (fp32) and seed (int64, low 32 bits used) are device
+ * scalars; workspace >= 4 bytes.  Backward: dtheta = g * dE[level]/dx of the
+ * CDL proxy with kappa (forward's or a fixed backward kappa), and, when
+ * scalars is given, scalars = {d kappa, d alpha}. */
+#define CDLB200_ECDL_NVFP4 0
+#define CDLB200_ECDL_MXFP4 1
+#define CDLB200_ECDL_MXFP8 2
+#define CDLB200_ECDL_NVIDIA 0
+#define CDLB200_ECDL_OCP 1
+int cdlb200_ecdl_fwd(const void* theta, int theta_f32, int64_t rows, int64_t nb, int format, int scale_mode,
+                     const float* kappa, const int64_t* seed, int topk, void* packed, void* scale, float* alpha,
+                     void* workspace, void* stream);
+int64_t cdlb200_ecdl_bwd_workspace_bytes(int64_t rows, int64_t nb, int format);
+int cdlb200_ecdl_bwd(const void* grad, const void* theta, int theta_f32, int64_t rows, int64_t nb, int format,
+                     const void* scale, const float* kappa, const float* alpha, int topk, void* dtheta,
+                     float* scalars, void* workspace, int64_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

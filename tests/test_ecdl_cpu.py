@@ -1,0 +1,84 @@
+"""CPU checks of the ECDL oracle (oracle/ecdl.py): the random stream against
+the Random123 known-answer vectors, the sampler's limits and distribution,
+and the proxy-gradient coefficients against finite differences."""
+
+import numpy as np
+import pytest
+
+from oracle import ecdl as E
+
+
+@pytest.mark.parametrize("ctr,key,want", [
+    ((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+    ((0xFFFFFFFF,) * 4, (0xFFFFFFFF, 0xFFFFFFFF), (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+    ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+     (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1)),
+])
+def test_philox_known_answers(ctr, key, want):
+    got = E.philox4x32(*[np.array([c]) for c in ctr], *key)
+    assert [int(g[0]) for g in got] == list(want)
+
+
+def test_uniform_range_and_mean():
+    u = E.uniform(7, np.arange(200000, dtype=np.uint64))
+    assert u.min() >= 0.0 and u.max() < 1.0
+    assert abs(float(u.mean()) - 0.5) < 5e-3
+
+
+@pytest.mark.parametrize("fmt", [E.NVFP4, E.MXFP8])
+def test_tables(fmt):
+    f = E.Format(fmt)
+    assert np.all(np.diff(f.level) >= 0) and np.all(f.gap > 0)
+    if fmt == E.NVFP4:
+        assert f.tn == 16 and f.qn == 126 and f.f_max == 2688.0 and f.emax == 2
+    else:
+        assert f.tn == 254 and f.level[0] == -448.0 and f.level[-1] == 448.0 and f.emax == 8
+
+
+@pytest.mark.parametrize("fmt,topk", [(E.NVFP4, 4), (E.NVFP4, 16), (E.MXFP8, 8)])
+def test_large_kappa_samples_the_nearest_level(fmt, topk):
+    f = E.Format(fmt)
+    rng = np.random.RandomState(0)
+    v = (rng.randn(5000) * (2.0 if fmt == E.NVFP4 else 60.0)).astype(np.float32)
+    u = rng.rand(5000).astype(np.float32)
+    idx = E.sample(f, v, 1e6, u, topk)
+    c, start, _ = E._window(f, v, topk)
+    near = np.clip(np.floor(c + np.float32(0.5)), start, start + topk - 1).astype(np.int64)
+    assert np.array_equal(idx, near)
+
+
+def test_sampler_follows_its_probabilities():
+    f = E.Format(E.NVFP4)
+    v = np.full(200000, 1.3, dtype=np.float32)
+    u = E.uniform(3, np.arange(v.size, dtype=np.uint64))
+    idx = E.sample(f, v, 2.0, u, 8)
+    start, p = E.probabilities(f, v[:1], 2.0, 8)
+    freq = np.bincount(idx - start[0], minlength=8) / v.size
+    assert np.max(np.abs(freq - p[0])) < 5 * np.sqrt(0.25 / v.size) + 1e-4
+
+
+@pytest.mark.parametrize("kappa", [0.5, 3.0])
+def test_proxy_coefficient_is_the_derivative_of_the_expected_level(kappa):
+    """dth = d E[level] / dv (per unit of v, the chain rule through x = v s
+    lives in the caller)."""
+    f = E.Format(E.NVFP4)
+    v = np.array([-2.7, -0.9, 0.1, 0.62, 1.1, 2.2, 3.3, 4.8], dtype=np.float64)
+    dth, _, _ = E.proxy_coeffs(f, v.astype(np.float32), kappa, 16)
+
+    def expect(x):
+        start, p = E.probabilities(f, x.astype(np.float32), kappa, 16)
+        lev = np.stack([f.level[start + j] for j in range(16)], -1)
+        return (p * lev).sum(-1)
+
+    h = 1e-3
+    num = (expect(v + h) - expect(v - h)) / (2 * h)
+    assert np.allclose(dth, num, rtol=2e-2, atol=2e-3), (dth, num)
+
+
+def test_ecdl_workspace_bytes_on_host():
+    from cdl_b200 import _lib
+
+    lib = _lib.lib()
+    assert lib.cdlb200_ecdl_bwd_workspace_bytes(0, 4, 0) == 0
+    assert lib.cdlb200_ecdl_bwd_workspace_bytes(64, 4, 0) > 0
+    assert lib.cdlb200_ecdl_bwd_workspace_bytes(64, 4, 7) == 0  # unknown format
