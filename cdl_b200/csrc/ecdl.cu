@@ -149,6 +149,41 @@ __device__ __forceinline__ int cdl_sample(float v, float kappa, float u, const f
     return w.start + (cnt < topk - 1 ? cnt : topk - 1);
 }
 
+// the same sampler for a window width K known at compile time: the weights
+// are computed once and kept in registers
+template <int K>
+__device__ __forceinline__ int cdl_sample_k(float v, float kappa, float u, const float* lev, const float* gap,
+                                            int tn) {
+    const Window w = cdl_window(v, lev, gap, tn, K);
+    const float fs = (float)w.start;
+    const float t_near = fminf(fmaxf(floorf(__fadd_rn(w.c, 0.5f)), fs), (float)(w.start + K - 1));
+    const float dn = __fsub_rn(t_near, w.c);
+    const float m = __fmul_rn(__fmul_rn(-kappa, dn), dn);
+    float wt[K];
+    float z = 0.0f;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+        wt[j] = cdl_weight(w.c, fs + (float)j, t_near, m, kappa);
+        z = __fadd_rn(z, wt[j]);
+    }
+    const float uz = __fmul_rn(u, z);
+    float acc = 0.0f;
+    int cnt = 0;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+        acc = __fadd_rn(acc, wt[j]);
+        cnt += acc <= uz;
+    }
+    return w.start + (cnt < K - 1 ? cnt : K - 1);
+}
+
+template <int K>
+__device__ __forceinline__ int sample_dispatch(float v, float kappa, float u, const float* lev, const float* gap,
+                                               int tn, int topk) {
+    if constexpr (K > 0) return cdl_sample_k<K>(v, kappa, u, lev, gap, tn);
+    else return cdl_sample(v, kappa, u, lev, gap, tn, topk);
+}
+
 struct Coeffs {
     float dth, ds, dk;
 };
@@ -253,7 +288,7 @@ __device__ __forceinline__ void block_scale(int mode, const EcdlFormat& f, float
     }
 }
 
-template <typename T>
+template <typename T, int K>
 __global__ void __launch_bounds__(kEcdlThreads) ecdl_fwd_kernel(const T* __restrict__ theta, int64_t npairs, int fmt,
                                                                 int mode, int topk, const float* __restrict__ kappa_p,
                                                                 const int64_t* __restrict__ seed_p,
@@ -285,8 +320,8 @@ __global__ void __launch_bounds__(kEcdlThreads) ecdl_fwd_kernel(const T* __restr
         float s;
         block_scale(mode, f, bamax, gmax, alpha, qi, s);
         const float u0 = rand_uniform((uint32_t)(2 * p), seed), u1 = rand_uniform((uint32_t)(2 * p + 1), seed);
-        const int i0 = cdl_sample(__fdiv_rn(x0, s), kappa, u0, lev, gap, f.tn, topk);
-        const int i1 = cdl_sample(__fdiv_rn(x1, s), kappa, u1, lev, gap, f.tn, topk);
+        const int i0 = sample_dispatch<K>(__fdiv_rn(x0, s), kappa, u0, lev, gap, f.tn, topk);
+        const int i1 = sample_dispatch<K>(__fdiv_rn(x1, s), kappa, u1, lev, gap, f.tn, topk);
         if (f.tn == 16) {
             const uint32_t c0 = i0 < 8 ? 15 - i0 : i0 - 8, c1 = i1 < 8 ? 15 - i1 : i1 - 8;
             packed[p] = (uint8_t)(c0 | (c1 << 4));
@@ -378,6 +413,22 @@ __global__ void ecdl_sum_kernel(const float* __restrict__ part, int n, float* __
     }
 }
 
+template <int K>
+void launch_fwd(const void* theta, int theta_f32, int64_t npairs, int format, int scale_mode, int topk,
+                const float* kappa, const int64_t* seed, const uint32_t* gbits, void* packed, void* scale,
+                float* alpha, int grid, cudaStream_t st) {
+    if (theta_f32)
+        ecdl_fwd_kernel<float, K><<<grid, kEcdlThreads, 0, st>>>(static_cast<const float*>(theta), npairs, format,
+                                                                 scale_mode, topk, kappa, seed, gbits,
+                                                                 static_cast<uint8_t*>(packed),
+                                                                 static_cast<uint8_t*>(scale), alpha);
+    else
+        ecdl_fwd_kernel<uint16_t, K><<<grid, kEcdlThreads, 0, st>>>(static_cast<const uint16_t*>(theta), npairs,
+                                                                    format, scale_mode, topk, kappa, seed, gbits,
+                                                                    static_cast<uint8_t*>(packed),
+                                                                    static_cast<uint8_t*>(scale), alpha);
+}
+
 int ecdl_grid(int64_t npairs) {
     const int64_t cap = (int64_t)num_sms() * 8;
     const int64_t g = (npairs + kEcdlThreads - 1) / kEcdlThreads;
@@ -424,16 +475,16 @@ extern "C" int cdlb200_ecdl_fwd(const void* theta, int theta_f32, int64_t rows, 
                                                                       gbits);
         CDLB200_CHECK_LAUNCH();
     }
-    if (theta_f32)
-        ecdl_fwd_kernel<float><<<grid, kEcdlThreads, 0, st>>>(static_cast<const float*>(theta), npairs, format,
-                                                              scale_mode, topk, kappa, seed, gbits,
-                                                              static_cast<uint8_t*>(packed),
-                                                              static_cast<uint8_t*>(scale), alpha);
-    else
-        ecdl_fwd_kernel<uint16_t><<<grid, kEcdlThreads, 0, st>>>(static_cast<const uint16_t*>(theta), npairs, format,
-                                                                 scale_mode, topk, kappa, seed, gbits,
-                                                                 static_cast<uint8_t*>(packed),
-                                                                 static_cast<uint8_t*>(scale), alpha);
+    // common window widths get a sampler unrolled for them (cdl's training
+    // default is 5; weights use the whole e2m1 grid, 16)
+    switch (topk) {
+        case 4: launch_fwd<4>(theta, theta_f32, npairs, format, scale_mode, topk, kappa, seed, gbits, packed, scale, alpha, grid, st); break;
+        case 5: launch_fwd<5>(theta, theta_f32, npairs, format, scale_mode, topk, kappa, seed, gbits, packed, scale, alpha, grid, st); break;
+        case 6: launch_fwd<6>(theta, theta_f32, npairs, format, scale_mode, topk, kappa, seed, gbits, packed, scale, alpha, grid, st); break;
+        case 8: launch_fwd<8>(theta, theta_f32, npairs, format, scale_mode, topk, kappa, seed, gbits, packed, scale, alpha, grid, st); break;
+        case 16: launch_fwd<16>(theta, theta_f32, npairs, format, scale_mode, topk, kappa, seed, gbits, packed, scale, alpha, grid, st); break;
+        default: launch_fwd<0>(theta, theta_f32, npairs, format, scale_mode, topk, kappa, seed, gbits, packed, scale, alpha, grid, st); break;
+    }
     CDLB200_CHECK_LAUNCH();
     return CDLB200_OK;
 }
