@@ -96,3 +96,35 @@ def test_ecdl_autograd_seed_and_gradients():
     dth, scalars = ecdl_quant_bwd(g, theta.detach(), scale, log_kappa.exp().detach(), alpha, 0, 16, "nvidia", True)
     assert torch.equal(theta.grad.reshape(-1), dth.reshape(-1))
     assert torch.allclose(log_kappa.grad, scalars[0] * log_kappa.exp().detach(), rtol=1e-5)
+
+
+@pytest.mark.parametrize("fmt", ["nvfp4", "mxfp4", "mxfp8"])
+def test_ecdl_modules_in_a_qlinear(fmt):
+    """ECDL activation + weight quantizers in a QLinear: the block-scaled GEMM
+    agrees with dequantize-then-matmul on the same sampled codes, gradients
+    reach the input, the weight and both log_kappa, and eval mode rounds."""
+    from cdl_b200.core.mm import native
+    from cdl_b200.model.components.linear import QLinear
+    from cdl_b200.model.components.quant import ecdl as Q
+
+    torch.manual_seed(0)
+    lin = QLinear(256, 128, bias=False, device="cuda", dtype=torch.bfloat16)
+    act_cls = {"nvfp4": Q.Nvfp4ExtendedCdlQuantForActivation, "mxfp4": Q.Mxfp4ExtendedCdlQuantForActivation,
+               "mxfp8": Q.Mxfp8ExtendedCdlQuantForActivation}[fmt]
+    w_cls = {"nvfp4": Q.Nvfp4ExtendedCdlQuantForWeight, "mxfp4": Q.Mxfp4ExtendedCdlQuantForWeight,
+             "mxfp8": Q.Mxfp8ExtendedCdlQuantForWeight}[fmt]
+    lin.set_activation_quant(act_cls((1, 256), 5, torch.bfloat16, 4.0).cuda())
+    lin.set_weight_quant(w_cls(lin.weight, torch.bfloat16, 4.0).cuda())
+    lin.set_backend(fmt)
+    x = torch.randn(64, 256, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    xq, wq = lin.activation_quant(x), lin.weight_quant(lin.weight)
+    out = lin.available_backend_fn[fmt](xq, wq)
+    ref = native.matmul(xq, wq)
+    assert float((out.float() - ref.float()).norm() / ref.float().norm()) < 2e-2
+    (out.float() ** 2).sum().backward()
+    for t in (x, lin.weight, lin.activation_quant.log_kappa, lin.weight_quant.log_kappa):
+        assert t.grad is not None and bool(torch.isfinite(t.grad).all())
+    assert int(lin.activation_quant.kernel_seed) == 1
+    lin.eval()
+    y = lin(x.detach())
+    assert y.shape == (64, 128) and bool(torch.isfinite(y.float()).all())
