@@ -24,6 +24,7 @@ ERR_LAUNCH = -4
 ERR_TIMEOUT = -5
 ERR_WORKSPACE = -6
 ERR_CUDA = -7
+AMAX_WORDS = 32  # CDLB200_AMAX_WORDS
 
 SCALE_LINEAR = 0
 SCALE_SWIZZLED = 1
@@ -79,8 +80,8 @@ class AdamwTensor(ctypes.Structure):
 class Nvfp4EncodeTensor(ctypes.Structure):
     """``cdlb200_nvfp4_encode_tensor`` (include/cdlb200_step.h)."""
 
-    _fields_ = [("x", _P), ("rows", _I64), ("k", _I64), ("amax", _P), ("packed", _P), ("scale", _P),
-                ("alpha", _P), ("deq", _P)]
+    _fields_ = [("x", _P), ("rows", _I64), ("k", _I64), ("amax", _P), ("amax_words", ctypes.c_int32),
+                ("pad", ctypes.c_int32), ("packed", _P), ("scale", _P), ("alpha", _P), ("deq", _P)]
 
 
 class CdlB200Error(RuntimeError):

@@ -9,6 +9,7 @@
 // and their backward passes (the gradients autograd forms for those modules,
 // with fp32 intermediates).  All tensors are bf16, row-major, 16-byte aligned
 // rows; each thread moves 8 values (16 bytes) at a time.
+#include "cdlb200_step.h"
 #include "common.cuh"
 
 namespace cdlb200 {
@@ -56,7 +57,7 @@ __device__ __forceinline__ void cta_amax(uint32_t m2, uint32_t* amax) {
     __syncthreads();
     if (threadIdx.x == 0) {
         for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m = max(m, red[w]);
-        atomicMax(amax, m);
+        atomicMax(amax + (blockIdx.x % CDLB200_AMAX_WORDS), m);  // spread: same-address atomics serialize
     }
 }
 

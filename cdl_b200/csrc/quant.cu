@@ -778,7 +778,8 @@ __global__ void __launch_bounds__(kEncThreads) nvfp4_encode_multi_kernel(const _
         const int64_t nblk = T.rows * (int64_t)nb.d;
         const int64_t c4 = (nb.d + 3) / 4;
         // the tensor's global scale, as the fused quantizer derives it from its amax
-        const uint32_t gm = *T.amax;
+        uint32_t gm = 0;
+        for (int i = 0; i < (T.amax_words > 1 ? T.amax_words : 1); ++i) gm = max(gm, __ldcg(T.amax + i));
         Nvfp4Tensor tn;
         tn.gmax = gm > 0x7f80u ? u2f(0x7fc00000u) : fmaxf(u2f(gm << 16), 1.1754943508222875e-38f);
         tn.alpha = __fdiv_rn(tn.gmax, 2688.0f);
@@ -1215,7 +1216,8 @@ extern "C" int cdlb200_nvfp4_encode_multi(const cdlb200_nvfp4_encode_tensor* ten
         const cdlb200_nvfp4_encode_tensor& t = tensors[i];
         if (t.rows < 0 || t.k < 0 || (t.k % 16) != 0) return CDLB200_ERR_INVALID_ARG;
         if (t.rows == 0 || t.k == 0) continue;
-        if (!t.x || !t.amax || !t.packed || !t.scale || !t.alpha) return CDLB200_ERR_INVALID_ARG;
+        if (!t.x || !t.amax || !t.packed || !t.scale || !t.alpha || t.amax_words < 0 || t.amax_words > 64)
+            return CDLB200_ERR_INVALID_ARG;
         if ((t.rows % 128) != 0 || ((t.k / 16) % 4) != 0 || t.rows * (t.k / 16) >= (1ll << 31))
             return CDLB200_ERR_INVALID_ARG;
         if (!aligned(t.x, 16) || !aligned(t.packed, 8) || (t.deq && !aligned(t.deq, 16))) return CDLB200_ERR_ALIGNMENT;

@@ -40,7 +40,7 @@ class RMSNormFn(torch.autograd.Function):
         x2 = x.reshape(-1, d).contiguous()
         y = torch.empty_like(x2)
         rstd = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device)
-        amax = torch.zeros(1, dtype=torch.int32, device=x.device)
+        amax = torch.zeros(_lib.AMAX_WORDS, dtype=torch.int32, device=x.device)
         _lib.call("cdlb200_rmsnorm_fwd", _lib.ptr(x2), _lib.ptr(w), x2.shape[0], d, float(eps), _lib.ptr(y),
                   _lib.ptr(rstd), _lib.ptr(amax), _lib.stream(x.device))
         attach_amax(y, amax)
@@ -96,7 +96,7 @@ class SwiGLUFn(torch.autograd.Function):
     def forward(ctx, g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
         g, u = g.contiguous(), u.contiguous()
         h = torch.empty_like(g)
-        amax = torch.zeros(1, dtype=torch.int32, device=g.device)
+        amax = torch.zeros(_lib.AMAX_WORDS, dtype=torch.int32, device=g.device)
         _lib.call("cdlb200_swiglu_fwd", _lib.ptr(g), _lib.ptr(u), g.numel(), _lib.ptr(h), _lib.ptr(amax),
                   _lib.stream(g.device))
         attach_amax(h, amax)

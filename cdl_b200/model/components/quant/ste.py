@@ -51,8 +51,8 @@ def _encode_with_amax(theta: torch.Tensor, amax: torch.Tensor):
     scale = torch.empty(rows, k // 16, dtype=torch.uint8, device=dev)
     alpha = torch.empty(1, dtype=torch.float32, device=dev)
     deq = torch.empty(rows, k, dtype=torch.bfloat16, device=dev)
-    t = _lib.Nvfp4EncodeTensor(theta.data_ptr(), rows, k, amax.data_ptr(), packed.data_ptr(), scale.data_ptr(),
-                               alpha.data_ptr(), deq.data_ptr())
+    t = _lib.Nvfp4EncodeTensor(theta.data_ptr(), rows, k, amax.data_ptr(), amax.numel(), 0, packed.data_ptr(),
+                               scale.data_ptr(), alpha.data_ptr(), deq.data_ptr())
     _lib.call("cdlb200_nvfp4_encode_multi", ctypes.addressof(t), 1, _lib.stream(dev))
     return (packed, scale, alpha), deq
 

@@ -129,7 +129,7 @@ class WeightEncoder:
             deq = torch.empty(rows, k, dtype=torch.bfloat16, device=dev)
             amax_ptr = self.amax.data_ptr() + 4 * j
             t = self.table[j]
-            t.x, t.rows, t.k, t.amax = w.data_ptr(), rows, k, amax_ptr
+            t.x, t.rows, t.k, t.amax, t.amax_words = w.data_ptr(), rows, k, amax_ptr, 1
             t.packed, t.scale, t.alpha, t.deq = packed.data_ptr(), scale.data_ptr(), alpha.data_ptr(), deq.data_ptr()
             opt._table[index[id(w)]].amax = amax_ptr
             self.buffers.append((packed, scale, alpha, deq))

@@ -19,9 +19,12 @@ extern "C" {
 
 /* y = bf16(w * bf16(x * rsqrt(mean(x^2) + eps))) per row of x[rows, d]
  * (d % 8 == 0, d <= 2048); rstd[rows] (fp32) receives rsqrt(mean(x^2) + eps).
- * amax (optional, zero on entry) receives the bf16 magnitude bits of max|y|:
- * the global amax the NVFP4 quantize of y needs, formed in the epilogue so
- * that the quantize skips its own amax pass (cdlb200_nvfp4_encode_multi). */
+ * amax (optional): CDLB200_AMAX_WORDS words, zero on entry, whose maximum
+ * becomes the bf16 magnitude bits of max|y| -- the global amax the NVFP4
+ * quantize of y needs, formed in the epilogue so that the quantize skips its
+ * own amax pass (cdlb200_nvfp4_encode_multi).  The CTAs spread their atomics
+ * over the words. */
+#define CDLB200_AMAX_WORDS 32
 int cdlb200_rmsnorm_fwd(const void* x, const void* w, int64_t rows, int64_t d, float eps, void* y, float* rstd,
                         uint32_t* amax, void* stream);
 
@@ -41,7 +44,7 @@ int cdlb200_rope(const void* x, const void* cos, const void* sin, int64_t tokens
                  int64_t cos_tokens, int backward, void* out, void* stream);
 
 /* h = bf16(bf16(silu(g)) * u) over n values (n % 8 == 0); amax (optional,
- * zero on entry) receives the bf16 magnitude bits of max|h|. */
+ * CDLB200_AMAX_WORDS words, zero on entry) as for the RMSNorm above. */
 int cdlb200_swiglu_fwd(const void* g, const void* u, int64_t n, void* h, uint32_t* amax, void* stream);
 
 /* dg, du of the SwiGLU product above, given dh. */
@@ -97,7 +100,9 @@ int cdlb200_clip_adamw(const cdlb200_adamw_tensor* tensors, int count, double ma
 typedef struct {
     const void* x;         /* bf16 [rows, k], contiguous, 16-byte aligned */
     int64_t rows, k;       /* k % 16 == 0; rows % 128 == 0 and (k/16) % 4 == 0 (swizzled scales need no padding) */
-    const uint32_t* amax;  /* bf16 magnitude bits of max|x| (as cdlb200_clip_adamw writes them) */
+    const uint32_t* amax;  /* bf16 magnitude bits of max|x|: the maximum of amax_words words */
+    int32_t amax_words;    /* 1 (cdlb200_clip_adamw's word) or CDLB200_AMAX_WORDS (the RMSNorm / SwiGLU epilogues) */
+    int32_t pad;
     void* packed;          /* uint8 [rows, k/2]: e2m1 codes, element 2j in the low nibble */
     void* scale;           /* uint8 [rows, k/16] in the 128x4 GEMM layout */
     float* alpha;          /* fp32 [1]: gmax / 2688 */

@@ -141,7 +141,7 @@ def test_encode_multi_matches_per_tensor_quantize():
              torch.empty(1, device=dev), torch.empty(r, k, dtype=torch.bfloat16, device=dev))
         outs.append(o)
         t = tab[i]
-        t.x, t.rows, t.k, t.amax = x.data_ptr(), r, k, amax.data_ptr() + 4 * i
+        t.x, t.rows, t.k, t.amax, t.amax_words = x.data_ptr(), r, k, amax.data_ptr() + 4 * i, 1
         t.packed, t.scale, t.alpha, t.deq = (v.data_ptr() for v in o)
     _lib.call("cdlb200_nvfp4_encode_multi", ctypes.addressof(tab), len(xs), _lib.stream(dev))
     for x, (p, s, a, d) in zip(xs, outs):
