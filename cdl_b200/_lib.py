@@ -65,6 +65,10 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_ecdl_fwd": (_I, [_P, _I, _I64, _I64, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P]),
     "cdlb200_ecdl_bwd_workspace_bytes": (_I64, [_I64, _I64, _I]),
     "cdlb200_ecdl_bwd": (_I, [_P, _P, _I, _I64, _I64, _I, _P, _P, _P, _I, _P, _P, _P, _I64, _P]),
+    "cdlb200_ccdl_fwd": (_I, [_P, _I, _I64, _I64, _I, _P, _I64, _P, _P, _P, _P, _I, _I, _P, _P, _P]),
+    "cdlb200_ccdl_bwd_workspace_bytes": (_I64, [_I64, _I64, _I]),
+    "cdlb200_ccdl_bwd": (_I, [_P, _P, _I, _I64, _I64, _I, _P, _I64, _P, _I64, _P, _P, _P, _I, _I, _P, _P, _P, _P,
+                              _I64, _P]),
     "cdlb200_clip_adamw_workspace_bytes": (_I64, [_P, _I]),
     "cdlb200_clip_adamw": (_I, [_P, _I, _D, _D, _D, _D, _D, _D, _P, _I64, _P, _P]),
     "cdlb200_nvfp4_encode_multi": (_I, [_P, _I, _P]),
@@ -115,7 +119,8 @@ def lib() -> ctypes.CDLL:
 
 # kernels one call of an entry point launches (default 1); `launches` counts
 # them over the process, so a benchmark can report how many ran
-KERNELS_PER_CALL = {"cdlb200_rmsnorm_bwd": 2, "cdlb200_clip_adamw": 3, "cdlb200_ecdl_fwd": 2, "cdlb200_ecdl_bwd": 2}
+KERNELS_PER_CALL = {"cdlb200_rmsnorm_bwd": 2, "cdlb200_clip_adamw": 3, "cdlb200_ecdl_fwd": 2, "cdlb200_ecdl_bwd": 2,
+                    "cdlb200_ccdl_bwd": 2}
 launches = 0
 
 

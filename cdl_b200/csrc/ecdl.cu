@@ -41,6 +41,8 @@ __host__ __device__ inline EcdlFormat ecdl_format(int fmt) {
 
 // level of index `key` (ascending; -0 sits just below +0)
 __device__ float theta_level(int tn, int key) {
+    if (tn == 126) return e4m3_to_f32((uint32_t)(key + 1));                     // UE4M3 without zero
+    if (tn == 255) return u2f(key == 0 ? 0x00400000u : ((uint32_t)key << 23));  // E8M0, byte 0 = 2^-127
     if (tn == 16) {
         const int m = key >= 8 ? key - 8 : 7 - key;
         const float mag = m < 4 ? 0.5f * (float)m : (float)(1 << ((m >> 1) - 1)) * ((m & 1) ? 1.5f : 1.0f);
@@ -66,8 +68,20 @@ __device__ void build_tables(int tn, float* lev, float* gap) {
 // fp32 -> e4m3 byte, round to nearest even, saturating (sign kept)
 __device__ __forceinline__ uint32_t ue4m3_cvt(float v) { return cvt_e4m3x2(0.0f, v) & 0xffu; }
 
-// nearest-level ordinal (cdl/core/kernel/formats/ordinals.py)
+// nearest-level ordinal (cdl/core/kernel/formats/ordinals.py) of a theta grid
+// (16: e2m1, 254: e4m3) or a scale grid (126: UE4M3 without zero, 255: E8M0)
 __device__ __forceinline__ int theta_ordinal(int tn, float v) {
+    if (tn == 126) {
+        const int b = (int)ue4m3_cvt(fminf(fmaxf(v, 0.001953125f), 448.0f)) - 1;
+        return b < 0 ? 0 : (b > 125 ? 125 : b);
+    }
+    if (tn == 255) {
+        const uint32_t bits = f2u(fminf(fmaxf(v, 0x1p-127f), 0x1p127f));
+        const int e8 = (int)(bits >> 23), mant = (int)(bits & 0x7fffff);
+        if (e8 == 0) return mant > 4194304 ? 1 : 0;
+        const int k = e8 + (mant >= 4194304);
+        return k < 254 ? k : 254;
+    }
     if (tn == 16) {
         const bool neg = (f2u(v) >> 31) != 0;
         const float av = fminf(fabsf(v), 6.0f);
@@ -184,9 +198,87 @@ __device__ __forceinline__ int sample_dispatch(float v, float kappa, float u, co
     else return cdl_sample(v, kappa, u, lev, gap, tn, topk);
 }
 
+// half-width of the truncated (scale-side) window: most of the weight of a
+// sharp window lies within sqrt(60 / kappa) levels of the nearest one
+__device__ __forceinline__ int half_window(int topk, float kappa) {
+    int hq = topk / 2;
+    if (kappa > 0.05f) hq = (int)fminf((float)(topk / 2), sqrtf(__fdiv_rn(60.0f, kappa))) + 1;
+    return hq;
+}
+
+// cdl_sample_truncated (primitives.py:73-135): the window [t_lo, t_lo + 2 hq]
+// around the nearest level, the left tail folded into one jump
+__device__ __forceinline__ int cdl_sample_truncated(float v, float kappa, float u, const float* lev,
+                                                    const float* gap, int tn, int topk) {
+    const Window w = cdl_window(v, lev, gap, tn, topk);
+    const float t_near = fminf(fmaxf(floorf(__fadd_rn(w.c, 0.5f)), (float)w.start), (float)(w.start + topk - 1));
+    const float dn = __fsub_rn(t_near, w.c);
+    const float m = __fmul_rn(__fmul_rn(-kappa, dn), dn);
+    const int hq = half_window(topk, kappa);
+    const int tn_i = (int)t_near;
+    const int t_lo = tn_i - hq > w.start ? tn_i - hq : w.start;
+    const int last = w.start + topk - 1;
+    float z = 0.0f;
+    for (int j = 0; j <= 2 * hq; ++j) {
+        const int t = t_lo + j;
+        if (t >= w.start && t <= last) z = __fadd_rn(z, cdl_weight(w.c, (float)t, t_near, m, kappa));
+    }
+    const float dl = __fsub_rn((float)(t_lo - 1), w.c);
+    const float e_left =
+        exp2f(__fmul_rn(fminf(__fsub_rn(__fmul_rn(__fmul_rn(-kappa, dl), dl), m), 0.0f), kLog2e));
+    const float uz = __fmul_rn(u, z);
+    const int off = uz >= __fmul_rn(e_left, __fadd_rn((float)(t_lo - w.start), 1.0f)) ? t_lo - w.start : 0;
+    float acc = 0.0f;
+    int cnt = 0;
+    for (int j = 0; j <= 2 * hq; ++j) {
+        const int t = t_lo + j;
+        if (t >= w.start && t <= last) {
+            acc = __fadd_rn(acc, cdl_weight(w.c, (float)t, t_near, m, kappa));
+            cnt += acc <= uz;
+        }
+    }
+    const int sub = off + cnt;
+    return w.start + (sub < topk - 1 ? sub : topk - 1);
+}
+
 struct Coeffs {
     float dth, ds, dk;
 };
+
+// cdl_proxy_coeffs_truncated (primitives.py:190-240)
+__device__ __forceinline__ Coeffs cdl_proxy_coeffs_truncated(float v, float kappa, const float* lev,
+                                                             const float* gap, int tn, int topk) {
+    const Window w = cdl_window(v, lev, gap, tn, topk);
+    const float t_near = fminf(fmaxf(floorf(__fadd_rn(w.c, 0.5f)), (float)w.start), (float)(w.start + topk - 1));
+    const float dn = __fsub_rn(t_near, w.c);
+    const float m = __fmul_rn(__fmul_rn(-kappa, dn), dn);
+    const int hq = half_window(topk, kappa);
+    const int tn_i = (int)t_near;
+    const int t_lo = tn_i - hq > w.start ? tn_i - hq : w.start;
+    const int last = w.start + topk - 1;
+    float z = 0.f, sl = 0.f, sa = 0.f, sal = 0.f, sb = 0.f, sbl = 0.f;
+    for (int j = 0; j <= 2 * hq; ++j) {
+        const int t = t_lo + j;
+        if (t < w.start || t > last) continue;
+        const float d = __fsub_rn(w.c, (float)t);
+        const float e = cdl_weight(w.c, (float)t, t_near, m, kappa);
+        const float lv = lev[t];
+        const float a = __fmul_rn(__fmul_rn(-2.0f, kappa), d);
+        const float dd = __fmul_rn(d, d);
+        z += e;
+        sl += e * lv;
+        sa += e * a;
+        sal += e * a * lv;
+        sb += e * dd;
+        sbl += e * dd * lv;
+    }
+    Coeffs r;
+    const float p = sl / z;
+    r.dth = (sal / z - p * (sa / z)) / w.kgap;
+    r.ds = p - v * r.dth;
+    r.dk = p * (sb / z) - sbl / z;
+    return r;
+}
 
 __device__ __forceinline__ Coeffs cdl_proxy_coeffs(float v, float kappa, const float* lev, const float* gap, int tn,
                                                    int topk) {
@@ -413,6 +505,152 @@ __global__ void ecdl_sum_kernel(const float* __restrict__ part, int n, float* __
     }
 }
 
+// ---------------------------------------------------------------------------
+// CCDL (cdl/core/kernel/ccdl/kernel.py): the block scale is a learnable
+// value q (one per block, or one row of q shared by every theta row when
+// q_stride is 0), sampled on the scale grid with the truncated window and
+// its own kappa from tl.rand(seed, rows * K + r * q_stride + b); then theta
+// is sampled as in ECDL with s = q_level * alpha.
+// ---------------------------------------------------------------------------
+struct CcdlArgs {
+    int64_t npairs, k, rows;
+    int fmt, topk, q_topk;
+    const float* q;
+    int64_t q_stride;
+    const float* kappa_t;
+    const float* kappa_q;
+    const float* alpha;
+};
+
+__device__ __forceinline__ int q_grid(int fmt) { return fmt == CDLB200_ECDL_NVFP4 ? 126 : 255; }
+
+template <typename T>
+__global__ void __launch_bounds__(kEcdlThreads) ccdl_fwd_kernel(const T* __restrict__ theta, CcdlArgs a,
+                                                                const int64_t* __restrict__ seed_p,
+                                                                uint8_t* __restrict__ packed,
+                                                                uint8_t* __restrict__ scale) {
+    __shared__ float lev[256], gap[256], qlev[256], qgap[256];
+    const EcdlFormat f = ecdl_format(a.fmt);
+    const int qn = q_grid(a.fmt);
+    build_tables(f.tn, lev, gap);
+    build_tables(qn, qlev, qgap);
+    const float kt = *a.kappa_t, kq = *a.kappa_q, alpha = *a.alpha;
+    const int32_t seed = (int32_t)(uint32_t)(*seed_p & 0xffffffffll);
+    const int lanes = f.tpb / 2;
+    const int lane = threadIdx.x & 31, leader = lane & ~(lanes - 1);
+    const int64_t nb = a.k / f.tpb;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t p0 = (int64_t)blockIdx.x * blockDim.x; p0 < a.npairs; p0 += stride) {
+        const int64_t p = p0 + threadIdx.x;
+        const bool ok = p < a.npairs;
+        int qi = 0;
+        if (ok && lane == leader) {  // the block's scale, sampled once
+            const int64_t e = 2 * p, r = e / a.k, b = (e - r * a.k) / f.tpb;
+            const float qv = a.q[r * a.q_stride + b];
+            const float uq = rand_uniform((uint32_t)(a.rows * a.k + r * a.q_stride + b), seed);
+            qi = cdl_sample_truncated(qv, kq, uq, qlev, qgap, qn, a.q_topk);
+            scale[r * nb + b] = (uint8_t)(qi + f.bias);
+        }
+        qi = __shfl_sync(0xffffffffu, qi, leader);
+        if (!ok) continue;
+        const float s = __fmul_rn(qlev[qi], alpha);
+        float x0, x1;
+        load2(theta, 2 * p, x0, x1);
+        const float u0 = rand_uniform((uint32_t)(2 * p), seed), u1 = rand_uniform((uint32_t)(2 * p + 1), seed);
+        const int i0 = cdl_sample(__fdiv_rn(x0, s), kt, u0, lev, gap, f.tn, a.topk);
+        const int i1 = cdl_sample(__fdiv_rn(x1, s), kt, u1, lev, gap, f.tn, a.topk);
+        if (f.tn == 16) {
+            const uint32_t c0 = i0 < 8 ? 15 - i0 : i0 - 8, c1 = i1 < 8 ? 15 - i1 : i1 - 8;
+            packed[p] = (uint8_t)(c0 | (c1 << 4));
+        } else {
+            const uint32_t b0 = i0 < 127 ? 254 - i0 : i0 - 127, b1 = i1 < 127 ? 254 - i1 : i1 - 127;
+            reinterpret_cast<uint16_t*>(packed)[p] = (uint16_t)(b0 | (b1 << 8));
+        }
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kEcdlThreads) ccdl_bwd_kernel(const T* __restrict__ grad, const T* __restrict__ theta,
+                                                                CcdlArgs a, const uint8_t* __restrict__ scale,
+                                                                int64_t scale_stride, T* __restrict__ dtheta,
+                                                                float* __restrict__ dq, float* __restrict__ part) {
+    __shared__ float lev[256], gap[256], qlev[256], qgap[256];
+    __shared__ float red[3][kEcdlThreads / 32];
+    const EcdlFormat f = ecdl_format(a.fmt);
+    const int qn = q_grid(a.fmt);
+    build_tables(f.tn, lev, gap);
+    build_tables(qn, qlev, qgap);
+    const float kt = *a.kappa_t, kq = *a.kappa_q, alpha = *a.alpha;
+    const int lanes = f.tpb / 2;
+    const int lane = threadIdx.x & 31, leader = lane & ~(lanes - 1);
+    const int64_t nb = a.k / f.tpb;
+    float dkt = 0.f, dkq = 0.f, dal = 0.f;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t p0 = (int64_t)blockIdx.x * blockDim.x; p0 < a.npairs; p0 += stride) {
+        const int64_t p = p0 + threadIdx.x;
+        const bool ok = p < a.npairs;
+        const int64_t e = 2 * p, r = e / a.k, b = (e - r * a.k) / f.tpb;
+        float ds_sum = 0.f;
+        if (ok) {
+            int qi = (int)scale[r * scale_stride + b] - f.bias;
+            qi = qi < 0 ? 0 : qi;
+            const float q_hat = qlev[qi];
+            const float s = __fmul_rn(q_hat, alpha);
+            float g0, g1, x0, x1;
+            load2(grad, 2 * p, g0, g1);
+            load2(theta, 2 * p, x0, x1);
+            const float v0 = __fdiv_rn(x0, s), v1 = __fdiv_rn(x1, s);
+            const Coeffs c0 = cdl_proxy_coeffs(v0, kt, lev, gap, f.tn, a.topk);
+            const Coeffs c1 = cdl_proxy_coeffs(v1, kt, lev, gap, f.tn, a.topk);
+            store2(dtheta, 2 * p, g0 * c0.dth, g1 * c1.dth);
+            dkt += g0 * s * c0.dk + g1 * s * c1.dk;
+            const float ds0 = g0 * c0.ds, ds1 = g1 * c1.ds;
+            dal += (ds0 + ds1) * q_hat;
+            ds_sum = ds0 + ds1;
+        }
+        // the block's d s, then its q gradient (one lane per block)
+        for (int o = lanes >> 1; o > 0; o >>= 1) ds_sum += __shfl_xor_sync(0xffffffffu, ds_sum, o);
+        if (ok && lane == leader) {
+            const float gq = alpha * ds_sum;
+            const Coeffs cq = cdl_proxy_coeffs_truncated(a.q[r * a.q_stride + b], kq, qlev, qgap, qn, a.q_topk);
+            if (dq) dq[r * nb + b] = gq * cq.dth;
+            dkq += gq * cq.dk;
+        }
+    }
+    if (!part) return;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        dkt += __shfl_xor_sync(0xffffffffu, dkt, o);
+        dkq += __shfl_xor_sync(0xffffffffu, dkq, o);
+        dal += __shfl_xor_sync(0xffffffffu, dal, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+        red[0][threadIdx.x >> 5] = dkt;
+        red[1][threadIdx.x >> 5] = dkq;
+        red[2][threadIdx.x >> 5] = dal;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float x = 0.f, y = 0.f, z = 0.f;
+        for (int w = 0; w < kEcdlThreads / 32; ++w) {
+            x += red[0][w];
+            y += red[1][w];
+            z += red[2][w];
+        }
+        part[3 * blockIdx.x] = x;
+        part[3 * blockIdx.x + 1] = y;
+        part[3 * blockIdx.x + 2] = z;
+    }
+}
+
+// fixed-order sum of n partial triples -> scalars[3]
+__global__ void ccdl_sum_kernel(const float* __restrict__ part, int n, float* __restrict__ scalars) {
+    if (threadIdx.x >= 3) return;
+    float acc = 0.f;
+    for (int i = 0; i < n; ++i) acc += part[3 * i + threadIdx.x];
+    scalars[threadIdx.x] = acc;
+}
+
 template <int K>
 void launch_fwd(const void* theta, int theta_f32, int64_t npairs, int format, int scale_mode, int topk,
                 const float* kappa, const int64_t* seed, const uint32_t* gbits, void* packed, void* scale,
@@ -523,6 +761,97 @@ extern "C" int cdlb200_ecdl_bwd(const void* grad, const void* theta, int theta_f
     CDLB200_CHECK_LAUNCH();
     if (scalars) {
         ecdl_sum_kernel<<<1, 256, 0, st>>>(part, grid, scalars);
+        CDLB200_CHECK_LAUNCH();
+    }
+    return CDLB200_OK;
+}
+
+extern "C" int cdlb200_ccdl_fwd(const void* theta, int theta_f32, int64_t rows, int64_t nb, int format, const float* q,
+                                int64_t q_stride, const float* kappa_t, const float* kappa_q, const float* alpha,
+                                const int64_t* seed, int theta_topk, int q_topk, void* packed, void* scale,
+                                void* stream) {
+    int rc = ecdl_check(rows, nb, format, theta_topk);
+    if (rc != CDLB200_OK) return rc;
+    if (q_topk < 1 || q_topk > (format == CDLB200_ECDL_NVFP4 ? 126 : 255)) return CDLB200_ERR_INVALID_ARG;
+    if (q_stride != 0 && q_stride != nb) return CDLB200_ERR_INVALID_ARG;
+    if (rows == 0 || nb == 0) return CDLB200_OK;
+    if (!theta || !q || !kappa_t || !kappa_q || !alpha || !seed || !packed || !scale) return CDLB200_ERR_INVALID_ARG;
+    if (!ecdl_aligned(theta, theta_f32 ? 8 : 4) || !ecdl_aligned(packed, 2)) return CDLB200_ERR_ALIGNMENT;
+    const EcdlFormat f = ecdl_format(format);
+    CcdlArgs a;
+    a.npairs = rows * nb * f.tpb / 2;
+    a.k = nb * f.tpb;
+    a.rows = rows;
+    a.fmt = format;
+    a.topk = theta_topk;
+    a.q_topk = q_topk;
+    a.q = q;
+    a.q_stride = q_stride;
+    a.kappa_t = kappa_t;
+    a.kappa_q = kappa_q;
+    a.alpha = alpha;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int grid = ecdl_grid(a.npairs);
+    if (theta_f32)
+        ccdl_fwd_kernel<float><<<grid, kEcdlThreads, 0, st>>>(static_cast<const float*>(theta), a, seed,
+                                                              static_cast<uint8_t*>(packed),
+                                                              static_cast<uint8_t*>(scale));
+    else
+        ccdl_fwd_kernel<uint16_t><<<grid, kEcdlThreads, 0, st>>>(static_cast<const uint16_t*>(theta), a, seed,
+                                                                 static_cast<uint8_t*>(packed),
+                                                                 static_cast<uint8_t*>(scale));
+    CDLB200_CHECK_LAUNCH();
+    return CDLB200_OK;
+}
+
+extern "C" int64_t cdlb200_ccdl_bwd_workspace_bytes(int64_t rows, int64_t nb, int format) {
+    if (ecdl_check(rows, nb, format, 1) != CDLB200_OK || rows == 0 || nb == 0) return 0;
+    const EcdlFormat f = ecdl_format(format);
+    return (int64_t)ecdl_grid(rows * nb * f.tpb / 2) * 3 * (int64_t)sizeof(float);
+}
+
+extern "C" int cdlb200_ccdl_bwd(const void* grad, const void* theta, int theta_f32, int64_t rows, int64_t nb,
+                                int format, const float* q, int64_t q_stride, const void* scale,
+                                int64_t scale_stride, const float* kappa_t, const float* kappa_q, const float* alpha,
+                                int theta_topk, int q_topk, void* dtheta, float* dq, float* scalars,
+                                void* workspace, int64_t workspace_bytes, void* stream) {
+    int rc = ecdl_check(rows, nb, format, theta_topk);
+    if (rc != CDLB200_OK) return rc;
+    if (q_topk < 1 || q_topk > (format == CDLB200_ECDL_NVFP4 ? 126 : 255)) return CDLB200_ERR_INVALID_ARG;
+    if ((q_stride != 0 && q_stride != nb) || (scale_stride != 0 && scale_stride != nb)) return CDLB200_ERR_INVALID_ARG;
+    if (rows == 0 || nb == 0) return CDLB200_OK;
+    if (!grad || !theta || !q || !scale || !kappa_t || !kappa_q || !alpha || !dtheta) return CDLB200_ERR_INVALID_ARG;
+    const int al = theta_f32 ? 8 : 4;
+    if (!ecdl_aligned(grad, al) || !ecdl_aligned(theta, al) || !ecdl_aligned(dtheta, al)) return CDLB200_ERR_ALIGNMENT;
+    if (scalars && (!workspace || workspace_bytes < cdlb200_ccdl_bwd_workspace_bytes(rows, nb, format)))
+        return CDLB200_ERR_WORKSPACE;
+    const EcdlFormat f = ecdl_format(format);
+    CcdlArgs a;
+    a.npairs = rows * nb * f.tpb / 2;
+    a.k = nb * f.tpb;
+    a.rows = rows;
+    a.fmt = format;
+    a.topk = theta_topk;
+    a.q_topk = q_topk;
+    a.q = q;
+    a.q_stride = q_stride;
+    a.kappa_t = kappa_t;
+    a.kappa_q = kappa_q;
+    a.alpha = alpha;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int grid = ecdl_grid(a.npairs);
+    float* part = scalars ? static_cast<float*>(workspace) : nullptr;
+    if (theta_f32)
+        ccdl_bwd_kernel<float><<<grid, kEcdlThreads, 0, st>>>(
+            static_cast<const float*>(grad), static_cast<const float*>(theta), a, static_cast<const uint8_t*>(scale),
+            scale_stride, static_cast<float*>(dtheta), dq, part);
+    else
+        ccdl_bwd_kernel<uint16_t><<<grid, kEcdlThreads, 0, st>>>(
+            static_cast<const uint16_t*>(grad), static_cast<const uint16_t*>(theta), a,
+            static_cast<const uint8_t*>(scale), scale_stride, static_cast<uint16_t*>(dtheta), dq, part);
+    CDLB200_CHECK_LAUNCH();
+    if (scalars) {
+        ccdl_sum_kernel<<<1, 32, 0, st>>>(part, grid, scalars);
         CDLB200_CHECK_LAUNCH();
     }
     return CDLB200_OK;

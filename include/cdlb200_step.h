@@ -145,6 +145,25 @@ int cdlb200_ecdl_bwd(const void* grad, const void* theta, int theta_f32, int64_t
                      const void* scale, const float* kappa, const float* alpha, int topk, void* dtheta,
                      float* scalars, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* CCDL stochastic quantizer (cdl/core/kernel/ccdl: launch.py launch_ccdl_fwd /
+ * launch_ccdl_bwd, kernel.py _ccdl_fwd / _ccdl_bwd).  As ECDL, except that
+ * each block's scale is a learnable value q (fp32 [rows, nb], or one shared
+ * row when q_stride is 0) sampled on the scale grid (UE4M3 without zero for
+ * NVFP4, E8M0 for MX) with the truncated window of q_topk levels and kappa_q,
+ * from tl.rand(seed, rows * nb * block + r * q_stride + b); s = q_level *
+ * alpha (alpha a learnable fp32 scalar).  scale: [rows, nb] bytes.
+ * Backward: dtheta; dq[rows, nb] (per theta row; optional) = alpha *
+ * sum_block(g * ds) * dE[q level]/dq; scalars (optional) = {d kappa_t,
+ * d kappa_q, d alpha}.  scale_stride 0 reads one shared scale row. */
+int cdlb200_ccdl_fwd(const void* theta, int theta_f32, int64_t rows, int64_t nb, int format, const float* q,
+                     int64_t q_stride, const float* kappa_t, const float* kappa_q, const float* alpha,
+                     const int64_t* seed, int theta_topk, int q_topk, void* packed, void* scale, void* stream);
+int64_t cdlb200_ccdl_bwd_workspace_bytes(int64_t rows, int64_t nb, int format);
+int cdlb200_ccdl_bwd(const void* grad, const void* theta, int theta_f32, int64_t rows, int64_t nb, int format,
+                     const float* q, int64_t q_stride, const void* scale, int64_t scale_stride, const float* kappa_t,
+                     const float* kappa_q, const float* alpha, int theta_topk, int q_topk, void* dtheta, float* dq,
+                     float* scalars, void* workspace, int64_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -289,3 +289,140 @@ def backward(fmt: int, g: np.ndarray, theta: np.ndarray, scale_bytes: np.ndarray
     dkt = float(np.sum(g.astype(np.float64) * s[..., None] * dk))
     dal = float(np.sum(g.astype(np.float64) * ds_c * q_hat[..., None]))
     return dtheta.astype(np.float32), (dkt, dal)
+
+
+# ---------------------------------------------------------------------------
+# CCDL (cdl/core/kernel/ccdl/kernel.py, primitives.py:73-135 and 190-240):
+# the block scale is itself a learnable value q, sampled on the scale levels
+# with the truncated window; theta as in ECDL
+# ---------------------------------------------------------------------------
+class QFormat:
+    """The scale format's levels as a sampling grid (UE4M3 without zero for
+    NVFP4, E8M0 for MX)."""
+
+    def __init__(self, fmt: int):
+        self.fmt = fmt
+        self.level = q_levels(fmt)
+        self.gap = gaps(self.level)
+        self.tn = self.level.size
+        self.bias = 1 if fmt == NVFP4 else 0
+
+    def ordinal(self, v):
+        if self.fmt == NVFP4:
+            b = e4m3_rne(np.clip(v, np.float32(2.0 ** -9), np.float32(448.0)))
+            return np.clip(b - 1, 0, self.tn - 1)
+        v = np.clip(np.asarray(v, np.float32), np.float32(2.0 ** -127), np.float32(2.0 ** 127)).astype(np.float32)
+        bits = v.view(np.uint32).astype(np.int64)
+        e8, mant = bits >> 23, bits & 0x7FFFFF
+        return np.where(e8 == 0, (mant > 4194304).astype(np.int64), np.minimum(e8 + (mant >= 4194304), self.tn - 1))
+
+
+def _half_window(topk, kappa):
+    hq = topk // 2
+    if kappa > 0.05:
+        hq = int(min(float(topk // 2), float(np.sqrt(np.float32(60.0) / np.float32(kappa))))) + 1
+    return hq
+
+
+def sample_truncated(f, v, kappa, u, topk):
+    kappa = np.float32(kappa)
+    c, start, _ = _window(f, v, topk)
+    t_near, m = _near(c, start, topk, kappa)
+    hq = _half_window(topk, kappa)
+    t_lo = np.maximum(start, t_near - hq)
+    z = np.zeros_like(c)
+    for j in range(2 * hq + 1):
+        t = t_lo + j
+        inw = (t >= start) & (t <= start + topk - 1)
+        w, _ = _weight(c, t.astype(np.float32), t_near, m, kappa)
+        z = (z + np.where(inw, w, np.float32(0.0))).astype(np.float32)
+    d_left = ((t_lo - 1).astype(np.float32) - c).astype(np.float32)
+    e_left = np.exp2((np.minimum((-kappa * d_left * d_left - m).astype(np.float32), np.float32(0.0))
+                      * LOG2E).astype(np.float32)).astype(np.float32)
+    uz = (u * z).astype(np.float32)
+    off = np.where(uz >= (e_left * ((t_lo - start).astype(np.float32) + np.float32(1.0))).astype(np.float32),
+                   t_lo - start, 0)
+    acc = np.zeros_like(c)
+    cnt = np.zeros(c.shape, dtype=np.int64)
+    for j in range(2 * hq + 1):
+        t = t_lo + j
+        inw = (t >= start) & (t <= start + topk - 1)
+        w, _ = _weight(c, t.astype(np.float32), t_near, m, kappa)
+        acc = (acc + np.where(inw, w, np.float32(0.0))).astype(np.float32)
+        cnt += (acc <= uz) & inw
+    return start + np.minimum(off + cnt, topk - 1)
+
+
+def proxy_coeffs_truncated(f, v, kappa, topk):
+    kappa = np.float32(kappa)
+    c, start, kgap = _window(f, v, topk)
+    t_near, m = _near(c, start, topk, kappa)
+    hq = _half_window(topk, kappa)
+    t_lo = np.maximum(start, t_near - hq)
+    z = sl = sa = sal = sb = sbl = np.zeros_like(c)
+    for j in range(2 * hq + 1):
+        t = t_lo + j
+        inw = (t >= start) & (t <= start + topk - 1)
+        e, d = _weight(c, t.astype(np.float32), t_near, m, kappa)
+        lv = f.level[np.minimum(t, start + topk - 1)]
+        a = np.float32(-2.0) * kappa * d
+        w = np.where(inw, e, np.float32(0.0))
+        z = z + w
+        sl = sl + w * lv
+        sa = sa + w * a
+        sal = sal + w * a * lv
+        sb = sb + w * d * d
+        sbl = sbl + w * d * d * lv
+    p_lt = sl / z
+    dth = (sal / z - p_lt * (sa / z)) / kgap
+    ds = p_lt - v * dth
+    dk = p_lt * (sb / z) - sbl / z
+    return dth.astype(np.float32), ds.astype(np.float32), dk.astype(np.float32)
+
+
+def ccdl_forward(fmt: int, theta: np.ndarray, q: np.ndarray, kappa_t: float, kappa_q: float, alpha: float,
+                 seed: int, topk: int, q_topk: int):
+    """theta [m, nb, tpb], q [m, nb] or [1, nb] (shared).  Returns (packed
+    codes, scale bytes [m, nb] (or [1, nb] when q is shared))."""
+    f, fq = Format(fmt), QFormat(fmt)
+    m_, nb, tpb = theta.shape
+    k = nb * tpb
+    qs = 0 if q.shape[0] == 1 and m_ > 1 else nb
+    qq = np.broadcast_to(q.astype(np.float32), (m_, nb))
+    uq_off = (m_ * k + np.arange(m_)[:, None] * qs + np.arange(nb)[None, :]).astype(np.uint64)
+    uq = uniform(seed, uq_off)
+    qi = sample_truncated(fq, qq, kappa_q, uq, q_topk)
+    s = (fq.level[qi] * np.float32(alpha)).astype(np.float32)
+    v = (theta.astype(np.float32) / s[..., None]).astype(np.float32)
+    offs = (np.arange(m_)[:, None, None] * k + np.arange(nb)[None, :, None] * tpb
+            + np.arange(tpb)[None, None, :]).astype(np.uint64)
+    idx = sample(f, v, kappa_t, uniform(seed, offs), topk)
+    if f.tn == 16:
+        code = np.where(idx < 8, 15 - idx, idx - 8).astype(np.uint8)
+        packed = (code[..., 0::2] | (code[..., 1::2] << 4)).astype(np.uint8).reshape(m_, nb * tpb // 2)
+    else:
+        packed = np.where(idx < 127, 254 - idx, idx - 127).astype(np.uint8).reshape(m_, nb * tpb)
+    scale = (qi + fq.bias).astype(np.uint8)
+    return packed, (scale[:1] if qs == 0 else scale)
+
+
+def ccdl_backward(fmt: int, g, theta, q, scale_bytes, kappa_t, kappa_q, alpha, topk, q_topk):
+    """(dtheta [m, nb, tpb], dq [m, nb] per theta row, (d kappa_t, d kappa_q, d alpha))."""
+    f, fq = Format(fmt), QFormat(fmt)
+    m_, nb, tpb = theta.shape
+    sb = np.broadcast_to(scale_bytes, (m_, nb))
+    qi = np.maximum(sb.astype(np.int64) - fq.bias, 0)
+    q_hat = fq.level[qi]
+    s = (q_hat * np.float32(alpha)).astype(np.float32)
+    v = (theta.astype(np.float32) / s[..., None]).astype(np.float32)
+    dth, ds_c, dk = proxy_coeffs(f, v, kappa_t, topk)
+    g = g.astype(np.float32)
+    ds = g * ds_c
+    dkt = float(np.sum(g.astype(np.float64) * s[..., None] * dk))
+    dal = float(np.sum(ds.astype(np.float64) * q_hat[..., None]))
+    qq = np.broadcast_to(q.astype(np.float32), (m_, nb))
+    dq_c, _, dkq_t = proxy_coeffs_truncated(fq, qq, kappa_q, q_topk)
+    gq = (np.float32(alpha) * ds.sum(-1)).astype(np.float32)
+    dq = (gq * dq_c).astype(np.float32)
+    dkq = float(np.sum(gq.astype(np.float64) * dkq_t))
+    return (g * dth).astype(np.float32), dq, (dkt, dkq, dal)

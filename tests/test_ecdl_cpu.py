@@ -82,3 +82,26 @@ def test_ecdl_workspace_bytes_on_host():
     assert lib.cdlb200_ecdl_bwd_workspace_bytes(0, 4, 0) == 0
     assert lib.cdlb200_ecdl_bwd_workspace_bytes(64, 4, 0) > 0
     assert lib.cdlb200_ecdl_bwd_workspace_bytes(64, 4, 7) == 0  # unknown format
+
+
+def test_ccdl_truncated_sampler_limits():
+    """The scale-side (truncated) sampler picks the nearest scale level for a
+    sharp window, on both scale grids."""
+    for fmt in (E.NVFP4, E.MXFP4):
+        fq = E.QFormat(fmt)
+        rng = np.random.RandomState(fmt)
+        v = np.exp(rng.uniform(-6, 5, 4000)).astype(np.float32)
+        u = rng.rand(4000).astype(np.float32)
+        idx = E.sample_truncated(fq, v, 1e6, u, 5)
+        c, start, _ = E._window(fq, v, 5)
+        near = np.clip(np.floor(c + np.float32(0.5)), start, start + 4).astype(np.int64)
+        assert np.array_equal(idx, near)
+
+
+def test_ccdl_oracle_shapes_and_shared_q():
+    th = np.random.RandomState(0).randn(4, 8, 16).astype(np.float32)
+    q = np.full((1, 8), 64.0, dtype=np.float32)
+    p, s = E.ccdl_forward(E.NVFP4, th, q, 3.0, 2.0, 0.01, 5, 5, 5)
+    assert p.shape == (4, 64) and s.shape == (1, 8)
+    dth, dq, sc = E.ccdl_backward(E.NVFP4, np.ones_like(th), th, q, s, 3.0, 2.0, 0.01, 5, 5)
+    assert dth.shape == th.shape and dq.shape == (4, 8) and len(sc) == 3 and np.all(np.isfinite(sc))
