@@ -426,3 +426,37 @@ def ccdl_backward(fmt: int, g, theta, q, scale_bytes, kappa_t, kappa_q, alpha, t
     dq = (gq * dq_c).astype(np.float32)
     dkq = float(np.sum(gq.astype(np.float64) * dkq_t))
     return (g * dth).astype(np.float32), dq, (dkt, dkq, dal)
+
+
+def _bf16(x: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 -> fp32, round to nearest even."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    r = (((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16).astype(np.uint32)
+    return r.view(np.float32)
+
+
+def ccdl_round(fmt: int, theta: np.ndarray, q: np.ndarray, alpha: float, theta_bf16: bool, levels_bf16: bool):
+    """CCDL eval forward, ``cascaded_nearest_round`` (cdl/core/ccdl.py:78-89):
+    ``q`` to its nearest scale level, ``s = level * alpha`` in the level dtype,
+    theta to the nearest level of ``theta / s`` in the promoted dtype of theta
+    and the levels (a bf16 tensor times or over a bf16 or 0-d fp32 tensor is
+    computed in fp32 and rounded once to bf16).  theta [m, nb, tpb] (values
+    already representable in its dtype), q [m, nb] or [1, nb].  Returns
+    (packed codes, scale bytes shaped like q)."""
+    f, fq = Format(fmt), QFormat(fmt)
+    m_, nb, tpb = theta.shape
+    qi = fq.ordinal(np.asarray(q, np.float32))
+    s = (fq.level[qi] * np.float32(alpha)).astype(np.float32)
+    if levels_bf16:
+        s = _bf16(s)
+    qb = np.broadcast_to(s, (m_, nb))
+    v = (theta.astype(np.float32) / qb[..., None]).astype(np.float32)
+    if levels_bf16 and theta_bf16:
+        v = _bf16(v)
+    idx = f.ordinal(v)
+    if f.tn == 16:
+        code = np.where(idx < 8, 15 - idx, idx - 8).astype(np.uint8)
+        packed = (code[..., 0::2] | (code[..., 1::2] << 4)).astype(np.uint8).reshape(m_, nb * tpb // 2)
+    else:
+        packed = np.where(idx < 127, 254 - idx, idx - 127).astype(np.uint8).reshape(m_, nb * tpb)
+    return packed, (qi + fq.bias).astype(np.uint8)

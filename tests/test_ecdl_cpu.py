@@ -105,3 +105,26 @@ def test_ccdl_oracle_shapes_and_shared_q():
     assert p.shape == (4, 64) and s.shape == (1, 8)
     dth, dq, sc = E.ccdl_backward(E.NVFP4, np.ones_like(th), th, q, s, 3.0, 2.0, 0.01, 5, 5)
     assert dth.shape == th.shape and dq.shape == (4, 8) and len(sc) == 3 and np.all(np.isfinite(sc))
+
+
+def _ccdl_round_cases():
+    import os
+
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "ccdl_round.npz"))
+    return [{k.split("_", 1)[1]: z[k] for k in z.files if k.startswith(f"c{i}_")} for i in range(int(z["count"]))]
+
+
+def test_ccdl_round_oracle_matches_reference_golden():
+    """The eval-mode round restated in the oracle reproduces the reference's
+    cascaded_nearest_round on every committed case (all formats, bf16 / fp32
+    theta and levels, per-row and shared scales)."""
+    cases = _ccdl_round_cases()
+    assert len(cases) == 24
+    for c in cases:
+        fmt = int(c["fmt"])
+        tpb = 16 if fmt == E.NVFP4 else 32
+        theta = c["theta"]
+        packed, scale = E.ccdl_round(fmt, theta.reshape(theta.shape[0], -1, tpb), c["q"], float(c["alpha"]),
+                                     bool(c["theta_bf16"]), bool(c["levels_bf16"]))
+        np.testing.assert_array_equal(packed, c["packed"])
+        np.testing.assert_array_equal(scale, c["scale"])
