@@ -66,6 +66,7 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_ecdl_bwd_workspace_bytes": (_I64, [_I64, _I64, _I]),
     "cdlb200_ecdl_bwd": (_I, [_P, _P, _I, _I64, _I64, _I, _P, _P, _P, _I, _P, _P, _P, _I64, _P]),
     "cdlb200_ccdl_fwd": (_I, [_P, _I, _I64, _I64, _I, _P, _I64, _P, _P, _P, _P, _I, _I, _P, _P, _P]),
+    "cdlb200_ccdl_round": (_I, [_P, _I, _I64, _I64, _I, _P, _I64, _P, _I, _P, _P, _P]),
     "cdlb200_ccdl_bwd_workspace_bytes": (_I64, [_I64, _I64, _I]),
     "cdlb200_ccdl_bwd": (_I, [_P, _P, _I, _I64, _I64, _I, _P, _I64, _P, _I64, _P, _P, _P, _I, _I, _P, _P, _P, _P,
                               _I64, _P]),

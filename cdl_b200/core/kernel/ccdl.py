@@ -137,6 +137,32 @@ class CcdlQuantFn(torch.autograd.Function):
                 None, None, None, None)
 
 
+@torch.no_grad()
+def ccdl_round(theta: torch.Tensor, q: torch.Tensor, alpha: torch.Tensor, format_id: int,
+               level_dtype: torch.dtype) -> tuple[torch.Tensor, torch.Tensor]:
+    """Deterministic CCDL quantize, cdl's ``cascaded_nearest_round``
+    (cdl/core/ccdl.py:78-89) with format levels of ``level_dtype`` (bf16 or
+    fp32), packed as the sampled forward packs: ``(packed [..., nb, cols],
+    scale bytes shaped like the sampled forward's)``."""
+    if level_dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError(f"ccdl_round: levels must be bf16 or fp32, got {level_dtype}")
+    dev = _lib.require_cuda(theta, q, alpha)
+    flat, lead, m, nb, tpb = _flat(theta, format_id)
+    lq, qs = _flatten_q(lead, nb, q)
+    fp4 = FormatId(format_id) != FormatId.MXFP8
+    cols = tpb // 2 if fp4 else tpb
+    packed = torch.empty((m, nb * cols), dtype=torch.uint8, device=dev)
+    scale = torch.empty((m, nb), dtype=torch.uint8, device=dev)
+    _lib.call("cdlb200_ccdl_round", _lib.ptr(flat), int(flat.dtype == torch.float32), m, nb, int(format_id),
+              _lib.ptr(lq), qs, _lib.ptr(_scalar(alpha)), int(level_dtype == torch.bfloat16), _lib.ptr(packed),
+              _lib.ptr(scale), _lib.stream(dev))
+    packed = packed.reshape(*lead, nb, cols)
+    if not fp4:
+        packed = packed.view(torch.float8_e4m3fn)
+    scale = scale[:1].reshape(q.shape) if qs == 0 else scale.reshape(*lead, nb, 1)
+    return packed, scale
+
+
 def ccdl_quant(theta, q, theta_kappa, q_kappa, alpha, seed, format_id, theta_topk, q_topk):
     return CcdlQuantFn.apply(theta, q, theta_kappa, q_kappa, alpha, seed, int(format_id), theta_topk, q_topk)
 

@@ -569,6 +569,53 @@ __global__ void __launch_bounds__(kEcdlThreads) ccdl_fwd_kernel(const T* __restr
     }
 }
 
+// fp32 -> bf16 -> fp32, round to nearest even
+__device__ __forceinline__ float bf16_round(float v) {
+    uint32_t h;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(0.0f), "f"(v));
+    return u2f(h << 16);
+}
+
+// CCDL eval forward (cdl/core/ccdl.py:78-89 cascaded_nearest_round): q's
+// nearest scale level, s = level * alpha in the level dtype, each element's
+// nearest theta level of theta / s in the promoted dtype of theta and levels.
+// lev_bf16: the levels are bf16, so s is rounded to bf16, and so is the
+// quotient when theta is bf16 as well (torch's bf16 arithmetic).
+template <typename T>
+__global__ void __launch_bounds__(kEcdlThreads) ccdl_round_kernel(const T* __restrict__ theta, CcdlArgs a,
+                                                                  int lev_bf16, uint8_t* __restrict__ packed,
+                                                                  uint8_t* __restrict__ scale) {
+    const EcdlFormat f = ecdl_format(a.fmt);
+    const int qn = q_grid(a.fmt);
+    const float alpha = *a.alpha;
+    const bool bf_quot = lev_bf16 && sizeof(T) == 2;
+    const int lanes = f.tpb / 2;
+    const int64_t nb = a.k / f.tpb;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < a.npairs; p += stride) {
+        const int64_t e = 2 * p, r = e / a.k, b = (e - r * a.k) / f.tpb;
+        const int qi = theta_ordinal(qn, a.q[r * a.q_stride + b]);
+        float s = __fmul_rn(theta_level(qn, qi), alpha);
+        if (lev_bf16) s = bf16_round(s);
+        float x0, x1;
+        load2(theta, e, x0, x1);
+        float v0 = __fdiv_rn(x0, s), v1 = __fdiv_rn(x1, s);
+        if (bf_quot) {
+            v0 = bf16_round(v0);
+            v1 = bf16_round(v1);
+        }
+        const int i0 = theta_ordinal(f.tn, v0), i1 = theta_ordinal(f.tn, v1);
+        if (f.tn == 16) {
+            const uint32_t c0 = i0 < 8 ? 15 - i0 : i0 - 8, c1 = i1 < 8 ? 15 - i1 : i1 - 8;
+            packed[p] = (uint8_t)(c0 | (c1 << 4));
+        } else {
+            const uint32_t b0 = i0 < 127 ? 254 - i0 : i0 - 127, b1 = i1 < 127 ? 254 - i1 : i1 - 127;
+            reinterpret_cast<uint16_t*>(packed)[p] = (uint16_t)(b0 | (b1 << 8));
+        }
+        if ((p % lanes) == 0) scale[r * nb + b] = (uint8_t)(qi + f.bias);
+    }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kEcdlThreads) ccdl_bwd_kernel(const T* __restrict__ grad, const T* __restrict__ theta,
                                                                 CcdlArgs a, const uint8_t* __restrict__ scale,
@@ -800,6 +847,38 @@ extern "C" int cdlb200_ccdl_fwd(const void* theta, int theta_f32, int64_t rows, 
         ccdl_fwd_kernel<uint16_t><<<grid, kEcdlThreads, 0, st>>>(static_cast<const uint16_t*>(theta), a, seed,
                                                                  static_cast<uint8_t*>(packed),
                                                                  static_cast<uint8_t*>(scale));
+    CDLB200_CHECK_LAUNCH();
+    return CDLB200_OK;
+}
+
+extern "C" int cdlb200_ccdl_round(const void* theta, int theta_f32, int64_t rows, int64_t nb, int format,
+                                  const float* q, int64_t q_stride, const float* alpha, int levels_bf16,
+                                  void* packed, void* scale, void* stream) {
+    int rc = ecdl_check(rows, nb, format, 1);
+    if (rc != CDLB200_OK) return rc;
+    if (q_stride != 0 && q_stride != nb) return CDLB200_ERR_INVALID_ARG;
+    if (rows == 0 || nb == 0) return CDLB200_OK;
+    if (!theta || !q || !alpha || !packed || !scale) return CDLB200_ERR_INVALID_ARG;
+    if (!ecdl_aligned(theta, theta_f32 ? 8 : 4) || !ecdl_aligned(packed, 2)) return CDLB200_ERR_ALIGNMENT;
+    const EcdlFormat f = ecdl_format(format);
+    CcdlArgs a{};
+    a.npairs = rows * nb * f.tpb / 2;
+    a.k = nb * f.tpb;
+    a.rows = rows;
+    a.fmt = format;
+    a.q = q;
+    a.q_stride = q_stride;
+    a.alpha = alpha;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int grid = ecdl_grid(a.npairs);
+    if (theta_f32)
+        ccdl_round_kernel<float><<<grid, kEcdlThreads, 0, st>>>(static_cast<const float*>(theta), a, levels_bf16 != 0,
+                                                                static_cast<uint8_t*>(packed),
+                                                                static_cast<uint8_t*>(scale));
+    else
+        ccdl_round_kernel<uint16_t><<<grid, kEcdlThreads, 0, st>>>(static_cast<const uint16_t*>(theta), a,
+                                                                   levels_bf16 != 0, static_cast<uint8_t*>(packed),
+                                                                   static_cast<uint8_t*>(scale));
     CDLB200_CHECK_LAUNCH();
     return CDLB200_OK;
 }

@@ -197,3 +197,36 @@ class Mxfp8ExtendedCdlQuantForActivation(_ForActivation):
 
 class Mxfp8ExtendedCdlQuantForWeight(_ForWeight):
     FMT = "mxfp8"
+
+
+class ExtendedCdlQuantMixin(nn.Module):
+    """Model-level helpers of cdl's ``ExtendedCdlQuantMixin``
+    (ecdl/ecdl.py:213-264): quantized-element counts, kappa statistics and
+    the optimizer parameter group of the temperatures."""
+
+    def extended_cdl_get_weight_quant_counts(self) -> int:
+        return sum(m.num_quantized_params for m in self.modules() if isinstance(m, _ForWeight))
+
+    def extended_cdl_get_activation_quant_counts(self) -> int:
+        return sum(m.num_quantized_params for m in self.modules() if isinstance(m, _ForActivation))
+
+    @torch.no_grad()
+    def extended_cdl_quant_stats(self) -> dict[str, float]:
+        return {f"{name.removeprefix('_orig_mod.')}.kappa": m.kappa.item()
+                for name, m in self.named_modules() if isinstance(m, ExtendedCdlQuant)}
+
+    @torch.no_grad()
+    def extended_cdl_get_param_groups(self, learning_rate: float,
+                                      train_kappa: bool) -> tuple[list[dict], set[nn.Parameter]]:
+        custom: set[nn.Parameter] = set()
+        params: list[nn.Parameter] = []
+        for m in self.modules():
+            if not isinstance(m, ExtendedCdlQuant):
+                continue
+            custom.update(m.parameters())
+            if train_kappa:
+                params.append(m.log_kappa)
+            else:
+                m.log_kappa.requires_grad_(False)
+        groups = [{"params": params, "lr": learning_rate, "weight_decay": 0.0}] if params else []
+        return groups, custom

@@ -164,6 +164,17 @@ int cdlb200_ccdl_bwd(const void* grad, const void* theta, int theta_f32, int64_t
                      const float* kappa_q, const float* alpha, int theta_topk, int q_topk, void* dtheta, float* dq,
                      float* scalars, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* CCDL deterministic (eval-mode) quantize, replacing the torch
+ * cascaded_nearest_round of cdl/core/ccdl.py:78-89 that
+ * CascadedCdlQuant.eval_forward (cdl/model/components/quant/ccdl/ccdl.py:147-162)
+ * calls: q to its nearest scale level, s = level * alpha in the level dtype
+ * (levels_bf16: rounded to bf16), theta to the nearest level of theta / s
+ * (rounded to bf16 when theta and the levels are both bf16).  Same layouts
+ * as cdlb200_ccdl_fwd; scale is written for every row. */
+int cdlb200_ccdl_round(const void* theta, int theta_f32, int64_t rows, int64_t nb, int format, const float* q,
+                       int64_t q_stride, const float* alpha, int levels_bf16, void* packed, void* scale,
+                       void* stream);
+
 #ifdef __cplusplus
 }
 #endif
