@@ -778,8 +778,11 @@ __global__ void __launch_bounds__(kEncThreads) nvfp4_encode_multi_kernel(const _
         const int64_t nblk = T.rows * (int64_t)nb.d;
         const int64_t c4 = (nb.d + 3) / 4;
         // the tensor's global scale, as the fused quantizer derives it from its amax
-        uint32_t gm = 0;
-        for (int i = 0; i < (T.amax_words > 1 ? T.amax_words : 1); ++i) gm = max(gm, __ldcg(T.amax + i));
+        // (up to 64 amax words: two per lane at most, reduced across the warp)
+        const int nw = T.amax_words > 1 ? T.amax_words : 1, lane = tid & 31;
+        uint32_t gm = lane < nw ? __ldcg(T.amax + lane) : 0u;
+        if (lane + 32 < nw) gm = max(gm, __ldcg(T.amax + lane + 32));
+        gm = __reduce_max_sync(0xffffffffu, gm);
         Nvfp4Tensor tn;
         tn.gmax = gm > 0x7f80u ? u2f(0x7fc00000u) : fmaxf(u2f(gm << 16), 1.1754943508222875e-38f);
         tn.alpha = __fdiv_rn(tn.gmax, 2688.0f);
