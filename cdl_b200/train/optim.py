@@ -25,27 +25,38 @@ from cdl_b200 import _lib
 ENCODED_ATTR = "_cdlb200_nvfp4"
 
 
-class ClipAdamW:
+class ClipAdamW(torch.optim.Optimizer):
     """``clip_grad_norm_(params, max_norm, foreach=True)`` followed by
     ``AdamW(params, lr, betas, eps, weight_decay).step()`` for bf16 CUDA
     parameters; moments are bf16 as torch keeps them for bf16 parameters.
     ``step()`` returns the total gradient norm (a 0-d fp32 tensor holding the
     bf16 value torch's clip returns).  Parameters whose ``grad`` is None are
-    skipped, as torch does."""
+    skipped, as torch does.
+
+    A ``torch.optim.Optimizer`` with one parameter group, so torch's LR
+    schedulers drive it (``lr``, ``betas``, ``eps`` and ``weight_decay`` are
+    read from the group at every step; a step captured in a CUDA graph keeps
+    the values of the capture).  ``state_dict()`` / ``load_state_dict()`` use
+    ``torch.optim.AdamW``'s layout (per-parameter ``step``, ``exp_avg``,
+    ``exp_avg_sq``), so checkpoints move between the two."""
 
     def __init__(self, params: Iterable[torch.Tensor], lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.999),
                  eps: float = 1e-8, weight_decay: float = 0.0, max_norm: float = 1.0,
                  encode: Iterable[torch.Tensor] = ()):
-        self.params = [p for p in params if p.requires_grad]
-        if not self.params:
+        params = [p for p in params if p.requires_grad]
+        if not params:
             raise ValueError("ClipAdamW: no parameters")
-        dev = self.params[0].device
-        for p in self.params:
+        dev = params[0].device
+        for p in params:
             if p.device != dev or not p.is_cuda:
                 raise ValueError("ClipAdamW: all parameters must be on one CUDA device")
             if p.dtype != torch.bfloat16 or not p.is_contiguous() or p.numel() % 8 or p.data_ptr() % 16:
                 raise ValueError("ClipAdamW: parameters must be contiguous bf16, numel % 8 == 0, 16-byte aligned")
-        self.lr, self.betas, self.eps, self.weight_decay, self.max_norm = lr, betas, eps, weight_decay, max_norm
+        defaults = dict(lr=lr, betas=tuple(betas), eps=eps, weight_decay=weight_decay, amsgrad=False,
+                        maximize=False, foreach=None, capturable=False, differentiable=False, fused=None)
+        super().__init__(params, defaults)
+        self.params = params
+        self.max_norm = max_norm
         self.exp_avg = [torch.zeros_like(p) for p in self.params]
         self.exp_avg_sq = [torch.zeros_like(p) for p in self.params]
         self._table = (_lib.AdamwTensor * len(self.params))()
@@ -53,6 +64,7 @@ class ClipAdamW:
             t = self._table[i]
             t.param, t.exp_avg, t.exp_avg_sq = p.data_ptr(), self.exp_avg[i].data_ptr(), self.exp_avg_sq[i].data_ptr()
             t.numel = p.numel()
+            self.state[p] = {"exp_avg": self.exp_avg[i], "exp_avg_sq": self.exp_avg_sq[i]}
         self._numel = [p.numel() for p in self.params]
         nbytes = int(_lib.lib().cdlb200_clip_adamw_workspace_bytes(ctypes.addressof(self._table), len(self.params)))
         self._ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
@@ -60,8 +72,18 @@ class ClipAdamW:
         self.device = dev
         self._encoder = WeightEncoder(self, list(encode)) if encode else None
 
+    @property
+    def lr(self) -> float:
+        return self.param_groups[0]["lr"]
+
+    @lr.setter
+    def lr(self, value: float) -> None:
+        self.param_groups[0]["lr"] = value
+
     @torch.no_grad()
-    def step(self) -> torch.Tensor:
+    def step(self, closure=None) -> torch.Tensor:
+        if closure is not None:
+            raise ValueError("ClipAdamW: closures are not supported")
         tab = self._table
         for i, p in enumerate(self.params):
             g = p.grad
@@ -71,9 +93,10 @@ class ClipAdamW:
             if g.dtype != torch.bfloat16 or not g.is_contiguous():
                 raise ValueError("ClipAdamW: gradients must be contiguous bf16")
             tab[i].grad, tab[i].numel = g.data_ptr(), self._numel[i]
-        b1, b2 = self.betas
+        group = self.param_groups[0]
+        b1, b2 = group["betas"]
         _lib.call("cdlb200_clip_adamw", ctypes.addressof(tab), len(self.params), float(self.max_norm),
-                  float(self.lr), float(b1), float(b2), float(self.eps), float(self.weight_decay),
+                  float(group["lr"]), float(b1), float(b2), float(group["eps"]), float(group["weight_decay"]),
                   _lib.ptr(self._ws), self._ws.numel(), _lib.ptr(self._norm), _lib.stream(self.device))
         # the kernels wrote the parameters in place: advance their version
         # counters as a torch in-place update would
@@ -82,17 +105,38 @@ class ClipAdamW:
             self._encoder.refresh()
         return self._norm.clone()
 
-    def zero_grad(self, set_to_none: bool = True) -> None:
-        for p in self.params:
-            if set_to_none:
-                p.grad = None
-            elif p.grad is not None:
-                p.grad.zero_()
-
     @property
     def steps_done(self) -> int:
         """Completed steps (reads the device counter: synchronizes)."""
         return int(self._ws[:4].view(torch.float32).item())
+
+    def state_dict(self) -> dict:
+        """AdamW's layout; ``step`` is a CPU fp32 tensor as AdamW keeps it
+        (reads the device counter: synchronizes)."""
+        sd = super().state_dict()
+        step = torch.tensor(float(self.steps_done), dtype=torch.float32)
+        for st in sd["state"].values():
+            st["step"] = step.clone()
+        return sd
+
+    def load_state_dict(self, state_dict: dict) -> None:
+        """Accepts this optimizer's or ``torch.optim.AdamW``'s state_dict with
+        one parameter group over the same parameters: copies the moments into
+        the buffers the kernels use and sets the step counter."""
+        super().load_state_dict(state_dict)
+        step = 0.0
+        for i, p in enumerate(self.params):
+            st = self.state.get(p, {})
+            if "exp_avg" in st:
+                self.exp_avg[i].copy_(st["exp_avg"])
+                self.exp_avg_sq[i].copy_(st["exp_avg_sq"])
+            else:  # never stepped in the saved run
+                self.exp_avg[i].zero_()
+                self.exp_avg_sq[i].zero_()
+            if "step" in st:
+                step = max(step, float(st["step"]))
+            self.state[p] = {"exp_avg": self.exp_avg[i], "exp_avg_sq": self.exp_avg_sq[i]}
+        self._ws[:4].view(torch.float32).fill_(step)
 
 
 class WeightEncoder:

@@ -176,3 +176,77 @@ def test_optimizer_weight_encoding_is_current():
     with torch.no_grad():
         ws[0].mul_(2)
     assert getattr(ws[0], ENCODED_ATTR)[0] != ws[0]._version
+
+
+def test_clip_adamw_state_dict_scheduler_and_torch_checkpoints():
+    """ClipAdamW is a torch Optimizer: a LambdaLR schedule drives its lr; its
+    state_dict has AdamW's layout; a run resumed from it continues bit for
+    bit; and a torch AdamW checkpoint loads into it (and back)."""
+    from cdl_b200.train.optim import ClipAdamW
+
+    dev = torch.device("cuda")
+    sizes = SIZES[:5]
+
+    def make(seed):
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        return [(torch.randn(n, device=dev, generator=gen) * 0.02).to(torch.bfloat16).requires_grad_() for n in sizes]
+
+    def grads(step):
+        gen = torch.Generator(device=dev).manual_seed(100 + step)
+        return [torch.randn(n, device=dev, generator=gen).to(torch.bfloat16) for n in sizes]
+
+    def run(opt, ps, sched, steps):
+        for s in steps:
+            for p, g in zip(ps, grads(s)):
+                p.grad = g
+            opt.step()
+            sched.step()
+            opt.zero_grad()
+
+    lam = lambda s: min(1.0, (s + 1) / 4)  # noqa: E731
+    ps = make(0)
+    opt = ClipAdamW(ps, lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1)
+    sched = torch.optim.lr_scheduler.LambdaLR(opt, lam)
+    run(opt, ps, sched, range(3))
+    assert opt.lr == pytest.approx(1e-3 * 1.0) and opt.param_groups[0]["lr"] == opt.lr
+    sd = opt.state_dict()
+    assert set(sd["state"][0]) == {"step", "exp_avg", "exp_avg_sq"} and float(sd["state"][0]["step"]) == 3.0
+    sd = {"state": {k: {n: t.clone() for n, t in v.items()} for k, v in sd["state"].items()},
+          "param_groups": [dict(g) for g in sd["param_groups"]]}
+    ssd = sched.state_dict()
+    saved = [p.detach().clone() for p in ps]
+    run(opt, ps, sched, range(3, 5))
+    want = [p.detach().clone() for p in ps]
+
+    # resume: fresh optimizer + scheduler on the saved parameters
+    ps2 = [t.clone().requires_grad_() for t in saved]
+    opt2 = ClipAdamW(ps2, lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1)
+    sched2 = torch.optim.lr_scheduler.LambdaLR(opt2, lam)
+    opt2.load_state_dict(sd)
+    sched2.load_state_dict(ssd)
+    assert opt2.steps_done == 3
+    run(opt2, ps2, sched2, range(3, 5))
+    for a, b in zip(want, ps2):
+        assert torch.equal(a, b.detach())
+
+    # torch AdamW loads our state and continues as our optimizer does
+    ref = [t.clone().requires_grad_() for t in saved]
+    topt = torch.optim.AdamW(ref, lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1, foreach=True)
+    tsched = torch.optim.lr_scheduler.LambdaLR(topt, lam)
+    topt.load_state_dict(sd)
+    tsched.load_state_dict(ssd)
+    for s in range(3, 5):
+        for p, g in zip(ref, grads(s)):
+            p.grad = g
+        torch.nn.utils.clip_grad_norm_(ref, 1.0, foreach=True)
+        topt.step()
+        tsched.step()
+        topt.zero_grad()
+    a = torch.cat([x.detach().reshape(-1) for x in want])
+    b = torch.cat([x.detach().reshape(-1) for x in ref])
+    assert float((a != b).float().mean()) < 1e-4 and float(_ulp_diff(a, b).max()) <= 1.0
+    # and its state_dict loads into ours
+    opt3 = ClipAdamW([t.clone().requires_grad_() for t in want], lr=1e-3)
+    opt3.load_state_dict(topt.state_dict())
+    assert opt3.steps_done == 5
+    assert torch.equal(opt3.exp_avg[2], topt.state[ref[2]]["exp_avg"])
