@@ -102,12 +102,65 @@ def build_model(spec: ModelSpec, device: torch.device, seed: int = 0, fused: boo
     return model
 
 
-def apply_quant(model: nn.Module, backend: str = "nvfp4", simulation: str | None = None) -> int:
-    """Swap every target nn.Linear for an STE-quantized QLinear (smollm2.py:408-424).
+def _cdl_variants() -> dict:
+    """cdl's quantizer variants (smollm2.py:86-135): name -> (family, activation class, weight class)."""
+    from cdl_b200.model.components.quant import ccdl, ecdl
+
+    return {
+        "nvfp4_ccdl": ("ccdl", ccdl.Nvfp4CascadedCdlQuantForActivation, ccdl.Nvfp4CascadedCdlQuantForWeight),
+        "mxfp4_ccdl": ("ccdl", ccdl.Mxfp4CascadedCdlQuantForActivation, ccdl.Mxfp4CascadedCdlQuantForWeight),
+        "mxfp8_ccdl": ("ccdl", ccdl.Mxfp8CascadedCdlQuantForActivation, ccdl.Mxfp8CascadedCdlQuantForWeight),
+        "nvfp4_ecdl": ("ecdl", ecdl.Nvfp4ExtendedCdlQuantForActivation, ecdl.Nvfp4ExtendedCdlQuantForWeight),
+        "mxfp4_ecdl": ("ecdl", ecdl.Mxfp4ExtendedCdlQuantForActivation, ecdl.Mxfp4ExtendedCdlQuantForWeight),
+        "mxfp8_ecdl": ("ecdl", ecdl.Mxfp8ExtendedCdlQuantForActivation, ecdl.Mxfp8ExtendedCdlQuantForWeight),
+    }
+
+
+def build_activation_quant(variant: str, in_features: int, sim: str, dtype: torch.dtype = torch.bfloat16, *,
+                           kappa: float = 2.0, kappa_bwd: float | None = None, theta_topk: int = 5,
+                           q_topk: int = 5, kernel: str = "triton"):
+    """cdl's ``_build_activation_quant`` (smollm2.py:352-374): "none", "ste"
+    (``sim`` is the STE format) or a CDL variant over inputs shaped
+    ``(1, in_features)``."""
+    from cdl_b200.model.components.quant.identity import IdentityQuant
+
+    if variant == "none":
+        return IdentityQuant()
+    if variant == "ste":
+        return SteQuant(sim)
+    family, act_cls, _ = _cdl_variants()[variant]
+    if family == "ccdl":
+        return act_cls((1, in_features), theta_topk, q_topk, dtype, kappa, kernel=kernel)
+    return act_cls((1, in_features), theta_topk, dtype, kappa, kappa_bwd, kernel=kernel)
+
+
+def build_weight_quant(variant: str, weight: torch.Tensor, sim: str, dtype: torch.dtype = torch.bfloat16, *,
+                       kappa: float = 2.0, kernel: str = "triton"):
+    """cdl's ``_build_weight_quant`` (smollm2.py:377-397), on the weight's device."""
+    from cdl_b200.model.components.quant.identity import IdentityQuant
+
+    if variant == "none":
+        return IdentityQuant()
+    if variant == "ste":
+        return SteQuant(sim)
+    _, _, w_cls = _cdl_variants()[variant]
+    return w_cls(weight.detach(), dtype, kappa, kernel=kernel).to(weight.device)
+
+
+def apply_quant(model: nn.Module, backend: str = "nvfp4", simulation: str | None = None, *,
+                activation: str = "ste", weight: str = "ste", dtype: torch.dtype = torch.bfloat16,
+                activation_kappa: float = 2.0, activation_kappa_bwd: float | None = None,
+                weight_kappa: float = 2.0, theta_topk: int = 5, q_topk: int = 5, kernel: str = "triton") -> int:
+    """Swap every target nn.Linear for a QLinear (smollm2.py:408-424) with
+    cdl's quantizer variants: ``activation`` / ``weight`` each "none", "ste"
+    or one of ``{nvfp4,mxfp4,mxfp8}_{ccdl,ecdl}``.
 
     ``backend="none"`` leaves the model unquantized (bf16 reference runs)."""
     if backend == "none":
         return 0
+    names = ("none", "ste", *_cdl_variants())
+    if activation not in names or weight not in names:
+        raise ValueError(f"unknown quantizer variant {activation!r} / {weight!r}")
     base = backend.split("_")[0]  # "nvfp4_qbwd" quantizes like "nvfp4"
     sim = simulation or (base if base.startswith("mx") else "nvfp4")
     count = 0
@@ -117,8 +170,11 @@ def apply_quant(model: nn.Module, backend: str = "nvfp4", simulation: str | None
             continue
         parent = model.get_submodule(parent_name) if parent_name else model
         q = QLinear.from_linear(module)
-        q.set_activation_quant(SteQuant(sim))
-        q.set_weight_quant(SteQuant(sim))
+        q.set_activation_quant(build_activation_quant(activation, q.in_features, sim, dtype,
+                                                      kappa=activation_kappa, kappa_bwd=activation_kappa_bwd,
+                                                      theta_topk=theta_topk, q_topk=q_topk,
+                                                      kernel=kernel).to(q.weight.device))
+        q.set_weight_quant(build_weight_quant(weight, q.weight, sim, dtype, kappa=weight_kappa, kernel=kernel))
         q.set_backend(backend)
         setattr(parent, leaf, q)
         count += 1
@@ -212,21 +268,36 @@ class QatStep:
 
     def __init__(self, spec: ModelSpec, device: torch.device, backend: str = "nvfp4", lr: float = 3e-4,
                  grad_clip: float = 1.0, seed: int = 0, ddp: bool = False, bucket_mb: int = 64,
-                 fused: bool | None = None, graph: bool = False, optimizer: str | None = None):
+                 fused: bool | None = None, graph: bool = False, optimizer: str | None = None,
+                 activation: str = "ste", weight: str = "ste", quant_lr: float = 3e-4, train_alpha: bool = True,
+                 train_kappa: bool = False, **quant_options):
         self.spec = spec
         self.device = device
+        self.backend = backend
         self.model = build_model(spec, device, seed, fused)
-        self.n_quant = apply_quant(self.model, backend)
+        self.n_quant = apply_quant(self.model, backend, activation=activation, weight=weight, **quant_options)
         self.model.train()
+        on_cuda = device.type == "cuda"
+        # the CDL quantizers' own parameters (fp32 log scales / temperatures)
+        # form one more AdamW group at quant_lr, as cdl's build_optimizer
+        # does (smollm2.py:555-604); the optimizer is then torch's AdamW
+        from cdl_b200.model.components.quant.ccdl import CascadedCdlQuantMixin
+        from cdl_b200.model.components.quant.ecdl import ExtendedCdlQuantMixin
+
+        cg, cp = CascadedCdlQuantMixin.cascaded_cdl_get_param_groups(self.model, quant_lr, train_alpha, train_kappa)
+        eg, ep = ExtendedCdlQuantMixin.extended_cdl_get_param_groups(self.model, quant_lr, train_kappa)
+        quant_ids = {id(p) for p in cp | ep}
+        quant_params = [p for g in cg + eg for p in g["params"]]
         params = [p for p in self.model.parameters() if p.requires_grad]
         self.params = params
-        decay = [p for p in params if p.ndim > 1]
-        no_decay = [p for p in params if p.ndim <= 1]
-        on_cuda = device.type == "cuda"
-        # "fused": clip + AdamW through cdlb200_clip_adamw (CUDA); "torch":
-        # clip_grad_norm_ + torch.optim.AdamW with its default (foreach)
-        # implementation, as cdl constructs it
-        self.optimizer = optimizer or ("fused" if on_cuda else "torch")
+        decay = [p for p in params if p.ndim > 1 and id(p) not in quant_ids]
+        no_decay = [p for p in params if p.ndim <= 1 and id(p) not in quant_ids]
+        # "fused": clip + AdamW through cdlb200_clip_adamw (CUDA, bf16
+        # parameters only); "torch": clip_grad_norm_ + torch.optim.AdamW with
+        # its default (foreach) implementation, as cdl constructs it
+        self.optimizer = optimizer or ("fused" if on_cuda and not quant_ids else "torch")
+        if self.optimizer == "fused" and quant_ids:
+            raise ValueError("the fused optimizer takes bf16 parameters only; CDL quantizers need optimizer='torch'")
         if self.optimizer == "fused":
             from cdl_b200.train.optim import ClipAdamW
 
@@ -235,9 +306,10 @@ class QatStep:
             self.opt = ClipAdamW(params, lr=lr, betas=(0.9, 0.95), weight_decay=0.0, max_norm=grad_clip,
                                  encode=encode)
         elif self.optimizer == "torch":
-            self.opt = torch.optim.AdamW(
-                [{"params": decay, "weight_decay": 0.0}, {"params": no_decay, "weight_decay": 0.0}],
-                lr=lr, betas=(0.9, 0.95), capturable=graph and on_cuda)
+            groups = [{"params": decay, "weight_decay": 0.0}, {"params": no_decay, "weight_decay": 0.0},
+                      {"params": quant_params, "lr": quant_lr, "weight_decay": 0.0}]
+            self.opt = torch.optim.AdamW([g for g in groups if g["params"]], lr=lr, betas=(0.9, 0.95),
+                                         capturable=graph and on_cuda)
         else:
             raise ValueError(f"unknown optimizer {optimizer!r}")
         self.graph_mode = graph and on_cuda
@@ -249,6 +321,22 @@ class QatStep:
 
             self.net = DDP(self.net, device_ids=[device.index] if device.type == "cuda" else None,
                            bucket_cap_mb=bucket_mb, gradient_as_bucket_view=True, static_graph=True)
+
+    @torch.no_grad()
+    def calibrate(self, samples) -> None:
+        """Initialize the CCDL activation quantizers' scales from calibration
+        batches of token ids, on the native backend, as cdl's
+        ``init_activation_q`` does (smollm2.py:478-491)."""
+        from cdl_b200.model.components.quant.ccdl import CascadedCdlQuantMixin
+
+        qls = [m for m in self.model.modules() if isinstance(m, QLinear)]
+        for m in qls:
+            m.set_backend("native")
+        try:
+            CascadedCdlQuantMixin.cascaded_cdl_init_act_q_pass(self.model, list(samples))
+        finally:
+            for m in qls:
+                m.set_backend(self.backend)
 
     def _eager_step(self, input_ids: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         loss = self.net(input_ids)

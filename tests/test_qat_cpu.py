@@ -34,3 +34,29 @@ def test_quantized_backward_backend_names():
         pass
     else:
         raise AssertionError("unknown backend accepted")
+
+
+def test_cdl_quantizer_variants_build_with_their_optimizer_group():
+    """cdl's quantizer variants in the QAT step: the classes apply_quant puts
+    in each QLinear, and the extra AdamW group of the quantizers' own
+    parameters at quant_lr (smollm2.py build_optimizer)."""
+    import pytest
+
+    from cdl_b200.model.components.linear import QLinear
+    from cdl_b200.model.components.quant import ccdl, ecdl
+    from cdl_b200.train import qat
+
+    step = qat.QatStep(qat.SPECS["tiny"], torch.device("cpu"), backend="nvfp4", weight="nvfp4_ccdl",
+                       activation="nvfp4_ecdl", quant_lr=1e-3)
+    qls = [m for m in step.model.modules() if isinstance(m, QLinear)]
+    assert len(qls) == step.n_quant == 14
+    assert all(isinstance(m.weight_quant, ccdl.Nvfp4CascadedCdlQuantForWeight) for m in qls)
+    assert all(isinstance(m.activation_quant, ecdl.Nvfp4ExtendedCdlQuantForActivation) for m in qls)
+    assert step.optimizer == "torch"
+    groups = step.opt.param_groups
+    assert groups[-1]["lr"] == 1e-3 and len(groups[-1]["params"]) == 2 * 14  # log_q, log_alpha per weight
+    assert not qls[0].activation_quant.log_kappa.requires_grad  # train_kappa=False
+    with pytest.raises(ValueError):
+        qat.QatStep(qat.SPECS["tiny"], torch.device("cpu"), weight="nvfp4_ccdl", optimizer="fused")
+    with pytest.raises(ValueError):
+        qat.apply_quant(torch.nn.Linear(4, 4), weight="fp3_cdl")

@@ -156,3 +156,33 @@ def test_graph_step_matches_eager():
     print("graph:", got[:4], "eager:", ref[:4])
     worst = max(abs(a - b) / b for a, b in zip(got, ref))
     assert worst < 5e-3
+
+
+@pytest.mark.parametrize("activation,weight", [("ste", "nvfp4_ccdl"), ("nvfp4_ccdl", "nvfp4_ccdl"),
+                                               ("nvfp4_ecdl", "nvfp4_ecdl")])
+def test_qat_step_with_cdl_quantizers(activation, weight):
+    """The QAT step with cdl's CDL quantizer variants (its default config is
+    CCDL weights with STE activations): CCDL activations are calibrated on the
+    native backend first; the loss starts near log(vocab), stays finite and
+    falls; the quantizer parameters move."""
+    from cdl_b200.model.components.linear import QLinear
+    from cdl_b200.train import qat
+
+    spec = qat.SPECS["tiny"]
+    dev = torch.device("cuda")
+    step = qat.QatStep(spec, dev, backend="nvfp4", lr=1e-3, seed=0, activation=activation, weight=weight,
+                       train_kappa=True)  # ECDL's only parameter is its temperature
+    if activation.endswith("ccdl"):
+        step.calibrate([qat.random_tokens(2, 128, spec.vocab, seed=7, device=dev)])
+    wq = next(m for m in step.model.modules() if isinstance(m, QLinear)).weight_quant
+    before = [p.detach().clone() for p in wq.parameters() if p.requires_grad]
+    losses = []
+    for i in range(12):
+        ids = qat.random_tokens(4, 128, spec.vocab, seed=i % 3, device=dev)
+        loss, gn = step.step(ids)
+        losses.append(float(loss))
+        assert torch.isfinite(gn)
+    assert abs(losses[0] - qat.expected_initial_loss(spec)) < 0.5
+    assert all(map(lambda v: v == v and abs(v) < 1e3, losses)) and min(losses[-3:]) < losses[0]
+    after = [p.detach() for p in wq.parameters() if p.requires_grad]
+    assert before and any(not torch.equal(a, b) for a, b in zip(before, after))
