@@ -102,6 +102,44 @@ def build_model(spec: ModelSpec, device: torch.device, seed: int = 0, fused: boo
     return model
 
 
+def untie_and_freeze(model: nn.Module, *, freeze_all: bool = True, train_head: bool = True) -> None:
+    """cdl's parameter policy (smollm2.py:456-476, applied at :947-951 with
+    ``freeze_all = use_lora or freeze_base`` and ``train_head = not use_lora
+    and train_head``): the LM head gets its own copy of a tied embedding;
+    then either everything but (optionally) the head is frozen, or only the
+    input embedding (and, optionally, the head)."""
+    embed, head = model.get_input_embeddings(), model.lm_head
+    if head.weight is embed.weight:
+        head.weight = nn.Parameter(embed.weight.detach().clone())
+        model.config.tie_word_embeddings = False
+    if not freeze_all:
+        embed.weight.requires_grad_(False)
+        if not train_head:
+            head.weight.requires_grad_(False)
+        return
+    for p in model.parameters():
+        p.requires_grad_(False)
+    if train_head:
+        head.weight.requires_grad_(True)
+
+
+def lr_lambda(warmup_steps: int = 0, lr_decay: str = "constant", max_steps: int = 0, min_lr_ratio: float = 0.1):
+    """cdl's learning-rate factor (smollm2.py:596-607): linear warmup to 1,
+    then constant or a cosine down to ``min_lr_ratio`` at ``max_steps``."""
+    if lr_decay not in ("constant", "cosine"):
+        raise ValueError(f"unknown lr_decay {lr_decay!r}")
+
+    def f(step: int) -> float:
+        if step < warmup_steps:
+            return (step + 1) / warmup_steps
+        if lr_decay == "cosine" and max_steps > warmup_steps:
+            progress = min(1.0, (step - warmup_steps) / (max_steps - warmup_steps))
+            return min_lr_ratio + 0.5 * (1.0 - min_lr_ratio) * (1.0 + math.cos(math.pi * progress))
+        return 1.0
+
+    return f
+
+
 def _cdl_variants() -> dict:
     """cdl's quantizer variants (smollm2.py:86-135): name -> (family, activation class, weight class)."""
     from cdl_b200.model.components.quant import ccdl, ecdl
@@ -150,10 +188,13 @@ def build_weight_quant(variant: str, weight: torch.Tensor, sim: str, dtype: torc
 def apply_quant(model: nn.Module, backend: str = "nvfp4", simulation: str | None = None, *,
                 activation: str = "ste", weight: str = "ste", dtype: torch.dtype = torch.bfloat16,
                 activation_kappa: float = 2.0, activation_kappa_bwd: float | None = None,
-                weight_kappa: float = 2.0, theta_topk: int = 5, q_topk: int = 5, kernel: str = "triton") -> int:
+                weight_kappa: float = 2.0, theta_topk: int = 5, q_topk: int = 5, kernel: str = "triton",
+                lora: tuple[int, int] | None = None) -> int:
     """Swap every target nn.Linear for a QLinear (smollm2.py:408-424) with
     cdl's quantizer variants: ``activation`` / ``weight`` each "none", "ste"
-    or one of ``{nvfp4,mxfp4,mxfp8}_{ccdl,ecdl}``.
+    or one of ``{nvfp4,mxfp4,mxfp8}_{ccdl,ecdl}``; ``lora = (r, alpha)``
+    adds cdl's merged LoRA adapter to each (the weight quantizer then sees
+    ``W + alpha / r * B A``).
 
     ``backend="none"`` leaves the model unquantized (bf16 reference runs)."""
     if backend == "none":
@@ -170,6 +211,8 @@ def apply_quant(model: nn.Module, backend: str = "nvfp4", simulation: str | None
             continue
         parent = model.get_submodule(parent_name) if parent_name else model
         q = QLinear.from_linear(module)
+        if lora is not None:
+            q.set_lora(*lora)
         q.set_activation_quant(build_activation_quant(activation, q.in_features, sim, dtype,
                                                       kappa=activation_kappa, kappa_bwd=activation_kappa_bwd,
                                                       theta_topk=theta_topk, q_topk=q_topk,
@@ -270,12 +313,20 @@ class QatStep:
                  grad_clip: float = 1.0, seed: int = 0, ddp: bool = False, bucket_mb: int = 64,
                  fused: bool | None = None, graph: bool = False, optimizer: str | None = None,
                  activation: str = "ste", weight: str = "ste", quant_lr: float = 3e-4, train_alpha: bool = True,
-                 train_kappa: bool = False, **quant_options):
+                 train_kappa: bool = False, use_lora: bool = False, lora_r: int = 8, lora_alpha: int = 16,
+                 freeze_base: bool = False, train_head: bool = True, untie: bool = False, warmup_steps: int = 0,
+                 lr_decay: str = "constant", max_steps: int = 0, min_lr_ratio: float = 0.1, **quant_options):
         self.spec = spec
         self.device = device
         self.backend = backend
         self.model = build_model(spec, device, seed, fused)
-        self.n_quant = apply_quant(self.model, backend, activation=activation, weight=weight, **quant_options)
+        # the BASELINE configs train every parameter with tied embeddings;
+        # cdl's script unties the head and applies its freeze policy
+        if untie or use_lora or freeze_base:
+            untie_and_freeze(self.model, freeze_all=use_lora or freeze_base,
+                             train_head=not use_lora and train_head)
+        self.n_quant = apply_quant(self.model, backend, activation=activation, weight=weight,
+                                   lora=(lora_r, lora_alpha) if use_lora else None, **quant_options)
         self.model.train()
         on_cuda = device.type == "cuda"
         # the CDL quantizers' own parameters (fp32 log scales / temperatures)
@@ -312,6 +363,11 @@ class QatStep:
                                          capturable=graph and on_cuda)
         else:
             raise ValueError(f"unknown optimizer {optimizer!r}")
+        schedule = warmup_steps > 0 or lr_decay != "constant"
+        if schedule and graph:
+            raise ValueError("a learning-rate schedule needs eager steps (a captured step keeps its lr)")
+        self.lr_scheduler = (torch.optim.lr_scheduler.LambdaLR(
+            self.opt, lr_lambda(warmup_steps, lr_decay, max_steps, min_lr_ratio)) if schedule else None)
         self.graph_mode = graph and on_cuda
         self._graph = None
         self.grad_clip = grad_clip
@@ -346,6 +402,8 @@ class QatStep:
         else:
             gnorm = torch.nn.utils.clip_grad_norm_(self.params, self.grad_clip, foreach=True)
             self.opt.step()
+        if self.lr_scheduler is not None:
+            self.lr_scheduler.step()
         self.opt.zero_grad(set_to_none=True)
         return loss.detach(), gnorm.detach()
 

@@ -60,3 +60,28 @@ def test_cdl_quantizer_variants_build_with_their_optimizer_group():
         qat.QatStep(qat.SPECS["tiny"], torch.device("cpu"), weight="nvfp4_ccdl", optimizer="fused")
     with pytest.raises(ValueError):
         qat.apply_quant(torch.nn.Linear(4, 4), weight="fp3_cdl")
+
+
+def test_lora_freeze_policy_and_lr_schedule():
+    """cdl's parameter policy and LR factor: LoRA trains only the adapters
+    (head untied and frozen); freeze_base trains the untied head; the plain
+    untied run freezes only the input embedding; warmup + cosine factors."""
+    import math
+
+    from cdl_b200.train import qat
+
+    spec, cpu = qat.SPECS["tiny"], torch.device("cpu")
+    lora = qat.QatStep(spec, cpu, backend="nvfp4", use_lora=True, lora_r=4, lora_alpha=8)
+    names = [n for n, p in lora.model.named_parameters() if p.requires_grad]
+    assert len(names) == 2 * 14 and all(n.endswith((".lora.a", ".lora.b")) for n in names)
+    assert lora.model.lm_head.weight is not lora.model.get_input_embeddings().weight
+    fb = qat.QatStep(spec, cpu, backend="nvfp4", freeze_base=True)
+    assert [n for n, p in fb.model.named_parameters() if p.requires_grad] == ["lm_head.weight"]
+    un = qat.QatStep(spec, cpu, backend="nvfp4", untie=True)
+    frozen = [n for n, p in un.model.named_parameters() if not p.requires_grad]
+    assert frozen == ["model.embed_tokens.weight"]
+    f = qat.lr_lambda(warmup_steps=4, lr_decay="cosine", max_steps=14, min_lr_ratio=0.1)
+    assert [f(s) for s in range(4)] == [0.25, 0.5, 0.75, 1.0]
+    assert f(4) == 1.0 and abs(f(9) - (0.1 + 0.45 * (1 + math.cos(math.pi * 0.5)))) < 1e-12 and f(20) == 0.1
+    st = qat.QatStep(spec, cpu, backend="nvfp4", lr=1e-3, warmup_steps=10)
+    assert st.opt.param_groups[0]["lr"] == 1e-4  # LambdaLR applies the first factor at construction

@@ -186,3 +186,26 @@ def test_qat_step_with_cdl_quantizers(activation, weight):
     assert all(map(lambda v: v == v and abs(v) < 1e3, losses)) and min(losses[-3:]) < losses[0]
     after = [p.detach() for p in wq.parameters() if p.requires_grad]
     assert before and any(not torch.equal(a, b) for a, b in zip(before, after))
+
+
+def test_qat_step_lora_with_warmup():
+    """cdl's default regime: LoRA adapters on every quantized linear, base
+    weights and head frozen, warmup schedule; the adapters move, the base
+    weights do not, and the loss falls."""
+    from cdl_b200.model.components.linear import QLinear
+    from cdl_b200.train import qat
+
+    spec = qat.SPECS["tiny"]
+    dev = torch.device("cuda")
+    step = qat.QatStep(spec, dev, backend="nvfp4", lr=3e-3, seed=0, use_lora=True, warmup_steps=3)
+    assert step.optimizer == "fused"
+    lin = next(m for m in step.model.modules() if isinstance(m, QLinear))
+    w0, b0 = lin.weight.detach().clone(), lin.lora.b.detach().clone()
+    losses = []
+    for i in range(10):
+        loss, gn = step.step(qat.random_tokens(4, 128, spec.vocab, seed=i % 2, device=dev))
+        losses.append(float(loss))
+        assert torch.isfinite(gn)
+    assert step.opt.param_groups[0]["lr"] == pytest.approx(3e-3)
+    assert torch.equal(lin.weight.detach(), w0) and not torch.equal(lin.lora.b.detach(), b0)
+    assert min(losses[-3:]) < losses[0]
