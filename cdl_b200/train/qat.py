@@ -283,7 +283,30 @@ def lm_loss(model: nn.Module, input_ids: torch.Tensor, chunk: int = 2048) -> tor
     targets = input_ids[:, 1:].reshape(-1)
     if chunk <= 0:  # plain path: full fp32 logits
         return F.cross_entropy(model.lm_head(h).float(), targets, reduction="mean")
-    return LinearCrossEntropy.apply(h, model.lm_head.weight, targets, chunk)
+    w = model.lm_head.weight
+    if not torch.is_grad_enabled():  # evaluation: no gradient buffers in the chunk loop
+        h, w = h.detach(), w.detach()
+    return LinearCrossEntropy.apply(h, w, targets, chunk)
+
+
+@torch.no_grad()
+def evaluate(model: nn.Module, loader, device: torch.device) -> float:
+    """Perplexity over ``loader``'s batches of token ids (smollm2.py:680-693):
+    exp of the token-weighted mean loss, in eval mode (deterministic
+    quantizers).  The sum stays on the device until the end."""
+    was_training = model.training
+    model.eval()
+    total = torch.zeros((), dtype=torch.float64, device=device)
+    tokens = 0
+    try:
+        for input_ids in loader:
+            input_ids = input_ids.to(device, non_blocking=True)
+            n = input_ids.numel() - input_ids.shape[0]
+            total += lm_loss(model, input_ids).double() * n
+            tokens += n
+    finally:
+        model.train(was_training)
+    return math.exp(float(total) / tokens)
 
 
 class LossModule(nn.Module):

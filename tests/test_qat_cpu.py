@@ -85,3 +85,22 @@ def test_lora_freeze_policy_and_lr_schedule():
     assert f(4) == 1.0 and abs(f(9) - (0.1 + 0.45 * (1 + math.cos(math.pi * 0.5)))) < 1e-12 and f(20) == 0.1
     st = qat.QatStep(spec, cpu, backend="nvfp4", lr=1e-3, warmup_steps=10)
     assert st.opt.param_groups[0]["lr"] == 1e-4  # LambdaLR applies the first factor at construction
+
+
+def test_evaluate_perplexity_on_cpu():
+    """evaluate() = exp(token-weighted mean loss) over the batches, model left
+    in its training mode (unquantized tiny model on the CPU)."""
+    import math
+
+    from cdl_b200.train import qat
+
+    spec = qat.SPECS["tiny"]
+    model = qat.build_model(spec, torch.device("cpu"), seed=0)
+    batches = [torch.randint(0, spec.vocab, (2, 16), generator=torch.Generator().manual_seed(i)) for i in range(3)]
+    model.train()
+    ppl = qat.evaluate(model, batches, torch.device("cpu"))
+    assert model.training
+    with torch.no_grad():
+        model.eval()
+        mean = sum(float(qat.lm_loss(model, b)) for b in batches) / 3  # equal token counts per batch
+    assert abs(ppl - math.exp(mean)) < 1e-6 * math.exp(mean) and abs(math.log(ppl) - math.log(spec.vocab)) < 0.5
