@@ -23,6 +23,7 @@ own activations (per-rank amax, as a single-GPU run would).
 
 from __future__ import annotations
 
+import contextlib
 import math
 from dataclasses import dataclass
 
@@ -417,9 +418,23 @@ class QatStep:
             for m in qls:
                 m.set_backend(self.backend)
 
-    def _eager_step(self, input_ids: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        loss = self.net(input_ids)
-        loss.backward()
+    def _eager_step(self, input_ids) -> tuple[torch.Tensor, torch.Tensor]:
+        if isinstance(input_ids, torch.Tensor):
+            loss = self.net(input_ids)
+            loss.backward()
+        else:  # gradient accumulation over micro-batches, as cdl's loop (smollm2.py:829-850)
+            micro = list(input_ids)
+            n = len(micro)
+            if n == 0:
+                raise ValueError("no micro-batches")
+            loss = None
+            for i, ids in enumerate(micro):
+                sync = i == n - 1 or not hasattr(self.net, "no_sync")
+                with contextlib.nullcontext() if sync else self.net.no_sync():
+                    part = self.net(ids)
+                    (part / n if n > 1 else part).backward()
+                part = part.detach() / n if n > 1 else part.detach()
+                loss = part if loss is None else loss + part
         if self.optimizer == "fused":
             gnorm = self.opt.step()
         else:
@@ -430,14 +445,20 @@ class QatStep:
         self.opt.zero_grad(set_to_none=True)
         return loss.detach(), gnorm.detach()
 
-    def step(self, input_ids: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        """One training step.  In graph mode the first call runs warm-up steps
+    def step(self, input_ids) -> tuple[torch.Tensor, torch.Tensor]:
+        """One training step on a batch of token ids, or on a list of
+        micro-batches whose gradients are accumulated (each loss divided by
+        their count; with data parallelism only the last one all-reduces)
+        before one optimizer step; the returned loss is their mean.  In graph
+        mode (one batch per step) the first call runs warm-up steps
         on a side stream and captures the whole step (forward, backward,
         clipping, AdamW) in a CUDA graph; every call then copies the tokens
         into the graph's input buffer and replays it.  The returned loss and
         gradient norm are the graph's output buffers."""
         if not self.graph_mode:
             return self._eager_step(input_ids)
+        if not isinstance(input_ids, torch.Tensor):
+            raise ValueError("graph mode takes one batch per step")
         if self._graph is None:
             self._capture(input_ids)
         self._static_ids.copy_(input_ids, non_blocking=True)

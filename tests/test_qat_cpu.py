@@ -104,3 +104,27 @@ def test_evaluate_perplexity_on_cpu():
         model.eval()
         mean = sum(float(qat.lm_loss(model, b)) for b in batches) / 3  # equal token counts per batch
     assert abs(ppl - math.exp(mean)) < 1e-6 * math.exp(mean) and abs(math.log(ppl) - math.log(spec.vocab)) < 0.5
+
+
+def test_gradient_accumulation_matches_one_big_batch():
+    """A list of micro-batches accumulates gradients before one optimizer
+    step: the returned loss is their mean, and the update equals the step on
+    the concatenated batch (equal token counts; unquantized model on CPU,
+    fp32 gradients compared before the optimizer)."""
+    from cdl_b200.train import qat
+
+    spec, cpu = qat.SPECS["tiny"], torch.device("cpu")
+    b1, b2 = (torch.randint(0, spec.vocab, (2, 16), generator=torch.Generator().manual_seed(i)) for i in (1, 2))
+    a = qat.QatStep(spec, cpu, backend="none", lr=1e-3, seed=0)
+    b = qat.QatStep(spec, cpu, backend="none", lr=1e-3, seed=0)
+    for m in (a.model, b.model):
+        m.float()
+    grads = {}
+    for name, st, ids in (("micro", a, [b1, b2]), ("whole", b, torch.cat([b1, b2]))):
+        st.opt.step = lambda: None  # keep the parameters: compare the accumulated gradients
+        st.opt.zero_grad = lambda set_to_none=True: None
+        loss, _ = st.step(ids)
+        grads[name] = (float(loss), [p.grad.clone() for p in st.params])
+    assert abs(grads["micro"][0] - grads["whole"][0]) < 1e-5
+    for x, y in zip(grads["micro"][1], grads["whole"][1]):
+        assert torch.allclose(x, y, rtol=1e-4, atol=1e-6)
