@@ -339,7 +339,8 @@ class QatStep:
                  activation: str = "ste", weight: str = "ste", quant_lr: float = 3e-4, train_alpha: bool = True,
                  train_kappa: bool = False, use_lora: bool = False, lora_r: int = 8, lora_alpha: int = 16,
                  freeze_base: bool = False, train_head: bool = True, untie: bool = False, warmup_steps: int = 0,
-                 lr_decay: str = "constant", max_steps: int = 0, min_lr_ratio: float = 0.1, **quant_options):
+                 lr_decay: str = "constant", max_steps: int = 0, min_lr_ratio: float = 0.1,
+                 fp32_master_weights: bool = False, **quant_options):
         self.spec = spec
         self.device = device
         self.backend = backend
@@ -370,7 +371,23 @@ class QatStep:
         # "fused": clip + AdamW through cdlb200_clip_adamw (CUDA, bf16
         # parameters only); "torch": clip_grad_norm_ + torch.optim.AdamW with
         # its default (foreach) implementation, as cdl constructs it
-        self.optimizer = optimizer or ("fused" if on_cuda and not quant_ids else "torch")
+        self.optimizer = optimizer or ("fused" if on_cuda and not quant_ids and not fp32_master_weights else "torch")
+        if self.optimizer == "fused" and fp32_master_weights:
+            raise ValueError("fp32 master weights need optimizer='torch'")
+        # fp32 master copies of the non-fp32 parameters, which the optimizer
+        # updates and copies back (smollm2.py:569-575, 649-657)
+        self.master_pairs: list[tuple[nn.Parameter, nn.Parameter]] = []
+
+        def opt_param(p):
+            if fp32_master_weights and p.dtype != torch.float32:
+                m = nn.Parameter(p.detach().float().clone())
+                self.master_pairs.append((p, m))
+                return m
+            return p
+
+        if fp32_master_weights:
+            decay, no_decay = [opt_param(p) for p in decay], [opt_param(p) for p in no_decay]
+            quant_params = [opt_param(p) for p in quant_params]
         if self.optimizer == "fused" and quant_ids:
             raise ValueError("the fused optimizer takes bf16 parameters only; CDL quantizers need optimizer='torch'")
         if self.optimizer == "fused":
@@ -439,10 +456,24 @@ class QatStep:
             gnorm = self.opt.step()
         else:
             gnorm = torch.nn.utils.clip_grad_norm_(self.params, self.grad_clip, foreach=True)
-            self.opt.step()
+            if self.master_pairs:
+                with torch.no_grad():
+                    for p, m in self.master_pairs:
+                        if p.grad is not None:
+                            m.grad = p.grad.float()
+                    self.opt.step()
+                    for p, m in self.master_pairs:
+                        p.copy_(m)
+                        m.grad = None
+            else:
+                self.opt.step()
         if self.lr_scheduler is not None:
             self.lr_scheduler.step()
-        self.opt.zero_grad(set_to_none=True)
+        if self.master_pairs:  # the optimizer holds the masters: clear the model's gradients
+            for p in self.params:
+                p.grad = None
+        else:
+            self.opt.zero_grad(set_to_none=True)
         return loss.detach(), gnorm.detach()
 
     def step(self, input_ids) -> tuple[torch.Tensor, torch.Tensor]:

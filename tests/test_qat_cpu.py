@@ -128,3 +128,19 @@ def test_gradient_accumulation_matches_one_big_batch():
     assert abs(grads["micro"][0] - grads["whole"][0]) < 1e-5
     for x, y in zip(grads["micro"][1], grads["whole"][1]):
         assert torch.allclose(x, y, rtol=1e-4, atol=1e-6)
+
+
+def test_fp32_master_weights_step():
+    """fp32 master weights: the optimizer steps fp32 copies and writes them
+    back into the bf16 parameters, which then equal the masters rounded."""
+    from cdl_b200.train import qat
+
+    spec, cpu = qat.SPECS["tiny"], torch.device("cpu")
+    st = qat.QatStep(spec, cpu, backend="none", lr=1e-2, seed=0, fp32_master_weights=True)
+    assert st.master_pairs and all(m.dtype == torch.float32 for _, m in st.master_pairs)
+    p, m = st.master_pairs[3]
+    before = p.detach().clone()
+    ids = torch.randint(0, spec.vocab, (2, 16), generator=torch.Generator().manual_seed(0))
+    st.step(ids)
+    assert not torch.equal(p.detach(), before) and torch.equal(p.detach(), m.detach().to(p.dtype))
+    assert all(q.grad is None for q in st.params)
