@@ -30,6 +30,7 @@ def into_orig_mod(model: nn.Module) -> nn.Module:
 
 
 def save_checkpoint(path: Path, model: nn.Module, optimizer, lr_scheduler, epoch: int, global_step: int) -> None:
+    """``lr_scheduler`` may be None (no schedule): its entry is then empty."""
     path = Path(path)
     tmp = path.with_suffix(path.suffix + ".tmp")
     torch.save({
@@ -37,7 +38,7 @@ def save_checkpoint(path: Path, model: nn.Module, optimizer, lr_scheduler, epoch
         "global_step": global_step,
         "model": into_orig_mod(model).state_dict(),
         "optimizer": optimizer.state_dict(),
-        "lr_scheduler": lr_scheduler.state_dict(),
+        "lr_scheduler": lr_scheduler.state_dict() if lr_scheduler is not None else {},
         "rng": {
             "python": random.getstate(),
             "torch": torch.get_rng_state(),
@@ -50,11 +51,13 @@ def save_checkpoint(path: Path, model: nn.Module, optimizer, lr_scheduler, epoch
 
 def load_checkpoint(resume_dir: Path, model: nn.Module, optimizer, lr_scheduler,
                     device: torch.device) -> tuple[int, int]:
-    """Restore ``resume_dir/last.ckpt``; returns (next epoch, global step)."""
+    """Restore ``resume_dir/last.ckpt``; returns (next epoch, global step).
+    ``lr_scheduler`` may be None (no schedule)."""
     ckpt = torch.load(Path(resume_dir) / "last.ckpt", map_location=device, weights_only=False)
     into_orig_mod(model).load_state_dict(ckpt["model"])
     optimizer.load_state_dict(ckpt["optimizer"])
-    lr_scheduler.load_state_dict(ckpt["lr_scheduler"])
+    if lr_scheduler is not None:
+        lr_scheduler.load_state_dict(ckpt["lr_scheduler"])
     random.setstate(ckpt["rng"]["python"])
     torch.set_rng_state(ckpt["rng"]["torch"].cpu())
     if torch.device(device).type == "cuda" and ckpt["rng"]["cuda"] is not None:

@@ -3,8 +3,9 @@
 Mirrors what cdl's training driver does per micro-batch (smollm2.py:667-677
 ``lm_loss``, :638-659 ``_step_optimizer``, :408-424 ``apply_quant``): every
 ``q/k/v/o/gate/up/down_proj`` linear of a Llama decoder becomes a
-``QLinear`` whose activation and weight pass through ``SteQuant`` and whose
-matmul backend is ``nvfp4`` (or ``mxfp4`` / ``mxfp8`` / ``native``); the loss
+``QLinear`` whose activation and weight pass through ``SteQuant`` (or one of
+cdl's CCDL / ECDL quantizer variants) and whose matmul backend is ``nvfp4``
+(or ``mxfp4`` / ``mxfp8`` / ``native``); the loss
 is next-token cross entropy through the unquantized LM head, computed the way
 cdl's Liger fused linear cross entropy does it (chunks of tokens; the logits
 are never materialised for the whole batch, and the gradients of the hidden
@@ -14,6 +15,11 @@ three launches of ``cdlb200_clip_adamw`` (``train/optim.py``).
 
 Models are built from the BASELINE configurations with random init (std
 0.02) -- no checkpoint is loaded -- and trained on uniform random tokens.
+
+The options of cdl's script around the step are here too: LoRA and its
+freeze policy, the warmup / cosine LR schedule, gradient accumulation, fp32
+master weights, ``evaluate`` (perplexity) and ``run_training`` (its loop with
+checkpoints and evaluation).
 
 Data parallel: one process per GPU; the model is wrapped in
 ``DistributedDataParallel`` (NCCL), which all-reduces the bf16 gradients in
@@ -507,6 +513,69 @@ class QatStep:
         self._graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self._graph):
             self._static_out = self._eager_step(self._static_ids)
+
+
+def run_training(step: QatStep, train_batches, *, epochs: int = 1, grad_accum_steps: int = 1, max_steps: int = 0,
+                 start_step: int = 0, test_batches=None, eval_every: int = 0, save_every: int = 0,
+                 checkpoint_path=None, log_every: int = 0, log=None) -> int:
+    """cdl's training loop (smollm2.py:779-927) around a ``QatStep``:
+    ``grad_accum_steps`` batches per optimizer step (a shorter window at the
+    end of an epoch), stop at ``max_steps``, resume by skipping the batches
+    of ``start_step`` steps, a checkpoint every ``save_every`` steps and at
+    the end (``cdl_b200.train.checkpoint``), perplexity on ``test_batches``
+    every ``eval_every`` steps and at the end.  ``train_batches`` is
+    re-iterated each epoch (a ``DeviceBlockLoader`` or any iterable of token
+    batches); ``log(step, loss, grad_norm, lr)`` runs every ``log_every``
+    steps (its arguments are device tensors but ``lr``).  Returns the global
+    step reached."""
+    from cdl_b200.train.checkpoint import save_checkpoint
+
+    def save(epoch, gs):
+        if checkpoint_path is not None:
+            save_checkpoint(checkpoint_path, step.model, step.opt, step.lr_scheduler, epoch, gs)
+
+    n_batches = len(train_batches)
+    per_epoch = -(-n_batches // grad_accum_steps)
+    start_epoch = min(start_step // per_epoch, epochs - 1) if per_epoch else 0
+    skip = max(start_step - start_epoch * per_epoch, 0) * grad_accum_steps
+    gs, last_saved, last_eval, epoch = start_step, -1, -1, start_epoch
+    for epoch in range(start_epoch, epochs):
+        step.model.train()
+        window: list = []
+        it = iter(train_batches)
+        for i, ids in enumerate(it):
+            if i < skip:
+                continue
+            if not window:
+                width = min(grad_accum_steps, n_batches - i)
+            window.append(ids)
+            if len(window) < width:
+                continue
+            loss, gnorm = step.step(window if len(window) > 1 else window[0])
+            window = []
+            gs += 1
+            if log is not None and log_every > 0 and gs % log_every == 0:
+                log(gs, loss, gnorm, step.opt.param_groups[0]["lr"])
+            if save_every > 0 and gs % save_every == 0:
+                save(epoch, gs)
+                last_saved = gs
+            if test_batches is not None and eval_every > 0 and gs % eval_every == 0:
+                ppl = evaluate(step.model, test_batches, step.device)
+                last_eval = gs
+                if log is not None:
+                    log(gs, None, None, ppl)
+            if max_steps and gs >= max_steps:
+                break
+        skip = 0
+        if max_steps and gs >= max_steps:
+            break
+    if gs != last_saved:
+        save(min(epoch, epochs - 1), gs)
+    if test_batches is not None and gs != last_eval:
+        ppl = evaluate(step.model, test_batches, step.device)
+        if log is not None:
+            log(gs, None, None, ppl)
+    return gs
 
 
 def random_tokens(batch: int, seq: int, vocab: int, seed: int, device: torch.device) -> torch.Tensor:

@@ -144,3 +144,41 @@ def test_fp32_master_weights_step():
     st.step(ids)
     assert not torch.equal(p.detach(), before) and torch.equal(p.detach(), m.detach().to(p.dtype))
     assert all(q.grad is None for q in st.params)
+
+
+def test_run_training_loop_checkpoints_and_resumes(tmp_path):
+    """cdl's loop around the step: accumulation windows, max_steps, periodic
+    checkpoint and evaluation, logging, then a resume from the checkpoint
+    that continues the step count (unquantized tiny model on CPU)."""
+    import numpy as np
+
+    from cdl_b200.data import DeviceBlockLoader, build_from_tokens
+    from cdl_b200.train import qat
+    from cdl_b200.train.checkpoint import load_checkpoint
+
+    spec, cpu = qat.SPECS["tiny"], torch.device("cpu")
+    toks = np.random.default_rng(0).integers(0, spec.vocab, 32 * 20)
+    cache = build_from_tokens(tmp_path / "cache", toks, seq_len=32, num_test_blocks=4)
+    train = DeviceBlockLoader(cache.train_dataset, 2, "cpu")
+    test = DeviceBlockLoader(cache.test_dataset, 2, "cpu", shuffle=False)
+    logs = []
+    st = qat.QatStep(spec, cpu, backend="none", lr=1e-3, seed=0, warmup_steps=2)
+    gs = qat.run_training(st, train, grad_accum_steps=2, max_steps=3, test_batches=test, eval_every=2,
+                          save_every=2, checkpoint_path=tmp_path / "last.ckpt", log_every=1,
+                          log=lambda *a: logs.append(a))
+    assert gs == 3
+    train_logs = [a for a in logs if a[1] is not None]
+    evals = [a for a in logs if a[1] is None]
+    assert [a[0] for a in train_logs] == [1, 2, 3] and [a[0] for a in evals] == [2, 3]
+    assert all(1.0 < a[3] < 2 * spec.vocab for a in evals)  # perplexities
+    ck = torch.load(tmp_path / "last.ckpt", weights_only=False)
+    assert ck["global_step"] == 3 and ck["lr_scheduler"]["last_epoch"] == 3
+
+    st2 = qat.QatStep(spec, cpu, backend="none", lr=1e-3, seed=1, warmup_steps=2)
+    _, start = load_checkpoint(tmp_path, st2.model, st2.opt, st2.lr_scheduler, cpu)
+    assert start == 3
+    for a, b in zip(st.model.parameters(), st2.model.parameters()):
+        assert torch.equal(a.detach(), b.detach())
+    # 8 batches = 4 steps per epoch: the resumed run ends its first epoch at step 4
+    assert qat.run_training(st2, train, grad_accum_steps=2, start_step=start, max_steps=10) == 4
+    assert qat.run_training(st2, train, epochs=2, grad_accum_steps=2, start_step=4, max_steps=6) == 6
