@@ -29,7 +29,6 @@ own activations (per-rank amax, as a single-GPU run would).
 
 from __future__ import annotations
 
-import contextlib
 import math
 from dataclasses import dataclass
 
@@ -451,11 +450,11 @@ class QatStep:
             if n == 0:
                 raise ValueError("no micro-batches")
             loss = None
-            for i, ids in enumerate(micro):
-                sync = i == n - 1 or not hasattr(self.net, "no_sync")
-                with contextlib.nullcontext() if sync else self.net.no_sync():
-                    part = self.net(ids)
-                    (part / n if n > 1 else part).backward()
+            for ids in micro:
+                # with DDP every micro-batch all-reduces: the static-graph DDP
+                # wrapper used here has no no_sync(), and averaging is linear
+                part = self.net(ids)
+                (part / n if n > 1 else part).backward()
                 part = part.detach() / n if n > 1 else part.detach()
                 loss = part if loss is None else loss + part
         if self.optimizer == "fused":
@@ -485,8 +484,8 @@ class QatStep:
     def step(self, input_ids) -> tuple[torch.Tensor, torch.Tensor]:
         """One training step on a batch of token ids, or on a list of
         micro-batches whose gradients are accumulated (each loss divided by
-        their count; with data parallelism only the last one all-reduces)
-        before one optimizer step; the returned loss is their mean.  In graph
+        their count; with data parallelism each one all-reduces) before one
+        optimizer step; the returned loss is their mean.  In graph
         mode (one batch per step) the first call runs warm-up steps
         on a side stream and captures the whole step (forward, backward,
         clipping, AdamW) in a CUDA graph; every call then copies the tokens

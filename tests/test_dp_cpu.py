@@ -1,6 +1,6 @@
 """Data-parallel step logic on CPU ranks (gloo): DDP-averaged gradients give
 every rank the same parameters, equal to one process stepping on the whole
-batch; a failing rank surfaces as an error, not a hang."""
+batch, also with gradient accumulation over micro-batches; a failing rank surfaces as an error, not a hang."""
 
 import os
 import socket
@@ -19,7 +19,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, out_dir, fail_rank):
+def _worker(rank, world, port, out_dir, fail_rank, accum=False):
     import datetime
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -34,16 +34,18 @@ def _worker(rank, world, port, out_dir, fail_rank):
     if rank == fail_rank:
         raise RuntimeError("injected rank failure")
     for _ in range(2):
-        step.step(mine)
+        # accum: two micro-batches of one sequence each
+        step.step([mine[:1], mine[1:]] if accum else mine)
     flat = torch.cat([p.detach().float().reshape(-1) for p in step.model.parameters()])
     torch.save(flat, os.path.join(out_dir, f"rank{rank}.pt"))
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_ddp_two_ranks_match_single_process(tmp_path):
+@pytest.mark.parametrize("accum", [False, True])
+def test_ddp_two_ranks_match_single_process(tmp_path, accum):
     port = _free_port()
-    mp.spawn(_worker, args=(2, port, str(tmp_path), -1), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, port, str(tmp_path), -1, accum), nprocs=2, join=True)
     p0 = torch.load(tmp_path / "rank0.pt")
     p1 = torch.load(tmp_path / "rank1.pt")
     assert torch.equal(p0, p1)
