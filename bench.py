@@ -2,7 +2,7 @@
 """Benchmark of the cdl_b200 hot path; prints ONE JSON line on rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload nvfp4_quant|mxfp4_quant|mxfp8_quant|fp4_gemm|qat_135m|qat_1.7b]
+                    [--workload nvfp4_quant|mxfp4_quant|mxfp8_quant|fp4_gemm|qat_135m|qat_1.7b|nvfp4_ecdl|nvfp4_ccdl]
 
 Workloads (synthetic data everywhere):
 
@@ -55,8 +55,10 @@ QUANT = {
     "mxfp4_quant": ("mxfp4", 16384, 8192, 2.53125, "C2"),
     "mxfp8_quant": ("mxfp8", 16384, 8192, 3.03125, "C2"),
 }
-WORKLOADS = sorted(list(QUANT) + ["fp4_gemm", "qat_135m", "qat_1.7b", "nvfp4_ecdl"])
+WORKLOADS = sorted(list(QUANT) + ["fp4_gemm", "qat_135m", "qat_1.7b", "nvfp4_ecdl", "nvfp4_ccdl"])
 ECDL_TOPK, ECDL_KAPPA = 5, 4.0  # theta_topk default of cdl's training config (smollm2.py:168)
+CCDL_TOPK, CCDL_KAPPA = 5, 2.0  # cdl's training defaults (theta_topk = q_topk = 5, kappa 2)
+CCDL_BPE = 2.0 + 4.0 / 16 + 0.5 + 1.0 / 16  # x, q (fp32 per block), codes, scale bytes
 
 
 def parse_args():
@@ -208,6 +210,77 @@ def cpu_ecdl_rate(rows, k, threads, target_s=10.0):
     dt = time.perf_counter() - t0
     return (2.5625 * sample_rows * k * cnt / dt / 1e9,
             f"{cnt} x NVFP4 ECDL forward (numpy oracle) of {sample_rows}x{k} of C1 (1 thread)")
+
+
+def _ccdl_q(x):
+    """Per-block learnable scales as a CCDL weight quantizer initialises them:
+    block amax / 6 (fp32), alpha 1."""
+    return (x.float().abs().amax(-1) / 6.0).clamp_min(2.0 ** -126)
+
+
+def cpu_ccdl_rate(rows, k, threads, target_s=10.0):
+    """The CCDL oracle (numpy restatement) on a bounded row sample of C1."""
+    import numpy as np
+
+    from cdl_b200 import workloads
+    from oracle import ecdl as E
+
+    x = workloads.c1_nvfp4(rows, k, seed=0).reshape(rows, k // 16, 16)
+    q = _ccdl_q(x).numpy()
+    x = x.float().numpy()
+    sample_rows = 64
+    t0, cnt = time.perf_counter(), 0
+    while cnt < 1 or time.perf_counter() - t0 < target_s:
+        E.ccdl_forward(E.NVFP4, x[:sample_rows], q[:sample_rows], CCDL_KAPPA, CCDL_KAPPA, 1.0, cnt + 1, CCDL_TOPK,
+                       CCDL_TOPK)
+        cnt += 1
+    dt = time.perf_counter() - t0
+    return (CCDL_BPE * sample_rows * k * cnt / dt / 1e9,
+            f"{cnt} x NVFP4 CCDL forward (numpy oracle) of {sample_rows}x{k} of C1 (1 thread)")
+
+
+def ccdl_workload(dev, rank):
+    import torch
+
+    from cdl_b200 import workloads
+    from cdl_b200.core.kernel.ccdl import ccdl_quant_fwd
+    from cdl_b200.core.kernel.ecdl import FormatId
+
+    rows, k = QUANT["nvfp4_quant"][1:3]
+    pool_n = max(2, -(-2 * L2_BYTES // (rows * k * 2)))
+    pool = [workloads.c1_nvfp4(rows, k, seed=1000 * rank + i, device=str(dev)).reshape(rows, k // 16, 16)
+            for i in range(pool_n)]
+    qs = [_ccdl_q(x) for x in pool]
+    kt = torch.tensor(CCDL_KAPPA, device=dev)
+    kq = torch.tensor(CCDL_KAPPA, device=dev)
+    alpha = torch.ones((), device=dev)
+    seeds = [torch.tensor(i + 1, dtype=torch.int64, device=dev) for i in range(pool_n)]
+    host_in, host_q = pool[0].cpu().pin_memory(), qs[0].cpu().pin_memory()
+
+    def run(x, q, seed):
+        return ccdl_quant_fwd(x, q, kt, kq, alpha, seed, int(FormatId.NVFP4), CCDL_TOPK, CCDL_TOPK)
+
+    p0, s0 = run(pool[0], qs[0], seeds[0])
+    host_p = torch.empty(p0.shape, dtype=p0.dtype, pin_memory=True)
+    host_s = torch.empty(s0.shape, dtype=s0.dtype, pin_memory=True)
+
+    def e2e_step():
+        p, s_ = run(host_in.to(dev, non_blocking=True), host_q.to(dev, non_blocking=True), seeds[0])
+        host_p.copy_(p, non_blocking=True)
+        host_s.copy_(s_, non_blocking=True)
+
+    return {
+        "step": lambda i: run(pool[i % pool_n], qs[i % pool_n], seeds[i % pool_n]),
+        "e2e_step": e2e_step, "graph": True,
+        "units_per_step": CCDL_BPE * rows * k / 1e9, "unit": "GB/s", "metric": "NVFP4 CCDL quant GB/s",
+        "dtype": "bf16->e2m1 with sampled ue4m3 scales (stochastic, Philox)",
+        "config": {"workload": f"nvfp4_ccdl C1 [{rows},{k}] bf16 per rank, theta_topk {CCDL_TOPK}, q_topk "
+                               f"{CCDL_TOPK}, kappa {CCDL_KAPPA}, q from block amax",
+                   "l2": f"inputs cycled over {pool_n} tensors (> 2x L2)"},
+        "h2d": host_in.numel() * 2 + host_q.numel() * 4, "d2h": p0.numel() + s0.numel(),
+        "bound": "hbm", "kernel": "ccdl_fwd_kernel",
+        "launches_per_step": 1,
+    }
 
 
 def ecdl_workload(dev, rank):
@@ -514,6 +587,9 @@ def main() -> None:
         elif wl == "nvfp4_ecdl":
             val, sample = cpu_ecdl_rate(4096, 4096, threads, target_s=5.0)
             unit, metric = "GB/s", "NVFP4 ECDL quant GB/s"
+        elif wl == "nvfp4_ccdl":
+            val, sample = cpu_ccdl_rate(4096, 4096, threads, target_s=5.0)
+            unit, metric = "GB/s", "NVFP4 CCDL quant GB/s"
         else:
             val, sample = cpu_qat_rate("135m" if wl == "qat_135m" else "1.7b", threads, target_s=10.0)
             unit, metric = "tokens/s", "SmolLM2 NVFP4 QAT tokens/s"
@@ -542,6 +618,8 @@ def main() -> None:
         w = gemm_workload(dev, rank)
     elif wl == "nvfp4_ecdl":
         w = ecdl_workload(dev, rank)
+    elif wl == "nvfp4_ccdl":
+        w = ccdl_workload(dev, rank)
     else:
         w = qat_workload(wl, dev, rank, world, args.backend)
 
@@ -618,6 +696,8 @@ def main() -> None:
             val, sample = cpu_gemm_rate(threads, target_s=10.0)
         elif wl == "nvfp4_ecdl":
             val, sample = cpu_ecdl_rate(4096, 4096, threads, target_s=10.0)
+        elif wl == "nvfp4_ccdl":
+            val, sample = cpu_ccdl_rate(4096, 4096, threads, target_s=10.0)
         else:
             val, sample = cpu_qat_rate("135m" if wl == "qat_135m" else "1.7b", threads, target_s=10.0)
         cpu = {"value": round(val, 4), "unit": w["unit"], "cores": threads, "kind": "port", "sample": sample}

@@ -524,7 +524,7 @@ struct CcdlArgs {
 
 __device__ __forceinline__ int q_grid(int fmt) { return fmt == CDLB200_ECDL_NVFP4 ? 126 : 255; }
 
-template <typename T>
+template <typename T, int K>
 __global__ void __launch_bounds__(kEcdlThreads) ccdl_fwd_kernel(const T* __restrict__ theta, CcdlArgs a,
                                                                 const int64_t* __restrict__ seed_p,
                                                                 uint8_t* __restrict__ packed,
@@ -557,8 +557,8 @@ __global__ void __launch_bounds__(kEcdlThreads) ccdl_fwd_kernel(const T* __restr
         float x0, x1;
         load2(theta, 2 * p, x0, x1);
         const float u0 = rand_uniform((uint32_t)(2 * p), seed), u1 = rand_uniform((uint32_t)(2 * p + 1), seed);
-        const int i0 = cdl_sample(__fdiv_rn(x0, s), kt, u0, lev, gap, f.tn, a.topk);
-        const int i1 = cdl_sample(__fdiv_rn(x1, s), kt, u1, lev, gap, f.tn, a.topk);
+        const int i0 = sample_dispatch<K>(__fdiv_rn(x0, s), kt, u0, lev, gap, f.tn, a.topk);
+        const int i1 = sample_dispatch<K>(__fdiv_rn(x1, s), kt, u1, lev, gap, f.tn, a.topk);
         if (f.tn == 16) {
             const uint32_t c0 = i0 < 8 ? 15 - i0 : i0 - 8, c1 = i1 < 8 ? 15 - i1 : i1 - 8;
             packed[p] = (uint8_t)(c0 | (c1 << 4));
@@ -714,6 +714,19 @@ void launch_fwd(const void* theta, int theta_f32, int64_t npairs, int format, in
                                                                     static_cast<uint8_t*>(scale), alpha);
 }
 
+template <int K>
+void launch_ccdl_fwd(const void* theta, int theta_f32, const CcdlArgs& a, const int64_t* seed, void* packed,
+                     void* scale, int grid, cudaStream_t st) {
+    if (theta_f32)
+        ccdl_fwd_kernel<float, K><<<grid, kEcdlThreads, 0, st>>>(static_cast<const float*>(theta), a, seed,
+                                                                 static_cast<uint8_t*>(packed),
+                                                                 static_cast<uint8_t*>(scale));
+    else
+        ccdl_fwd_kernel<uint16_t, K><<<grid, kEcdlThreads, 0, st>>>(static_cast<const uint16_t*>(theta), a, seed,
+                                                                    static_cast<uint8_t*>(packed),
+                                                                    static_cast<uint8_t*>(scale));
+}
+
 int ecdl_grid(int64_t npairs) {
     const int64_t cap = (int64_t)num_sms() * 8;
     const int64_t g = (npairs + kEcdlThreads - 1) / kEcdlThreads;
@@ -839,14 +852,14 @@ extern "C" int cdlb200_ccdl_fwd(const void* theta, int theta_f32, int64_t rows, 
     a.alpha = alpha;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int grid = ecdl_grid(a.npairs);
-    if (theta_f32)
-        ccdl_fwd_kernel<float><<<grid, kEcdlThreads, 0, st>>>(static_cast<const float*>(theta), a, seed,
-                                                              static_cast<uint8_t*>(packed),
-                                                              static_cast<uint8_t*>(scale));
-    else
-        ccdl_fwd_kernel<uint16_t><<<grid, kEcdlThreads, 0, st>>>(static_cast<const uint16_t*>(theta), a, seed,
-                                                                 static_cast<uint8_t*>(packed),
-                                                                 static_cast<uint8_t*>(scale));
+    switch (theta_topk) {  // the theta window width as a compile-time constant where common
+        case 4: launch_ccdl_fwd<4>(theta, theta_f32, a, seed, packed, scale, grid, st); break;
+        case 5: launch_ccdl_fwd<5>(theta, theta_f32, a, seed, packed, scale, grid, st); break;
+        case 6: launch_ccdl_fwd<6>(theta, theta_f32, a, seed, packed, scale, grid, st); break;
+        case 8: launch_ccdl_fwd<8>(theta, theta_f32, a, seed, packed, scale, grid, st); break;
+        case 16: launch_ccdl_fwd<16>(theta, theta_f32, a, seed, packed, scale, grid, st); break;
+        default: launch_ccdl_fwd<0>(theta, theta_f32, a, seed, packed, scale, grid, st); break;
+    }
     CDLB200_CHECK_LAUNCH();
     return CDLB200_OK;
 }
