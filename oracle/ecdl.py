@@ -20,7 +20,12 @@ with the uniform numbers of Triton's ``tl.rand(seed, offset)``: Philox4x32-10
 and key ``(seed_lo, seed_hi)``, first output word, mapped to [0, 1) as
 ``(x < 0 ? -x - 1 : x) * 4.6566127342e-10`` on its int32 view (Triton
 ``python/triton/language/random.py``, 3.x).  Checked against the Random123
-known-answer vectors in ``tests/test_ecdl_cpu.py``.
+known-answer vectors in ``tests/test_ecdl_cpu.py``; the window, the sampling
+probabilities, the expected level and its derivatives against the
+reference's torch formulae (``cdl/core/formulae.py`` topk_cpmf_companded /
+topk_q_d and their autograd gradients; ``tests/golden/cdl_window.npz``, made
+by ``tests/golden/make_cdl_golden.py``); the CCDL eval round against the
+reference's ``cascaded_nearest_round`` (``tests/golden/ccdl_round.npz``).
 
 Parity of the sampled codes is statistical at the edges: an element whose
 ``u * z`` falls within float rounding of a cumulative boundary may pick the

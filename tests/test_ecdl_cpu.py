@@ -128,3 +128,34 @@ def test_ccdl_round_oracle_matches_reference_golden():
                                      bool(c["theta_bf16"]), bool(c["levels_bf16"]))
         np.testing.assert_array_equal(packed, c["packed"])
         np.testing.assert_array_equal(scale, c["scale"])
+
+
+def test_window_probabilities_and_proxy_match_reference_formulae():
+    """The oracle's CDL window, sampling distribution, expected level and
+    proxy derivatives against the reference's own torch formulae
+    (topk_cpmf_companded / topk_q_d and their autograd gradients, fp32;
+    tests/golden/cdl_window.npz): window starts equal, probabilities within
+    3e-7, the expected level within 2e-6 relative, the derivatives within
+    fp32 rounding of the sums they are formed from (terms of size
+    max|level| * kappa * dmax / gap for d/dx, max|level| * dmax^2 for
+    d/dkappa, dmax the farthest window level)."""
+    import os
+
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "cdl_window.npz"))
+    assert int(z["count"]) == 18
+    for i in range(int(z["count"])):
+        c = {k.split("_", 1)[1]: z[k] for k in z.files if k.startswith(f"c{i}_")}
+        f = E.Format(E.NVFP4 if str(c["fmt"]) == "e2m1" else E.MXFP8)
+        v, kappa, topk = c["v"], float(c["kappa"]), int(c["topk"])
+        start, p = E.probabilities(f, v, kappa, topk)
+        assert np.array_equal(start, c["start"])
+        assert float(np.abs(p - c["pmf"]).max()) < 3e-7
+        lv = np.stack([f.level[start + j] for j in range(topk)], -1)
+        ev = (p * lv).sum(-1)
+        assert float(np.max(np.abs(ev - c["ev"]) / np.maximum(np.abs(c["ev"]), 1e-3))) < 2e-6
+        dth, _, dk = E.proxy_coeffs(f, v, kappa, topk)
+        cpos, _, kgap = E._window(f, v, topk)
+        dmax = np.max(np.abs(cpos[:, None] - (start[:, None] + np.arange(topk))), -1) + 1.0
+        top = float(np.abs(f.level).max())
+        assert np.all(np.abs(dth - c["dv"]) <= 1e-5 * top * kappa * dmax / kgap + 1e-7), i
+        assert np.all(np.abs(dk - c["dk"]) <= 1e-5 * top * dmax ** 2 + 1e-7), i
