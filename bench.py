@@ -76,6 +76,9 @@ def parse_args():
     ap.add_argument("--backend", default="nvfp4", choices=["nvfp4", "nvfp4_qbwd", "mxfp4", "mxfp8"],
                     help="QAT workloads: QLinear backend (nvfp4 = cdl's numerics: bf16 backward)")
     ap.add_argument("--spinup-s", type=float, default=1.0, help="untimed clock ramp before warm-up")
+    ap.add_argument("--gemm-shape", default="8192,8192,8192", metavar="M,N,K",
+                    help="fp4_gemm: the GEMM shape (C3 is 8192^3; its sweep: M in {2048, 16384} x "
+                         "(N, K) in {(2048, 8192), (8192, 2048), (49152, 576)})")
     a = ap.parse_args()
     qat = a.workload.startswith("qat")
     if a.steps is None:
@@ -408,7 +411,7 @@ def quant_workload(name, dev, rank):
     }
 
 
-def gemm_workload(dev, rank):
+def gemm_workload(dev, rank, shape=(8192, 8192, 8192)):
     import torch
 
     from cdl_b200 import workloads
@@ -416,8 +419,8 @@ def gemm_workload(dev, rank):
     from cdl_b200.core.mm.swizzle import swizzle_scale_factors
     from cdl_b200.model.wrapper.ops import mm_fp4
 
-    m = n = k = 8192
-    pool_n = 2  # 2 x (128 MiB bf16 A) > L2
+    m, n, k = shape
+    pool_n = max(2, -(-2 * L2_BYTES // (m * k * 2)))  # bf16 A cycled over more than twice L2
     pool = []
     for i in range(pool_n):
         a, w = workloads.c3_gemm(m, n, k, seed=100 * rank + i, device=str(dev))
@@ -449,7 +452,7 @@ def gemm_workload(dev, rank):
         "units_per_step": 2.0 * m * n * k / 1e12, "unit": "TFLOP/s", "metric": "FP4 GEMM TFLOPS",
         "dtype": "e2m1 x e2m1 (ue4m3 block scales) -> fp32 acc -> bf16",
         "config": {"workload": f"fp4_gemm C3 NVFP4 {m}x{n}x{k}: quantize bf16 A + tcgen05 GEMM vs pre-quantized W",
-                   "l2": f"A cycled over {pool_n} tensors of 128 MiB (> L2)"},
+                   "l2": f"A cycled over {pool_n} tensors of {m * k * 2 / 2**20:.0f} MiB (> 2x L2 in total)"},
         "h2d": host_a.numel() * 2, "d2h": m * n * 2, "bound": "tensor",
         "kernel": "bs_gemm_pair_kernel<NVFP4> (persistent 2-SM tcgen05 block-scaled GEMM)",
         "launches_per_step": 3,  # nvfp4_fused_kernel (A), the GEMM, the alpha product
@@ -615,7 +618,7 @@ def main() -> None:
     if wl in QUANT:
         w = quant_workload(wl, dev, rank)
     elif wl == "fp4_gemm":
-        w = gemm_workload(dev, rank)
+        w = gemm_workload(dev, rank, tuple(int(v) for v in args.gemm_shape.split(",")))
     elif wl == "nvfp4_ecdl":
         w = ecdl_workload(dev, rank)
     elif wl == "nvfp4_ccdl":
