@@ -379,6 +379,8 @@ class QatStep:
         self.optimizer = optimizer or ("fused" if on_cuda and not quant_ids and not fp32_master_weights else "torch")
         if self.optimizer == "fused" and fp32_master_weights:
             raise ValueError("fp32 master weights need optimizer='torch'")
+        if self.optimizer == "fused" and quant_ids:
+            raise ValueError("the fused optimizer takes bf16 parameters only; CDL quantizers need optimizer='torch'")
         # fp32 master copies of the non-fp32 parameters, which the optimizer
         # updates and copies back (smollm2.py:569-575, 649-657)
         self.master_pairs: list[tuple[nn.Parameter, nn.Parameter]] = []
@@ -393,8 +395,6 @@ class QatStep:
         if fp32_master_weights:
             decay, no_decay = [opt_param(p) for p in decay], [opt_param(p) for p in no_decay]
             quant_params = [opt_param(p) for p in quant_params]
-        if self.optimizer == "fused" and quant_ids:
-            raise ValueError("the fused optimizer takes bf16 parameters only; CDL quantizers need optimizer='torch'")
         if self.optimizer == "fused":
             from cdl_b200.train.optim import ClipAdamW
 
