@@ -70,3 +70,28 @@ def test_python_api_refuses_cpu_tensors():
         quant.nvfp4_quant(torch.randn(2, 3, 4).bfloat16())
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         dequant.nvfp4_dequant(torch.zeros(4, 16, dtype=torch.uint8), torch.zeros(4, 2, dtype=torch.uint8), torch.ones(1))
+
+
+def test_cdl_entry_points_validate_arguments_on_the_host():
+    """ECDL / CCDL entry points reject bad formats, window widths, strides,
+    null buffers and misalignment before touching the GPU, and treat empty
+    problems as no-ops."""
+    lib = _lib.lib()
+    bad, ok, align = _lib.ERR_INVALID_ARG, _lib.OK, _lib.ERR_ALIGNMENT
+    d = ctypes.c_void_p(256)
+    # cdlb200_ccdl_round(theta, theta_f32, rows, nb, format, q, q_stride, alpha, levels_bf16, packed, scale, stream)
+    assert lib.cdlb200_ccdl_round(d, 0, 4, 2, 7, d, 2, d, 1, d, d, None) == bad          # unknown format
+    assert lib.cdlb200_ccdl_round(d, 0, 4, 2, 0, d, 3, d, 1, d, d, None) == bad          # q_stride not 0 / nb
+    assert lib.cdlb200_ccdl_round(d, 0, -1, 2, 0, d, 2, d, 1, d, d, None) == bad         # negative rows
+    assert lib.cdlb200_ccdl_round(None, 0, 4, 2, 0, d, 2, d, 1, d, d, None) == bad       # null theta
+    assert lib.cdlb200_ccdl_round(ctypes.c_void_p(258), 0, 4, 2, 0, d, 2, d, 1, d, d, None) == align
+    assert lib.cdlb200_ccdl_round(None, 0, 0, 2, 0, None, 2, None, 1, None, None, None) == ok  # empty
+    # cdlb200_ccdl_fwd: theta window wider than the grid, q window wider than the scale grid
+    assert lib.cdlb200_ccdl_fwd(d, 0, 4, 2, 0, d, 2, d, d, d, d, 17, 5, d, d, None) == bad
+    assert lib.cdlb200_ccdl_fwd(d, 0, 4, 2, 0, d, 2, d, d, d, d, 5, 127, d, d, None) == bad
+    # cdlb200_ecdl_fwd: unknown scale mode; topk 0
+    assert lib.cdlb200_ecdl_fwd(d, 0, 4, 2, 0, 5, d, d, 5, d, d, d, d, None) == bad
+    assert lib.cdlb200_ecdl_fwd(d, 0, 4, 2, 0, 0, d, d, 0, d, d, d, d, None) == bad
+    # workspace sizes are host arithmetic
+    assert lib.cdlb200_ccdl_bwd_workspace_bytes(0, 4, 0) == 0
+    assert lib.cdlb200_ecdl_bwd_workspace_bytes(-1, 4, 0) == 0
