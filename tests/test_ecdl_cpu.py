@@ -130,6 +130,13 @@ def test_ccdl_round_oracle_matches_reference_golden():
         np.testing.assert_array_equal(scale, c["scale"])
 
 
+def _cdl_window_cases():
+    import os
+
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "cdl_window.npz"))
+    return [{k.split("_", 1)[1]: z[k] for k in z.files if k.startswith(f"c{i}_")} for i in range(int(z["count"]))]
+
+
 def test_window_probabilities_and_proxy_match_reference_formulae():
     """The oracle's CDL window, sampling distribution, expected level and
     proxy derivatives against the reference's own torch formulae
@@ -139,12 +146,9 @@ def test_window_probabilities_and_proxy_match_reference_formulae():
     fp32 rounding of the sums they are formed from (terms of size
     max|level| * kappa * dmax / gap for d/dx, max|level| * dmax^2 for
     d/dkappa, dmax the farthest window level)."""
-    import os
-
-    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "cdl_window.npz"))
-    assert int(z["count"]) == 18
-    for i in range(int(z["count"])):
-        c = {k.split("_", 1)[1]: z[k] for k in z.files if k.startswith(f"c{i}_")}
+    cases = [c for c in _cdl_window_cases() if str(c["fmt"]) in ("e2m1", "e4m3")]
+    assert len(cases) == 18
+    for i, c in enumerate(cases):
         f = E.Format(E.NVFP4 if str(c["fmt"]) == "e2m1" else E.MXFP8)
         v, kappa, topk = c["v"], float(c["kappa"]), int(c["topk"])
         start, p = E.probabilities(f, v, kappa, topk)
@@ -159,3 +163,31 @@ def test_window_probabilities_and_proxy_match_reference_formulae():
         top = float(np.abs(f.level).max())
         assert np.all(np.abs(dth - c["dv"]) <= 1e-5 * top * kappa * dmax / kgap + 1e-7), i
         assert np.all(np.abs(dk - c["dk"]) <= 1e-5 * top * dmax ** 2 + 1e-7), i
+
+
+def test_truncated_scale_window_matches_reference_formulae():
+    """The CCDL scale sampler's truncated window (UE4M3 without zero, E8M0)
+    against the reference's full-window torch formulae: window starts equal;
+    where the truncated window covers the whole top-k window, the expected
+    level and its derivatives agree to fp32 rounding of their terms (scaled by
+    the window's largest level); where it leaves out far levels, by at most
+    their weight, exp(-kappa (hq - 1/2)^2) each (the truncation the reference's
+    Triton primitive makes)."""
+    cases = [c for c in _cdl_window_cases() if str(c["fmt"]) in ("ue4m3", "e8m0")]
+    assert len(cases) == 12
+    for i, c in enumerate(cases):
+        f = E.QFormat(E.NVFP4 if str(c["fmt"]) == "ue4m3" else E.MXFP4)
+        v, kappa, topk = c["v"], float(c["kappa"]), int(c["topk"])
+        cpos, start, kgap = E._window(f, v, topk)
+        assert np.array_equal(start, c["start"]), i
+        dth, ds, dk = E.proxy_coeffs_truncated(f, v, kappa, topk)
+        ev = ds + v * dth
+        lmax = np.abs(np.stack([f.level[start + j] for j in range(topk)], -1)).max(-1)
+        dmax = np.max(np.abs(cpos[:, None] - (start[:, None] + np.arange(topk))), -1) + 1.0
+        hq = E._half_window(topk, kappa)
+        t_near, _ = E._near(cpos, start, topk, np.float32(kappa))
+        cut = np.maximum(start, t_near - hq) > start  # levels left out of the truncated window
+        tail = np.where(cut, topk * np.exp(-kappa * (hq - 0.5) ** 2), 0.0)
+        assert np.all(np.abs(ev - c["ev"]) <= lmax * (2e-6 + tail)), i
+        assert np.all(np.abs(dth - c["dv"]) <= lmax * kappa * dmax / kgap * (1e-5 + tail * dmax)), i
+        assert np.all(np.abs(dk - c["dk"]) <= lmax * dmax ** 2 * (1e-5 + tail)), i
