@@ -95,7 +95,7 @@ class PackedCcdlTensor(QTensor):
             scale = scale.expand(packed.shape[0], -1)
         if self.eval_dtype is not None:
             # (level * q_level) is exact; alpha enters rounded to the level
-            # dtype, as ``alpha.to(theta.dtype)`` in cdl (ccdl.py:42-47)
+            # dtype, as ``alpha.to(theta.dtype)`` in cdl (ccdl.py:43-48)
             alpha = alpha.to(self.eval_dtype).float()
         out = _SPECS[self.fmt].dequant(packed, scale, alpha)
         out = out.reshape(*lead, -1)[..., : self.k_dim]
@@ -119,7 +119,7 @@ class CascadedCdlBypassTensor(QTensor):
 
 
 class CascadedCdlQuant(Quant):
-    """One CCDL quantizer (ccdl.py:67-203)."""
+    """One CCDL quantizer (ccdl.py:67-207)."""
 
     def __init__(self, fmt: str, input_shape: tuple[int, ...], theta_topk: int, q_topk: int, dtype: torch.dtype,
                  kappa: float, kernel: Kernel = "triton"):
@@ -168,7 +168,7 @@ class CascadedCdlQuant(Quant):
     def alpha(self) -> torch.Tensor:
         return self.log_alpha.exp()
 
-    # learning rates (ccdl.py:118-126, 225-235, 257-265)
+    # learning rates (ccdl.py:124-134, 231-240, 264-273)
     def _lr_bits(self) -> int:
         return self.spec.theta_bits
 
@@ -192,7 +192,7 @@ class CascadedCdlQuant(Quant):
     @torch.no_grad()
     def init_q_from_block_amax(self, block_amax: torch.Tensor) -> None:
         """q = block amax / largest theta level, floored at the smallest
-        normal fp32, logarithm in the amax dtype (ccdl.py:134-138)."""
+        normal fp32, logarithm in the amax dtype (ccdl.py:141-144)."""
         top = torch.tensor(self.spec.q_max_theta, dtype=self.dtype, device=block_amax.device)
         q = block_amax / top
         self.copy_log_q(q.clamp_min(torch.finfo(torch.float32).tiny).log())
@@ -231,7 +231,7 @@ class CascadedCdlQuantForActivation(CascadedCdlQuant):
 
 class CascadedCdlQuantForWeight(CascadedCdlQuant):
     """Weight quantizer: samples from the whole grids, scales from the
-    weight's block amax (ccdl.py:238-276)."""
+    weight's block amax (ccdl.py:242-278)."""
 
     FMT = ""
 
@@ -275,7 +275,7 @@ class Mxfp8CascadedCdlQuantForWeight(CascadedCdlQuantForWeight):
 
 
 class CascadedCdlQuantMixin(nn.Module):
-    """Model-level helpers of cdl's ``CascadedCdlQuantMixin`` (ccdl.py:279-393):
+    """Model-level helpers of cdl's ``CascadedCdlQuantMixin`` (ccdl.py:280-393):
     quantized-element counts, statistics, optimizer parameter groups and the
     activation-scale calibration pass.  (cdl's mixin also puts BatchNorm2d
     layers in batch-statistics mode during calibration; the decoder models

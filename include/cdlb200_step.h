@@ -166,7 +166,7 @@ int cdlb200_ccdl_bwd(const void* grad, const void* theta, int theta_f32, int64_t
 
 /* CCDL deterministic (eval-mode) quantize, replacing the torch
  * cascaded_nearest_round of cdl/core/ccdl.py:78-89 that
- * CascadedCdlQuant.eval_forward (cdl/model/components/quant/ccdl/ccdl.py:147-162)
+ * CascadedCdlQuant.eval_forward (cdl/model/components/quant/ccdl/ccdl.py:146-162)
  * calls: q to its nearest scale level, s = level * alpha in the level dtype
  * (levels_bf16: rounded to bf16), theta to the nearest level of theta / s
  * (rounded to bf16 when theta and the levels are both bf16).  Same layouts

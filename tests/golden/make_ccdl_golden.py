@@ -7,7 +7,7 @@ levels, ``cdl/model/components/quant/ccdl/{nvfp4,mxfp4,mxfp8}.py``), on seeded
 inputs, packs the indices with the formats' ``pack`` and writes
 ``ccdl_round.npz`` beside this script: per case the theta values (fp32 holding
 values of the case's theta dtype), q, alpha, the packed codes and scale bytes,
-and for bf16 levels the eval tensor's ``dequantize()`` (ccdl.py:42-47).
+and for bf16 levels the eval tensor's ``dequantize()`` (ccdl.py:43-48).
 
 Usage: ``python tests/golden/make_ccdl_golden.py --reference <path to cdl/src>``.
 Needs the reference checkout; the committed outputs do not.
