@@ -130,7 +130,7 @@ def untie_and_freeze(model: nn.Module, *, freeze_all: bool = True, train_head: b
 
 
 def lr_lambda(warmup_steps: int = 0, lr_decay: str = "constant", max_steps: int = 0, min_lr_ratio: float = 0.1):
-    """cdl's learning-rate factor (smollm2.py:596-607): linear warmup to 1,
+    """cdl's learning-rate factor (smollm2.py:599-610): linear warmup to 1,
     then constant or a cosine down to ``min_lr_ratio`` at ``max_steps``."""
     if lr_decay not in ("constant", "cosine"):
         raise ValueError(f"unknown lr_decay {lr_decay!r}")
@@ -297,7 +297,7 @@ def lm_loss(model: nn.Module, input_ids: torch.Tensor, chunk: int = 2048) -> tor
 
 @torch.no_grad()
 def evaluate(model: nn.Module, loader, device: torch.device) -> float:
-    """Perplexity over ``loader``'s batches of token ids (smollm2.py:680-693):
+    """Perplexity over ``loader``'s batches of token ids (smollm2.py:681-694):
     exp of the token-weighted mean loss, in eval mode (deterministic
     quantizers).  The sum stays on the device until the end."""
     was_training = model.training
@@ -382,7 +382,7 @@ class QatStep:
         if self.optimizer == "fused" and quant_ids:
             raise ValueError("the fused optimizer takes bf16 parameters only; CDL quantizers need optimizer='torch'")
         # fp32 master copies of the non-fp32 parameters, which the optimizer
-        # updates and copies back (smollm2.py:569-575, 649-657)
+        # updates and copies back (smollm2.py:570-575, 649-657)
         self.master_pairs: list[tuple[nn.Parameter, nn.Parameter]] = []
 
         def opt_param(p):
@@ -444,7 +444,7 @@ class QatStep:
         if isinstance(input_ids, torch.Tensor):
             loss = self.net(input_ids)
             loss.backward()
-        else:  # gradient accumulation over micro-batches, as cdl's loop (smollm2.py:829-850)
+        else:  # gradient accumulation over micro-batches, as cdl's loop (smollm2.py:816-851)
             micro = list(input_ids)
             n = len(micro)
             if n == 0:
@@ -517,7 +517,7 @@ class QatStep:
 def run_training(step: QatStep, train_batches, *, epochs: int = 1, grad_accum_steps: int = 1, max_steps: int = 0,
                  start_step: int = 0, test_batches=None, eval_every: int = 0, save_every: int = 0,
                  checkpoint_path=None, log_every: int = 0, log=None) -> int:
-    """cdl's training loop (smollm2.py:779-927) around a ``QatStep``:
+    """cdl's training loop (smollm2.py:777-930) around a ``QatStep``:
     ``grad_accum_steps`` batches per optimizer step (a shorter window at the
     end of an epoch), stop at ``max_steps``, resume by skipping the batches
     of ``start_step`` steps, a checkpoint every ``save_every`` steps and at
