@@ -50,12 +50,20 @@ sys.path.insert(0, ROOT)
 L2_BYTES = 126 * 1024 * 1024
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 QUANT = {
-    # name: (fmt, rows, k, bytes per element, config id)
+    # name: (fmt, rows, k, bytes per element, config id[, transpose])
     "nvfp4_quant": ("nvfp4", 4096, 4096, 2.5625, "C1"),
     "mxfp4_quant": ("mxfp4", 16384, 8192, 2.53125, "C2"),
     "mxfp8_quant": ("mxfp8", 16384, 8192, 3.03125, "C2"),
+    # the transposed (dim-0) requantize of the wgrad operands, C2 shape
+    "mxfp4_quant_t": ("mxfp4", 16384, 8192, 2.53125, "C2 transposed", True),
+    "mxfp8_quant_t": ("mxfp8", 16384, 8192, 3.03125, "C2 transposed", True),
+    "nvfp4_quant_t": ("nvfp4", 16384, 8192, 2.5625, "C2 shape, transposed", True),
+    # NVFP4 on a tensor twice the size of L2 (C1's 32 MiB fits in L2)
+    "nvfp4_quant_large": ("nvfp4", 16384, 8192, 2.5625, "C2 shape"),
 }
-WORKLOADS = sorted(list(QUANT) + ["fp4_gemm", "qat_135m", "qat_1.7b", "nvfp4_ecdl", "nvfp4_ccdl"])
+WORKLOADS = sorted(list(QUANT) + ["fp4_gemm", "qat_135m", "qat_1.7b", "nvfp4_ecdl", "nvfp4_ccdl",
+                                  "nvfp4_encode_multi"])
+QAT_BATCH = {"qat_135m": (8, 2048), "qat_1.7b": (4, 2048)}  # configs C4 / C5, tokens per rank
 ECDL_TOPK, ECDL_KAPPA = 5, 4.0  # theta_topk default of cdl's training config (smollm2.py:168)
 CCDL_TOPK, CCDL_KAPPA = 5, 2.0  # cdl's training defaults (theta_topk = q_topk = 5, kappa 2)
 CCDL_BPE = 2.0 + 4.0 / 16 + 0.5 + 1.0 / 16  # x, q (fp32 per block), codes, scale bytes
@@ -348,27 +356,17 @@ def cpu_gemm_rate(threads, target_s=10.0):
             f"{cnt} x NVFP4 quantize(A) + dequantize + fp32 matmul at {m}^3 ({threads} threads)")
 
 
-def cpu_qat_rate(spec_name, threads, target_s=20.0):
-    """CPU restatement of the QAT step (unquantized, fp32 on CPU) at reduced size."""
-    import torch
-
+def cpu_qat_rate(workload, threads):
+    """The CPU NVFP4 QAT step with the reference's native-backend numerics
+    (``oracle/qat_cpu.py``): one step of the full model on a 1x256-token
+    sample, its fixed per-step weight quantize timed apart, projected to the
+    workload's tokens per step."""
     from cdl_b200.train import qat
+    from oracle import qat_cpu
 
-    torch.set_num_threads(threads)
-    spec = qat.SPECS[spec_name]
-    step = qat.QatStep(spec, torch.device("cpu"), backend="none", seed=0)
-    step.model.float()
-    step.opt = torch.optim.AdamW(step.params, lr=3e-4, betas=(0.9, 0.95))
-    batch, seq = 1, 256
-    ids = qat.random_tokens(batch, seq, spec.vocab, seed=0, device=torch.device("cpu"))
-    step.step(ids)
-    t0, cnt = time.perf_counter(), 0
-    while cnt < 1 or time.perf_counter() - t0 < target_s:
-        step.step(ids)
-        cnt += 1
-    dt = time.perf_counter() - t0
-    return (batch * seq * cnt / dt,
-            f"{cnt} fp32 train steps of {spec.name} on {batch}x{seq} tokens ({threads} threads, unquantized)")
+    spec = qat.SPECS["135m" if workload == "qat_135m" else "1.7b"]
+    batch, seq = QAT_BATCH[workload]
+    return qat_cpu.qat_step_rate(spec, 1, 256, threads, steps=1, full_tokens=batch * seq)
 
 
 # ---------------------------------------------------------------------------
@@ -380,8 +378,13 @@ def quant_workload(name, dev, rank):
     from cdl_b200 import workloads
     from cdl_b200.core.kernel import quant
 
-    fmt, rows, k, bpe, cfg = QUANT[name]
-    qfn = {"nvfp4": quant.nvfp4_quant, "mxfp4": quant.mxfp4_quant, "mxfp8": quant.mxfp8_quant}[fmt]
+    fmt, rows, k, bpe, cfg = QUANT[name][:5]
+    tr = len(QUANT[name]) > 5 and QUANT[name][5]
+    qf = {"nvfp4": quant.nvfp4_quant, "mxfp4": quant.mxfp4_quant, "mxfp8": quant.mxfp8_quant}[fmt]
+
+    def qfn(x):
+        return qf(x, transpose=tr)
+
     in_bytes = rows * k * 2
     pool_n = max(2, -(-2 * L2_BYTES // in_bytes))
     gen = workloads.c1_nvfp4 if fmt == "nvfp4" else workloads.c2_mx
@@ -399,15 +402,68 @@ def quant_workload(name, dev, rank):
         if a is not None:
             host_a.copy_(a, non_blocking=True)
 
+    if tr:
+        kernel, launches = "quant_transpose_kernel" + (" (+ amax_kernel)" if fmt == "nvfp4" else ""), (
+            2 if fmt == "nvfp4" else 1)
+    else:
+        kernel, launches = ("nvfp4_fused_kernel" if fmt == "nvfp4" else "quant_flat_kernel"), 1
     return {
         "step": lambda i: qfn(pool[i % pool_n]), "e2e_step": e2e_step, "graph": True,
         "units_per_step": bpe * rows * k / 1e9, "unit": "GB/s", "metric": f"{fmt.upper()} quant GB/s",
         "dtype": "bf16->e2m1/e4m3" if fmt != "mxfp8" else "bf16->e4m3/e8m0",
-        "config": {"workload": f"{name} {cfg} [{rows},{k}] bf16 per rank",
+        "config": {"workload": f"{name} {cfg} [{rows},{k}] bf16 per rank" + (", blocks along dim 0" if tr else ""),
                    "l2": f"inputs cycled over {pool_n} tensors ({pool_n * in_bytes >> 20} MiB > 2x L2)"},
         "h2d": host_in.numel() * 2, "d2h": p0.numel() * p0.element_size() + s0.numel() + (4 if a0 is not None else 0),
-        "bound": "hbm", "kernel": "nvfp4_fused_kernel" if fmt == "nvfp4" else "quant_flat_kernel",
-        "launches_per_step": 1,
+        "bound": "hbm", "kernel": kernel, "launches_per_step": launches,
+    }
+
+
+def encode_multi_workload(dev, rank, spec_name="1.7b", with_deq=True):
+    """The QAT step's weight re-encode: one ``cdlb200_nvfp4_encode_multi``
+    launch over the 168 quantized weights of SmolLM2-1.7B (N(0, 0.02)), amax
+    given (the optimizer forms it), codes + GEMM-layout scales + alpha and,
+    for the bf16 backward, the dequantized copy."""
+    import ctypes
+
+    import torch
+
+    from cdl_b200 import _lib
+    from cdl_b200.train import qat
+
+    spec = qat.SPECS[spec_name]
+    h, f = spec.hidden, spec.intermediate
+    kvd = spec.kv_heads * (h // spec.heads)
+    shapes = [(h, h), (kvd, h), (kvd, h), (h, h), (f, h), (f, h), (h, f)] * spec.layers
+    g = torch.Generator(device=dev)
+    g.manual_seed(rank)
+    ws = [(torch.randn(r, c, generator=g, device=dev) * 0.02).to(torch.bfloat16) for r, c in shapes]
+    amax = torch.stack([w.abs().max().float() for w in ws]).to(torch.bfloat16).view(torch.int16).to(torch.int32)
+    amax = amax & 0x7FFF
+    table = (_lib.Nvfp4EncodeTensor * len(ws))()
+    bufs = []
+    for j, w in enumerate(ws):
+        r, c = w.shape
+        b = (torch.empty(r, c // 2, dtype=torch.uint8, device=dev), torch.empty(r, c // 16, dtype=torch.uint8,
+             device=dev), torch.empty(1, dtype=torch.float32, device=dev),
+             torch.empty(r, c, dtype=torch.bfloat16, device=dev) if with_deq else None)
+        bufs.append(b)
+        t = table[j]
+        t.x, t.rows, t.k, t.amax, t.amax_words = w.data_ptr(), r, c, amax.data_ptr() + 4 * j, 1
+        t.packed, t.scale, t.alpha, t.deq = b[0].data_ptr(), b[1].data_ptr(), b[2].data_ptr(), _lib.ptr(b[3])
+    n = sum(w.numel() for w in ws)
+    bpe = 2 + 0.5 + 1 / 16 + (2 if with_deq else 0)
+
+    def step(i):
+        _lib.call("cdlb200_nvfp4_encode_multi", ctypes.addressof(table), len(ws), _lib.stream(dev))
+
+    return {
+        "step": step, "e2e_step": step, "graph": True, "keep": (ws, bufs, amax, table),
+        "units_per_step": bpe * n / 1e9, "unit": "GB/s", "metric": "NVFP4 weight encode GB/s",
+        "dtype": "bf16->e2m1/ue4m3 (+ bf16 dequantized copy)" if with_deq else "bf16->e2m1/ue4m3",
+        "config": {"workload": f"nvfp4_encode_multi: the {len(ws)} quantized weights of {spec.name} "
+                               f"({n / 1e9:.2f} G elements) in one launch, amax given",
+                   "l2": f"{2 * n / 2**30:.1f} GiB of inputs >> L2"},
+        "h2d": 0, "d2h": 0, "bound": "hbm", "kernel": "nvfp4_encode_multi_kernel", "launches_per_step": 1,
     }
 
 
@@ -465,8 +521,11 @@ def qat_workload(name, dev, rank, world, backend="nvfp4"):
     from cdl_b200.train import qat
 
     spec = qat.SPECS["135m" if name == "qat_135m" else "1.7b"]
-    batch, seq = (8, 2048) if name == "qat_135m" else (4, 2048)
-    step = qat.QatStep(spec, dev, backend=backend, seed=0, ddp=world > 1)
+    batch, seq = QAT_BATCH[name]
+    # one process per GPU: the whole step is one CUDA graph; data-parallel
+    # steps stay eager (their NCCL all-reduce runs from DDP's backward hooks)
+    graph = world == 1
+    step = qat.QatStep(spec, dev, backend=backend, seed=0, ddp=world > 1, graph=graph)
     qbwd = backend.endswith("_qbwd")
     pool = [qat.random_tokens(batch, seq, spec.vocab, seed=1000 * rank + i, device=dev) for i in range(4)]
     host_ids = pool[0].cpu().pin_memory()
@@ -488,9 +547,13 @@ def qat_workload(name, dev, rank, world, backend="nvfp4"):
                    "model": spec.name, "global_batch": batch * world, "seq_len": seq,
                    "parallelism": f"dp{world}" if world > 1 else "single", "l2": "activations >> L2"},
         "h2d": host_ids.numel() * 8, "d2h": 4, "bound": "tensor",
-        "flops_per_unit": qat.flops_per_token(spec, seq), "kernel": "full QAT step",
-        # eager steps: the library counts its kernel launches as they are issued
+        "flops_per_unit": qat.flops_per_token(spec, seq),
+        "kernel": "full QAT step (one CUDA graph per step)" if graph else "full QAT step (eager)",
+        # eager steps: the library counts its kernel launches as they are
+        # issued; a graph step replays the launches counted at its capture
         "launches_per_step": None, "count_launches": True,
+        "graph_launches": (lambda: getattr(step, "graph_launches", 0)) if graph else None,
+        "check_status": step.check_status,
     }
 
 
@@ -544,7 +607,12 @@ def measure_component(name, dev, steps, warmup, peaks):
     """Device-timed throughput and roofline of one kernel-level workload (N=1)."""
     import torch
 
-    w = quant_workload(name, dev, 0) if name in QUANT else gemm_workload(dev, 0)
+    if name in QUANT:
+        w = quant_workload(name, dev, 0)
+    elif name == "nvfp4_encode_multi":
+        w = encode_multi_workload(dev, 0)
+    else:
+        w = gemm_workload(dev, 0)
     for i in range(warmup):
         w["step"](i)
     torch.cuda.synchronize()
@@ -581,7 +649,7 @@ def main() -> None:
         if rank != 0:
             return
         if wl in QUANT:
-            fmt, rows, k, bpe, cfg = QUANT[wl]
+            fmt, rows, k, bpe, cfg = QUANT[wl][:5]
             val, sample = cpu_quant_rate(fmt, rows, k, bpe, max(args.steps // 20, 3), min(args.warmup, 1), threads)
             unit, metric = "GB/s", f"{fmt.upper()} quant GB/s"
         elif wl == "fp4_gemm":
@@ -593,8 +661,11 @@ def main() -> None:
         elif wl == "nvfp4_ccdl":
             val, sample = cpu_ccdl_rate(4096, 4096, threads, target_s=5.0)
             unit, metric = "GB/s", "NVFP4 CCDL quant GB/s"
+        elif wl == "nvfp4_encode_multi":
+            val, sample = cpu_quant_rate("nvfp4", 4096, 4096, 2.5625, 3, 1, threads)
+            unit, metric = "GB/s", "NVFP4 weight encode GB/s"
         else:
-            val, sample = cpu_qat_rate("135m" if wl == "qat_135m" else "1.7b", threads, target_s=10.0)
+            val, sample = cpu_qat_rate(wl, threads)
             unit, metric = "tokens/s", "SmolLM2 NVFP4 QAT tokens/s"
         print(json.dumps({
             "impl": "reference", "metric": metric, "value": round(val, 4), "unit": unit, "n_gpus": args.gpus,
@@ -623,6 +694,8 @@ def main() -> None:
         w = ecdl_workload(dev, rank)
     elif wl == "nvfp4_ccdl":
         w = ccdl_workload(dev, rank)
+    elif wl == "nvfp4_encode_multi":
+        w = encode_multi_workload(dev, rank)
     else:
         w = qat_workload(wl, dev, rank, world, args.backend)
 
@@ -656,9 +729,17 @@ def main() -> None:
     torch.cuda.synchronize()
     barrier()
     counted_launches = _cdl_lib.launches - launches0
+    if w.get("graph_launches") is not None:
+        counted_launches = w["graph_launches"]() * args.steps
     ms = e0.elapsed_time(e1)
     clocks = sampler.stop()
     del keep, run
+    # a bounded device-side wait that timed out in the timed steps is an error
+    # (read outside the timed region)
+    if w.get("check_status") is not None:
+        w["check_status"]()
+    else:
+        _cdl_lib.check_status(dev)
     if args.torch_profile and world == 1:  # kernel breakdown, outside the timed region
         from torch.profiler import ProfilerActivity, profile
 
@@ -693,7 +774,7 @@ def main() -> None:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         if wl in QUANT:
-            fmt, rows, k, bpe, cfg = QUANT[wl]
+            fmt, rows, k, bpe, cfg = QUANT[wl][:5]
             val, sample = cpu_quant_rate(fmt, rows, k, bpe, 3, 1, threads, target_s=10.0)
         elif wl == "fp4_gemm":
             val, sample = cpu_gemm_rate(threads, target_s=10.0)
@@ -701,8 +782,10 @@ def main() -> None:
             val, sample = cpu_ecdl_rate(4096, 4096, threads, target_s=10.0)
         elif wl == "nvfp4_ccdl":
             val, sample = cpu_ccdl_rate(4096, 4096, threads, target_s=10.0)
+        elif wl == "nvfp4_encode_multi":
+            val, sample = cpu_quant_rate("nvfp4", 4096, 4096, 2.5625, 3, 1, threads, target_s=10.0)
         else:
-            val, sample = cpu_qat_rate("135m" if wl == "qat_135m" else "1.7b", threads, target_s=10.0)
+            val, sample = cpu_qat_rate(wl, threads)
         cpu = {"value": round(val, 4), "unit": w["unit"], "cores": threads, "kind": "port", "sample": sample}
 
     peaks, peak_src = load_peaks()
@@ -735,10 +818,19 @@ def main() -> None:
     if wl.startswith("qat"):
         line["roofline"]["peak_note"] = "model FLOPs (6P + 12 L d s per token) vs measured sustained bf16 peak"
     if world == 1 and wl.startswith("qat") and not args.no_components:
+        import gc
+
+        del w  # the QAT step's memory (its graph pool) before the component workloads
+        gc.collect()
+        torch.cuda.empty_cache()
         line["components"] = {
             "nvfp4_quant": measure_component("nvfp4_quant", dev, 200, 10, peaks),
             "fp4_gemm": measure_component("fp4_gemm", dev, 20, 5, peaks),
         }
+        for name in ("nvfp4_quant_large", "nvfp4_quant_t", "mxfp4_quant", "mxfp8_quant", "mxfp4_quant_t",
+                     "mxfp8_quant_t", "nvfp4_encode_multi"):
+            line["components"][name] = measure_component(name, dev, 20, 3, peaks)
+            torch.cuda.empty_cache()
         line["components"]["fp4_gemm"]["roofline"]["peak_note"] = FP4_PEAK_NOTE
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -43,6 +43,7 @@ _D = ctypes.c_double
 SIGNATURES: dict[str, tuple] = {
     "cdlb200_status_string": (ctypes.c_char_p, [_I]),
     "cdlb200_version": (_I, []),
+    "cdlb200_set_wait_limit": (ctypes.c_uint32, [ctypes.c_uint32]),
     "cdlb200_nvfp4_quant_workspace_bytes": (_SZ, [_I64, _I64]),
     "cdlb200_nvfp4_quant": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P, _P, _P, _SZ, _P]),
     "cdlb200_nvfp4_quant_noalloc": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P, _P, _P]),
@@ -159,6 +160,44 @@ def require_cuda(*tensors: torch.Tensor) -> torch.device:
 
 
 _WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
+_STATUS: dict[int, torch.Tensor] = {}
+WS_STATUS_OFFSET = 8  # status word of an NVFP4 quantize workspace (include/cdlb200.h)
+
+
+def _dev_index(device: torch.device) -> int:
+    return device.index if device.index is not None else torch.cuda.current_device()
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """Per-device uint32 status word (as int32) that every block-scaled GEMM
+    call of this package passes to the kernel: a timed-out bounded wait sets
+    it non-zero.  Allocated (zeroed) on first use; ``check_status`` reads and
+    clears it."""
+    idx = _dev_index(device)
+    st = _STATUS.get(idx)
+    if st is None:
+        st = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _STATUS[idx] = st
+    return st
+
+
+def check_status(device: torch.device | None = None) -> None:
+    """Raise ``CdlB200Error`` (``ERR_TIMEOUT``) if a kernel of this package on
+    ``device`` (default: every device used) recorded a timed-out bounded wait
+    since the last check: the GEMM status word, or the status word of an NVFP4
+    quantize workspace.  The words are cleared.  This reads device memory
+    (a synchronizing copy): call it between steps, not inside a timed region
+    or a graph capture."""
+    idx = None if device is None else _dev_index(device)
+    words = [(f"GEMM status (cuda:{d})", t[0:1]) for d, t in _STATUS.items() if idx is None or d == idx]
+    words += [(f"NVFP4 quantize workspace (cuda:{d})", ws[WS_STATUS_OFFSET:WS_STATUS_OFFSET + 4].view(torch.int32))
+              for (d, _s), ws in _WORKSPACES.items() if idx is None or d == idx]
+    bad = [name for name, w in words if int(w.item()) != 0]
+    for _name, w in words:
+        w.zero_()
+    if bad:
+        raise CdlB200Error("check_status", ERR_TIMEOUT,
+                           f"{lib().cdlb200_status_string(ERR_TIMEOUT).decode()} in: {', '.join(bad)}")
 
 
 def nvfp4_workspace(device: torch.device) -> torch.Tensor:
@@ -167,7 +206,7 @@ def nvfp4_workspace(device: torch.device) -> torch.Tensor:
     The kernels leave it re-armed, so one buffer serves every stream-ordered
     call.  Calls on different streams get different buffers.
     """
-    key = (device.index if device.index is not None else torch.cuda.current_device(), stream(device))
+    key = (_dev_index(device), stream(device))
     ws = _WORKSPACES.get(key)
     if ws is None:
         nbytes = lib().cdlb200_nvfp4_quant_workspace_bytes(0, 0)

@@ -1,8 +1,16 @@
 // lib.cu -- library-wide helpers of libcdlb200: status strings, version,
 // per-device SM count cache.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace cdlb200 {
+
+// Poll limit of the grid-wide barrier in the fused NVFP4 quantizer (about a
+// second at the default); read by the host at each launch.
+std::atomic<uint32_t> g_wait_limit{1u << 20};
+
+uint32_t wait_limit() { return g_wait_limit.load(std::memory_order_relaxed); }
 
 int num_sms() {
     static int cache[128] = {0};
@@ -32,4 +40,8 @@ extern "C" const char* cdlb200_status_string(int status) {
     }
 }
 
-extern "C" int cdlb200_version(void) { return 100; }
+extern "C" int cdlb200_version(void) { return 101; }
+
+extern "C" uint32_t cdlb200_set_wait_limit(uint32_t polls) {
+    return cdlb200::g_wait_limit.exchange(polls, std::memory_order_relaxed);
+}

@@ -432,8 +432,6 @@ __global__ void __launch_bounds__(256) nvfp4_flat_kernel(const uint4* __restrict
     }
 }
 
-constexpr uint32_t kBarrierSpins = 1u << 20;
-
 __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -549,9 +547,11 @@ __device__ __forceinline__ uint32_t search8(const uint4& w, const uint32_t* tt) 
 //   phase 2  every CTA reads the global amax, builds the 126-entry scale
 //            table (4 lanes per entry), and re-encodes its chunks in reverse
 //            order -- most recently streamed first, so they come from L2.
-// The grid-barrier wait is bounded (kBarrierSpins polls, about a second): on
-// a timeout the CTA writes a non-zero status word into the workspace and
-// carries on, so a failed wait never hangs the GPU.  The last CTA to finish
+// The grid-barrier wait is bounded (cdlb200_set_wait_limit polls, by default
+// 2^20, about a second): on a timeout the CTA writes a non-zero status word
+// into the workspace (byte offset 8) and carries on with the maxima that have
+// arrived, so a failed wait never hangs the GPU; the host reads and clears
+// that word (cdl_b200._lib.check_status).  The last CTA to finish
 // re-arms the barrier words for the next stream-ordered call.
 constexpr int kFusedThreads = 512;  // threads of the fused NVFP4 kernel (two CTAs per SM)
 constexpr int kChunkBlocks = kFusedThreads;  // one block per thread per chunk (16 KiB)
@@ -588,7 +588,7 @@ template <bool SWZ>
 __global__ void __launch_bounds__(kFusedThreads, 2) nvfp4_fused_kernel(
     const uint4* __restrict__ x, int64_t nblk, uint2* __restrict__ packed, uint8_t* __restrict__ scale,
     FastDiv nb, int64_t c4, uint8_t* __restrict__ ws, float* __restrict__ gmax_out,
-    float* __restrict__ alpha_out) {
+    float* __restrict__ alpha_out, uint32_t spin_limit) {
     __shared__ uint32_t red[kFusedThreads / 32];
     __shared__ ScaleEntry table[128];
     __shared__ float ctab[128];  // the cvt multiplier of a kCvt entry, else -1: one 4-byte lookup per block
@@ -639,7 +639,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2) nvfp4_fused_kernel(
         atomicAdd(arrive, 1u);
         uint32_t spins = 0;
         while (ld_acquire_u32(arrive) < G) {
-            if (++spins > kBarrierSpins) {
+            if (++spins > spin_limit) {
                 atomicExch(status, 1u);
                 break;
             }
@@ -1131,7 +1131,7 @@ int launch_fused_impl(const void* x, int64_t rows, int64_t k, void* packed, void
     cfg.numAttrs = 1;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, nvfp4_fused_kernel<SWZ>, reinterpret_cast<const uint4*>(x),
                                              nblk, static_cast<uint2*>(packed), static_cast<uint8_t*>(scale),
-                                             nbd, c4, ws, gmax, alpha);
+                                             nbd, c4, ws, gmax, alpha, wait_limit());
     if (e != cudaSuccess) {
         (void)cudaGetLastError();
         return CDLB200_ERR_LAUNCH;

@@ -14,10 +14,15 @@
 // library, for as long as the library stays loaded.  The first call on each
 // device looks up the array's device address (cudaGetSymbolAddress) while
 // that device is current; make that first call before any stream capture.
+// The address is cached per device together with the CUDA context it was
+// looked up in: a call in another context (after cudaDeviceReset, or once
+// the primary context was released and created again) looks it up afresh.
 // Every call on a device shares the one array: the arrival counter is cleared
 // at the start of each call, and two calls that run at the same time on the
 // GPU (different streams without ordering between them) race on it.
 // No cudaMalloc, cudaFree or other allocating routine is called here.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -42,24 +47,50 @@ constexpr size_t kGmaxOff = kPartialOff + 4 * 1024;
 
 static __device__ __align__(256) unsigned char g_nvfp4_scratch[kNoAllocScratchBytes];
 
-std::mutex g_scratch_mu;
-void* g_scratch_ptr[128] = {nullptr};
+// cuCtxGetCurrent through the runtime's driver entry point query, so the
+// library does not need libcuda at load time (it loads on hosts without a GPU)
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CUcontext current_context() {
+    static CtxGetCurrentFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    }
+    CUcontext ctx = nullptr;
+    if (!fn || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+    return ctx;
+}
 
-// Device address of g_nvfp4_scratch on the current device (set up once per device).
+struct ScratchAddress {
+    CUcontext ctx;  // context the address was looked up in
+    void* ptr;
+};
+std::mutex g_scratch_mu;
+ScratchAddress g_scratch[128] = {};
+
+// Device address of g_nvfp4_scratch on the current device, looked up once per
+// device and context.
 int scratch_for_current_device(unsigned char** out) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return CDLB200_ERR_CUDA;
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (g_scratch_ptr[dev] == nullptr) {
+    CUcontext ctx = current_context();
+    if (ctx == nullptr || g_scratch[dev].ctx != ctx || g_scratch[dev].ptr == nullptr) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_nvfp4_scratch);
         if (e != cudaSuccess || p == nullptr) {
             (void)cudaGetLastError();
             return CDLB200_ERR_CUDA;
         }
-        g_scratch_ptr[dev] = p;
+        // the lookup made the device's primary context current if none was
+        if (ctx == nullptr) ctx = current_context();
+        g_scratch[dev].ctx = ctx;
+        g_scratch[dev].ptr = p;
     }
-    *out = static_cast<unsigned char*>(g_scratch_ptr[dev]);
+    *out = static_cast<unsigned char*>(g_scratch[dev].ptr);
     return CDLB200_OK;
 }
 

@@ -12,6 +12,10 @@ Argument conventions (cdl's): ``a`` is the row-major operand codes ``[M, K/2]``
 view whose storage is the row-major ``[N, K']`` weight codes; the scales are
 ``swizzle_scale_factors`` outputs (``b_scale`` possibly transposed, as cdl
 passes ``swizzle_scale_factors(w_q).T``), flattened for FP8.
+
+Every call passes the device's status word (``_lib.status_word``): a bounded
+wait inside the GEMM that times out sets it, and ``_lib.check_status`` turns
+it into an error between steps.
 """
 
 from __future__ import annotations
@@ -56,7 +60,8 @@ def mm_fp4_direct(
     al = alpha.reshape(-1).float().contiguous()
     _lib.call(
         "cdlb200_mm_fp4", _lib.ptr(a), _lib.ptr(brows), _lib.ptr(_flat(a_scale)), _lib.ptr(_flat(b_scale)),
-        _lib.ptr(al), m, n, k, int(block_size), int(bool(use_nvfp4)), _lib.ptr(out), n, None, _lib.stream(dev),
+        _lib.ptr(al), m, n, k, int(block_size), int(bool(use_nvfp4)), _lib.ptr(out), n,
+        _lib.ptr(_lib.status_word(dev)), _lib.stream(dev),
     )
     return out
 
@@ -91,7 +96,7 @@ def mm_mxfp8_direct(a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor, b_s
         return out
     _lib.call(
         "cdlb200_mm_mxfp8", _lib.ptr(a), _lib.ptr(brows), _lib.ptr(_flat(a_scale)), _lib.ptr(_flat(b_scale)),
-        None, m, n, k, _lib.ptr(out), n, None, _lib.stream(dev),
+        None, m, n, k, _lib.ptr(out), n, _lib.ptr(_lib.status_word(dev)), _lib.stream(dev),
     )
     return out
 

@@ -424,6 +424,14 @@ class QatStep:
             self.net = DDP(self.net, device_ids=[device.index] if device.type == "cuda" else None,
                            bucket_cap_mb=bucket_mb, gradient_as_bucket_view=True, static_graph=True)
 
+    def check_status(self) -> None:
+        """Raise ``CdlB200Error`` if a kernel of this step recorded a timed-out
+        bounded wait (a GEMM, or the one-launch NVFP4 quantizer's grid
+        barrier) since the last check.  Reads device memory: call it between
+        steps, outside a timed region."""
+        if self.device.type == "cuda":
+            _lib.check_status(self.device)
+
     @torch.no_grad()
     def calibrate(self, samples) -> None:
         """Initialize the CCDL activation quantizers' scales from calibration
@@ -510,8 +518,11 @@ class QatStep:
                 self._eager_step(self._static_ids)
         torch.cuda.current_stream(self.device).wait_stream(side)
         self._graph = torch.cuda.CUDAGraph()
+        launches0 = _lib.launches
         with torch.cuda.graph(self._graph):
             self._static_out = self._eager_step(self._static_ids)
+        # kernels of this library in the captured step (each replay runs them all)
+        self.graph_launches = _lib.launches - launches0
 
 
 def run_training(step: QatStep, train_batches, *, epochs: int = 1, grad_accum_steps: int = 1, max_steps: int = 0,

@@ -53,6 +53,15 @@ def c3_gemm(m: int, n: int, k: int, seed: int = 0, device: str = "cpu") -> tuple
     return a, w
 
 
+def token_batches(batch: int, seq: int, vocab: int, seed: int, steps: int):
+    """``steps`` batches of uniform random token ids ``[batch, seq]`` (int64,
+    CPU), drawn one after another from one CPU generator seeded with ``seed``:
+    the same sequence of batches on every machine."""
+    g = _gen(seed, "cpu")
+    for _ in range(steps):
+        yield torch.randint(0, vocab, (batch, seq), generator=g, dtype=torch.int64)
+
+
 C3_SHAPES = [(8192, 8192, 8192)] + [
     (m, n, k) for m in (2048, 16384) for (n, k) in ((2048, 8192), (8192, 2048), (49152, 576))
 ]

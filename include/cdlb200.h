@@ -56,6 +56,17 @@ const char* cdlb200_status_string(int status);
 int cdlb200_version(void);
 
 /*
+ * Poll limit of the bounded grid-wide wait in the one-launch NVFP4 quantizer
+ * (default 2^20 polls, about a second); returns the previous limit.  A wait
+ * that reaches the limit does not hang: the kernel records the timeout in the
+ * status word of its workspace (see cdlb200_nvfp4_quant) and finishes with
+ * the partial amax.  A diagnostic knob with no counterpart in the reference:
+ * tests set a limit of 0 to make the wait give up and check that the timeout
+ * reaches the host.
+ */
+uint32_t cdlb200_set_wait_limit(uint32_t polls);
+
+/*
  * NVFP4 quantize of a bf16 matrix.
  * Replaces cdl/core/kernel/quant.py:126-131 `nvfp4_quant` (its `_quant` host
  * code at quant.py:71-123 with group 16, e4m3 scales, and the torch global
@@ -71,7 +82,12 @@ int cdlb200_version(void);
  *   alpha    fp32 [1] output: gmax / 2688
  *   workspace device scratch of cdlb200_nvfp4_quant_workspace_bytes() bytes,
  *            zero-filled before its first use; the call leaves it re-usable
- *            (calls sharing one workspace must be stream-ordered).
+ *            (calls sharing one workspace must be stream-ordered).  The
+ *            32-bit word at byte offset 8 is the status word: the call sets
+ *            it non-zero if its bounded grid-wide wait timed out (the codes
+ *            of that call are then unreliable).  It stays set until the
+ *            caller reads and clears it, which needs no ordering beyond the
+ *            stream's.
  */
 size_t cdlb200_nvfp4_quant_workspace_bytes(int64_t rows, int64_t k);
 int cdlb200_nvfp4_quant(const void* x, int64_t rows, int64_t k, int64_t ldx, int transpose,

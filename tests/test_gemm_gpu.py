@@ -53,3 +53,65 @@ def test_gemm_vs_oracle(fmt_name, shape):
     # the kernel rounds its fp32 accumulator to bf16, as cdl's op returns bf16
     assert _rel_l2(got, ref_bf16) <= 1e-3, _rel_l2(got, ref_bf16)
     assert _rel_l2(got, ref) <= 3e-3, _rel_l2(got, ref)
+
+
+def _sample_rows(m: int, rng: np.random.Generator) -> np.ndarray:
+    """Every row of two whole 256-row output tiles (the first and a random
+    one) plus 96 random rows: covers whole tiles, tile edges and the last
+    (possibly ragged) row block."""
+    tiles = {0, int(rng.integers(0, (m + 255) // 256))}
+    rows = {r for t in tiles for r in range(256 * t, min(256 * t + 256, m))}
+    rows |= {int(r) for r in rng.integers(0, m, 96)} | {m - 1}
+    return np.array(sorted(rows))
+
+
+# BASELINE config C3: 8192^3 and the shape sweep, plus a long-K case in which
+# the persistent kernel's K pipeline wraps its stage ring many times
+C3_PARITY_SHAPES = workloads.C3_SHAPES + [(256, 256, 16384)]
+
+
+@pytest.mark.parametrize("fmt_name", ["nvfp4", "mxfp4", "mxfp8"])
+@pytest.mark.parametrize("shape", C3_PARITY_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_gemm_c3_shapes_vs_oracle(fmt_name, shape):
+    """Full GEMM on the GPU; the fp32 oracle on a row sample of the output.
+
+    Tolerances (the contract is the fp32 dequantize-then-matmul oracle):
+    rel-L2 <= 1e-3 against the oracle rounded to bf16 -- the kernel's output
+    is bf16, whose rounding alone is ~1.1e-3 rel-L2 against unrounded fp32 --
+    and <= 3e-3 against fp32; elementwise |got - ref| <= 2^-7 |ref| (one bf16
+    ulp: the fp32 accumulation order may move a value across a bf16 rounding
+    boundary) + 1e-4 * rms(ref row)."""
+    from cdl_b200.core.kernel import quant
+    from cdl_b200.model.wrapper.ops import mm_fp4_direct, mm_mxfp8_direct
+
+    m, n, k = shape
+    a, w = workloads.c3_gemm(m, n, k, seed=5, device="cuda")
+    qf = {"nvfp4": quant.nvfp4_quant, "mxfp4": quant.mxfp4_quant, "mxfp8": quant.mxfp8_quant}[fmt_name]
+    ap, asf, aal = qf(a, swizzled=True)
+    wp, wsf, wal = qf(w, swizzled=True)
+    if fmt_name == "mxfp8":
+        out = mm_mxfp8_direct(ap, wp.T, asf.flatten(), wsf.flatten())
+        alpha = 1.0
+    else:
+        alpha_t = aal * wal
+        out = mm_fp4_direct(ap, wp.T, asf, wsf.T, alpha_t, 16 if fmt_name == "nvfp4" else 32,
+                            fmt_name == "nvfp4")
+        alpha = float(alpha_t.item())
+    rows = _sample_rows(m, np.random.default_rng(m * 7 + n * 3 + k))
+    rows_t = torch.from_numpy(rows).cuda()
+    got = out[rows_t].float().cpu().numpy()
+    # linear scales of the same operands (same bytes, other layout) for the oracle
+    a_lin = qf(a)
+    w_lin = qf(w)
+    ap_s = a_lin[0].view(torch.uint8)[rows_t].cpu().numpy()
+    as_s = a_lin[1][rows_t].cpu().numpy()
+    ref = oracle.mm(ap_s, as_s, w_lin[0].view(torch.uint8).cpu().numpy(), w_lin[1].cpu().numpy(), FMT[fmt_name],
+                    alpha)
+    del out
+    ref_bf16 = torch.from_numpy(ref).bfloat16().float().numpy()
+    assert _rel_l2(got, ref_bf16) <= 1e-3, _rel_l2(got, ref_bf16)
+    assert _rel_l2(got, ref) <= 3e-3, _rel_l2(got, ref)
+    row_rms = np.sqrt(np.mean(ref.astype(np.float64) ** 2, axis=1, keepdims=True))
+    bound = 2.0 ** -7 * np.abs(ref) + 1e-4 * row_rms
+    bad = np.abs(got - ref) > bound
+    assert not bad.any(), (int(bad.sum()), np.argwhere(bad)[:5])

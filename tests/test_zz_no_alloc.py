@@ -17,39 +17,43 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _quant_with_workspace(lib, x, transpose):
+def _outputs(x, transpose, layout, with_gmax):
     from cdl_b200 import _lib
+    from cdl_b200.core.kernel.quant import scale_shape
 
     rows, k = x.shape
     r, c = (k, rows) if transpose else (rows, k)
     nb = (c + 15) // 16
     packed = torch.empty((r, nb * 8), dtype=torch.uint8, device=x.device)
-    scale = torch.empty((r, nb), dtype=torch.uint8, device=x.device)
-    gmax = torch.empty(1, dtype=torch.float32, device=x.device)
+    scale = torch.empty(scale_shape(r, nb, layout == _lib.SCALE_SWIZZLED), dtype=torch.uint8, device=x.device)
+    gmax = torch.empty(1, dtype=torch.float32, device=x.device) if with_gmax else None
     alpha = torch.empty(1, dtype=torch.float32, device=x.device)
+    return packed, scale, gmax, alpha
+
+
+def _quant_with_workspace(lib, x, transpose, layout=0, with_gmax=True):
+    from cdl_b200 import _lib
+
+    rows, k = x.shape
+    packed, scale, gmax, alpha = _outputs(x, transpose, layout, with_gmax)
     ws = torch.zeros(lib.cdlb200_nvfp4_quant_workspace_bytes(rows, k), dtype=torch.uint8, device=x.device)
     rc = lib.cdlb200_nvfp4_quant(x.data_ptr(), rows, k, k, int(transpose), packed.data_ptr(), scale.data_ptr(),
-                                 _lib.SCALE_LINEAR, gmax.data_ptr(), alpha.data_ptr(), ws.data_ptr(), ws.numel(),
+                                 layout, _lib.ptr(gmax), alpha.data_ptr(), ws.data_ptr(), ws.numel(),
                                  _lib.stream(x.device))
     assert rc == 0, rc
-    return packed, scale, gmax, alpha
+    return [t for t in (packed, scale, gmax, alpha) if t is not None]
 
 
-def _quant_noalloc(lib, x, transpose):
+def _quant_noalloc(lib, x, transpose, layout=0, with_gmax=True):
     from cdl_b200 import _lib
 
     rows, k = x.shape
-    r, c = (k, rows) if transpose else (rows, k)
-    nb = (c + 15) // 16
-    packed = torch.empty((r, nb * 8), dtype=torch.uint8, device=x.device)
-    scale = torch.empty((r, nb), dtype=torch.uint8, device=x.device)
-    gmax = torch.empty(1, dtype=torch.float32, device=x.device)
-    alpha = torch.empty(1, dtype=torch.float32, device=x.device)
+    packed, scale, gmax, alpha = _outputs(x, transpose, layout, with_gmax)
     rc = lib.cdlb200_nvfp4_quant_noalloc(x.data_ptr(), rows, k, k, int(transpose), packed.data_ptr(),
-                                         scale.data_ptr(), _lib.SCALE_LINEAR, gmax.data_ptr(), alpha.data_ptr(),
+                                         scale.data_ptr(), layout, _lib.ptr(gmax), alpha.data_ptr(),
                                          _lib.stream(x.device))
     assert rc == 0, rc
-    return packed, scale, gmax, alpha
+    return [t for t in (packed, scale, gmax, alpha) if t is not None]
 
 
 def test_noalloc_matches_workspace_entry_point_two_calls():
@@ -62,6 +66,23 @@ def test_noalloc_matches_workspace_entry_point_two_calls():
         ref = _quant_with_workspace(lib, x, transpose)
         got = _quant_noalloc(lib, x, transpose)
         torch.cuda.synchronize()
+        for a, b in zip(ref, got):
+            assert torch.equal(a.view(torch.uint8), b.view(torch.uint8))
+
+
+def test_noalloc_scratch_gmax_and_swizzled_scales():
+    """No gmax output (the global amax then lives in the fixed scratch array)
+    and scales in the GEMM's 128x4 layout: same packed codes, scales and
+    alpha as the workspace entry point, on two calls in a row."""
+    from cdl_b200 import _lib, workloads
+
+    lib = _lib.lib()
+    inputs = [workloads.c2_mx(384, 2048, seed=42).cuda(), (workloads.c1_nvfp4(256, 1024, seed=43) * 3.0).cuda()]
+    for x in inputs:
+        ref = _quant_with_workspace(lib, x, False, _lib.SCALE_SWIZZLED, with_gmax=False)
+        got = _quant_noalloc(lib, x, False, _lib.SCALE_SWIZZLED, with_gmax=False)
+        torch.cuda.synchronize()
+        assert len(got) == 3
         for a, b in zip(ref, got):
             assert torch.equal(a.view(torch.uint8), b.view(torch.uint8))
 
