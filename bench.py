@@ -84,6 +84,7 @@ def parse_args():
     ap.add_argument("--backend", default="nvfp4", choices=["nvfp4", "nvfp4_qbwd", "mxfp4", "mxfp8"],
                     help="QAT workloads: QLinear backend (nvfp4 = cdl's numerics: bf16 backward)")
     ap.add_argument("--spinup-s", type=float, default=1.0, help="untimed clock ramp before warm-up")
+    ap.add_argument("--no-graph", action="store_true", help="QAT workloads: eager steps even at N=1")
     ap.add_argument("--gemm-shape", default="8192,8192,8192", metavar="M,N,K",
                     help="fp4_gemm: the GEMM shape (C3 is 8192^3; its sweep: M in {2048, 16384} x "
                          "(N, K) in {(2048, 8192), (8192, 2048), (49152, 576)})")
@@ -515,7 +516,7 @@ def gemm_workload(dev, rank, shape=(8192, 8192, 8192)):
     }
 
 
-def qat_workload(name, dev, rank, world, backend="nvfp4"):
+def qat_workload(name, dev, rank, world, backend="nvfp4", use_graph=True):
     import torch
 
     from cdl_b200.train import qat
@@ -524,7 +525,7 @@ def qat_workload(name, dev, rank, world, backend="nvfp4"):
     batch, seq = QAT_BATCH[name]
     # one process per GPU: the whole step is one CUDA graph; data-parallel
     # steps stay eager (their NCCL all-reduce runs from DDP's backward hooks)
-    graph = world == 1
+    graph = world == 1 and use_graph
     step = qat.QatStep(spec, dev, backend=backend, seed=0, ddp=world > 1, graph=graph)
     qbwd = backend.endswith("_qbwd")
     pool = [qat.random_tokens(batch, seq, spec.vocab, seed=1000 * rank + i, device=dev) for i in range(4)]
@@ -697,7 +698,7 @@ def main() -> None:
     elif wl == "nvfp4_encode_multi":
         w = encode_multi_workload(dev, rank)
     else:
-        w = qat_workload(wl, dev, rank, world, args.backend)
+        w = qat_workload(wl, dev, rank, world, args.backend, not args.no_graph)
 
     def barrier():
         if world > 1:

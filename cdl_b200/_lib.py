@@ -47,6 +47,7 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_nvfp4_quant_workspace_bytes": (_SZ, [_I64, _I64]),
     "cdlb200_nvfp4_quant": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P, _P, _P, _SZ, _P]),
     "cdlb200_nvfp4_quant_noalloc": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P, _P, _P]),
+    "cdlb200_nvfp4_amax": (_I, [_P, _I64, _I64, _I64, _P, _P, _P, _SZ, _P]),
     "cdlb200_mxfp4_quant": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P]),
     "cdlb200_mxfp8_quant": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P]),
     "cdlb200_fp4_dequant": (_I, [_P, _P, _P, _I64, _I64, _I, _I, _P, _P]),
@@ -74,6 +75,7 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_clip_adamw_workspace_bytes": (_I64, [_P, _I]),
     "cdlb200_clip_adamw": (_I, [_P, _I, _D, _D, _D, _D, _D, _D, _P, _I64, _P, _P]),
     "cdlb200_nvfp4_encode_multi": (_I, [_P, _I, _P]),
+    "cdlb200_nvfp4_dual_multi": (_I, [_P, _I, _P]),
 }
 
 
@@ -88,6 +90,14 @@ class Nvfp4EncodeTensor(ctypes.Structure):
 
     _fields_ = [("x", _P), ("rows", _I64), ("k", _I64), ("amax", _P), ("amax_words", ctypes.c_int32),
                 ("pad", ctypes.c_int32), ("packed", _P), ("scale", _P), ("alpha", _P), ("deq", _P)]
+
+
+class Nvfp4DualTensor(ctypes.Structure):
+    """``cdlb200_nvfp4_dual_tensor`` (include/cdlb200_step.h)."""
+
+    _fields_ = [("x", _P), ("rows", _I64), ("cols", _I64), ("amax", _P), ("gmax", _P),
+                ("amax_words", ctypes.c_int32), ("pad", ctypes.c_int32), ("alpha", _P), ("row_packed", _P),
+                ("row_scale", _P), ("col_packed", _P), ("col_scale", _P)]
 
 
 class CdlB200Error(RuntimeError):

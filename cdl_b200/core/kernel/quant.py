@@ -18,6 +18,8 @@ The input must be a bf16 CUDA tensor; there is no CPU path.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from cdl_b200 import _lib
@@ -87,3 +89,63 @@ def mxfp8_quant(
 ) -> tuple[torch.Tensor, torch.Tensor, None]:
     packed, scale, _ = _quant(x, MXFP8, transpose, swizzled)
     return packed, scale, None
+
+
+def nvfp4_amax(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """``(gmax, alpha)`` fp32 ``[1]`` device tensors of a 2-D bf16 tensor: the
+    global NVFP4 scale cdl's ``_quant`` forms (quant.py:96-101), alone."""
+    if x.ndim != 2:
+        raise ValueError(f"expected a 2D tensor [rows, k], got shape {tuple(x.shape)}")
+    dev = _lib.require_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise TypeError(f"cdl_b200 quantize takes bfloat16 input, got {x.dtype}")
+    if x.stride(1) != 1 or x.stride(0) < x.shape[1]:
+        x = x.contiguous()
+    gmax = torch.empty(1, dtype=torch.float32, device=dev)
+    alpha = torch.empty(1, dtype=torch.float32, device=dev)
+    ws = _lib.nvfp4_workspace(dev)
+    _lib.call("cdlb200_nvfp4_amax", _lib.ptr(x), x.shape[0], x.shape[1], max(x.stride(0), 1), _lib.ptr(gmax),
+              _lib.ptr(alpha), _lib.ptr(ws), ws.numel(), _lib.stream(dev))
+    return gmax, alpha
+
+
+def nvfp4_dual_quant(x: torch.Tensor, *, amax: torch.Tensor | None = None, gmax: torch.Tensor | None = None,
+                     rows: bool = True, cols: bool = True):
+    """NVFP4 encodings of ``x`` (blocks of 16 along dim 1) and of ``x.T``
+    (blocks of 16 along dim 0) from one read of ``x``, both with the scales in
+    the 128x4 GEMM layout: the same codes, scale bytes and alpha as
+    ``nvfp4_quant(x, swizzled=True)`` and ``nvfp4_quant(x, transpose=True,
+    swizzled=True)``.  ``x``: contiguous bf16 ``[R, C]``, R and C multiples of
+    64.  The global amax is given as ``amax`` (int32 words holding bf16
+    magnitude bits, e.g. a producer kernel's epilogue words) or ``gmax`` (fp32
+    ``[1]``), else computed here first.  Returns ``(row, col)``, each
+    ``(packed, scale, alpha)`` or None when not requested."""
+    if x.ndim != 2:
+        raise ValueError(f"expected a 2D tensor [rows, k], got shape {tuple(x.shape)}")
+    dev = _lib.require_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise TypeError(f"cdl_b200 quantize takes bfloat16 input, got {x.dtype}")
+    r, c = x.shape
+    if r % 64 or c % 64:
+        raise ValueError(f"nvfp4_dual_quant needs both dimensions to be multiples of 64, got {tuple(x.shape)}")
+    x = x.contiguous()
+    if amax is None and gmax is None:
+        gmax, _ = nvfp4_amax(x)
+    alpha = torch.empty(1, dtype=torch.float32, device=dev)
+    row = col = None
+    t = _lib.Nvfp4DualTensor()
+    t.x, t.rows, t.cols, t.alpha = x.data_ptr(), r, c, alpha.data_ptr()
+    if amax is not None:
+        t.amax, t.amax_words = amax.data_ptr(), amax.numel()
+    else:
+        t.gmax = gmax.data_ptr()
+    if rows:
+        row = (torch.empty(r, c // 2, dtype=torch.uint8, device=dev),
+               torch.empty(scale_shape(r, c // 16, True), dtype=torch.uint8, device=dev), alpha)
+        t.row_packed, t.row_scale = row[0].data_ptr(), row[1].data_ptr()
+    if cols:
+        col = (torch.empty(c, r // 2, dtype=torch.uint8, device=dev),
+               torch.empty(scale_shape(c, r // 16, True), dtype=torch.uint8, device=dev), alpha)
+        t.col_packed, t.col_scale = col[0].data_ptr(), col[1].data_ptr()
+    _lib.call("cdlb200_nvfp4_dual_multi", ctypes.addressof(t), 1, _lib.stream(dev))
+    return row, col

@@ -15,7 +15,10 @@ flow to the unquantized proxies):
   the same block-scaled format on the tensor cores --
   ``dx = Q(g) . Q(w^T)^T`` (both quantized along N) and
   ``dw = Q(g^T) . Q(x^T)^T`` (both quantized along M, the transposed
-  requantize) -- so all three GEMMs of a linear layer are FP4 (FP8).
+  requantize) -- so all three GEMMs of a linear layer are FP4 (FP8).  For
+  NVFP4 with every dimension a multiple of 64 each operand is read once for
+  both of its encodings (``nvfp4_dual_quant``): x and w in the forward (the
+  weights by the optimizer's encoder when it ran), g in the backward.
 """
 
 from __future__ import annotations
@@ -26,7 +29,7 @@ import torch
 
 from cdl_b200.api.quant import QTensor
 from cdl_b200.core.kernel.dequant import mxfp4_dequant, mxfp8_dequant, nvfp4_dequant
-from cdl_b200.core.kernel.quant import mxfp4_quant, mxfp8_quant, nvfp4_quant
+from cdl_b200.core.kernel.quant import mxfp4_quant, mxfp8_quant, nvfp4_dual_quant, nvfp4_quant
 from cdl_b200.core.mm.swizzle import expand_rows, pad_k, pad_n, swizzle_scale_factors
 from cdl_b200.model.wrapper.ops import mm_fp4_direct as mm_fp4
 from cdl_b200.model.wrapper.ops import mm_mxfp8_direct as mm_mxfp8
@@ -77,6 +80,17 @@ class BlockScaledMatMul(torch.autograd.Function):
     def forward(ctx, fmt: str, x: QTensor, x_proxy, w: QTensor, w_proxy, quantized_backward: bool = False):
         ctx.fmt = fmt
         ctx.swizzled = False
+        ctx.dual = False
+        if (quantized_backward and fmt == "nvfp4" and x_proxy is not None and w_proxy is not None
+                and hasattr(x, "encode_dual") and hasattr(w, "encode_dual") and x.k == w.k
+                and all(d % 64 == 0 for d in (x_proxy.numel() // x.k, x.k, w.theta.shape[0]))):
+            # NVFP4 forward and quantized backward from dual encodings: x and w
+            # each read once for their operand of this GEMM and the transposed
+            # one of the wgrad / dgrad GEMM
+            (x_row, x_col), (w_row, w_col) = x.encode_dual(), w.encode_dual()
+            ctx.dual = True
+            ctx.save_for_backward(*x_col, *w_col)
+            return mm_fp4(x_row[0], w_row[0].T, x_row[1], w_row[1].T, x_row[2] * w_row[2], 16, True)
         # the quantized backward needs every GEMM dimension to be a multiple of 32
         ctx.qbwd = bool(quantized_backward) and x_proxy is not None and w_proxy is not None and all(
             d % 32 == 0 for d in (*x_proxy.shape, w_proxy.shape[0]))
@@ -129,6 +143,16 @@ class BlockScaledMatMul(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_output):
         grad_output = grad_output.contiguous()
+        if ctx.dual:
+            # dx = Q(g) . Q(w^T)^T (both along N), dw = Q(g^T) . Q(x^T)^T (both
+            # along M); g is read once for both of its encodings
+            xc_p, xc_s, xc_a, wc_p, wc_s, wc_a = ctx.saved_tensors
+            need_dx, need_dw = ctx.needs_input_grad[2], ctx.needs_input_grad[4]
+            g_row, g_col = nvfp4_dual_quant(grad_output.reshape(-1, grad_output.shape[-1]), rows=need_dx,
+                                            cols=need_dw)
+            dx = mm_fp4(g_row[0], wc_p.T, g_row[1], wc_s.T, g_row[2] * wc_a, 16, True) if need_dx else None
+            dw = mm_fp4(g_col[0], xc_p.T, g_col[1], xc_s.T, g_col[2] * xc_a, 16, True) if need_dw else None
+            return None, None, dx, None, dw, None
         if ctx.qbwd:
             x_src, w_src = ctx.proxies
             dx, dw = _quantized_grads(ctx.fmt, grad_output, x_src if ctx.w_k is not None else None,

@@ -822,6 +822,159 @@ __global__ void __launch_bounds__(kEncThreads) nvfp4_encode_multi_kernel(const _
 }
 
 // ---------------------------------------------------------------------------
+// Dual NVFP4 encode: x and x^T from one read of x (the operands of the
+// quantized dgrad / wgrad GEMMs).  The tiles of all tensors of a launch form
+// one list; a CTA walks its share of it.  Per 64 x 64 tile:
+//   * 256 threads load the tile (two 16-byte vectors each, whole 128-byte
+//     row segments) and stage it in shared memory; the next tile's loads are
+//     issued right after, so they are in flight while this one is encoded;
+//   * row-wise: thread (r, b) encodes row r's 16-element block b with the
+//     exact block encoder (nvfp4_block16), stores its 8 code bytes (a warp
+//     covers whole 32-byte row segments) and the four lanes of a row combine
+//     their scale bytes into the one 4-byte word of the 128x4 layout;
+//   * column-wise: thread (c, b) gathers column c's 16 values of block b from
+//     shared memory (a warp reads 32 consecutive columns of one row per load:
+//     conflict-free), encodes them the same way and stages codes and scale
+//     bytes, which then leave as one 32-byte segment per output row and one
+//     scale word per output row.
+// ---------------------------------------------------------------------------
+constexpr int kDualT = 64;                  // tile rows = tile columns
+constexpr int kDualPitch = kDualT + 8;      // staged row: 64 bf16 + 16 bytes of padding
+constexpr int kDualThreads = 256;
+constexpr int kDualGroup = 128;             // tensors per launch (table in the parameter block)
+
+struct DualGroup {
+    int count, pad;
+    int64_t tile0[kDualGroup + 1];  // global index of each tensor's first tile
+    int32_t tiles_c[kDualGroup];    // cols / 64
+    cdlb200_nvfp4_dual_tensor t[kDualGroup];
+};
+
+__device__ __forceinline__ int dual_tensor_of(const DualGroup& g, int64_t tile) {
+    int lo = 0, hi = g.count - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (g.tile0[mid] <= tile) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+// The tensor's NVFP4 constants from its amax words (warp-wide max) or gmax.
+__device__ __forceinline__ Nvfp4Tensor dual_scale(const cdlb200_nvfp4_dual_tensor& T, int lane) {
+    float gmax;
+    if (T.amax != nullptr) {
+        const int nw = T.amax_words > 1 ? T.amax_words : 1;
+        uint32_t gm = lane < nw ? __ldcg(T.amax + lane) : 0u;
+        if (lane + 32 < nw) gm = max(gm, __ldcg(T.amax + lane + 32));
+        gm = __reduce_max_sync(0xffffffffu, gm);
+        gmax = gm > 0x7f80u ? u2f(0x7fc00000u) : fmaxf(u2f(gm << 16), 1.1754943508222875e-38f);
+    } else {
+        gmax = __ldcg(T.gmax);
+    }
+    Nvfp4Tensor tn;
+    tn.gmax = gmax;
+    tn.alpha = __fdiv_rn(gmax, 2688.0f);
+    tn.markstein = gmax >= 0x1p-100f && gmax <= 1.0e35f;
+    tn.yg = tn.markstein ? __frcp_rn(gmax) : 0.0f;
+    return tn;
+}
+
+__global__ void __launch_bounds__(kDualThreads, 4) nvfp4_dual_multi_kernel(const __grid_constant__ DualGroup g) {
+    __shared__ __align__(16) uint16_t xs[kDualT * kDualPitch];
+    __shared__ __align__(16) uint2 ccodes[kDualT * 4];  // column c, block b -> [4c + b]
+    __shared__ __align__(4) uint8_t cscale[kDualT * 4];
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int64_t total = g.tile0[g.count];
+
+    // tile -> (tensor, row0, col0)
+    auto locate = [&](int64_t tile, int& ti, int64_t& row0, int64_t& col0) {
+        ti = dual_tensor_of(g, tile);
+        const int64_t lt = tile - g.tile0[ti];
+        const int64_t tc = g.tiles_c[ti];
+        row0 = (lt / tc) * kDualT;
+        col0 = (lt % tc) * kDualT;
+    };
+    auto load = [&](int64_t tile, uint4 (&v)[2]) {
+        int ti;
+        int64_t row0, col0;
+        locate(tile, ti, row0, col0);
+        const cdlb200_nvfp4_dual_tensor& T = g.t[ti];
+        const uint16_t* x = static_cast<const uint16_t*>(T.x);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int e = tid + kDualThreads * j, r = e >> 3, c8 = (e & 7) * 8;
+            v[j] = ldg_stream(reinterpret_cast<const uint4*>(x + (row0 + r) * T.cols + col0 + c8));
+        }
+    };
+
+    uint4 v[2];
+    int64_t tile = blockIdx.x;
+    if (tile < total) load(tile, v);
+    for (; tile < total; tile += gridDim.x) {
+        int ti;
+        int64_t row0, col0;
+        locate(tile, ti, row0, col0);
+        const cdlb200_nvfp4_dual_tensor& T = g.t[ti];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int e = tid + kDualThreads * j, r = e >> 3, c8 = (e & 7) * 8;
+            *reinterpret_cast<uint4*>(&xs[r * kDualPitch + c8]) = v[j];
+        }
+        __syncthreads();
+        if (tile + gridDim.x < total) load(tile + gridDim.x, v);  // in flight during the encode
+        const Nvfp4Tensor tn = dual_scale(T, lane);
+        if (tile == g.tile0[ti] && tid == 0) *T.alpha = tn.alpha;
+
+        if (T.row_packed != nullptr) {  // ---- x: row r, block b
+            const int r = tid >> 2, b = tid & 3;
+            const uint4 w0 = *reinterpret_cast<const uint4*>(&xs[r * kDualPitch + 16 * b]);
+            const uint4 w1 = *reinterpret_cast<const uint4*>(&xs[r * kDualPitch + 16 * b + 8]);
+            uint2 out;
+            const uint32_t byte = nvfp4_block16(w0, w1, max(amax8(w0), amax8(w1)), tn, out);
+            *reinterpret_cast<uint2*>(static_cast<uint8_t*>(T.row_packed) + (row0 + r) * (T.cols / 2) + col0 / 2 +
+                                      8 * b) = out;
+            uint32_t word = byte << (8 * b);
+            word |= __shfl_xor_sync(0xffffffffu, word, 1);
+            word |= __shfl_xor_sync(0xffffffffu, word, 2);
+            if (b == 0) {
+                const int64_t c4 = (T.cols / 16 + 3) / 4;
+                *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(T.row_scale) +
+                                             swizzle_offset(row0 + r, col0 / 16, c4)) = word;
+            }
+        }
+        if (T.col_packed != nullptr) {  // ---- x^T: column c, block b (rows 16b .. 16b + 15 of the tile)
+            const int c = tid & (kDualT - 1), b = tid >> 6;
+            uint32_t h[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                h[i] = (uint32_t)xs[(16 * b + 2 * i) * kDualPitch + c] |
+                       ((uint32_t)xs[(16 * b + 2 * i + 1) * kDualPitch + c] << 16);
+            const uint4 w0 = make_uint4(h[0], h[1], h[2], h[3]), w1 = make_uint4(h[4], h[5], h[6], h[7]);
+            uint2 out;
+            const uint32_t byte = nvfp4_block16(w0, w1, max(amax8(w0), amax8(w1)), tn, out);
+            ccodes[4 * c + b] = out;
+            cscale[4 * c + b] = (uint8_t)byte;
+        }
+        __syncthreads();  // staged columns complete; xs free for the next tile
+        if (T.col_packed != nullptr) {
+            if (tid < 2 * kDualT) {  // output row col0 + c: 32 code bytes, two 16-byte halves
+                const int c = tid >> 1, half = tid & 1;
+                const uint4 q = *reinterpret_cast<const uint4*>(&ccodes[4 * c + 2 * half]);
+                *reinterpret_cast<uint4*>(static_cast<uint8_t*>(T.col_packed) + (col0 + c) * (T.rows / 2) + row0 / 2 +
+                                          16 * half) = q;
+            } else if (tid < 3 * kDualT) {  // its scale word (blocks row0/16 .. +3)
+                const int c = tid - 2 * kDualT;
+                const int64_t c4 = (T.rows / 16 + 3) / 4;
+                *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(T.col_scale) +
+                                             swizzle_offset(col0 + c, row0 / 16, c4)) =
+                    *reinterpret_cast<const uint32_t*>(&cscale[4 * c]);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // general path: any leading dimension, ragged k, transposed (dim-0) blocks.
 // One thread per (output row r, block b); element (r, c) is x[r*sr + c*sc].
 // Threads are ordered r-fastest so a transposed input is read coalesced.
@@ -1195,6 +1348,20 @@ extern "C" int cdlb200_nvfp4_quant(const void* x, int64_t rows, int64_t k, int64
     return launch_nvfp4_encode(x, rows, k, ldx, transpose, packed, scale, scale_layout, g, alpha, st);
 }
 
+extern "C" int cdlb200_nvfp4_amax(const void* x, int64_t rows, int64_t k, int64_t ldx, float* gmax, float* alpha,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+    if (rows < 0 || k < 0 || !gmax || !alpha) return CDLB200_ERR_INVALID_ARG;
+    if (rows > 0 && k > 0 && (!x || ldx < k)) return CDLB200_ERR_INVALID_ARG;
+    if (x && !aligned(x, 2)) return CDLB200_ERR_ALIGNMENT;
+    if (!workspace || workspace_bytes < cdlb200_nvfp4_quant_workspace_bytes(rows, k)) return CDLB200_ERR_WORKSPACE;
+    if (!aligned(workspace, 256)) return CDLB200_ERR_ALIGNMENT;
+    int rc;
+    if ((rc = device_ok()) != CDLB200_OK) return rc;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    return launch_amax(x, rows, k, ldx, reinterpret_cast<uint32_t*>(ws + kWsPartialOff),
+                       reinterpret_cast<uint32_t*>(ws + kWsCounterOff), gmax, alpha, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int cdlb200_mxfp4_quant(const void* x, int64_t rows, int64_t k, int64_t ldx, int transpose,
                                    void* packed, void* scale, int scale_layout, void* stream) {
     int rc = check_args(x, rows, k, ldx, transpose, packed, scale, scale_layout);
@@ -1249,6 +1416,67 @@ extern "C" int cdlb200_nvfp4_encode_multi(const cdlb200_nvfp4_encode_tensor* ten
     for (const EncGroup& g : groups) {
         const int64_t n = g.chunk0[g.count] - g.chunk0[0];
         nvfp4_encode_multi_kernel<<<(unsigned)(n < cap ? n : cap), kEncThreads, 0, st>>>(g);
+        CDLB200_CHECK_LAUNCH();
+    }
+    return CDLB200_OK;
+}
+
+namespace {
+// Zero the last 128-row block of a 128x4-layout scale matrix of `rows` rows
+// and `nb` blocks when rows is not a multiple of 128 (its padding rows are
+// interleaved with the valid ones; the kernel then writes the valid rows).
+int zero_scale_tail(void* scale, int64_t rows, int64_t nb, cudaStream_t st) {
+    if ((rows % 128) == 0) return CDLB200_OK;
+    const int64_t c4 = (nb + 3) / 4;
+    const int64_t off = (rows / 128) * c4 * 512;
+    return cudaMemsetAsync(static_cast<uint8_t*>(scale) + off, 0, (size_t)(c4 * 512), st) == cudaSuccess
+               ? CDLB200_OK
+               : CDLB200_ERR_CUDA;
+}
+}  // namespace
+
+extern "C" int cdlb200_nvfp4_dual_multi(const cdlb200_nvfp4_dual_tensor* tensors, int count, void* stream) {
+    if (count < 0 || (count > 0 && !tensors)) return CDLB200_ERR_INVALID_ARG;
+    for (int i = 0; i < count; ++i) {
+        const cdlb200_nvfp4_dual_tensor& t = tensors[i];
+        if (t.rows < 0 || t.cols < 0 || (t.rows % kDualT) != 0 || (t.cols % kDualT) != 0) return CDLB200_ERR_INVALID_ARG;
+        if (t.rows == 0 || t.cols == 0) continue;
+        if (!t.x || !t.alpha || (!t.amax && !t.gmax) || (t.amax && (t.amax_words < 1 || t.amax_words > 64)))
+            return CDLB200_ERR_INVALID_ARG;
+        if ((t.row_packed && !t.row_scale) || (t.col_packed && !t.col_scale)) return CDLB200_ERR_INVALID_ARG;
+        if (t.rows * t.cols / 16 >= (1ll << 40)) return CDLB200_ERR_INVALID_ARG;
+        if (!aligned(t.x, 16) || (t.row_packed && !aligned(t.row_packed, 8)) ||
+            (t.col_packed && !aligned(t.col_packed, 16)) || (t.row_scale && !aligned(t.row_scale, 4)) ||
+            (t.col_scale && !aligned(t.col_scale, 4)))
+            return CDLB200_ERR_ALIGNMENT;
+    }
+    int rc;
+    if ((rc = device_ok()) != CDLB200_OK) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    std::vector<DualGroup> groups;
+    int64_t tiles = 0;
+    for (int i = 0; i < count; ++i) {
+        const cdlb200_nvfp4_dual_tensor& t = tensors[i];
+        if (t.rows == 0 || t.cols == 0) continue;
+        if (t.row_packed && (rc = zero_scale_tail(t.row_scale, t.rows, t.cols / 16, st)) != CDLB200_OK) return rc;
+        if (t.col_packed && (rc = zero_scale_tail(t.col_scale, t.cols, t.rows / 16, st)) != CDLB200_OK) return rc;
+        if (groups.empty() || groups.back().count == kDualGroup) {
+            groups.emplace_back();
+            groups.back().count = 0;
+            groups.back().pad = 0;
+            tiles = 0;
+        }
+        DualGroup& g = groups.back();
+        g.t[g.count] = t;
+        g.tiles_c[g.count] = (int32_t)(t.cols / kDualT);
+        g.tile0[g.count] = tiles;
+        tiles += (t.rows / kDualT) * (t.cols / kDualT);
+        g.tile0[++g.count] = tiles;
+    }
+    const int64_t cap = (int64_t)num_sms() * 4;  // four resident CTAs per SM
+    for (const DualGroup& g : groups) {
+        const int64_t n = g.tile0[g.count];
+        nvfp4_dual_multi_kernel<<<(unsigned)(n < cap ? n : cap), kDualThreads, 0, st>>>(g);
         CDLB200_CHECK_LAUNCH();
     }
     return CDLB200_OK;

@@ -20,7 +20,7 @@ from cdl_b200 import _lib
 
 from cdl_b200.api.quant import QTensor, Quant
 from cdl_b200.core.kernel.dequant import mxfp4_dequant, mxfp8_dequant, nvfp4_dequant
-from cdl_b200.core.kernel.quant import mxfp4_quant, mxfp8_quant, nvfp4_quant
+from cdl_b200.core.kernel.quant import mxfp4_quant, mxfp8_quant, nvfp4_dual_quant, nvfp4_quant
 
 Simulation = Literal["nvfp4", "mxfp4", "mxfp8"]
 
@@ -121,6 +121,39 @@ class SteTensor(QTensor):
                 res = fn(theta, swizzled=True)
         if cacheable:
             _ENCODED.insert(0, (weakref.ref(owner), key, (*res, deq)))
+            del _ENCODED[_ENCODED_MAX:]
+        return res
+
+    def encode_dual(self):
+        """NVFP4 encodings ``(row, col)`` of ``theta`` flattened to 2-D
+        ``[R, C]`` (R and C multiples of 64): ``row`` = ``encode_swizzled
+        ("nvfp4")`` and ``col`` the encoding of its transpose (blocks of 16
+        along dim 0), each ``(codes, GEMM-layout scales, alpha)``, from one
+        read of ``theta`` -- the forward GEMM's operand and the quantized
+        backward's.  A weight uses the optimizer's dual encoding while it is
+        current; an activation is kept, as in ``encode_swizzled``, for the
+        linears that share it, and uses its producer's amax words when they
+        exist."""
+        enc = self._weight_encoding("nvfp4")
+        if enc is not None and len(enc) > 5:
+            return (enc[1], enc[2], enc[3]), (enc[5], enc[6], enc[3])
+        theta = self.theta.reshape(-1, self.k)
+        owner = theta._base if theta._base is not None else theta
+        cacheable = not (owner.is_leaf and owner.requires_grad)
+        key = ("nvfp4_dual", theta.data_ptr(), tuple(theta.shape), theta.stride(), theta.dtype, theta._version)
+        if cacheable:
+            hit = _lookup(owner, key)
+            if hit is not None:
+                return hit
+        with torch.no_grad():
+            amax = getattr(owner, _AMAX_ATTR, None)
+            words = None
+            if (amax is not None and amax[1] == owner._version and theta.is_contiguous()
+                    and theta.data_ptr() == owner.data_ptr() and theta.numel() == owner.numel()):
+                words = amax[0]
+            res = nvfp4_dual_quant(theta, amax=words)
+        if cacheable:
+            _ENCODED.insert(0, (weakref.ref(owner), key, res))
             del _ENCODED[_ENCODED_MAX:]
         return res
 

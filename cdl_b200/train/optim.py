@@ -21,7 +21,8 @@ from torch.autograd.graph import increment_version
 
 from cdl_b200 import _lib
 
-# attribute of an encoded weight: (version, packed, scales, alpha, dequantized)
+# attribute of an encoded weight: (version, packed, scales, alpha, dequantized
+# or None[, packed of w^T, scales of w^T])
 ENCODED_ATTR = "_cdlb200_nvfp4"
 
 
@@ -42,7 +43,7 @@ class ClipAdamW(torch.optim.Optimizer):
 
     def __init__(self, params: Iterable[torch.Tensor], lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.999),
                  eps: float = 1e-8, weight_decay: float = 0.0, max_norm: float = 1.0,
-                 encode: Iterable[torch.Tensor] = ()):
+                 encode: Iterable[torch.Tensor] = (), encode_dual: Iterable[torch.Tensor] = ()):
         params = [p for p in params if p.requires_grad]
         if not params:
             raise ValueError("ClipAdamW: no parameters")
@@ -70,7 +71,9 @@ class ClipAdamW(torch.optim.Optimizer):
         self._ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
         self._norm = torch.zeros((), dtype=torch.float32, device=dev)
         self.device = dev
-        self._encoder = WeightEncoder(self, list(encode)) if encode else None
+        encode, encode_dual = list(encode), list(encode_dual)
+        self._encoders = ([WeightEncoder(self, encode)] if encode else []) + (
+            [WeightEncoder(self, encode_dual, dual=True)] if encode_dual else [])
 
     @property
     def lr(self) -> float:
@@ -101,8 +104,8 @@ class ClipAdamW(torch.optim.Optimizer):
         # the kernels wrote the parameters in place: advance their version
         # counters as a torch in-place update would
         increment_version([p for i, p in enumerate(self.params) if tab[i].numel])
-        if self._encoder is not None:
-            self._encoder.refresh()
+        for enc in self._encoders:
+            enc.refresh()
         return self._norm.clone()
 
     @property
@@ -146,37 +149,50 @@ class WeightEncoder:
     cdl quantizes every weight in each forward and dequantizes it again for
     the bf16 dgrad GEMM of the backward (core/mm/nvfp4.py).  The weights only
     change in the optimizer step, so here the update kernel also folds each
-    weight's new max|w| into an amax word, and right after it one launch of
-    ``cdlb200_nvfp4_encode_multi`` writes, for every weight, the codes, the
-    GEMM-layout scales, alpha and the dequantized copy -- the same values the
-    per-layer quantize and dequantize would produce.  Each weight carries them
-    as ``ENCODED_ATTR`` together with its version; the linear layer uses them
-    while the version matches (see ``SteTensor``), else it quantizes as usual.
-    Weights that do not fit the encoder's layout (rows % 128, (k/16) % 4) are
+    weight's new max|w| into an amax word, and right after it one launch
+    writes, for every weight, the codes, the GEMM-layout scales, alpha and
+    either the dequantized copy the bf16 backward reads
+    (``cdlb200_nvfp4_encode_multi``) or, with ``dual``, the encoding of
+    ``w^T`` the quantized dgrad GEMM reads (``cdlb200_nvfp4_dual_multi``) --
+    the same values the per-layer quantize and dequantize would produce.
+    Each weight carries them as ``ENCODED_ATTR`` together with its version;
+    the linear layer uses them while the version matches (see ``SteTensor``),
+    else it quantizes as usual.  Weights that do not fit the encoder's layout
+    (rows % 128 and (k/16) % 4; with ``dual`` rows and k multiples of 64) are
     left to the per-layer path."""
 
-    def __init__(self, opt: ClipAdamW, weights: list[torch.Tensor]):
+    def __init__(self, opt: ClipAdamW, weights: list[torch.Tensor], dual: bool = False):
         index = {id(p): i for i, p in enumerate(opt.params)}
         self.opt = opt
-        self.weights = [w for w in weights if id(w) in index and w.dim() == 2 and w.shape[0] % 128 == 0
-                        and w.shape[1] % 64 == 0]
+        self.dual = dual
+        fits = ((lambda w: w.shape[0] % 64 == 0 and w.shape[1] % 64 == 0) if dual
+                else (lambda w: w.shape[0] % 128 == 0 and w.shape[1] % 64 == 0))
+        self.weights = [w for w in weights if id(w) in index and w.dim() == 2 and fits(w)]
         dev = opt.device
         n = len(self.weights)
         self.amax = torch.zeros(max(n, 1), dtype=torch.int32, device=dev)
-        self.table = (_lib.Nvfp4EncodeTensor * max(n, 1))()
+        self.table = ((_lib.Nvfp4DualTensor if dual else _lib.Nvfp4EncodeTensor) * max(n, 1))()
         self.buffers = []
         for j, w in enumerate(self.weights):
             rows, k = w.shape
             packed = torch.empty(rows, k // 2, dtype=torch.uint8, device=dev)
-            scale = torch.empty(rows, k // 16, dtype=torch.uint8, device=dev)
+            scale = torch.empty((rows + 127) // 128 * 128, k // 16, dtype=torch.uint8, device=dev)
             alpha = torch.empty(1, dtype=torch.float32, device=dev)
-            deq = torch.empty(rows, k, dtype=torch.bfloat16, device=dev)
             amax_ptr = self.amax.data_ptr() + 4 * j
             t = self.table[j]
-            t.x, t.rows, t.k, t.amax, t.amax_words = w.data_ptr(), rows, k, amax_ptr, 1
-            t.packed, t.scale, t.alpha, t.deq = packed.data_ptr(), scale.data_ptr(), alpha.data_ptr(), deq.data_ptr()
+            if dual:
+                tpacked = torch.empty(k, rows // 2, dtype=torch.uint8, device=dev)
+                tscale = torch.empty((k + 127) // 128 * 128, rows // 16, dtype=torch.uint8, device=dev)
+                t.x, t.rows, t.cols, t.amax, t.amax_words, t.alpha = w.data_ptr(), rows, k, amax_ptr, 1, alpha.data_ptr()
+                t.row_packed, t.row_scale = packed.data_ptr(), scale.data_ptr()
+                t.col_packed, t.col_scale = tpacked.data_ptr(), tscale.data_ptr()
+                self.buffers.append((packed, scale, alpha, None, tpacked, tscale))
+            else:
+                deq = torch.empty(rows, k, dtype=torch.bfloat16, device=dev)
+                t.x, t.rows, t.k, t.amax, t.amax_words = w.data_ptr(), rows, k, amax_ptr, 1
+                t.packed, t.scale, t.alpha, t.deq = packed.data_ptr(), scale.data_ptr(), alpha.data_ptr(), deq.data_ptr()
+                self.buffers.append((packed, scale, alpha, deq))
             opt._table[index[id(w)]].amax = amax_ptr
-            self.buffers.append((packed, scale, alpha, deq))
 
     def refresh(self) -> None:
         """Encode the weights the last update wrote (those that had a grad)."""
@@ -190,8 +206,8 @@ class WeightEncoder:
                 live.append(j)
         if not live:
             return
-        _lib.call("cdlb200_nvfp4_encode_multi", ctypes.addressof(self.table), len(self.weights),
-                  _lib.stream(opt.device))
+        fn = "cdlb200_nvfp4_dual_multi" if self.dual else "cdlb200_nvfp4_encode_multi"
+        _lib.call(fn, ctypes.addressof(self.table), len(self.weights), _lib.stream(opt.device))
         for j in live:
             w = self.weights[j]
             setattr(w, ENCODED_ATTR, (w._version, *self.buffers[j]))

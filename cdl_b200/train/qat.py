@@ -398,10 +398,15 @@ class QatStep:
         if self.optimizer == "fused":
             from cdl_b200.train.optim import ClipAdamW
 
-            # the QLinear weights of the nvfp4 backend are re-encoded by the step that updates them
-            encode = [m.weight for m in self.model.modules() if isinstance(m, QLinear) and m.backend == "nvfp4"]
+            # the QLinear weights of the nvfp4 backends are re-encoded by the
+            # step that updates them: with the dequantized copy the bf16
+            # backward reads (nvfp4), or with the encoding of w^T the quantized
+            # dgrad reads (nvfp4_qbwd)
+            qls = [m for m in self.model.modules() if isinstance(m, QLinear) and isinstance(m.weight_quant, SteQuant)]
+            encode = [m.weight for m in qls if m.backend == "nvfp4"]
+            encode_dual = [m.weight for m in qls if m.backend == "nvfp4_qbwd"]
             self.opt = ClipAdamW(params, lr=lr, betas=(0.9, 0.95), weight_decay=0.0, max_norm=grad_clip,
-                                 encode=encode)
+                                 encode=encode, encode_dual=encode_dual)
         elif self.optimizer == "torch":
             groups = [{"params": decay, "weight_decay": 0.0}, {"params": no_decay, "weight_decay": 0.0},
                       {"params": quant_params, "lr": quant_lr, "weight_decay": 0.0}]

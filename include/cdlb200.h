@@ -95,6 +95,16 @@ int cdlb200_nvfp4_quant(const void* x, int64_t rows, int64_t k, int64_t ldx, int
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * The global-amax pass of cdlb200_nvfp4_quant on its own: gmax = max|x|
+ * clamped to FLT_MIN (NaN if x holds one), alpha = gmax / 2688, as cdl's
+ * `_quant` forms them before its Triton kernel (cdl/core/kernel/quant.py:96-101).
+ * gmax and alpha are fp32 [1] device outputs; workspace as for
+ * cdlb200_nvfp4_quant.  Feeds cdlb200_nvfp4_dual_multi (cdlb200_step.h).
+ */
+int cdlb200_nvfp4_amax(const void* x, int64_t rows, int64_t k, int64_t ldx, float* gmax, float* alpha,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * NVFP4 quantize that allocates nothing and takes no workspace.  It has no
  * counterpart in the reference: it exists for callers that cannot allocate
  * device memory (a host binding this C ABI from another runtime without a

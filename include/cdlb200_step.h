@@ -118,6 +118,33 @@ typedef struct {
  * the weight dequantize of the backward (dequant.py:103-109). */
 int cdlb200_nvfp4_encode_multi(const cdlb200_nvfp4_encode_tensor* tensors, int count, void* stream);
 
+/* One tensor of the dual NVFP4 encoder below. */
+typedef struct {
+    const void* x;          /* bf16 [rows, cols], contiguous, 16-byte aligned; rows % 64 == 0, cols % 64 == 0 */
+    int64_t rows, cols;
+    const uint32_t* amax;   /* bf16 magnitude bits of max|x| (the maximum of amax_words words), or NULL and ... */
+    const float* gmax;      /* ... max|x| as fp32 (cdlb200_nvfp4_quant's gmax output, e.g. of its amax pass) */
+    int32_t amax_words;     /* 1..64 with amax */
+    int32_t pad;
+    float* alpha;           /* fp32 [1] output: gmax / 2688, the alpha of both encodings */
+    void* row_packed;       /* optional (NULL: skipped): uint8 [rows, cols/2], x in blocks of 16 along cols, 8-byte aligned */
+    void* row_scale;        /* uint8, the 128x4 GEMM layout of [rows, cols/16] (rows padded to 128) */
+    void* col_packed;       /* optional: uint8 [cols, rows/2], x^T in blocks of 16 along rows, 16-byte aligned */
+    void* col_scale;        /* uint8, the 128x4 GEMM layout of [cols, rows/16] (cols padded to 128) */
+} cdlb200_nvfp4_dual_tensor;
+
+/* NVFP4 encodings of x and of x^T from one read of x, for many tensors in one
+ * launch (per 128 tensors): the codes, scale bytes and alpha that
+ * cdlb200_nvfp4_quant (CDLB200_SCALE_SWIZZLED) writes for x (transpose 0) and
+ * for x^T (transpose 1), with the global amax given.  They are the operands of
+ * the quantized backward GEMMs of a linear layer out = x w^T with gradient g:
+ * dgrad = Q(g) Q(w^T)^T, wgrad = Q(g^T) Q(x^T)^T, where cdl's backward
+ * (cdl/core/mm/nvfp4.py:46-63) multiplies bf16 g by dequantized operands
+ * instead; each encoding is cdl's quantize (cdl/core/kernel/quant.py:71-131)
+ * of that matrix.  Padding rows of a scale matrix (rows or cols not a
+ * multiple of 128) are zeroed. */
+int cdlb200_nvfp4_dual_multi(const cdlb200_nvfp4_dual_tensor* tensors, int count, void* stream);
+
 /* ECDL stochastic quantizer (cdl/core/kernel/ecdl: launch.py launch_ecdl_fwd /
  * launch_ecdl_bwd, kernel.py _ecdl_fwd / _ecdl_bwd).  theta is bf16 (theta_f32
  * = 0) or fp32, [rows, nb * block] with block 16 (NVFP4) or 32 (MXFP4 /

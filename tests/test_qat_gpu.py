@@ -47,7 +47,7 @@ def test_loss_curve_nvfp4_vs_native():
     spec = qat.SPECS["tiny"]
     dev = torch.device("cuda")
     curves, norms = {}, {}
-    for be in ("native", "nvfp4"):
+    for be in ("native", "nvfp4", "nvfp4_qbwd"):
         step = qat.QatStep(spec, dev, backend=be, lr=3e-4, seed=0)
         losses, gns = [], []
         for i in range(60):
@@ -57,8 +57,9 @@ def test_loss_curve_nvfp4_vs_native():
             gns.append(float(gn))
         curves[be], norms[be] = losses, gns
     assert abs(curves["native"][0] - qat.expected_initial_loss(spec)) < 0.5
-    for a, b in zip(curves["nvfp4"], curves["native"]):
-        assert abs(a - b) / b < 5e-3, (a, b)
+    for be in ("nvfp4", "nvfp4_qbwd"):
+        for a, b in zip(curves[be], curves["native"]):
+            assert abs(a - b) / b < 5e-3, (be, a, b)
     for a, b in zip(norms["nvfp4"][:10], norms["native"][:10]):
         assert abs(a - b) / b < 5e-2, (a, b)
 
@@ -209,3 +210,56 @@ def test_qat_step_lora_with_warmup():
     assert step.opt.param_groups[0]["lr"] == pytest.approx(3e-3)
     assert torch.equal(lin.weight.detach(), w0) and not torch.equal(lin.lora.b.detach(), b0)
     assert min(losses[-3:]) < losses[0]
+
+
+def test_dual_quantized_backward_matches_oracle_checked_path():
+    """The nvfp4_qbwd QLinear with every dimension a multiple of 64 runs on
+    the dual encodings (x, w in the forward, g in the backward); its output
+    and gradients equal, bit for bit, the nvfp4 forward and the quantized
+    gradients of the single-direction path checked against the oracle above."""
+    from cdl_b200.core.mm.blockscaled import _quantized_grads
+    from cdl_b200.model.components.linear import QLinear
+    from cdl_b200.model.components.quant.ste import SteQuant
+
+    torch.manual_seed(0)
+    lin = torch.nn.Linear(576, 320, bias=False).cuda().bfloat16()
+    res = {}
+    for be in ("nvfp4", "nvfp4_qbwd"):
+        q = QLinear.from_linear(lin)
+        q.set_activation_quant(SteQuant("nvfp4"))
+        q.set_weight_quant(SteQuant("nvfp4"))
+        q.set_backend(be)
+        x = torch.randn(3, 128, 576, device="cuda", dtype=torch.bfloat16,
+                        generator=torch.Generator("cuda").manual_seed(1)).requires_grad_(True)
+        y = q(x)
+        g = torch.randn_like(y, generator=torch.Generator("cuda").manual_seed(2))
+        y.backward(g)
+        res[be] = (y.detach(), x.grad.detach(), q.weight.grad.detach(), x.detach(), g)
+    assert torch.equal(res["nvfp4"][0], res["nvfp4_qbwd"][0])
+    y, dx, dw, x, g = res["nvfp4_qbwd"]
+    rdx, rdw = _quantized_grads("nvfp4", g.reshape(-1, 320).contiguous(), x.reshape(-1, 576), lin.weight.detach())
+    assert torch.equal(dx.reshape(-1, 576), rdx)
+    assert torch.equal(dw, rdw)
+
+
+def test_optimizer_dual_weight_encodings():
+    """After a step of the nvfp4_qbwd QAT step, every weight carries the
+    optimizer's encodings of w and w^T, equal to the quantizers' own."""
+    from cdl_b200.core.kernel.quant import nvfp4_quant
+    from cdl_b200.model.components.linear import QLinear
+    from cdl_b200.train import qat
+    from cdl_b200.train.optim import ENCODED_ATTR
+
+    spec = qat.SPECS["tiny"]
+    dev = torch.device("cuda")
+    step = qat.QatStep(spec, dev, backend="nvfp4_qbwd", seed=0)
+    step.step(qat.random_tokens(2, 128, spec.vocab, seed=0, device=dev))
+    qls = [m for m in step.model.modules() if isinstance(m, QLinear)]
+    assert qls
+    for m in qls:
+        enc = getattr(m.weight, ENCODED_ATTR)
+        assert enc[0] == m.weight._version and enc[4] is None
+        p, s, a = nvfp4_quant(m.weight.detach(), swizzled=True)
+        tp, ts, _ = nvfp4_quant(m.weight.detach(), transpose=True, swizzled=True)
+        assert torch.equal(enc[1], p) and torch.equal(enc[2], s) and torch.equal(enc[3], a)
+        assert torch.equal(enc[5], tp) and torch.equal(enc[6], ts)
