@@ -33,6 +33,7 @@ from cdl_b200.core.kernel.quant import mxfp4_quant, mxfp8_quant, nvfp4_dual_quan
 from cdl_b200.core.mm.swizzle import expand_rows, pad_k, pad_n, swizzle_scale_factors
 from cdl_b200.model.wrapper.ops import mm_fp4_direct as mm_fp4
 from cdl_b200.model.wrapper.ops import mm_mxfp8_direct as mm_mxfp8
+from cdl_b200.model.wrapper.ops import mm_nvfp4_alpha2
 
 _DEQ = {"nvfp4": nvfp4_dequant, "mxfp4": mxfp4_dequant, "mxfp8": mxfp8_dequant}
 _QUANT = {"nvfp4": nvfp4_quant, "mxfp4": mxfp4_quant, "mxfp8": mxfp8_quant}
@@ -90,7 +91,7 @@ class BlockScaledMatMul(torch.autograd.Function):
             (x_row, x_col), (w_row, w_col) = x.encode_dual(), w.encode_dual()
             ctx.dual = True
             ctx.save_for_backward(*x_col, *w_col)
-            return mm_fp4(x_row[0], w_row[0].T, x_row[1], w_row[1].T, x_row[2] * w_row[2], 16, True)
+            return mm_nvfp4_alpha2(x_row[0], w_row[0].T, x_row[1], w_row[1].T, x_row[2], w_row[2])
         # the quantized backward needs every GEMM dimension to be a multiple of 32
         ctx.qbwd = bool(quantized_backward) and x_proxy is not None and w_proxy is not None and all(
             d % 32 == 0 for d in (*x_proxy.shape, w_proxy.shape[0]))
@@ -150,8 +151,8 @@ class BlockScaledMatMul(torch.autograd.Function):
             need_dx, need_dw = ctx.needs_input_grad[2], ctx.needs_input_grad[4]
             g_row, g_col = nvfp4_dual_quant(grad_output.reshape(-1, grad_output.shape[-1]), rows=need_dx,
                                             cols=need_dw)
-            dx = mm_fp4(g_row[0], wc_p.T, g_row[1], wc_s.T, g_row[2] * wc_a, 16, True) if need_dx else None
-            dw = mm_fp4(g_col[0], xc_p.T, g_col[1], xc_s.T, g_col[2] * xc_a, 16, True) if need_dw else None
+            dx = mm_nvfp4_alpha2(g_row[0], wc_p.T, g_row[1], wc_s.T, g_row[2], wc_a) if need_dx else None
+            dw = mm_nvfp4_alpha2(g_col[0], xc_p.T, g_col[1], xc_s.T, g_col[2], xc_a) if need_dw else None
             return None, None, dx, None, dw, None
         if ctx.qbwd:
             x_src, w_src = ctx.proxies

@@ -172,16 +172,27 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                  : "memory");
 }
 
+struct GemmArgs;
+__device__ __forceinline__ float epilogue_alpha(const GemmArgs& args);
+
 struct GemmArgs {
     const uint8_t* sfa;  // swizzled scale atoms of A
     const uint8_t* sfb;  // swizzled scale atoms of B
-    const float* alpha;  // device scalar, may be null (1.0)
+    const float* alpha;    // device scalar, may be null (1.0)
+    const float* alpha_b;  // second device scalar multiplied in (fp32, RN), may be null
     uint16_t* out;       // bf16 [M, ldo]
     int m, n, kbytes;    // kbytes = K in bytes per row (K/2 FP4, K FP8)
     int ldo;
     int c4a, c4b;        // scale atoms per 128-row block (ceil(nb/4))
     uint32_t* status;    // optional: non-zero after a timed-out wait
 };
+
+// alpha * alpha_b as one fp32 product (what a torch multiply of the two
+// scalars would give)
+__device__ __forceinline__ float epilogue_alpha(const GemmArgs& args) {
+    const float a = args.alpha ? *args.alpha : 1.0f;
+    return args.alpha_b ? __fmul_rn(a, *args.alpha_b) : a;
+}
 
 template <int KIND>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -299,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) atomicExch(&abort_s, 1);
         ok = __all_sync(0xffffffffu, ok && !*(volatile int*)&abort_s);  // tcgen05.ld is warp-collective
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const float alpha = args.alpha ? *args.alpha : 1.0f;
+        const float alpha = epilogue_alpha(args);
         const int row = m0 + 32 * q + lane;
         if (ok) {
 #pragma unroll 1
@@ -726,7 +737,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
         const int r = 32 * q + lane;  // row of the tile = TMEM lane
         const uint32_t lane_off = (uint32_t)(32 * q) << 16;
         const uint32_t acc_empty0 = map_rank(&acc_empty, 0);
-        const float alpha = args.alpha ? *args.alpha : 1.0f;
+        const float alpha = epilogue_alpha(args);
         // staging: four 64-column blocks of 128 rows x 128 bytes, 16-byte chunk c
         // of row r at chunk c ^ (r & 7) (the TMA 128-byte swizzle)
         uint8_t* out_s = smem + (size_t)k2Stages * k2StageBytes;
@@ -841,8 +852,9 @@ bool make_out_map(CUtensorMap* map, void* base, int64_t rows, int64_t cols, int6
 }
 
 template <int KIND>
-int launch_gemm(const void* a, const void* b, const void* sfa, const void* sfb, const float* alpha, int64_t m,
-                int64_t n, int64_t k, void* out, int64_t ldo, void* status, cudaStream_t st) {
+int launch_gemm(const void* a, const void* b, const void* sfa, const void* sfb, const float* alpha,
+                const float* alpha_b, int64_t m, int64_t n, int64_t k, void* out, int64_t ldo, void* status,
+                cudaStream_t st) {
     using T = KindTraits<KIND>;
     const int64_t kbytes = KIND == kMx8 ? k : k / 2;
     CUtensorMap ma, mb;
@@ -859,6 +871,7 @@ int launch_gemm(const void* a, const void* b, const void* sfa, const void* sfb, 
     args.sfa = static_cast<const uint8_t*>(sfa);
     args.sfb = static_cast<const uint8_t*>(sfb);
     args.alpha = alpha;
+    args.alpha_b = alpha_b;
     args.out = static_cast<uint16_t*>(out);
     args.m = (int)m;
     args.n = (int)n;
@@ -922,8 +935,20 @@ extern "C" int cdlb200_mm_fp4(const void* a, const void* b, const void* a_scale,
     int rc = gemm_checks(a, b, a_scale, b_scale, m, n, k, 32, out, ldo);
     if (rc != CDLB200_OK || m == 0 || n == 0) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    return use_nvfp4 ? launch_gemm<kNv>(a, b, a_scale, b_scale, alpha, m, n, k, out, ldo, status, st)
-                     : launch_gemm<kMx4>(a, b, a_scale, b_scale, alpha, m, n, k, out, ldo, status, st);
+    return use_nvfp4 ? launch_gemm<kNv>(a, b, a_scale, b_scale, alpha, nullptr, m, n, k, out, ldo, status, st)
+                     : launch_gemm<kMx4>(a, b, a_scale, b_scale, alpha, nullptr, m, n, k, out, ldo, status, st);
+}
+
+extern "C" int cdlb200_mm_fp4_alpha2(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                                     const float* alpha_a, const float* alpha_b, int64_t m, int64_t n, int64_t k,
+                                     int block_size, int use_nvfp4, void* out, int64_t ldo, void* status,
+                                     void* stream) {
+    if ((use_nvfp4 && block_size != 16) || (!use_nvfp4 && block_size != 32)) return CDLB200_ERR_INVALID_ARG;
+    int rc = gemm_checks(a, b, a_scale, b_scale, m, n, k, 32, out, ldo);
+    if (rc != CDLB200_OK || m == 0 || n == 0) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return use_nvfp4 ? launch_gemm<kNv>(a, b, a_scale, b_scale, alpha_a, alpha_b, m, n, k, out, ldo, status, st)
+                     : launch_gemm<kMx4>(a, b, a_scale, b_scale, alpha_a, alpha_b, m, n, k, out, ldo, status, st);
 }
 
 extern "C" int cdlb200_mm_mxfp8(const void* a, const void* b, const void* a_scale, const void* b_scale,
@@ -931,6 +956,6 @@ extern "C" int cdlb200_mm_mxfp8(const void* a, const void* b, const void* a_scal
                                 void* status, void* stream) {
     int rc = gemm_checks(a, b, a_scale, b_scale, m, n, k, 16, out, ldo);
     if (rc != CDLB200_OK || m == 0 || n == 0) return rc;
-    return launch_gemm<kMx8>(a, b, a_scale, b_scale, alpha, m, n, k, out, ldo, status,
+    return launch_gemm<kMx8>(a, b, a_scale, b_scale, alpha, nullptr, m, n, k, out, ldo, status,
                              static_cast<cudaStream_t>(stream));
 }

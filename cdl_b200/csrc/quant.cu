@@ -222,6 +222,35 @@ __device__ __forceinline__ float recip_nr(float s) {
     return __fmaf_rn(y0, e, y0);
 }
 
+__device__ __forceinline__ uint32_t bf16x2_gt(uint32_t a, uint32_t b) {
+    uint32_t m;
+    asm("set.gt.u32.bf16x2 %0, %1, %2;" : "=r"(m) : "r"(a), "r"(b));
+    return m;  // 0xffff in each half where a > b
+}
+
+// 8 elements (one uint4: pairs (x0,x1) .. (x6,x7)) -> 8 nibbles, exact, by a
+// three-level binary search of each bf16 magnitude against the thresholds.
+// Words are regrouped as (x_k, x_k+4) so that each lane's result bits land in
+// its own 16-bit half: nibble k in bits 4k.., nibble k+4 in bits 16+4k...
+__device__ __forceinline__ uint32_t search8(const uint4& w, const uint32_t* tt) {
+    const uint32_t r[4] = {__byte_perm(w.x, w.z, 0x5410), __byte_perm(w.x, w.z, 0x7632),
+                           __byte_perm(w.y, w.w, 0x5410), __byte_perm(w.y, w.w, 0x7632)};
+    uint32_t out = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint32_t a = r[k] & 0x7fff7fffu;
+        const uint32_t c3 = bf16x2_gt(a, tt[3]);
+        const uint32_t c2 = bf16x2_gt(a, (c3 & tt[5]) | (~c3 & tt[1]));
+        const uint32_t hi = (c2 & tt[6]) | (~c2 & tt[4]);
+        const uint32_t lo = (c2 & tt[2]) | (~c2 & tt[0]);
+        const uint32_t c1 = bf16x2_gt(a, (c3 & hi) | (~c3 & lo));
+        const uint32_t sh = 4 * k;
+        out |= (c1 & (0x00010001u << sh)) | (c2 & (0x00020002u << sh)) | (c3 & (0x00040004u << sh)) |
+               ((r[k] >> (12 - sh)) & (0x00080008u << sh));
+    }
+    return out;
+}
+
 // One NVFP4 block of 16 elements (w0, w1) with amax bits `mag`: returns the
 // scale byte and writes the 8 code bytes to out.x / out.y.
 //
@@ -246,12 +275,14 @@ __device__ __forceinline__ uint32_t nvfp4_block16(const uint4& w0, const uint4& 
             out.x = cvt8_scaled(w0, c);
             out.y = cvt8_scaled(w1, c);
         } else {
-            BlockCode bc;
+            // a threshold lies within 64 ulp below a bf16 value: compare the
+            // bf16 magnitudes against t_j = RD_bf16(T_j) (x > T_j <=> x > t_j
+            // for bf16 x), packed two per word
+            uint32_t tt[7];
 #pragma unroll
-            for (int j = 0; j < 7; ++j) bc.t[j] = __fmaf_rd(mid_j(j), s, __fmul_rn(s, half_ulp_j(j)));
-            bc.exact_div = false;
-            out.x = encode8_fp4(w0, bc);
-            out.y = encode8_fp4(w1, bc);
+            for (int j = 0; j < 7; ++j) tt[j] = (f2u(__fmaf_rd(mid_j(j), s, __fmul_rn(s, half_ulp_j(j)))) >> 16) * 0x00010001u;
+            out.x = search8(w0, tt);
+            out.y = search8(w1, tt);
         }
     } else {
         BlockCode bc;
@@ -505,35 +536,6 @@ __device__ __forceinline__ ScaleEntry make_scale_entry(uint32_t byte, float alph
     e.c = __shfl_sync(0xffffffffu, c, (int)grp + (first < 0 ? 0 : first));
     e.kind = divide ? kDivide : (first < 0 ? kSearch : kCvt);
     return e;
-}
-
-__device__ __forceinline__ uint32_t bf16x2_gt(uint32_t a, uint32_t b) {
-    uint32_t m;
-    asm("set.gt.u32.bf16x2 %0, %1, %2;" : "=r"(m) : "r"(a), "r"(b));
-    return m;  // 0xffff in each half where a > b
-}
-
-// 8 elements (one uint4: pairs (x0,x1) .. (x6,x7)) -> 8 nibbles, exact, by a
-// three-level binary search of each bf16 magnitude against the thresholds.
-// Words are regrouped as (x_k, x_k+4) so that each lane's result bits land in
-// its own 16-bit half: nibble k in bits 4k.., nibble k+4 in bits 16+4k...
-__device__ __forceinline__ uint32_t search8(const uint4& w, const uint32_t* tt) {
-    const uint32_t r[4] = {__byte_perm(w.x, w.z, 0x5410), __byte_perm(w.x, w.z, 0x7632),
-                           __byte_perm(w.y, w.w, 0x5410), __byte_perm(w.y, w.w, 0x7632)};
-    uint32_t out = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const uint32_t a = r[k] & 0x7fff7fffu;
-        const uint32_t c3 = bf16x2_gt(a, tt[3]);
-        const uint32_t c2 = bf16x2_gt(a, (c3 & tt[5]) | (~c3 & tt[1]));
-        const uint32_t hi = (c2 & tt[6]) | (~c2 & tt[4]);
-        const uint32_t lo = (c2 & tt[2]) | (~c2 & tt[0]);
-        const uint32_t c1 = bf16x2_gt(a, (c3 & hi) | (~c3 & lo));
-        const uint32_t sh = 4 * k;
-        out |= (c1 & (0x00010001u << sh)) | (c2 & (0x00020002u << sh)) | (c3 & (0x00040004u << sh)) |
-               ((r[k] >> (12 - sh)) & (0x00080008u << sh));
-    }
-    return out;
 }
 
 // NVFP4 fused path: global amax and encode in ONE persistent cooperative
@@ -841,16 +843,17 @@ __global__ void __launch_bounds__(kEncThreads) nvfp4_encode_multi_kernel(const _
 constexpr int kDualT = 64;                  // tile rows = tile columns
 constexpr int kDualPitch = kDualT + 8;      // staged row: 64 bf16 + 16 bytes of padding
 constexpr int kDualThreads = 256;
+constexpr int kDualStages = 3;              // tiles in shared memory: one encoded, two loading
 constexpr int kDualGroup = 128;             // tensors per launch (table in the parameter block)
 
 struct DualGroup {
     int count, pad;
-    int64_t tile0[kDualGroup + 1];  // global index of each tensor's first tile
-    int32_t tiles_c[kDualGroup];    // cols / 64
+    int32_t tile0[kDualGroup + 1];  // index of each tensor's first tile in the launch
+    FastDiv tiles_c[kDualGroup];    // cols / 64
     cdlb200_nvfp4_dual_tensor t[kDualGroup];
 };
 
-__device__ __forceinline__ int dual_tensor_of(const DualGroup& g, int64_t tile) {
+__device__ __forceinline__ int dual_tensor_of(const DualGroup& g, int32_t tile) {
     int lo = 0, hi = g.count - 1;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
@@ -880,99 +883,170 @@ __device__ __forceinline__ Nvfp4Tensor dual_scale(const cdlb200_nvfp4_dual_tenso
     return tn;
 }
 
+struct DualTile {
+    int ti;
+    int64_t row0, col0;
+};
+
+__device__ __forceinline__ DualTile dual_locate(const DualGroup& g, int32_t tile) {
+    DualTile d;
+    d.ti = dual_tensor_of(g, tile);
+    const uint32_t lt = (uint32_t)(tile - g.tile0[d.ti]);
+    const uint32_t tr = g.tiles_c[d.ti].div(lt);
+    d.row0 = (int64_t)tr * kDualT;
+    d.col0 = (int64_t)(lt - tr * g.tiles_c[d.ti].d) * kDualT;
+    return d;
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+                 "l"(gmem)
+                 : "memory");
+}
+
+// One block with the tensor's scale table (see the fused kernel): the cvt
+// multiplier of the block's scale byte when it separates every threshold,
+// else the exact search (or the divide); `all_search` when the tensor has
+// many search entries, so that the warps do not diverge.
+__device__ __forceinline__ uint32_t table_block16(const uint4& a0, const uint4& a1, const Nvfp4Tensor& tn,
+                                                  const ScaleEntry* table, const float* ctab, bool all_search,
+                                                  uint2& out) {
+    const uint32_t byte = nvfp4_scale_byte(max(amax8(a0), amax8(a1)), tn) & 127u;
+    const float c = all_search ? -1.0f : ctab[byte];
+    if (c > 0.0f) {
+        out.x = cvt8_scaled(a0, c);
+        out.y = cvt8_scaled(a1, c);
+    } else {
+        out = encode_block(a0, a1, table[byte], all_search);
+    }
+    return byte;
+}
+
 __global__ void __launch_bounds__(kDualThreads, 4) nvfp4_dual_multi_kernel(const __grid_constant__ DualGroup g) {
-    __shared__ __align__(16) uint16_t xs[kDualT * kDualPitch];
-    __shared__ __align__(16) uint2 ccodes[kDualT * 4];  // column c, block b -> [4c + b]
-    __shared__ __align__(4) uint8_t cscale[kDualT * 4];
+    extern __shared__ __align__(16) uint8_t dual_smem[];
+    __shared__ ScaleEntry table[128];
+    __shared__ float ctab[128];  // the cvt multiplier of a kCvt entry, else -1
+    __shared__ int s_search;     // count of kSearch entries
+    uint16_t* xs0 = reinterpret_cast<uint16_t*>(dual_smem);  // kDualStages tiles of kDualT x kDualPitch
+    uint2* ccodes = reinterpret_cast<uint2*>(dual_smem + kDualStages * kDualT * kDualPitch * 2);  // [64 b + c]
+    uint8_t* cscale = reinterpret_cast<uint8_t*>(ccodes + kDualT * 4);                           // [4 c + b]
     const int tid = threadIdx.x, lane = tid & 31;
-    const int64_t total = g.tile0[g.count];
+    const int32_t total = g.tile0[g.count];
+    const int32_t first = (int32_t)blockIdx.x, stride = (int32_t)gridDim.x;
 
-    // tile -> (tensor, row0, col0)
-    auto locate = [&](int64_t tile, int& ti, int64_t& row0, int64_t& col0) {
-        ti = dual_tensor_of(g, tile);
-        const int64_t lt = tile - g.tile0[ti];
-        const int64_t tc = g.tiles_c[ti];
-        row0 = (lt / tc) * kDualT;
-        col0 = (lt % tc) * kDualT;
-    };
-    auto load = [&](int64_t tile, uint4 (&v)[2]) {
-        int ti;
-        int64_t row0, col0;
-        locate(tile, ti, row0, col0);
-        const cdlb200_nvfp4_dual_tensor& T = g.t[ti];
-        const uint16_t* x = static_cast<const uint16_t*>(T.x);
+    // copies of tile `tile` into stage `s`: two 16-byte pieces per thread,
+    // whole 128-byte row segments per 8 lanes
+    auto issue = [&](int32_t tile, int s) {
+        if (tile < total) {
+            const DualTile d = dual_locate(g, tile);
+            const cdlb200_nvfp4_dual_tensor& T = g.t[d.ti];
+            const uint16_t* x = static_cast<const uint16_t*>(T.x);
+            uint16_t* xs = xs0 + s * (kDualT * kDualPitch);
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const int e = tid + kDualThreads * j, r = e >> 3, c8 = (e & 7) * 8;
-            v[j] = ldg_stream(reinterpret_cast<const uint4*>(x + (row0 + r) * T.cols + col0 + c8));
-        }
-    };
-
-    uint4 v[2];
-    int64_t tile = blockIdx.x;
-    if (tile < total) load(tile, v);
-    for (; tile < total; tile += gridDim.x) {
-        int ti;
-        int64_t row0, col0;
-        locate(tile, ti, row0, col0);
-        const cdlb200_nvfp4_dual_tensor& T = g.t[ti];
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const int e = tid + kDualThreads * j, r = e >> 3, c8 = (e & 7) * 8;
-            *reinterpret_cast<uint4*>(&xs[r * kDualPitch + c8]) = v[j];
-        }
-        __syncthreads();
-        if (tile + gridDim.x < total) load(tile + gridDim.x, v);  // in flight during the encode
-        const Nvfp4Tensor tn = dual_scale(T, lane);
-        if (tile == g.tile0[ti] && tid == 0) *T.alpha = tn.alpha;
-
-        if (T.row_packed != nullptr) {  // ---- x: row r, block b
-            const int r = tid >> 2, b = tid & 3;
-            const uint4 w0 = *reinterpret_cast<const uint4*>(&xs[r * kDualPitch + 16 * b]);
-            const uint4 w1 = *reinterpret_cast<const uint4*>(&xs[r * kDualPitch + 16 * b + 8]);
-            uint2 out;
-            const uint32_t byte = nvfp4_block16(w0, w1, max(amax8(w0), amax8(w1)), tn, out);
-            *reinterpret_cast<uint2*>(static_cast<uint8_t*>(T.row_packed) + (row0 + r) * (T.cols / 2) + col0 / 2 +
-                                      8 * b) = out;
-            uint32_t word = byte << (8 * b);
-            word |= __shfl_xor_sync(0xffffffffu, word, 1);
-            word |= __shfl_xor_sync(0xffffffffu, word, 2);
-            if (b == 0) {
-                const int64_t c4 = (T.cols / 16 + 3) / 4;
-                *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(T.row_scale) +
-                                             swizzle_offset(row0 + r, col0 / 16, c4)) = word;
+            for (int j = 0; j < 2; ++j) {
+                const int e = tid + kDualThreads * j, r = e >> 3, c8 = (e & 7) * 8;
+                cp_async16(&xs[r * kDualPitch + c8], x + (d.row0 + r) * T.cols + d.col0 + c8);
             }
         }
-        if (T.col_packed != nullptr) {  // ---- x^T: column c, block b (rows 16b .. 16b + 15 of the tile)
-            const int c = tid & (kDualT - 1), b = tid >> 6;
-            uint32_t h[8];
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+
+    issue(first, 0);
+    issue(first + stride, 1);
+    int k = 0, cur_ti = -1;
+    Nvfp4Tensor tn;
+    bool all_search = false;
+    for (int32_t tile = first; tile < total; tile += stride, ++k) {
+        issue(tile + 2 * stride, (k + 2) % kDualStages);
+        asm volatile("cp.async.wait_group 2;" ::: "memory");  // this thread's copies of `tile` landed
+        __syncthreads();                                      // ... and every other thread's
+        const uint16_t* xs = xs0 + (k % kDualStages) * (kDualT * kDualPitch);
+        const DualTile d = dual_locate(g, tile);
+        const cdlb200_nvfp4_dual_tensor& T = g.t[d.ti];
+        const int64_t row0 = d.row0, col0 = d.col0;
+        if (d.ti != cur_ti) {  // the tensor's constants and scale table, once per tensor a CTA meets
+            tn = dual_scale(T, lane);
+            cur_ti = d.ti;
+            if (tid == 0) s_search = 0;
+            __syncthreads();  // the previous table is no longer read
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                h[i] = (uint32_t)xs[(16 * b + 2 * i) * kDualPitch + c] |
-                       ((uint32_t)xs[(16 * b + 2 * i + 1) * kDualPitch + c] << 16);
-            const uint4 w0 = make_uint4(h[0], h[1], h[2], h[3]), w1 = make_uint4(h[4], h[5], h[6], h[7]);
-            uint2 out;
-            const uint32_t byte = nvfp4_block16(w0, w1, max(amax8(w0), amax8(w1)), tn, out);
-            ccodes[4 * c + b] = out;
-            cscale[4 * c + b] = (uint8_t)byte;
+            for (int half = 0; half < 2; ++half) {  // 4 lanes per scale byte, one candidate multiplier each
+                const uint32_t byte = (uint32_t)((tid >> 2) + 64 * half);
+                const ScaleEntry e = make_scale_entry(byte < 1 ? 1u : (byte > 126 ? 126u : byte), tn.alpha, tid & 3);
+                if ((tid & 3) == 0) {
+                    table[byte] = e;
+                    ctab[byte] = e.kind == kCvt ? e.c : -1.0f;
+                    if (e.kind == kSearch && byte >= 1 && byte <= 126) atomicAdd(&s_search, 1);
+                }
+            }
+            __syncthreads();
+            all_search = s_search > kMaxSearchEntries;
         }
-        __syncthreads();  // staged columns complete; xs free for the next tile
+        if (tile == g.tile0[d.ti] && tid == 0) *T.alpha = tn.alpha;
+
+        if (tid < 128) {
+            // ---- x, warps 0-3: row r, blocks 2h and 2h + 1 (32 contiguous values)
+            if (T.row_packed != nullptr) {
+                const int r = tid >> 1, h = tid & 1;
+                const uint16_t* src = &xs[r * kDualPitch + 32 * h];
+                const uint4 a0 = *reinterpret_cast<const uint4*>(src), a1 = *reinterpret_cast<const uint4*>(src + 8);
+                const uint4 b0 = *reinterpret_cast<const uint4*>(src + 16), b1 = *reinterpret_cast<const uint4*>(src + 24);
+                uint2 oa, ob;
+                const uint32_t sa = table_block16(a0, a1, tn, table, ctab, all_search, oa);
+                const uint32_t sb = table_block16(b0, b1, tn, table, ctab, all_search, ob);
+                *reinterpret_cast<uint4*>(static_cast<uint8_t*>(T.row_packed) + (row0 + r) * (T.cols / 2) + col0 / 2 +
+                                          16 * h) = make_uint4(oa.x, oa.y, ob.x, ob.y);
+                uint32_t word = (sa | (sb << 8)) << (16 * h);
+                word |= __shfl_xor_sync(0xffffffffu, word, 1);
+                if (h == 0) {
+                    const int64_t c4 = T.cols / 64;  // (cols / 16) / 4: cols is a multiple of 64
+                    *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(T.row_scale) +
+                                                 swizzle_offset(row0 + r, col0 / 16, c4)) = word;
+                }
+            }
+        } else if (T.col_packed != nullptr) {
+            // ---- x^T, warps 4-7: columns 2p and 2p + 1, block b (tile rows 16b .. 16b + 15);
+            // one 32-bit load holds both columns' values of a row
+            const int t = tid - 128, p = t & 31, b = t >> 5;
+            const uint32_t* src = reinterpret_cast<const uint32_t*>(&xs[16 * b * kDualPitch + 2 * p]);
+            uint32_t v[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = src[i * (kDualPitch / 2)];
+            uint32_t e[8], o[8];  // column 2p / 2p + 1, rows (2i, 2i + 1)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                e[i] = __byte_perm(v[2 * i], v[2 * i + 1], 0x5410);
+                o[i] = __byte_perm(v[2 * i], v[2 * i + 1], 0x7632);
+            }
+            const uint4 e0 = make_uint4(e[0], e[1], e[2], e[3]), e1 = make_uint4(e[4], e[5], e[6], e[7]);
+            const uint4 o0 = make_uint4(o[0], o[1], o[2], o[3]), o1 = make_uint4(o[4], o[5], o[6], o[7]);
+            uint2 ce, co;
+            const uint32_t se = table_block16(e0, e1, tn, table, ctab, all_search, ce);
+            const uint32_t so = table_block16(o0, o1, tn, table, ctab, all_search, co);
+            *reinterpret_cast<uint4*>(&ccodes[kDualT * b + 2 * p]) = make_uint4(ce.x, ce.y, co.x, co.y);
+            cscale[4 * (2 * p) + b] = (uint8_t)se;
+            cscale[4 * (2 * p + 1) + b] = (uint8_t)so;
+        }
+        __syncthreads();  // staged columns complete; the stage is free for the copies issued next
         if (T.col_packed != nullptr) {
-            if (tid < 2 * kDualT) {  // output row col0 + c: 32 code bytes, two 16-byte halves
-                const int c = tid >> 1, half = tid & 1;
-                const uint4 q = *reinterpret_cast<const uint4*>(&ccodes[4 * c + 2 * half]);
+            if (tid < 2 * kDualT) {  // output row col0 + c: 32 code bytes, blocks (2h, 2h + 1) per half
+                const int c = tid >> 1, h = tid & 1;
+                const uint2 q0 = ccodes[kDualT * (2 * h) + c], q1 = ccodes[kDualT * (2 * h + 1) + c];
                 *reinterpret_cast<uint4*>(static_cast<uint8_t*>(T.col_packed) + (col0 + c) * (T.rows / 2) + row0 / 2 +
-                                          16 * half) = q;
+                                          16 * h) = make_uint4(q0.x, q0.y, q1.x, q1.y);
             } else if (tid < 3 * kDualT) {  // its scale word (blocks row0/16 .. +3)
                 const int c = tid - 2 * kDualT;
-                const int64_t c4 = (T.rows / 16 + 3) / 4;
+                const int64_t c4 = T.rows / 64;
                 *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(T.col_scale) +
                                              swizzle_offset(col0 + c, row0 / 16, c4)) =
                     *reinterpret_cast<const uint32_t*>(&cscale[4 * c]);
             }
         }
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
+
+constexpr int kDualSmem = kDualStages * kDualT * kDualPitch * 2 + kDualT * 4 * 8 + kDualT * 4;
 
 // ---------------------------------------------------------------------------
 // general path: any leading dimension, ragged k, transposed (dim-0) blocks.
@@ -1444,7 +1518,7 @@ extern "C" int cdlb200_nvfp4_dual_multi(const cdlb200_nvfp4_dual_tensor* tensors
         if (!t.x || !t.alpha || (!t.amax && !t.gmax) || (t.amax && (t.amax_words < 1 || t.amax_words > 64)))
             return CDLB200_ERR_INVALID_ARG;
         if ((t.row_packed && !t.row_scale) || (t.col_packed && !t.col_scale)) return CDLB200_ERR_INVALID_ARG;
-        if (t.rows * t.cols / 16 >= (1ll << 40)) return CDLB200_ERR_INVALID_ARG;
+        if ((t.rows / kDualT) * (t.cols / kDualT) >= (1ll << 31)) return CDLB200_ERR_INVALID_ARG;
         if (!aligned(t.x, 16) || (t.row_packed && !aligned(t.row_packed, 8)) ||
             (t.col_packed && !aligned(t.col_packed, 16)) || (t.row_scale && !aligned(t.row_scale, 4)) ||
             (t.col_scale && !aligned(t.col_scale, 4)))
@@ -1460,7 +1534,8 @@ extern "C" int cdlb200_nvfp4_dual_multi(const cdlb200_nvfp4_dual_tensor* tensors
         if (t.rows == 0 || t.cols == 0) continue;
         if (t.row_packed && (rc = zero_scale_tail(t.row_scale, t.rows, t.cols / 16, st)) != CDLB200_OK) return rc;
         if (t.col_packed && (rc = zero_scale_tail(t.col_scale, t.cols, t.rows / 16, st)) != CDLB200_OK) return rc;
-        if (groups.empty() || groups.back().count == kDualGroup) {
+        const int64_t nt = (t.rows / kDualT) * (t.cols / kDualT);
+        if (groups.empty() || groups.back().count == kDualGroup || tiles + nt >= (1ll << 31)) {
             groups.emplace_back();
             groups.back().count = 0;
             groups.back().pad = 0;
@@ -1468,15 +1543,22 @@ extern "C" int cdlb200_nvfp4_dual_multi(const cdlb200_nvfp4_dual_tensor* tensors
         }
         DualGroup& g = groups.back();
         g.t[g.count] = t;
-        g.tiles_c[g.count] = (int32_t)(t.cols / kDualT);
-        g.tile0[g.count] = tiles;
-        tiles += (t.rows / kDualT) * (t.cols / kDualT);
-        g.tile0[++g.count] = tiles;
+        g.tiles_c[g.count] = FastDiv((uint32_t)(t.cols / kDualT));
+        g.tile0[g.count] = (int32_t)tiles;
+        tiles += nt;
+        g.tile0[++g.count] = (int32_t)tiles;
+    }
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(nvfp4_dual_multi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDualSmem) !=
+            cudaSuccess)
+            return CDLB200_ERR_CUDA;
+        attr_set = true;
     }
     const int64_t cap = (int64_t)num_sms() * 4;  // four resident CTAs per SM
     for (const DualGroup& g : groups) {
         const int64_t n = g.tile0[g.count];
-        nvfp4_dual_multi_kernel<<<(unsigned)(n < cap ? n : cap), kDualThreads, 0, st>>>(g);
+        nvfp4_dual_multi_kernel<<<(unsigned)(n < cap ? n : cap), kDualThreads, kDualSmem, st>>>(g);
         CDLB200_CHECK_LAUNCH();
     }
     return CDLB200_OK;

@@ -66,6 +66,26 @@ def mm_fp4_direct(
     return out
 
 
+def mm_nvfp4_alpha2(a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor, b_scale: torch.Tensor,
+                    alpha_a: torch.Tensor, alpha_b: torch.Tensor) -> torch.Tensor:
+    """NVFP4 ``mm_fp4_direct`` with the two operands' alphas multiplied in the
+    GEMM epilogue (``cdlb200_mm_fp4_alpha2``) instead of by a separate launch."""
+    dev = _lib.require_cuda(a, b, a_scale, b_scale, alpha_a, alpha_b)
+    a = a.contiguous().view(torch.uint8)
+    brows = _storage_rows(b).view(torch.uint8)
+    m, k = a.shape[0], a.shape[1] * 2
+    n = brows.shape[0]
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    if m == 0 or n == 0:
+        return out
+    _lib.call(
+        "cdlb200_mm_fp4_alpha2", _lib.ptr(a), _lib.ptr(brows), _lib.ptr(_flat(a_scale)), _lib.ptr(_flat(b_scale)),
+        _lib.ptr(alpha_a), _lib.ptr(alpha_b), m, n, k, 16, 1, _lib.ptr(out), n, _lib.ptr(_lib.status_word(dev)),
+        _lib.stream(dev),
+    )
+    return out
+
+
 @torch.library.custom_op("cdl_b200::mm_fp4", mutates_args=())
 def mm_fp4(
     a: torch.Tensor,

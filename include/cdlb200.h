@@ -191,6 +191,16 @@ int cdlb200_mm_fp4(const void* a, const void* b, const void* a_scale, const void
                    void* out, int64_t ldo, void* status, void* stream);
 
 /*
+ * cdlb200_mm_fp4 with the alpha of each operand passed separately: the
+ * epilogue multiplies by RN(alpha_a * alpha_b), the product cdl forms on the
+ * host side of the call (cdl/core/mm/nvfp4.py:36-44 passes x_alpha * w_alpha),
+ * so the same GEMM needs no separate multiply launch.  Either may be NULL (1).
+ */
+int cdlb200_mm_fp4_alpha2(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                          const float* alpha_a, const float* alpha_b, int64_t m, int64_t n, int64_t k,
+                          int block_size, int use_nvfp4, void* out, int64_t ldo, void* status, void* stream);
+
+/*
  * Block-scaled MXFP8 GEMM (e4m3 elements, e8m0 scales, blocks of 32):
  * replaces cdl/model/wrapper/flashinfer.py:41-52 `cdl::mm_mxfp8` as called by
  * cdl/core/mm/mxfp8.py:36-51.  a: e4m3 [m, k], b: e4m3 [n, k] (storage of the
