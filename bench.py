@@ -81,8 +81,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--torch-profile", default="", metavar="PATH",
                     help="after the timed region, profile 2 more steps (CUDA kernels) and write the table to PATH")
-    ap.add_argument("--backend", default="nvfp4", choices=["nvfp4", "nvfp4_qbwd", "mxfp4", "mxfp8"],
-                    help="QAT workloads: QLinear backend (nvfp4 = cdl's numerics: bf16 backward)")
+    ap.add_argument("--backend", default="nvfp4_qbwd", choices=["nvfp4_qbwd", "nvfp4", "mxfp4", "mxfp8"],
+                    help="QAT workloads: QLinear backend (nvfp4_qbwd = NVFP4 forward, dgrad and wgrad, the "
+                         "configuration BASELINE names; nvfp4 = cdl's numerics: bf16 dgrad / wgrad)")
     ap.add_argument("--spinup-s", type=float, default=1.0, help="untimed clock ramp before warm-up")
     ap.add_argument("--no-graph", action="store_true", help="QAT workloads: eager steps even at N=1")
     ap.add_argument("--gemm-shape", default="8192,8192,8192", metavar="M,N,K",

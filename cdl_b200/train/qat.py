@@ -84,9 +84,13 @@ def _causal_attention() -> str:
     return _CAUSAL_SDPA
 
 
-def build_model(spec: ModelSpec, device: torch.device, seed: int = 0, fused: bool | None = None) -> nn.Module:
+def build_model(spec: ModelSpec, device: torch.device, seed: int = 0, fused: bool | None = None,
+                init_device: torch.device | str | None = None) -> nn.Module:
     """Random-init Llama of ``spec`` in bf16.  ``fused`` (default: on CUDA)
-    routes its RMSNorm / rotary / SwiGLU through the fused kernels."""
+    routes its RMSNorm / rotary / SwiGLU through the fused kernels.  The
+    weights are drawn on ``init_device`` (default ``device``) from
+    ``torch.manual_seed(seed)``: with ``init_device="cpu"`` they are the ones a
+    CPU run of the reference's script draws from the same seed."""
     from transformers import LlamaConfig, LlamaForCausalLM
 
     cfg = LlamaConfig(
@@ -98,9 +102,9 @@ def build_model(spec: ModelSpec, device: torch.device, seed: int = 0, fused: boo
     )
     cfg._attn_implementation = _causal_attention()
     torch.manual_seed(seed)
-    with torch.device(device):
+    with torch.device(init_device if init_device is not None else device):
         model = LlamaForCausalLM(cfg)
-    model = model.to(dtype=torch.bfloat16)
+    model = model.to(dtype=torch.bfloat16).to(device)
     if fused if fused is not None else device.type == "cuda":
         from cdl_b200.model.components.fused import patch_llama
 
@@ -345,11 +349,12 @@ class QatStep:
                  train_kappa: bool = False, use_lora: bool = False, lora_r: int = 8, lora_alpha: int = 16,
                  freeze_base: bool = False, train_head: bool = True, untie: bool = False, warmup_steps: int = 0,
                  lr_decay: str = "constant", max_steps: int = 0, min_lr_ratio: float = 0.1,
-                 fp32_master_weights: bool = False, **quant_options):
+                 fp32_master_weights: bool = False, init_device: torch.device | str | None = None,
+                 **quant_options):
         self.spec = spec
         self.device = device
         self.backend = backend
-        self.model = build_model(spec, device, seed, fused)
+        self.model = build_model(spec, device, seed, fused, init_device)
         # the BASELINE configs train every parameter with tied embeddings;
         # cdl's script unties the head and applies its freeze policy
         if untie or use_lora or freeze_base:

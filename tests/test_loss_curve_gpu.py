@@ -1,0 +1,57 @@
+"""Loss-curve parity of the B200 QAT step against the reference's own step.
+
+``tests/golden/loss_curve_135m.json`` was made by
+``tests/golden/make_loss_curve.py``: the reference's QLinear + SteQuant
+("nvfp4") + native backend (dequantize, bf16 matmul, STE) on every linear of a
+random-init SmolLM2-135M (BASELINE config C4 dimensions), cross entropy
+through the unquantized head, clip 1.0 + AdamW (lr 3e-4, betas 0.9/0.95),
+run on the CPU from seed 0 for 200 steps on seeded uniform token batches
+(smaller than C4's 8 x 2048 tokens per step so that the reference run on the
+host cores ends in about half an hour; the fixture records its batch).
+
+Here the same model (drawn on the CPU from the same seed) and the same
+batches train on the GPU with the ``nvfp4`` backend (FP4 forward GEMM, bf16
+backward: the reference's numerics) and the ``nvfp4_qbwd`` backend (FP4
+forward, dgrad and wgrad).  BASELINE criterion: the loss stays within 0.5 %
+of the reference's at every one of the 200 steps.  The gradient norms of the
+first steps, which move most, are compared too.
+"""
+
+import json
+import os
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _reference():
+    with open(os.path.join(HERE, "golden", "loss_curve_135m.json")) as f:
+        return json.load(f)
+
+
+@pytest.mark.parametrize("backend,gnorm_tol", [("nvfp4", 0.05), ("nvfp4_qbwd", 0.15)])
+def test_loss_curve_matches_reference_200_steps(backend, gnorm_tol):
+    from cdl_b200 import workloads
+    from cdl_b200.train import qat
+
+    ref = _reference()
+    assert ref["steps"] >= 200 and len(ref["loss"]) == ref["steps"]
+    spec = qat.SPECS[ref["spec"]]
+    dev = torch.device("cuda")
+    step = qat.QatStep(spec, dev, backend=backend, lr=3e-4, seed=ref["seed"], init_device="cpu")
+    losses, gnorms = [], []
+    for ids in workloads.token_batches(ref["batch"], ref["seq"], spec.vocab, ref["seed"], ref["steps"]):
+        loss, gn = step.step(ids.to(dev))
+        losses.append(loss)
+        gnorms.append(gn)
+    step.check_status()
+    losses = [float(v) for v in losses]
+    gnorms = [float(v) for v in gnorms]
+    worst = max(abs(a - b) / b for a, b in zip(losses, ref["loss"]))
+    assert worst < 5e-3, worst
+    for i, (a, b) in enumerate(zip(gnorms[:10], ref["grad_norm"][:10])):
+        assert abs(a - b) / b < gnorm_tol, (i, a, b)
