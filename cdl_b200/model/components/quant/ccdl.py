@@ -32,8 +32,30 @@ from cdl_b200.core.kernel.ccdl import ccdl_quant, ccdl_round
 from cdl_b200.core.kernel.dequant import mxfp4_dequant, mxfp8_dequant, nvfp4_dequant
 from cdl_b200.core.kernel.ecdl import FormatId
 from cdl_b200.model.components.quant.ecdl import group_tensor_into_blocks
+from cdl_b200.model.components.quant.identity import IdentityTensor
 
 Kernel = Literal["torch", "triton"]
+
+
+def _unblock(t: torch.Tensor, k: int) -> torch.Tensor:
+    """``[..., nb, block]`` back to ``[..., k]`` (the padded tail dropped)."""
+    return t.flatten(-2)[..., :k]
+
+
+def _block_amax(t: torch.Tensor, block: int) -> torch.Tensor:
+    """max |t| of each block of ``block`` along the last dim, ``[..., nb, 1]``."""
+    blocked, _ = group_tensor_into_blocks(t, block)
+    return blocked.abs().amax(dim=-1, keepdim=True)
+
+
+class _Exp:
+    """Read-only attribute ``exp(<name>)`` of a log-parameterised parameter."""
+
+    def __init__(self, name: str):
+        self.name = name
+
+    def __get__(self, obj, owner=None):
+        return self if obj is None else getattr(obj, self.name).exp()
 
 
 @dataclass(frozen=True)
@@ -102,20 +124,12 @@ class PackedCcdlTensor(QTensor):
         return out.to(self.eval_dtype if self.eval_dtype is not None else self.dtype)
 
     def proxy(self) -> torch.Tensor | None:
-        if self.grad_proxy is None:
-            return None
-        return self.grad_proxy.flatten(-2)[..., : self.k_dim]
+        return None if self.grad_proxy is None else _unblock(self.grad_proxy, self.k_dim)
 
 
-@dataclass
-class CascadedCdlBypassTensor(QTensor):
-    theta: torch.Tensor
-
-    def dequantize(self) -> torch.Tensor:
-        return self.theta
-
-    def proxy(self) -> torch.Tensor | None:
-        return None
+class CascadedCdlBypassTensor(IdentityTensor):
+    """What a bypassing quantizer (activation calibration) returns: the input
+    itself, no gradient proxy -- cdl's ``CascadedCdlBypassTensor``."""
 
 
 class CascadedCdlQuant(Quant):
@@ -152,21 +166,11 @@ class CascadedCdlQuant(Quant):
         self.initialized = False
         self.bypassing = False
 
-    @property
-    def theta_kappa(self) -> torch.Tensor:
-        return self.log_theta_kappa.exp()
-
-    @property
-    def q_kappa(self) -> torch.Tensor:
-        return self.log_q_kappa.exp()
-
-    @property
-    def q(self) -> torch.Tensor:
-        return self.log_q.exp()
-
-    @property
-    def alpha(self) -> torch.Tensor:
-        return self.log_alpha.exp()
+    # the learned quantities, stored as logarithms
+    theta_kappa = _Exp("log_theta_kappa")
+    q_kappa = _Exp("log_q_kappa")
+    q = _Exp("log_q")
+    alpha = _Exp("log_alpha")
 
     # learning rates (ccdl.py:124-134, 231-240, 264-273)
     def _lr_bits(self) -> int:
@@ -186,8 +190,9 @@ class CascadedCdlQuant(Quant):
 
     @torch.no_grad()
     def copy_log_q(self, log_q_tensor: torch.Tensor) -> None:
-        self.log_q.copy_(log_q_tensor)
-        self.log_q_init.copy_(log_q_tensor)
+        """Set log q and remember it as the starting point of ``q_rel``."""
+        for dst in (self.log_q, self.log_q_init):
+            dst.copy_(log_q_tensor)
 
     @torch.no_grad()
     def init_q_from_block_amax(self, block_amax: torch.Tensor) -> None:
@@ -246,8 +251,8 @@ class CascadedCdlQuantForWeight(CascadedCdlQuant):
 
     @torch.no_grad()
     def init_q_from_weight(self, weight: torch.Tensor) -> None:
-        blocked, _ = group_tensor_into_blocks(weight, self.block_size)
-        self.init_q_from_block_amax(blocked.abs().amax(dim=-1, keepdim=True))
+        """q from the weight's own block maxima (cdl: ccdl.py:273-279)."""
+        self.init_q_from_block_amax(_block_amax(weight, self.block_size))
 
 
 class Nvfp4CascadedCdlQuantForActivation(CascadedCdlQuantForActivation):
@@ -274,6 +279,52 @@ class Mxfp8CascadedCdlQuantForWeight(CascadedCdlQuantForWeight):
     FMT = "mxfp8"
 
 
+# per-quantizer statistics of cdl's ``cascaded_cdl_quant_stats``
+# (ccdl.py:294-310): name suffix -> value
+_STATS = {
+    "theta_kappa": lambda m: m.theta_kappa,
+    "q": lambda m: m.q.detach().float().mean(),
+    "q_rel": lambda m: (m.log_q - m.log_q_init).float().abs().mean(),
+    "q_kappa": lambda m: m.q_kappa,
+    "alpha": lambda m: m.alpha,
+}
+
+
+class _AmaxRecorder:
+    """Calibration context: the activation quantizers pass their input through
+    (``bypassing``), the model runs in eval mode, and a forward pre-hook keeps
+    the running block amax of each quantizer's input, reduced over the
+    dimensions its declared input shape marks as 1 (shared scales)."""
+
+    def __init__(self, model: nn.Module, quantizers: list):
+        self.model, self.quantizers = model, quantizers
+        self.amax: dict = {}
+        self._handles: list = []
+        self._was_training = model.training
+
+    def _hook(self, m, args):
+        blocked, _ = group_tensor_into_blocks(args[0], m.block_size)
+        shared = [i for i in range(blocked.ndim - 2) if m.input_shape[i] == 1]
+        seen = blocked.abs().amax(dim=(*shared, blocked.ndim - 1))
+        old = self.amax.get(m)
+        self.amax[m] = seen if old is None else torch.maximum(old, seen)
+
+    def __enter__(self):
+        self._handles = [m.register_forward_pre_hook(self._hook) for m in self.quantizers]
+        self.model.eval()
+        for m in self.quantizers:
+            m.bypassing = True
+        return self
+
+    def __exit__(self, *exc):
+        for h in self._handles:
+            h.remove()
+        for m in self.quantizers:
+            m.bypassing = False
+        self.model.train(self._was_training)
+        return False
+
+
 class CascadedCdlQuantMixin(nn.Module):
     """Model-level helpers of cdl's ``CascadedCdlQuantMixin`` (ccdl.py:280-393):
     quantized-element counts, statistics, optimizer parameter groups and the
@@ -281,83 +332,58 @@ class CascadedCdlQuantMixin(nn.Module):
     layers in batch-statistics mode during calibration; the decoder models
     here have none.)"""
 
+    def _ccdl_quantizers(self, kind=None) -> list:
+        kind = kind or CascadedCdlQuant
+        return [m for m in self.modules() if isinstance(m, kind)]
+
     def cascaded_cdl_get_weight_quant_counts(self) -> int:
-        return sum(m.theta_num_quantized_params for m in self.modules() if isinstance(m, CascadedCdlQuantForWeight))
+        return sum(m.theta_num_quantized_params for m in CascadedCdlQuantMixin._ccdl_quantizers(
+            self, CascadedCdlQuantForWeight))
 
     def cascaded_cdl_get_activation_quant_counts(self) -> int:
-        return sum(m.theta_num_quantized_params for m in self.modules()
-                   if isinstance(m, CascadedCdlQuantForActivation))
+        return sum(m.theta_num_quantized_params for m in CascadedCdlQuantMixin._ccdl_quantizers(
+            self, CascadedCdlQuantForActivation))
 
     @torch.no_grad()
     def cascaded_cdl_quant_stats(self) -> dict[str, float]:
-        out: dict[str, float] = {}
-        for name, m in self.named_modules():
-            if not isinstance(m, CascadedCdlQuant):
-                continue
-            name = name.removeprefix("_orig_mod.")
-            out[f"{name}.theta_kappa"] = m.theta_kappa.item()
-            out[f"{name}.q"] = m.q.detach().float().mean().item()
-            out[f"{name}.q_rel"] = (m.log_q - m.log_q_init).float().abs().mean().item()
-            out[f"{name}.q_kappa"] = m.q_kappa.item()
-            out[f"{name}.alpha"] = m.alpha.item()
-        return out
+        """``<module name>.<stat>`` for every quantizer and statistic in _STATS
+        (names without a torch.compile ``_orig_mod.`` prefix)."""
+        return {f"{name.removeprefix('_orig_mod.')}.{stat}": float(fn(m))
+                for name, m in self.named_modules() if isinstance(m, CascadedCdlQuant)
+                for stat, fn in _STATS.items()}
 
     @torch.no_grad()
     def cascaded_cdl_get_param_groups(self, learning_rate: float, train_alpha: bool,
                                       train_kappa: bool) -> tuple[list[dict], set[nn.Parameter]]:
-        custom: set[nn.Parameter] = set()
-        buckets: dict[float, list[nn.Parameter]] = {}
-        for m in self.modules():
-            if not isinstance(m, CascadedCdlQuant):
-                continue
-            custom.update(m.parameters())
-            buckets.setdefault(m.get_q_lr(learning_rate), []).append(m.log_q)
-            if train_alpha:
-                buckets.setdefault(m.get_alpha_lr(learning_rate), []).append(m.log_alpha)
-            else:
-                m.log_alpha.requires_grad_(False)
-            if train_kappa:
-                buckets.setdefault(m.get_theta_kappa_lr(learning_rate), []).append(m.log_theta_kappa)
-                buckets.setdefault(m.get_q_kappa_lr(learning_rate), []).append(m.log_q_kappa)
-            else:
-                m.log_theta_kappa.requires_grad_(False)
-                m.log_q_kappa.requires_grad_(False)
-        groups = [{"params": params, "lr": lr, "weight_decay": 0.0} for lr, params in buckets.items()]
-        return groups, custom
+        """One AdamW group per distinct learning rate: log q always, log alpha
+        and the two log kappas when trained (else frozen); returns the groups
+        and the set of every quantizer parameter."""
+        owned: set[nn.Parameter] = set()
+        by_lr: dict[float, list[nn.Parameter]] = {}
+        for m in CascadedCdlQuantMixin._ccdl_quantizers(self):
+            owned.update(m.parameters())
+            entries = [(m.log_q, m.get_q_lr, True), (m.log_alpha, m.get_alpha_lr, train_alpha),
+                       (m.log_theta_kappa, m.get_theta_kappa_lr, train_kappa),
+                       (m.log_q_kappa, m.get_q_kappa_lr, train_kappa)]
+            for param, lr_of, trained in entries:
+                if trained:
+                    by_lr.setdefault(lr_of(learning_rate), []).append(param)
+                else:
+                    param.requires_grad_(False)
+        return [{"params": ps, "lr": lr, "weight_decay": 0.0} for lr, ps in by_lr.items()], owned
 
     @torch.no_grad()
     def cascaded_cdl_init_act_q_pass(self, samples: Iterable[torch.Tensor]) -> None:
-        """Runs the model in eval mode with the activation quantizers bypassed,
-        records each one's block amax (max over the batch-like dimensions its
-        input shape declares as 1, and over the samples) and sets q from it."""
-        modules = [m for m in self.modules() if isinstance(m, CascadedCdlQuantForActivation)]
-        if not modules:
+        """Calibrate every activation quantizer's q from the block amax of its
+        input over ``samples`` (cdl: ccdl.py:356-393)."""
+        quantizers = CascadedCdlQuantMixin._ccdl_quantizers(self, CascadedCdlQuantForActivation)
+        if not quantizers:
             return
-        stats: dict[CascadedCdlQuantForActivation, torch.Tensor] = {}
-
-        def hook(m, args):
-            blocked, _ = group_tensor_into_blocks(args[0], m.block_size)
-            dims = tuple(i for i in range(blocked.ndim - 2) if m.input_shape[i] == 1) + (blocked.ndim - 1,)
-            amax = blocked.abs().amax(dim=dims)
-            prev = stats.get(m)
-            stats[m] = amax if prev is None else torch.maximum(prev, amax)
-
-        handles = [m.register_forward_pre_hook(hook) for m in modules]
-        was_training = self.training
-        self.eval()
-        for m in modules:
-            m.bypassing = True
-        try:
+        with _AmaxRecorder(self, quantizers) as rec:
             for x in samples:
                 self(x)
-        finally:
-            for h in handles:
-                h.remove()
-            for m in modules:
-                m.bypassing = False
-            self.train(was_training)
-        for m in modules:
-            if m not in stats:
+        for m in quantizers:
+            if m not in rec.amax:
                 raise RuntimeError("an activation quantizer saw no calibration input")
-            m.init_q_from_block_amax(stats[m].flatten().reshape(m.input_shape[:-1] + (-1, 1)))
+            m.init_q_from_block_amax(rec.amax[m].flatten().reshape(m.input_shape[:-1] + (-1, 1)))
             m.initialized = True

@@ -1,13 +1,23 @@
-"""Training checkpoints in the dictionary format of cdl's ``checkpoint.py``
-(cdl/checkpoint.py:12-64), so that a run can resume from a checkpoint either
-side wrote:
+"""Training checkpoints in cdl's dictionary format (cdl/checkpoint.py:12-64),
+so that a run resumes from a file either side wrote.
 
-    {"epoch", "global_step", "model" (state_dict of the unwrapped model),
-     "optimizer" (torch.optim.AdamW's state_dict layout), "lr_scheduler",
-     "rng": {"python", "torch", "cuda"}}
+The format is a flat ``torch.save`` dictionary:
 
-written to ``<path>.tmp`` and renamed over ``path``.  ``ClipAdamW``
-(cdl_b200.train.optim) reads and writes the AdamW layout.
+=================  ==========================================================
+``epoch``          int, the epoch the checkpoint was taken in
+``global_step``    int, optimizer steps taken
+``model``          ``state_dict`` of the bare model (no compile / DDP wrapper)
+``optimizer``      ``state_dict`` in ``torch.optim.AdamW``'s layout
+                   (``ClipAdamW`` in ``cdl_b200.train.optim`` reads and
+                   writes it too)
+``lr_scheduler``   the scheduler's ``state_dict``; ``{}`` without a schedule
+``rng``            ``{"python", "torch", "cuda"}``: the three generator
+                   states (``cuda`` is None on a host without CUDA)
+=================  ==========================================================
+
+A file is written next to its destination (``<name>.tmp``) and renamed over
+it, so a crash never leaves a half-written checkpoint under the real name.
+Resuming reads ``<dir>/last.ckpt`` and continues with the next epoch.
 """
 
 from __future__ import annotations
@@ -22,45 +32,64 @@ from torch import nn
 
 logger = logging.getLogger(__name__)
 
+KEYS = ("epoch", "global_step", "model", "optimizer", "lr_scheduler", "rng")
+LAST = "last.ckpt"
+
 
 def into_orig_mod(model: nn.Module) -> nn.Module:
-    """The module under a ``torch.compile`` wrapper (``_orig_mod``) or DDP (``module``)."""
-    model = getattr(model, "_orig_mod", model)
-    return model.module if isinstance(model, nn.parallel.DistributedDataParallel) else model
+    """The module whose ``state_dict`` is stored: unwraps ``torch.compile``
+    (``_orig_mod``) and ``DistributedDataParallel`` (``module``), in any order."""
+    while True:
+        if hasattr(model, "_orig_mod"):
+            model = model._orig_mod
+        elif isinstance(model, nn.parallel.DistributedDataParallel):
+            model = model.module
+        else:
+            return model
+
+
+def _rng_snapshot() -> dict:
+    cuda = torch.cuda.get_rng_state_all() if torch.cuda.is_available() else None
+    return {"python": random.getstate(), "torch": torch.get_rng_state(), "cuda": cuda}
+
+
+def _rng_restore(rng: dict, device: torch.device) -> None:
+    random.setstate(rng["python"])
+    torch.set_rng_state(rng["torch"].cpu())
+    if torch.device(device).type == "cuda" and rng.get("cuda") is not None:
+        torch.cuda.set_rng_state_all([s.cpu() for s in rng["cuda"]])
 
 
 def save_checkpoint(path: Path, model: nn.Module, optimizer, lr_scheduler, epoch: int, global_step: int) -> None:
-    """``lr_scheduler`` may be None (no schedule): its entry is then empty."""
+    """Write the checkpoint of this point of training to ``path`` (atomically).
+    ``lr_scheduler`` may be None (constant learning rate)."""
     path = Path(path)
-    tmp = path.with_suffix(path.suffix + ".tmp")
-    torch.save({
-        "epoch": epoch,
-        "global_step": global_step,
-        "model": into_orig_mod(model).state_dict(),
-        "optimizer": optimizer.state_dict(),
-        "lr_scheduler": lr_scheduler.state_dict() if lr_scheduler is not None else {},
-        "rng": {
-            "python": random.getstate(),
-            "torch": torch.get_rng_state(),
-            "cuda": torch.cuda.get_rng_state_all() if torch.cuda.is_available() else None,
-        },
-    }, tmp)
-    os.replace(tmp, path)
+    state = dict(zip(KEYS, (
+        epoch,
+        global_step,
+        into_orig_mod(model).state_dict(),
+        optimizer.state_dict(),
+        {} if lr_scheduler is None else lr_scheduler.state_dict(),
+        _rng_snapshot(),
+    )))
+    partial = path.parent / (path.name + ".tmp")
+    torch.save(state, partial)
+    os.replace(partial, path)
     logger.info("checkpoint saved to %s", path)
 
 
 def load_checkpoint(resume_dir: Path, model: nn.Module, optimizer, lr_scheduler,
                     device: torch.device) -> tuple[int, int]:
-    """Restore ``resume_dir/last.ckpt``; returns (next epoch, global step).
-    ``lr_scheduler`` may be None (no schedule)."""
-    ckpt = torch.load(Path(resume_dir) / "last.ckpt", map_location=device, weights_only=False)
-    into_orig_mod(model).load_state_dict(ckpt["model"])
-    optimizer.load_state_dict(ckpt["optimizer"])
+    """Restore model, optimizer, scheduler (if any) and the generators from
+    ``resume_dir/last.ckpt``; returns ``(epoch to start, global step)``."""
+    state = torch.load(Path(resume_dir) / LAST, map_location=device, weights_only=False)
+    missing = [k for k in KEYS if k not in state]
+    if missing:
+        raise KeyError(f"{Path(resume_dir) / LAST} is not a training checkpoint (missing {missing})")
+    into_orig_mod(model).load_state_dict(state["model"])
+    optimizer.load_state_dict(state["optimizer"])
     if lr_scheduler is not None:
-        lr_scheduler.load_state_dict(ckpt["lr_scheduler"])
-    random.setstate(ckpt["rng"]["python"])
-    torch.set_rng_state(ckpt["rng"]["torch"].cpu())
-    if torch.device(device).type == "cuda" and ckpt["rng"]["cuda"] is not None:
-        torch.cuda.set_rng_state_all([s.cpu() for s in ckpt["rng"]["cuda"]])
+        lr_scheduler.load_state_dict(state["lr_scheduler"])
+    _rng_restore(state["rng"], device)
     logger.info("checkpoint loaded from %s", resume_dir)
-    return ckpt["epoch"] + 1, ckpt["global_step"]
+    return state["epoch"] + 1, state["global_step"]
