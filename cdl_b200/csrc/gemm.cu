@@ -43,7 +43,12 @@ constexpr int kStageBytes = 2 * kTileBytes + 2 * kSfStageBytes;
 constexpr int kThreads = 192;
 constexpr int kSfBufs = 4;  // scale-factor TMEM buffers, rotated per K tile
 constexpr uint32_t kTmemCols = 256;  // 128 accumulator + 4 x 16 SFA + 4 x 16 SFB
-constexpr uint32_t kSpinLimit = 1u << 20;
+// A bounded wait polls mbarrier.try_wait, each poll suspending the thread
+// for at most kWaitHintNs unless the phase completes first (measured at
+// 8192^3: 261 us against 277 us without the hint): at most about
+// kSpinLimit * kWaitHintNs (~2.6 s) before a wait gives up.
+constexpr uint32_t kSpinLimit = 1u << 18;
+constexpr uint32_t kWaitHintNs = 10000;
 
 enum Kind : int { kNv = 0, kMx4 = 1, kMx8 = 2 };
 
@@ -76,9 +81,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     for (uint32_t i = 0; i < kSpinLimit; ++i) {
         uint32_t done;
         asm volatile(
-            "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
+            "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}"
             : "=r"(done)
-            : "r"(a), "r"(parity)
+            : "r"(a), "r"(parity), "n"(kWaitHintNs)
             : "memory");
         if (done) return true;
     }
