@@ -205,11 +205,27 @@ __device__ __forceinline__ uint32_t cvt_e2m1x8(float f0, float f1, float f2, flo
     return out;
 }
 
+// Two bf16 of one word (lo, hi) times c, as one packed fp32 multiply
+// (mul.rn.f32x2: each lane an IEEE round-to-nearest product, the same as two
+// __fmul_rn), converted to two e2m1 nibbles (lo in bits 0-3).
+__device__ __forceinline__ uint32_t cvt2_scaled(uint32_t w, uint64_t cc) {
+    uint64_t v, p;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(w << 16), "r"(w & 0xffff0000u));
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(v), "l"(cc));
+    uint16_t r;
+    asm("{\n.reg .f32 lo, hi;\n.reg .b8 b;\nmov.b64 {lo, hi}, %1;\ncvt.rn.satfinite.e2m1x2.f32 b, hi, lo;\n"
+        "cvt.u16.u8 %0, b;\n}"
+        : "=h"(r)
+        : "l"(p));
+    return r;
+}
+
 // 8 bf16 (one uint4) times c -> 8 nibbles via the hardware converter.
 __device__ __forceinline__ uint32_t cvt8_scaled(const uint4& w, float c) {
-    return cvt_e2m1x8(__fmul_rn(bf16lo(w.x), c), __fmul_rn(bf16hi(w.x), c), __fmul_rn(bf16lo(w.y), c),
-                      __fmul_rn(bf16hi(w.y), c), __fmul_rn(bf16lo(w.z), c), __fmul_rn(bf16hi(w.z), c),
-                      __fmul_rn(bf16lo(w.w), c), __fmul_rn(bf16hi(w.w), c));
+    uint64_t cc;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(cc) : "f"(c));
+    return cvt2_scaled(w.x, cc) | (cvt2_scaled(w.y, cc) << 8) | (cvt2_scaled(w.z, cc) << 16) |
+           (cvt2_scaled(w.w, cc) << 24);
 }
 
 // RN(1/s) to within 2^-22 relative: hardware approximation refined by one
@@ -840,24 +856,25 @@ __global__ void __launch_bounds__(kEncThreads) nvfp4_encode_multi_kernel(const _
 //     bytes, which then leave as one 32-byte segment per output row and one
 //     scale word per output row.
 // ---------------------------------------------------------------------------
-constexpr int kDualT = 64;                  // tile rows = tile columns
-constexpr int kDualPitch = kDualT + 8;      // staged row: 64 bf16 + 16 bytes of padding
+constexpr int kDualT = 64;                  // rows of a work item = columns of a sub-tile
+constexpr int kDualW = 2 * kDualT;          // columns of a work item: two 64 x 64 sub-tiles
+constexpr int kDualPitch = kDualW + 8;      // staged row: 128 bf16 + 16 bytes of padding
 constexpr int kDualThreads = 256;
-constexpr int kDualStages = 3;              // tiles in shared memory: one encoded, two loading
+constexpr int kDualStages = 2;              // items in shared memory: one encoded, one loading
 constexpr int kDualGroup = 128;             // tensors per launch (table in the parameter block)
 
 struct DualGroup {
     int count, pad;
-    int32_t tile0[kDualGroup + 1];  // index of each tensor's first tile in the launch
-    FastDiv tiles_c[kDualGroup];    // cols / 64
+    int32_t item0[kDualGroup + 1];  // index of each tensor's first work item in the launch
+    FastDiv items_c[kDualGroup];    // ceil(cols / 128)
     cdlb200_nvfp4_dual_tensor t[kDualGroup];
 };
 
-__device__ __forceinline__ int dual_tensor_of(const DualGroup& g, int32_t tile) {
+__device__ __forceinline__ int dual_tensor_of(const DualGroup& g, int32_t item) {
     int lo = 0, hi = g.count - 1;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
-        if (g.tile0[mid] <= tile) lo = mid;
+        if (g.item0[mid] <= item) lo = mid;
         else hi = mid - 1;
     }
     return lo;
@@ -883,18 +900,18 @@ __device__ __forceinline__ Nvfp4Tensor dual_scale(const cdlb200_nvfp4_dual_tenso
     return tn;
 }
 
-struct DualTile {
+struct DualItem {
     int ti;
     int64_t row0, col0;
 };
 
-__device__ __forceinline__ DualTile dual_locate(const DualGroup& g, int32_t tile) {
-    DualTile d;
-    d.ti = dual_tensor_of(g, tile);
-    const uint32_t lt = (uint32_t)(tile - g.tile0[d.ti]);
-    const uint32_t tr = g.tiles_c[d.ti].div(lt);
-    d.row0 = (int64_t)tr * kDualT;
-    d.col0 = (int64_t)(lt - tr * g.tiles_c[d.ti].d) * kDualT;
+__device__ __forceinline__ DualItem dual_locate(const DualGroup& g, int32_t item) {
+    DualItem d;
+    d.ti = dual_tensor_of(g, item);
+    const uint32_t li = (uint32_t)(item - g.item0[d.ti]);
+    const uint32_t ir = g.items_c[d.ti].div(li);
+    d.row0 = (int64_t)ir * kDualT;
+    d.col0 = (int64_t)(li - ir * g.items_c[d.ti].d) * kDualW;
     return d;
 }
 
@@ -927,43 +944,46 @@ __global__ void __launch_bounds__(kDualThreads, 4) nvfp4_dual_multi_kernel(const
     __shared__ ScaleEntry table[128];
     __shared__ float ctab[128];  // the cvt multiplier of a kCvt entry, else -1
     __shared__ int s_search;     // count of kSearch entries
-    uint16_t* xs0 = reinterpret_cast<uint16_t*>(dual_smem);  // kDualStages tiles of kDualT x kDualPitch
-    uint2* ccodes = reinterpret_cast<uint2*>(dual_smem + kDualStages * kDualT * kDualPitch * 2);  // [64 b + c]
-    uint8_t* cscale = reinterpret_cast<uint8_t*>(ccodes + kDualT * 4);                           // [4 c + b]
+    uint16_t* xs0 = reinterpret_cast<uint16_t*>(dual_smem);  // kDualStages items of kDualT x kDualPitch
+    // staged column codes [h][b][c] (sub-tile h, block b, column c) and scale bytes [h][4c + b]
+    uint2* ccodes = reinterpret_cast<uint2*>(dual_smem + kDualStages * kDualT * kDualPitch * 2);
+    uint8_t* cscale = reinterpret_cast<uint8_t*>(ccodes + 2 * 4 * kDualT);
     const int tid = threadIdx.x, lane = tid & 31;
-    const int32_t total = g.tile0[g.count];
+    const int32_t total = g.item0[g.count];
     const int32_t first = (int32_t)blockIdx.x, stride = (int32_t)gridDim.x;
 
-    // copies of tile `tile` into stage `s`: two 16-byte pieces per thread,
-    // whole 128-byte row segments per 8 lanes
-    auto issue = [&](int32_t tile, int s) {
-        if (tile < total) {
-            const DualTile d = dual_locate(g, tile);
+    // copies of item `item` into stage `s`: four 16-byte pieces per thread,
+    // whole 128-byte row segments per 8 lanes (a missing second sub-tile is
+    // not loaded)
+    auto issue = [&](int32_t item, int s) {
+        if (item < total) {
+            const DualItem d = dual_locate(g, item);
             const cdlb200_nvfp4_dual_tensor& T = g.t[d.ti];
-            const uint16_t* x = static_cast<const uint16_t*>(T.x);
+            const uint16_t* x = static_cast<const uint16_t*>(T.x) + d.row0 * T.cols + d.col0;
+            const int ncols = T.cols - d.col0 < kDualW ? kDualT : kDualW;
             uint16_t* xs = xs0 + s * (kDualT * kDualPitch);
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int e = tid + kDualThreads * j, r = e >> 3, c8 = (e & 7) * 8;
-                cp_async16(&xs[r * kDualPitch + c8], x + (d.row0 + r) * T.cols + d.col0 + c8);
+            for (int j = 0; j < 4; ++j) {
+                const int e = tid + kDualThreads * j, r = e >> 4, c8 = (e & 15) * 8;
+                if (c8 < ncols) cp_async16(&xs[r * kDualPitch + c8], x + r * T.cols + c8);
             }
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
 
     issue(first, 0);
-    issue(first + stride, 1);
     int k = 0, cur_ti = -1;
     Nvfp4Tensor tn;
     bool all_search = false;
-    for (int32_t tile = first; tile < total; tile += stride, ++k) {
-        issue(tile + 2 * stride, (k + 2) % kDualStages);
-        asm volatile("cp.async.wait_group 2;" ::: "memory");  // this thread's copies of `tile` landed
+    for (int32_t item = first; item < total; item += stride, ++k) {
+        issue(item + stride, (k + 1) % kDualStages);
+        asm volatile("cp.async.wait_group 1;" ::: "memory");  // this thread's copies of `item` landed
         __syncthreads();                                      // ... and every other thread's
         const uint16_t* xs = xs0 + (k % kDualStages) * (kDualT * kDualPitch);
-        const DualTile d = dual_locate(g, tile);
+        const DualItem d = dual_locate(g, item);
         const cdlb200_nvfp4_dual_tensor& T = g.t[d.ti];
         const int64_t row0 = d.row0, col0 = d.col0;
+        const int nsub = T.cols - col0 < kDualW ? 1 : 2;  // sub-tiles of this item
         if (d.ti != cur_ti) {  // the tensor's constants and scale table, once per tensor a CTA meets
             tn = dual_scale(T, lane);
             cur_ti = d.ti;
@@ -982,71 +1002,76 @@ __global__ void __launch_bounds__(kDualThreads, 4) nvfp4_dual_multi_kernel(const
             __syncthreads();
             all_search = s_search > kMaxSearchEntries;
         }
-        if (tile == g.tile0[d.ti] && tid == 0) *T.alpha = tn.alpha;
+        if (item == g.item0[d.ti] && tid == 0) *T.alpha = tn.alpha;
 
         if (tid < 128) {
-            // ---- x, warps 0-3: row r, blocks 2h and 2h + 1 (32 contiguous values)
-            if (T.row_packed != nullptr) {
-                const int r = tid >> 1, h = tid & 1;
-                const uint16_t* src = &xs[r * kDualPitch + 32 * h];
-                const uint4 a0 = *reinterpret_cast<const uint4*>(src), a1 = *reinterpret_cast<const uint4*>(src + 8);
-                const uint4 b0 = *reinterpret_cast<const uint4*>(src + 16), b1 = *reinterpret_cast<const uint4*>(src + 24);
-                uint2 oa, ob;
-                const uint32_t sa = table_block16(a0, a1, tn, table, ctab, all_search, oa);
-                const uint32_t sb = table_block16(b0, b1, tn, table, ctab, all_search, ob);
-                *reinterpret_cast<uint4*>(static_cast<uint8_t*>(T.row_packed) + (row0 + r) * (T.cols / 2) + col0 / 2 +
-                                          16 * h) = make_uint4(oa.x, oa.y, ob.x, ob.y);
-                uint32_t word = (sa | (sb << 8)) << (16 * h);
-                word |= __shfl_xor_sync(0xffffffffu, word, 1);
-                if (h == 0) {
-                    const int64_t c4 = T.cols / 64;  // (cols / 16) / 4: cols is a multiple of 64
-                    *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(T.row_scale) +
-                                                 swizzle_offset(row0 + r, col0 / 16, c4)) = word;
+            // ---- x, warps 0-3: row r of sub-tile h, its four blocks (64 contiguous values)
+            const int r = tid >> 1, h = tid & 1;
+            if (T.row_packed != nullptr && h < nsub) {
+                const uint16_t* src = &xs[r * kDualPitch + kDualT * h];
+                uint32_t word = 0;
+                uint2 o[4];
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const uint4 w0 = *reinterpret_cast<const uint4*>(src + 16 * b);
+                    const uint4 w1 = *reinterpret_cast<const uint4*>(src + 16 * b + 8);
+                    word |= table_block16(w0, w1, tn, table, ctab, all_search, o[b]) << (8 * b);
                 }
+                uint8_t* dst = static_cast<uint8_t*>(T.row_packed) + (row0 + r) * (T.cols / 2) + col0 / 2 + 32 * h;
+                *reinterpret_cast<uint4*>(dst) = make_uint4(o[0].x, o[0].y, o[1].x, o[1].y);
+                *reinterpret_cast<uint4*>(dst + 16) = make_uint4(o[2].x, o[2].y, o[3].x, o[3].y);
+                *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(T.row_scale) +
+                                             swizzle_offset(row0 + r, (col0 + kDualT * h) / 16, T.cols / 64)) = word;
             }
         } else if (T.col_packed != nullptr) {
-            // ---- x^T, warps 4-7: columns 2p and 2p + 1, block b (tile rows 16b .. 16b + 15);
+            // ---- x^T, warps 4-7: columns 2p and 2p + 1 of each sub-tile, block b (tile rows 16b .. 16b + 15);
             // one 32-bit load holds both columns' values of a row
             const int t = tid - 128, p = t & 31, b = t >> 5;
-            const uint32_t* src = reinterpret_cast<const uint32_t*>(&xs[16 * b * kDualPitch + 2 * p]);
-            uint32_t v[16];
+            for (int h = 0; h < nsub; ++h) {
+                const uint32_t* src = reinterpret_cast<const uint32_t*>(&xs[16 * b * kDualPitch + kDualT * h + 2 * p]);
+                uint32_t v[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = src[i * (kDualPitch / 2)];
-            uint32_t e[8], o[8];  // column 2p / 2p + 1, rows (2i, 2i + 1)
+                for (int i = 0; i < 16; ++i) v[i] = src[i * (kDualPitch / 2)];
+                uint32_t e[8], o[8];  // column 2p / 2p + 1, rows (2i, 2i + 1)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                e[i] = __byte_perm(v[2 * i], v[2 * i + 1], 0x5410);
-                o[i] = __byte_perm(v[2 * i], v[2 * i + 1], 0x7632);
+                for (int i = 0; i < 8; ++i) {
+                    e[i] = __byte_perm(v[2 * i], v[2 * i + 1], 0x5410);
+                    o[i] = __byte_perm(v[2 * i], v[2 * i + 1], 0x7632);
+                }
+                const uint4 e0 = make_uint4(e[0], e[1], e[2], e[3]), e1 = make_uint4(e[4], e[5], e[6], e[7]);
+                const uint4 o0 = make_uint4(o[0], o[1], o[2], o[3]), o1 = make_uint4(o[4], o[5], o[6], o[7]);
+                uint2 ce, co;
+                const uint32_t se = table_block16(e0, e1, tn, table, ctab, all_search, ce);
+                const uint32_t so = table_block16(o0, o1, tn, table, ctab, all_search, co);
+                *reinterpret_cast<uint4*>(&ccodes[(4 * h + b) * kDualT + 2 * p]) = make_uint4(ce.x, ce.y, co.x, co.y);
+                cscale[256 * h + 4 * (2 * p) + b] = (uint8_t)se;
+                cscale[256 * h + 4 * (2 * p + 1) + b] = (uint8_t)so;
             }
-            const uint4 e0 = make_uint4(e[0], e[1], e[2], e[3]), e1 = make_uint4(e[4], e[5], e[6], e[7]);
-            const uint4 o0 = make_uint4(o[0], o[1], o[2], o[3]), o1 = make_uint4(o[4], o[5], o[6], o[7]);
-            uint2 ce, co;
-            const uint32_t se = table_block16(e0, e1, tn, table, ctab, all_search, ce);
-            const uint32_t so = table_block16(o0, o1, tn, table, ctab, all_search, co);
-            *reinterpret_cast<uint4*>(&ccodes[kDualT * b + 2 * p]) = make_uint4(ce.x, ce.y, co.x, co.y);
-            cscale[4 * (2 * p) + b] = (uint8_t)se;
-            cscale[4 * (2 * p + 1) + b] = (uint8_t)so;
         }
         __syncthreads();  // staged columns complete; the stage is free for the copies issued next
         if (T.col_packed != nullptr) {
-            if (tid < 2 * kDualT) {  // output row col0 + c: 32 code bytes, blocks (2h, 2h + 1) per half
-                const int c = tid >> 1, h = tid & 1;
-                const uint2 q0 = ccodes[kDualT * (2 * h) + c], q1 = ccodes[kDualT * (2 * h + 1) + c];
-                *reinterpret_cast<uint4*>(static_cast<uint8_t*>(T.col_packed) + (col0 + c) * (T.rows / 2) + row0 / 2 +
-                                          16 * h) = make_uint4(q0.x, q0.y, q1.x, q1.y);
-            } else if (tid < 3 * kDualT) {  // its scale word (blocks row0/16 .. +3)
-                const int c = tid - 2 * kDualT;
-                const int64_t c4 = T.rows / 64;
-                *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(T.col_scale) +
-                                             swizzle_offset(col0 + c, row0 / 16, c4)) =
-                    *reinterpret_cast<const uint32_t*>(&cscale[4 * c]);
+            {  // output row col0 + 64h + c: 32 code bytes, blocks (2q, 2q + 1) per half q
+                const int h = tid >> 7, c = (tid >> 1) & 63, qh = tid & 1;
+                if (h < nsub) {
+                    const uint2 q0 = ccodes[(4 * h + 2 * qh) * kDualT + c], q1 = ccodes[(4 * h + 2 * qh + 1) * kDualT + c];
+                    *reinterpret_cast<uint4*>(static_cast<uint8_t*>(T.col_packed) +
+                                              (col0 + kDualT * h + c) * (T.rows / 2) + row0 / 2 + 16 * qh) =
+                        make_uint4(q0.x, q0.y, q1.x, q1.y);
+                }
+            }
+            if (tid < 2 * kDualT) {  // its scale word (blocks row0/16 .. +3)
+                const int h = tid >> 6, c = tid & 63;
+                if (h < nsub)
+                    *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(T.col_scale) +
+                                                 swizzle_offset(col0 + kDualT * h + c, row0 / 16, T.rows / 64)) =
+                        *reinterpret_cast<const uint32_t*>(&cscale[256 * h + 4 * c]);
             }
         }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
-constexpr int kDualSmem = kDualStages * kDualT * kDualPitch * 2 + kDualT * 4 * 8 + kDualT * 4;
+constexpr int kDualSmem = kDualStages * kDualT * kDualPitch * 2 + 2 * kDualT * 4 * 8 + 2 * kDualT * 4;
 
 // ---------------------------------------------------------------------------
 // general path: any leading dimension, ragged k, transposed (dim-0) blocks.
@@ -1534,7 +1559,7 @@ extern "C" int cdlb200_nvfp4_dual_multi(const cdlb200_nvfp4_dual_tensor* tensors
         if (t.rows == 0 || t.cols == 0) continue;
         if (t.row_packed && (rc = zero_scale_tail(t.row_scale, t.rows, t.cols / 16, st)) != CDLB200_OK) return rc;
         if (t.col_packed && (rc = zero_scale_tail(t.col_scale, t.cols, t.rows / 16, st)) != CDLB200_OK) return rc;
-        const int64_t nt = (t.rows / kDualT) * (t.cols / kDualT);
+        const int64_t nt = (t.rows / kDualT) * ((t.cols + kDualW - 1) / kDualW);
         if (groups.empty() || groups.back().count == kDualGroup || tiles + nt >= (1ll << 31)) {
             groups.emplace_back();
             groups.back().count = 0;
@@ -1543,10 +1568,10 @@ extern "C" int cdlb200_nvfp4_dual_multi(const cdlb200_nvfp4_dual_tensor* tensors
         }
         DualGroup& g = groups.back();
         g.t[g.count] = t;
-        g.tiles_c[g.count] = FastDiv((uint32_t)(t.cols / kDualT));
-        g.tile0[g.count] = (int32_t)tiles;
+        g.items_c[g.count] = FastDiv((uint32_t)((t.cols + kDualW - 1) / kDualW));
+        g.item0[g.count] = (int32_t)tiles;
         tiles += nt;
-        g.tile0[++g.count] = (int32_t)tiles;
+        g.item0[++g.count] = (int32_t)tiles;
     }
     static bool attr_set = false;
     if (!attr_set) {
@@ -1557,7 +1582,7 @@ extern "C" int cdlb200_nvfp4_dual_multi(const cdlb200_nvfp4_dual_tensor* tensors
     }
     const int64_t cap = (int64_t)num_sms() * 4;  // four resident CTAs per SM
     for (const DualGroup& g : groups) {
-        const int64_t n = g.tile0[g.count];
+        const int64_t n = g.item0[g.count];
         nvfp4_dual_multi_kernel<<<(unsigned)(n < cap ? n : cap), kDualThreads, kDualSmem, st>>>(g);
         CDLB200_CHECK_LAUNCH();
     }
