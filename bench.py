@@ -1,35 +1,42 @@
 #!/usr/bin/env python
 """Benchmark of the cdl_b200 hot path; prints ONE JSON line on rank 0.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload nvfp4_quant|mxfp4_quant|mxfp8_quant|fp4_gemm|qat_135m|qat_1.7b|nvfp4_ecdl|nvfp4_ccdl]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--workload NAME]
 
 Workloads (synthetic data everywhere):
 
-* ``qat_1.7b`` (default) -- config C5, see below.  At N=1 the line also
-  carries ``components``: the NVFP4 quantize GB/s (C1) and FP4 GEMM TFLOP/s
-  (C3 8192^3) of the other two BASELINE metrics, each with its roofline.
-* ``nvfp4_quant`` -- one step = NVFP4 quantize of one 4096x4096
-  bf16 activation tensor (config C1: N(0,1), 0.1% x20 outliers) through the
-  public ``nvfp4_quant`` API.  Inputs cycle through a pool of distinct
-  tensors totalling more than twice the 126 MB L2, so every step reads cold
-  HBM.  Metric: algorithmic GB/s at 2.5625 B/element.
-* ``mxfp4_quant`` / ``mxfp8_quant`` -- config C2 shape [16384, 8192].
-* ``fp4_gemm`` -- config C3: NVFP4 GEMM 8192^3, one step = quantize the bf16
-  activations A (the GEMM prologue) + the tcgen05 block-scaled GEMM against
+* ``qat_1.7b`` (default) -- config C5: one SmolLM2-1.7B NVFP4 QAT training
+  step (forward, backward, clip + AdamW) on 4x2048 uniform random tokens per
+  rank, backend ``nvfp4_qbwd`` (NVFP4 forward, dgrad and wgrad GEMMs); one
+  CUDA graph per step at N=1, data parallel with an NCCL bf16 gradient
+  all-reduce for N > 1.  Metric: tokens/s over all ranks.  At N=1 the line
+  also carries ``components``: the other BASELINE metrics (NVFP4 quantize
+  GB/s on C1 and on a larger-than-L2 tensor, MXFP4 / MXFP8 on C2, the
+  transposed requantizes, the optimizer's weight encode, NVFP4 dequantize,
+  FP4 GEMM TFLOP/s on C3 8192^3), each with its roofline, and, where they
+  exist, the same workload through the reference's own Triton kernels
+  (``reference_gpu``, from the unmodified reference package in
+  ``baseline/_ref``) and through cuBLAS (``library_gpu``, the GEMM).
+* ``qat_135m`` -- config C4 (8x2048 tokens).
+* ``nvfp4_quant`` (C1 4096x4096), ``nvfp4_quant_large`` / ``nvfp4_quant_t``
+  (C2 shape, row-wise / transposed), ``mxfp4_quant`` / ``mxfp8_quant`` (+
+  ``_t``: C2 [16384, 8192]), ``nvfp4_dequant`` (C1), ``nvfp4_encode_multi``
+  (the 1.7B model's 168 weights in one launch): one step = one call of the
+  public API; inputs cycle through a pool larger than twice the 126 MB L2.
+  Metric: algorithmic GB/s (2.5625 B/element for NVFP4).
+* ``fp4_gemm`` -- config C3 (``--gemm-shape``, default 8192^3): one step =
+  quantize the bf16 activations + the tcgen05 block-scaled GEMM against
   pre-quantized NVFP4 weights.  Metric: TFLOP/s (2 M N K per step).
-* ``qat_135m`` / ``qat_1.7b`` -- configs C4 / C5: one SmolLM2 NVFP4 QAT
-  training step (forward, backward, AdamW) on uniform random tokens; for
-  N > 1 data parallel with an NCCL bf16 gradient all-reduce.  Metric:
-  tokens/s over all ranks.
+* ``nvfp4_ecdl`` / ``nvfp4_ccdl`` -- the stochastic quantizers on C1.
 
 Every step sequence is timed with CUDA events over exactly K steps with the
 inputs resident in HBM (max over ranks; each rank processes its own data, so
 scaling is weak).  ``e2e`` is the same metric through the same public API
 with host-resident inputs: each step copies its input host->device and its
-result back.  ``--impl reference`` times the CPU implementation of the path
-(``oracle/``, a C restatement of cdl's torch path, on all host threads) on
-rank 0.
+result back.  ``--impl reference`` times the reference's algorithm on the
+host cores (rank 0): the CPU oracle (``oracle/``, a C restatement of cdl's
+torch path) for the kernels, and for the QAT step the reference's training
+step with its native-backend numerics (``oracle/qat_cpu.py``).
 """
 
 from __future__ import annotations
@@ -62,7 +69,7 @@ QUANT = {
     "nvfp4_quant_large": ("nvfp4", 16384, 8192, 2.5625, "C2 shape"),
 }
 WORKLOADS = sorted(list(QUANT) + ["fp4_gemm", "qat_135m", "qat_1.7b", "nvfp4_ecdl", "nvfp4_ccdl",
-                                  "nvfp4_encode_multi"])
+                                  "nvfp4_encode_multi", "nvfp4_dequant", "nvfp4_dual"])
 QAT_BATCH = {"qat_135m": (8, 2048), "qat_1.7b": (4, 2048)}  # configs C4 / C5, tokens per rank
 ECDL_TOPK, ECDL_KAPPA = 5, 4.0  # theta_topk default of cdl's training config (smollm2.py:168)
 CCDL_TOPK, CCDL_KAPPA = 5, 2.0  # cdl's training defaults (theta_topk = q_topk = 5, kappa 2)
@@ -205,6 +212,59 @@ def cpu_quant_rate(fmt_name, rows, k, bpe, steps, warmup, threads, target_s=None
         n += 1
     dt = time.perf_counter() - t0
     return bpe * rows * k * n / dt / 1e9, f"{n} x {fmt_name} quantize of [{rows},{k}] bf16 ({threads} threads)"
+
+
+def cpu_dual_rate(threads, target_s=10.0, rows=4096, k=4096):
+    """The oracle's two NVFP4 quantizes the dual encoder replaces, of a bounded
+    [rows, k] sample and of its transpose, in dual-encode GB/s (3.125 B per
+    element)."""
+    import numpy as np
+    import torch
+
+    from cdl_b200 import workloads
+
+    bits = workloads.c2_mx(rows, k).view(torch.int16).numpy().view(np.uint16)
+    bits_t = np.ascontiguousarray(bits.T)
+    cpu_quant_threads(bits, "nvfp4", threads)
+    t0 = time.perf_counter()
+    n = 0
+    while n < 2 or time.perf_counter() - t0 < target_s:
+        cpu_quant_threads(bits, "nvfp4", threads)
+        cpu_quant_threads(bits_t, "nvfp4", threads)
+        n += 1
+    dt = time.perf_counter() - t0
+    return 3.125 * rows * k * n / dt / 1e9, (f"{n} x (nvfp4 quantize of [{rows},{k}] bf16 and of its transpose) "
+                                             f"({threads} threads)")
+
+
+def cpu_dequant_rate(threads, target_s=10.0, rows=4096, k=4096):
+    """The oracle's NVFP4 dequantize of C1's encoding, rows split over
+    ``threads`` host threads."""
+    import concurrent.futures
+
+    import numpy as np
+    import torch
+
+    import oracle
+    from cdl_b200 import workloads
+
+    bits = workloads.c1_nvfp4(rows, k).view(torch.int16).numpy().view(np.uint16)
+    packed, scale, alpha = oracle.quant(bits, oracle.NVFP4)
+    parts = np.array_split(np.arange(rows), threads)
+
+    def run():
+        with concurrent.futures.ThreadPoolExecutor(threads) as ex:
+            list(ex.map(lambda idx: oracle.dequant(packed[idx[0]: idx[-1] + 1], scale[idx[0]: idx[-1] + 1],
+                                                   oracle.NVFP4, alpha), parts))
+
+    run()
+    t0 = time.perf_counter()
+    n = 0
+    while n < 3 or time.perf_counter() - t0 < target_s:
+        run()
+        n += 1
+    dt = time.perf_counter() - t0
+    return 2.5625 * rows * k * n / dt / 1e9, f"{n} x nvfp4 dequantize of [{rows},{k}] ({threads} threads)"
 
 
 def cpu_ecdl_rate(rows, k, threads, target_s=10.0):
@@ -409,7 +469,7 @@ def quant_workload(name, dev, rank):
             2 if fmt == "nvfp4" else 1)
     else:
         kernel, launches = ("nvfp4_fused_kernel" if fmt == "nvfp4" else "quant_flat_kernel"), 1
-    return {
+    w = {
         "step": lambda i: qfn(pool[i % pool_n]), "e2e_step": e2e_step, "graph": True,
         "units_per_step": bpe * rows * k / 1e9, "unit": "GB/s", "metric": f"{fmt.upper()} quant GB/s",
         "dtype": "bf16->e2m1/e4m3" if fmt != "mxfp8" else "bf16->e4m3/e8m0",
@@ -417,6 +477,104 @@ def quant_workload(name, dev, rank):
                    "l2": f"inputs cycled over {pool_n} tensors ({pool_n * in_bytes >> 20} MiB > 2x L2)"},
         "h2d": host_in.numel() * 2, "d2h": p0.numel() * p0.element_size() + s0.numel() + (4 if a0 is not None else 0),
         "bound": "hbm", "kernel": kernel, "launches_per_step": launches,
+    }
+    ref = reference_kernels()
+    if ref is not None:
+        rfn = getattr(ref[0], f"{fmt}_quant")
+        # cdl has no transposed quantize: its caller quantizes a transposed copy
+        w["reference_step"] = ((lambda i: rfn(pool[i % pool_n].t().contiguous())) if tr
+                               else (lambda i: rfn(pool[i % pool_n])))
+        w["reference_impl"] = (f"cdl.core.kernel.quant.{fmt}_quant (Triton _quant_kernel"
+                               + (", torch amax" if fmt == "nvfp4" else "") + ")"
+                               + (" of x.t().contiguous()" if tr else ""))
+    return w
+
+
+def reference_kernels():
+    """cdl's own quantize / dequantize modules (Triton kernels), from the
+    unmodified reference package installed under ``baseline/_ref``; None
+    when it is not installed or does not import."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "cdl")):
+        return None
+    if ref not in sys.path:
+        sys.path.append(ref)
+    try:
+        import cdl.core.kernel.dequant as rdq
+        import cdl.core.kernel.quant as rq
+    except Exception:
+        return None
+    return rq, rdq
+
+
+def dequant_workload(dev, rank):
+    """NVFP4 dequantize on C1 (4096 x 4096): codes + linear scales + alpha ->
+    bf16, the operand cdl's bf16 backward reads (``dequant.py:103-109``)."""
+    import torch
+
+    from cdl_b200 import workloads
+    from cdl_b200.core.kernel import dequant, quant
+
+    rows, k = 4096, 4096
+    pool_n = 8
+    pool = [quant.nvfp4_quant(workloads.c1_nvfp4(rows, k, seed=1000 * rank + i, device=str(dev)))
+            for i in range(pool_n)]
+    host = [t.cpu().pin_memory() for t in pool[0]]
+    host_out = torch.empty(rows, k, dtype=torch.bfloat16, pin_memory=True)
+
+    def e2e_step():
+        p, s, a = (t.to(dev, non_blocking=True) for t in host)
+        host_out.copy_(dequant.nvfp4_dequant(p, s, a), non_blocking=True)
+
+    w = {
+        "step": lambda i: dequant.nvfp4_dequant(*pool[i % pool_n]), "e2e_step": e2e_step, "graph": True,
+        "units_per_step": 2.5625 * rows * k / 1e9, "unit": "GB/s", "metric": "NVFP4 dequant GB/s",
+        "dtype": "e2m1/e4m3->bf16",
+        "config": {"workload": f"nvfp4_dequant C1 [{rows},{k}] per rank",
+                   "l2": f"inputs cycled over {pool_n} encodings, {pool_n} x 32 MiB of outputs (> 2x L2)"},
+        "h2d": sum(t.numel() * t.element_size() for t in host), "d2h": rows * k * 2,
+        "bound": "hbm", "kernel": "fp4_dequant32_kernel", "launches_per_step": 1,
+    }
+    ref = reference_kernels()
+    if ref is not None:
+        w["reference_step"] = lambda i: ref[1].nvfp4_dequant(*pool[i % pool_n])
+        w["reference_impl"] = "cdl.core.kernel.dequant.nvfp4_dequant (Triton _fp4_dequant_kernel)"
+    return w
+
+
+def dual_workload(dev, rank, shape=(8192, 8192)):
+    """The dual NVFP4 encode of the quantized backward (``nvfp4_dual_quant``):
+    ``Q(x)`` and ``Q(x^T)`` of one bf16 [R, C] tensor from one read, amax
+    given (as from a producer kernel's epilogue).  Default [8192, 8192]: the
+    1.7B step's gate / up gradients (8192 tokens x 8192)."""
+    import torch
+
+    from cdl_b200 import workloads
+    from cdl_b200.core.kernel.quant import nvfp4_amax, nvfp4_dual_quant
+
+    r, c = shape
+    in_bytes = r * c * 2
+    pool_n = max(2, -(-2 * L2_BYTES // in_bytes))
+    pool = [workloads.c2_mx(r, c, seed=1000 * rank + i, device=str(dev)) for i in range(pool_n)]
+    gmax = [nvfp4_amax(x)[0] for x in pool]
+    host_in = pool[0].cpu().pin_memory()
+    (p0, s0, _), (q0, t0, _) = nvfp4_dual_quant(pool[0], gmax=gmax[0])
+    host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (p0, s0, q0, t0)]
+
+    def e2e_step():
+        x = host_in.to(dev, non_blocking=True)
+        (p, s, _), (q, t, _) = nvfp4_dual_quant(x)
+        for h, d in zip(host_out, (p, s, q, t)):
+            h.copy_(d, non_blocking=True)
+
+    return {
+        "step": lambda i: nvfp4_dual_quant(pool[i % pool_n], gmax=gmax[i % pool_n]), "e2e_step": e2e_step,
+        "graph": True, "units_per_step": 3.125 * r * c / 1e9, "unit": "GB/s",
+        "metric": "NVFP4 dual encode GB/s", "dtype": "bf16->e2m1/e4m3 (rows and columns)",
+        "config": {"workload": f"nvfp4_dual [{r},{c}] bf16 per rank: Q(x) and Q(x^T), amax given",
+                   "l2": f"inputs cycled over {pool_n} tensors ({pool_n * in_bytes >> 20} MiB > 2x L2)"},
+        "h2d": in_bytes, "d2h": sum(t.numel() for t in (p0, s0, q0, t0)),
+        "bound": "hbm", "kernel": "nvfp4_dual_multi_kernel", "launches_per_step": 1,
     }
 
 
@@ -475,7 +633,7 @@ def gemm_workload(dev, rank, shape=(8192, 8192, 8192)):
     from cdl_b200 import workloads
     from cdl_b200.core.kernel import quant
     from cdl_b200.core.mm.swizzle import swizzle_scale_factors
-    from cdl_b200.model.wrapper.ops import mm_fp4
+    from cdl_b200.model.wrapper.ops import mm_nvfp4_alpha2
 
     m, n, k = shape
     pool_n = max(2, -(-2 * L2_BYTES // (m * k * 2)))  # bf16 A cycled over more than twice L2
@@ -488,32 +646,46 @@ def gemm_workload(dev, rank, shape=(8192, 8192, 8192)):
 
     def step(i):
         ap, asf, aal = quant.nvfp4_quant(pool[i % pool_n], swizzled=True)
-        return mm_fp4(ap, wp.T, asf, wsw.T, aal * wal, 16, True)
+        return mm_nvfp4_alpha2(ap, wp.T, asf, wsw.T, aal, wal)
 
     # the GEMM kernel alone (A already quantized), for the roofline of the dominant kernel
     pre = [quant.nvfp4_quant(a, swizzled=True) for a in pool]
-    alphas = [p[2] * wal for p in pre]
 
     def kernel_step(i):
-        ap, asf, _ = pre[i % pool_n]
-        return mm_fp4(ap, wp.T, asf, wsw.T, alphas[i % pool_n], 16, True)
+        ap, asf, aal = pre[i % pool_n]
+        return mm_nvfp4_alpha2(ap, wp.T, asf, wsw.T, aal, wal)
 
     host_a = pool[0].cpu().pin_memory()
     host_out = torch.empty(m, n, dtype=torch.bfloat16, pin_memory=True)
 
     def e2e_step():
         ap, asf, aal = quant.nvfp4_quant(host_a.to(dev, non_blocking=True), swizzled=True)
-        host_out.copy_(mm_fp4(ap, wp.T, asf, wsw.T, aal * wal, 16, True), non_blocking=True)
+        host_out.copy_(mm_nvfp4_alpha2(ap, wp.T, asf, wsw.T, aal, wal), non_blocking=True)
+
+    def library_step(i):
+        """The same GEMM through cuBLAS's NVFP4 path (torch scaled_mm), for comparison."""
+        from torch.nn.functional import ScalingType, SwizzleType, scaled_mm
+
+        ap, asf, aal = pre[i % pool_n]
+        f4 = torch.float4_e2m1fn_x2
+        return scaled_mm(ap.view(f4), wp.view(f4).T, [asf.view(torch.float8_e4m3fn).flatten(), aal],
+                         [ScalingType.BlockWise1x16, ScalingType.TensorWise],
+                         [wsw.view(torch.float8_e4m3fn).flatten(), wal],
+                         [ScalingType.BlockWise1x16, ScalingType.TensorWise],
+                         swizzle_a=[SwizzleType.SWIZZLE_32_4_4, SwizzleType.NO_SWIZZLE],
+                         swizzle_b=[SwizzleType.SWIZZLE_32_4_4, SwizzleType.NO_SWIZZLE],
+                         output_dtype=torch.bfloat16)
 
     return {
         "step": step, "e2e_step": e2e_step, "kernel_step": kernel_step, "graph": True,
+        "library_step": library_step, "library_impl": "cuBLAS NVFP4 (torch.nn.functional.scaled_mm, 1x16 blocks)",
         "units_per_step": 2.0 * m * n * k / 1e12, "unit": "TFLOP/s", "metric": "FP4 GEMM TFLOPS",
         "dtype": "e2m1 x e2m1 (ue4m3 block scales) -> fp32 acc -> bf16",
         "config": {"workload": f"fp4_gemm C3 NVFP4 {m}x{n}x{k}: quantize bf16 A + tcgen05 GEMM vs pre-quantized W",
                    "l2": f"A cycled over {pool_n} tensors of {m * k * 2 / 2**20:.0f} MiB (> 2x L2 in total)"},
         "h2d": host_a.numel() * 2, "d2h": m * n * 2, "bound": "tensor",
         "kernel": "bs_gemm_pair_kernel<NVFP4> (persistent 2-SM tcgen05 block-scaled GEMM)",
-        "launches_per_step": 3,  # nvfp4_fused_kernel (A), the GEMM, the alpha product
+        "launches_per_step": 2,  # nvfp4_fused_kernel (A), the GEMM (alpha_a * alpha_b in its epilogue)
     }
 
 
@@ -605,20 +777,49 @@ def time_kernel(fn, steps, dev):
     return e0.elapsed_time(e1) / steps
 
 
-def measure_component(name, dev, steps, warmup, peaks):
-    """Device-timed throughput and roofline of one kernel-level workload (N=1)."""
+def reference_qat_gpu(workload, dev, steps, warmup):
+    """The reference's own QAT step (``baseline/reference_step.py``: cdl's
+    QLinear + SteQuant("nvfp4") with its Triton quantizers, the native
+    backend, Liger's loss, torch AdamW) on the same workload and GPU, eager as
+    the reference's script runs it; None when the reference is not installed."""
     import torch
 
-    if name in QUANT:
-        w = quant_workload(name, dev, 0)
-    elif name == "nvfp4_encode_multi":
-        w = encode_multi_workload(dev, 0)
-    else:
-        w = gemm_workload(dev, 0)
+    from baseline import reference_step
+    from cdl_b200.train import qat
+
+    if reference_step.unavailable() is not None:
+        return {"impl": "cdl smollm2.py step (native backend)", "unavailable": reference_step.unavailable()}
+    spec = qat.SPECS["135m" if workload == "qat_135m" else "1.7b"]
+    batch, seq = QAT_BATCH[workload]
+    ref = reference_step.ReferenceQatStep(spec, dev, lr=3e-4, seed=0)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    ids = [torch.randint(0, spec.vocab, (batch, seq), device=dev, generator=gen) for _ in range(2)]
     for i in range(warmup):
-        w["step"](i)
+        ref.step(ids[i % 2])
     torch.cuda.synchronize()
-    run, keep = time_steps(w, steps, dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        ref.step(ids[i % 2])
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    del ref
+    return {"impl": "cdl smollm2.py step: QLinear + SteQuant('nvfp4') (Triton quantize / dequantize), native "
+                    "backend (bf16 cuBLAS matmuls), Liger fused linear CE, torch AdamW; eager",
+            "value": round(batch * seq / (ms / 1e3), 2), "unit": "tokens/s", "ms_per_step": round(ms, 3),
+            "steps": steps}
+
+
+def graph_ms(step, steps, warmup, dev):
+    """Device time (ms) of ``steps`` calls of ``step(i)``, captured in one CUDA
+    graph after ``warmup`` eager calls."""
+    import torch
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    run, keep = time_steps({"graph": True, "step": step}, steps, dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     run()
@@ -626,6 +827,37 @@ def measure_component(name, dev, steps, warmup, peaks):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
     del keep, run
+    return ms
+
+
+def reference_gpu(w, steps, warmup, dev, key="reference"):
+    """The reference's own GPU implementation of the workload (``key`` =
+    "reference"), or a library's (``key`` = "library"), timed like this
+    library's kernels (same inputs, one CUDA graph); None when there is none,
+    ``{"unavailable": reason}`` when it raises."""
+    if f"{key}_step" not in w:
+        return None
+    try:
+        ms = graph_ms(w[f"{key}_step"], steps, warmup, dev)
+    except Exception as e:  # a Python-level error of the other implementation, not of this library
+        return {"impl": w[f"{key}_impl"], "unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}"}
+    return {"impl": w[f"{key}_impl"], "value": round(w["units_per_step"] * steps / (ms / 1e3), 2),
+            "unit": w["unit"], "ms_per_step": round(ms / steps, 5)}
+
+
+def measure_component(name, dev, steps, warmup, peaks):
+    """Device-timed throughput and roofline of one kernel-level workload (N=1)."""
+    if name in QUANT:
+        w = quant_workload(name, dev, 0)
+    elif name == "nvfp4_encode_multi":
+        w = encode_multi_workload(dev, 0)
+    elif name == "nvfp4_dequant":
+        w = dequant_workload(dev, 0)
+    elif name == "nvfp4_dual":
+        w = dual_workload(dev, 0)
+    else:
+        w = gemm_workload(dev, 0)
+    ms = graph_ms(w["step"], steps, warmup, dev)
     value = w["units_per_step"] * steps / (ms / 1e3)
     achieved = value
     if "kernel_step" in w:  # the dominant kernel alone
@@ -635,7 +867,9 @@ def measure_component(name, dev, steps, warmup, peaks):
             "ms_per_step": round(ms / steps, 5), "config": w["config"]["workload"],
             "roofline": {"bound": w["bound"], "achieved": round(achieved, 2), "peak": peak, "unit": punit,
                          "frac": round(achieved / peak, 4), "traffic": profile_traffic(name), "kernel": w["kernel"]},
-            "gpu_launches": w["launches_per_step"] * steps}
+            "gpu_launches": w["launches_per_step"] * steps,
+            "reference_gpu": reference_gpu(w, steps, warmup, dev),
+            "library_gpu": reference_gpu(w, steps, warmup, dev, "library")}
 
 
 # ---------------------------------------------------------------------------
@@ -666,6 +900,12 @@ def main() -> None:
         elif wl == "nvfp4_encode_multi":
             val, sample = cpu_quant_rate("nvfp4", 4096, 4096, 2.5625, 3, 1, threads)
             unit, metric = "GB/s", "NVFP4 weight encode GB/s"
+        elif wl == "nvfp4_dequant":
+            val, sample = cpu_dequant_rate(threads, target_s=5.0)
+            unit, metric = "GB/s", "NVFP4 dequant GB/s"
+        elif wl == "nvfp4_dual":
+            val, sample = cpu_dual_rate(threads, target_s=5.0)
+            unit, metric = "GB/s", "NVFP4 dual encode GB/s"
         else:
             val, sample = cpu_qat_rate(wl, threads)
             unit, metric = "tokens/s", "SmolLM2 NVFP4 QAT tokens/s"
@@ -698,6 +938,10 @@ def main() -> None:
         w = ccdl_workload(dev, rank)
     elif wl == "nvfp4_encode_multi":
         w = encode_multi_workload(dev, rank)
+    elif wl == "nvfp4_dequant":
+        w = dequant_workload(dev, rank)
+    elif wl == "nvfp4_dual":
+        w = dual_workload(dev, rank)
     else:
         w = qat_workload(wl, dev, rank, world, args.backend, not args.no_graph)
 
@@ -786,6 +1030,10 @@ def main() -> None:
             val, sample = cpu_ccdl_rate(4096, 4096, threads, target_s=10.0)
         elif wl == "nvfp4_encode_multi":
             val, sample = cpu_quant_rate("nvfp4", 4096, 4096, 2.5625, 3, 1, threads, target_s=10.0)
+        elif wl == "nvfp4_dequant":
+            val, sample = cpu_dequant_rate(threads, target_s=10.0)
+        elif wl == "nvfp4_dual":
+            val, sample = cpu_dual_rate(threads, target_s=10.0)
         else:
             val, sample = cpu_qat_rate(wl, threads)
         cpu = {"value": round(val, 4), "unit": w["unit"], "cores": threads, "kind": "port", "sample": sample}
@@ -815,6 +1063,11 @@ def main() -> None:
                          else (w["launches_per_step"] * args.steps) if w["launches_per_step"] else None),
         "clocks": clocks,
     }
+    if world == 1:  # the reference's own GPU kernels (and cuBLAS for the GEMM) on the same inputs
+        for key in ("reference", "library"):
+            other = reference_gpu(w, args.steps, 3, dev, key)
+            if other is not None:
+                line[f"{key}_gpu"] = other
     if wl == "fp4_gemm":
         line["roofline"]["peak_note"] = FP4_PEAK_NOTE
     if wl.startswith("qat"):
@@ -825,12 +1078,15 @@ def main() -> None:
         del w  # the QAT step's memory (its graph pool) before the component workloads
         gc.collect()
         torch.cuda.empty_cache()
+        line["reference_gpu"] = reference_qat_gpu(wl, dev, min(args.steps, 10), 2)
+        gc.collect()
+        torch.cuda.empty_cache()
         line["components"] = {
             "nvfp4_quant": measure_component("nvfp4_quant", dev, 200, 10, peaks),
             "fp4_gemm": measure_component("fp4_gemm", dev, 20, 5, peaks),
         }
         for name in ("nvfp4_quant_large", "nvfp4_quant_t", "mxfp4_quant", "mxfp8_quant", "mxfp4_quant_t",
-                     "mxfp8_quant_t", "nvfp4_encode_multi"):
+                     "mxfp8_quant_t", "nvfp4_encode_multi", "nvfp4_dequant", "nvfp4_dual"):
             line["components"][name] = measure_component(name, dev, 20, 3, peaks)
             torch.cuda.empty_cache()
         line["components"]["fp4_gemm"]["roofline"]["peak_note"] = FP4_PEAK_NOTE

@@ -28,6 +28,7 @@ AMAX_WORDS = 32  # CDLB200_AMAX_WORDS
 
 SCALE_LINEAR = 0
 SCALE_SWIZZLED = 1
+DTYPE_F32, DTYPE_F16 = 1, 2
 
 _lib = None
 _lock = threading.Lock()
@@ -50,6 +51,7 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_nvfp4_amax": (_I, [_P, _I64, _I64, _I64, _P, _P, _P, _SZ, _P]),
     "cdlb200_mxfp4_quant": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P]),
     "cdlb200_mxfp8_quant": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P]),
+    "cdlb200_quant_wide": (_I, [_P, _I, _I, _I64, _I64, _I64, _I, _P, _P, _I, _P, _P, _SZ, _P]),
     "cdlb200_fp4_dequant": (_I, [_P, _P, _P, _I64, _I64, _I, _I, _P, _P]),
     "cdlb200_fp4_dequant_swizzled": (_I, [_P, _P, _P, _I64, _I64, _I, _I, _P, _P]),
     "cdlb200_mxfp8_dequant": (_I, [_P, _P, _P, _I64, _I64, _P, _P]),
@@ -61,9 +63,9 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_rmsnorm_fwd": (_I, [_P, _P, _I64, _I64, ctypes.c_float, _P, _P, _P, _P]),
     "cdlb200_rmsnorm_bwd_workspace_bytes": (_I64, [_I64, _I64]),
     "cdlb200_rmsnorm_bwd": (_I, [_P, _P, _P, _P, _I64, _I64, _P, _P, _P, _I64, _P]),
-    "cdlb200_rope": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _P, _P]),
+    "cdlb200_rope": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _P, _P, _P]),
     "cdlb200_swiglu_fwd": (_I, [_P, _P, _I64, _P, _P, _P]),
-    "cdlb200_swiglu_bwd": (_I, [_P, _P, _P, _I64, _P, _P, _P]),
+    "cdlb200_swiglu_bwd": (_I, [_P, _P, _P, _I64, _P, _P, _P, _P, _P]),
     "cdlb200_cross_entropy": (_I, [_P, _P, _I64, _I64, _F, _P, _P]),
     "cdlb200_ecdl_fwd": (_I, [_P, _I, _I64, _I64, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P]),
     "cdlb200_ecdl_bwd_workspace_bytes": (_I64, [_I64, _I64, _I]),

@@ -13,7 +13,9 @@ serve the GEMM path: ``transpose=True`` quantizes ``x.T`` along dim 0 without
 materialising the transpose (the wgrad requantize), and ``swizzled=True``
 writes the scales directly in the 128x4 tiled GEMM layout.
 
-The input must be a bf16 CUDA tensor; there is no CPU path.
+The input is a CUDA tensor of bf16 (the tuned kernels) or fp32 / fp16 (the
+reference's own fp32 arithmetic, ``cdlb200_quant_wide``), as cdl's Triton
+kernel accepts any floating input; there is no CPU path.
 """
 
 from __future__ import annotations
@@ -26,6 +28,8 @@ from cdl_b200 import _lib
 
 NVFP4, MXFP4, MXFP8 = 0, 1, 2
 _BLOCK = {NVFP4: 16, MXFP4: 32, MXFP8: 32}
+# input dtypes: bf16 takes the tuned kernels, fp32 / fp16 cdl's literal fp32 path
+_DTYPES = {torch.bfloat16: 0, torch.float32: _lib.DTYPE_F32, torch.float16: _lib.DTYPE_F16}
 
 
 def scale_shape(r: int, nb: int, swizzled: bool) -> tuple[int, int]:
@@ -40,8 +44,8 @@ def _quant(
     if x.ndim != 2:
         raise ValueError(f"expected a 2D tensor [rows, k], got shape {tuple(x.shape)}")
     dev = _lib.require_cuda(x)
-    if x.dtype != torch.bfloat16:
-        raise TypeError(f"cdl_b200 quantize takes bfloat16 input, got {x.dtype}")
+    if x.dtype not in _DTYPES:
+        raise TypeError(f"cdl_b200 quantize takes a floating tensor (bf16, fp16, fp32), got {x.dtype}")
     if x.stride(1) != 1 or x.stride(0) < x.shape[1] or x.data_ptr() % 16:
         x = x.contiguous()
     rows, k = x.shape
@@ -54,6 +58,16 @@ def _quant(
     layout = _lib.SCALE_SWIZZLED if swizzled else _lib.SCALE_LINEAR
     ld = max(x.stride(0), 1)
     st = _lib.stream(dev)
+    if x.dtype != torch.bfloat16:
+        # cdl's kernel casts each block to fp32: the literal fp32 path
+        alpha = torch.empty(1, dtype=torch.float32, device=dev) if fmt == NVFP4 else None
+        ws = _lib.nvfp4_workspace(dev)
+        _lib.call("cdlb200_quant_wide", _lib.ptr(x), _DTYPES[x.dtype], fmt, rows, k, ld, int(transpose),
+                  _lib.ptr(packed), _lib.ptr(scale), layout, _lib.ptr(alpha) if alpha is not None else None,
+                  _lib.ptr(ws), ws.numel(), st)
+        if fmt == MXFP4:
+            alpha = torch.ones(1, dtype=torch.float32, device=dev)
+        return packed, scale, alpha
     if fmt == NVFP4:
         alpha = torch.empty(1, dtype=torch.float32, device=dev)
         ws = _lib.nvfp4_workspace(dev)

@@ -31,6 +31,7 @@ from cdl_b200.api.quant import QTensor
 from cdl_b200.core.kernel.dequant import mxfp4_dequant, mxfp8_dequant, nvfp4_dequant
 from cdl_b200.core.kernel.quant import mxfp4_quant, mxfp8_quant, nvfp4_dual_quant, nvfp4_quant
 from cdl_b200.core.mm.swizzle import expand_rows, pad_k, pad_n, swizzle_scale_factors
+from cdl_b200.model.components.fused import grad_amax
 from cdl_b200.model.wrapper.ops import mm_fp4_direct as mm_fp4
 from cdl_b200.model.wrapper.ops import mm_mxfp8_direct as mm_mxfp8
 from cdl_b200.model.wrapper.ops import mm_nvfp4_alpha2
@@ -149,8 +150,8 @@ class BlockScaledMatMul(torch.autograd.Function):
             # along M); g is read once for both of its encodings
             xc_p, xc_s, xc_a, wc_p, wc_s, wc_a = ctx.saved_tensors
             need_dx, need_dw = ctx.needs_input_grad[2], ctx.needs_input_grad[4]
-            g_row, g_col = nvfp4_dual_quant(grad_output.reshape(-1, grad_output.shape[-1]), rows=need_dx,
-                                            cols=need_dw)
+            g2 = grad_output.reshape(-1, grad_output.shape[-1])
+            g_row, g_col = nvfp4_dual_quant(g2, amax=grad_amax(g2), rows=need_dx, cols=need_dw)
             dx = mm_nvfp4_alpha2(g_row[0], wc_p.T, g_row[1], wc_s.T, g_row[2], wc_a) if need_dx else None
             dw = mm_nvfp4_alpha2(g_col[0], xc_p.T, g_col[1], xc_s.T, g_col[2], xc_a) if need_dw else None
             return None, None, dx, None, dw, None

@@ -93,6 +93,13 @@ __device__ __forceinline__ uint32_t ue4m3_scale_byte(float q) {
     return cvt_e4m3x2(0.0f, q) & 0xffu;
 }
 
+// NVFP4 per-tensor scale alpha = gmax / (6 * 448).  cdl forms it with torch on
+// the device (cdl/core/kernel/quant.py:96-101, core/ecdl.py:46-56), where
+// `tensor / python_float` runs as a multiply by the fp32 reciprocal of the
+// scalar; a true division (what the same line computes on the CPU) differs in
+// the last bit for about a fifth of all gmax values.
+__device__ __forceinline__ float nvfp4_alpha(float gmax) { return __fmul_rn(gmax, __frcp_rn(2688.0f)); }
+
 // e8m0 scale value 2^(b-127); byte 0 is the fp32 subnormal 2^-127.
 __device__ __forceinline__ float e8m0_to_f32(uint32_t b) {
     return u2f(b == 0 ? 0x00400000u : (b << 23));

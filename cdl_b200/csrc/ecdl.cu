@@ -395,7 +395,7 @@ __global__ void __launch_bounds__(kEcdlThreads) ecdl_fwd_kernel(const T* __restr
     float gmax = 1.0f, alpha = 1.0f;
     if (mode == CDLB200_ECDL_NVIDIA) {
         gmax = fmaxf(u2f(*gmax_bits), kTiny);
-        alpha = __fmul_rn(gmax, __frcp_rn(2688.0f));  // torch: tensor / 2688.0 as a reciprocal multiply
+        alpha = nvfp4_alpha(gmax);
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) *alpha_out = alpha;
     const int lanes = f.tpb / 2;

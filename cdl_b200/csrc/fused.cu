@@ -61,6 +61,26 @@ __device__ __forceinline__ void cta_amax(uint32_t m2, uint32_t* amax) {
     }
 }
 
+// cta_amax for two outputs at once (one shared round trip); null pointers skip
+__device__ __forceinline__ void cta_amax2(uint32_t m2a, uint32_t* amax_a, uint32_t m2b, uint32_t* amax_b) {
+    __shared__ uint32_t red[2][32];
+    uint32_t ma = __reduce_max_sync(0xffffffffu, max(m2a & 0xffffu, m2a >> 16));
+    uint32_t mb = __reduce_max_sync(0xffffffffu, max(m2b & 0xffffu, m2b >> 16));
+    if ((threadIdx.x & 31) == 0) {
+        red[0][threadIdx.x >> 5] = ma;
+        red[1][threadIdx.x >> 5] = mb;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
+            ma = max(ma, red[0][w]);
+            mb = max(mb, red[1][w]);
+        }
+        if (amax_a) atomicMax(amax_a + (blockIdx.x % CDLB200_AMAX_WORDS), ma);
+        if (amax_b) atomicMax(amax_b + (blockIdx.x % CDLB200_AMAX_WORDS), mb);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // RMSNorm: one warp per row; lane l owns the 8-value vectors l, l + 32, ...
 // (VPL vectors at most, d = 8 * nvec).
@@ -201,8 +221,9 @@ __global__ void __launch_bounds__(256) colsum_kernel(const float* __restrict__ p
 __global__ void __launch_bounds__(256) rope_kernel(const uint4* __restrict__ x, const uint4* __restrict__ cosv,
                                                    const uint4* __restrict__ sinv, int64_t tokens, int heads,
                                                    int halfv, int64_t cos_tokens, int backward,
-                                                   uint4* __restrict__ out) {
+                                                   uint4* __restrict__ out, uint32_t* __restrict__ amax) {
     const int64_t total = tokens * heads * halfv;
+    uint32_t am = 0;
     for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
         const int v = (int)(t % halfv);
         const int64_t th = t / halfv, tok = (th / heads) % cos_tokens;  // cos/sin repeat every cos_tokens
@@ -224,9 +245,12 @@ __global__ void __launch_bounds__(256) rope_kernel(const uint4* __restrict__ x, 
                 o2[i] = rbf(b[i] * c2[i]) - rbf(a[i] * s1[i]);
             }
         }
-        out[base + v] = pack8(o1);
-        out[base + halfv + v] = pack8(o2);
+        const uint4 p1 = pack8(o1), p2 = pack8(o2);
+        out[base + v] = p1;
+        out[base + halfv + v] = p2;
+        am = mag8(mag8(am, p1), p2);
     }
+    if (amax) cta_amax(am, amax);
 }
 
 // ---------------------------------------------------------------------------
@@ -254,7 +278,9 @@ __global__ void __launch_bounds__(256) swiglu_fwd_kernel(const uint4* __restrict
 
 __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const uint4* __restrict__ dh, const uint4* __restrict__ g,
                                                          const uint4* __restrict__ u, int64_t nvec,
-                                                         uint4* __restrict__ dg, uint4* __restrict__ du) {
+                                                         uint4* __restrict__ dg, uint4* __restrict__ du,
+                                                         uint32_t* __restrict__ amax_g, uint32_t* __restrict__ amax_u) {
+    uint32_t ag = 0, au = 0;
     for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < nvec; t += (int64_t)gridDim.x * blockDim.x) {
         float d[8], a[8], b[8], og[8], ou[8];
         unpack8(dh[t], d);
@@ -267,9 +293,13 @@ __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const uint4* __restrict
             ou[i] = d[i] * rbf(a[i] * s);
             og[i] = ds * (s * (1.0f + a[i] * (1.0f - s)));
         }
-        dg[t] = pack8(og);
-        du[t] = pack8(ou);
+        const uint4 pg = pack8(og), pu = pack8(ou);
+        dg[t] = pg;
+        du[t] = pu;
+        ag = mag8(ag, pg);
+        au = mag8(au, pu);
     }
+    if (amax_g || amax_u) cta_amax2(ag, amax_g, au, amax_u);
 }
 
 // ---------------------------------------------------------------------------
@@ -420,7 +450,8 @@ extern "C" int cdlb200_rmsnorm_bwd(const void* dy, const void* x, const void* w,
 }
 
 extern "C" int cdlb200_rope(const void* x, const void* cos, const void* sin, int64_t tokens, int64_t heads,
-                            int64_t head_dim, int64_t cos_tokens, int backward, void* out, void* stream) {
+                            int64_t head_dim, int64_t cos_tokens, int backward, void* out, uint32_t* amax,
+                            void* stream) {
     if (tokens < 0 || heads <= 0 || head_dim <= 0 || (head_dim % 16) != 0 || (backward != 0 && backward != 1) ||
         cos_tokens <= 0)
         return CDLB200_ERR_INVALID_ARG;
@@ -431,7 +462,7 @@ extern "C" int cdlb200_rope(const void* x, const void* cos, const void* sin, int
     const int64_t items = tokens * heads * halfv;
     rope_kernel<<<grid_for(items, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint4*>(x), static_cast<const uint4*>(cos), static_cast<const uint4*>(sin), tokens,
-        (int)heads, halfv, cos_tokens, backward, static_cast<uint4*>(out));
+        (int)heads, halfv, cos_tokens, backward, static_cast<uint4*>(out), amax);
     CDLB200_CHECK_LAUNCH();
     return CDLB200_OK;
 }
@@ -448,14 +479,14 @@ extern "C" int cdlb200_swiglu_fwd(const void* g, const void* u, int64_t n, void*
 }
 
 extern "C" int cdlb200_swiglu_bwd(const void* dh, const void* g, const void* u, int64_t n, void* dg, void* du,
-                                  void* stream) {
+                                  uint32_t* amax_dg, uint32_t* amax_du, void* stream) {
     if (n < 0 || (n % 8) != 0) return CDLB200_ERR_INVALID_ARG;
     if (n == 0) return CDLB200_OK;
     if (!dh || !g || !u || !dg || !du) return CDLB200_ERR_INVALID_ARG;
     if (!al16(dh) || !al16(g) || !al16(u) || !al16(dg) || !al16(du)) return CDLB200_ERR_ALIGNMENT;
     swiglu_bwd_kernel<<<grid_for(n / 8, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint4*>(dh), static_cast<const uint4*>(g), static_cast<const uint4*>(u), n / 8,
-        static_cast<uint4*>(dg), static_cast<uint4*>(du));
+        static_cast<uint4*>(dg), static_cast<uint4*>(du), amax_dg, amax_du);
     CDLB200_CHECK_LAUNCH();
     return CDLB200_OK;
 }

@@ -58,7 +58,9 @@ __device__ __forceinline__ constexpr float half_ulp_j(int j) {
     return j == 0 ? 0x1p-26f : j == 1 ? 0x1p-25f : j <= 3 ? 0x1p-24f : j <= 5 ? 0x1p-23f : 0x1p-22f;
 }
 // NVFP4 workspace: [0] arrival counter, [4] departure counter (fused kernel),
-// [8] status word (non-zero after a timed-out grid barrier), [256..) partial maxima.
+// [8] status word (non-zero after a timed-out grid barrier), [12] running max
+// of the fused kernel, [16] global amax of the fp32 / fp16 path (quant_wide.cu),
+// [256..) partial maxima.
 constexpr int kWsCounterOff = 0;
 constexpr int kWsDepartOff = 4;
 constexpr int kWsStatusOff = 8;
@@ -205,27 +207,40 @@ __device__ __forceinline__ uint32_t cvt_e2m1x8(float f0, float f1, float f2, flo
     return out;
 }
 
-// Two bf16 of one word (lo, hi) times c, as one packed fp32 multiply
+// 8 bf16 (one uint4: pairs (x0, x1) .. (x6, x7)) times c -> 8 e2m1 nibbles,
+// element i at bits 4i..4i+3.  Each pair is one packed fp32 multiply
 // (mul.rn.f32x2: each lane an IEEE round-to-nearest product, the same as two
-// __fmul_rn), converted to two e2m1 nibbles (lo in bits 0-3).
-__device__ __forceinline__ uint32_t cvt2_scaled(uint32_t w, uint64_t cc) {
-    uint64_t v, p;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(w << 16), "r"(w & 0xffff0000u));
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(v), "l"(cc));
-    uint16_t r;
-    asm("{\n.reg .f32 lo, hi;\n.reg .b8 b;\nmov.b64 {lo, hi}, %1;\ncvt.rn.satfinite.e2m1x2.f32 b, hi, lo;\n"
-        "cvt.u16.u8 %0, b;\n}"
-        : "=h"(r)
-        : "l"(p));
-    return r;
-}
-
-// 8 bf16 (one uint4) times c -> 8 nibbles via the hardware converter.
+// __fmul_rn) and one hardware conversion (RNE, saturating); the four code
+// bytes are packed by one move.
 __device__ __forceinline__ uint32_t cvt8_scaled(const uint4& w, float c) {
-    uint64_t cc;
-    asm("mov.b64 %0, {%1, %1};" : "=l"(cc) : "f"(c));
-    return cvt2_scaled(w.x, cc) | (cvt2_scaled(w.y, cc) << 8) | (cvt2_scaled(w.z, cc) << 16) |
-           (cvt2_scaled(w.w, cc) << 24);
+    uint32_t out;
+    asm("{\n"
+        ".reg .b64 cc, p0, p1, p2, p3;\n"
+        ".reg .f32 l0, h0, l1, h1, l2, h2, l3, h3;\n"
+        ".reg .b8 b0, b1, b2, b3;\n"
+        "mov.b64 cc, {%9, %9};\n"
+        "mov.b64 p0, {%1, %2};\n"
+        "mov.b64 p1, {%3, %4};\n"
+        "mov.b64 p2, {%5, %6};\n"
+        "mov.b64 p3, {%7, %8};\n"
+        "mul.rn.f32x2 p0, p0, cc;\n"
+        "mul.rn.f32x2 p1, p1, cc;\n"
+        "mul.rn.f32x2 p2, p2, cc;\n"
+        "mul.rn.f32x2 p3, p3, cc;\n"
+        "mov.b64 {l0, h0}, p0;\n"
+        "mov.b64 {l1, h1}, p1;\n"
+        "mov.b64 {l2, h2}, p2;\n"
+        "mov.b64 {l3, h3}, p3;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b0, h0, l0;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b1, h1, l1;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b2, h2, l2;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b3, h3, l3;\n"
+        "mov.b32 %0, {b0, b1, b2, b3};\n"
+        "}"
+        : "=r"(out)
+        : "r"(w.x << 16), "r"(w.x & 0xffff0000u), "r"(w.y << 16), "r"(w.y & 0xffff0000u), "r"(w.z << 16),
+          "r"(w.z & 0xffff0000u), "r"(w.w << 16), "r"(w.w & 0xffff0000u), "f"(c));
+    return out;
 }
 
 // RN(1/s) to within 2^-22 relative: hardware approximation refined by one
@@ -371,16 +386,16 @@ __global__ void __launch_bounds__(512, 2) amax_kernel(const uint16_t* __restrict
         if (gm > 0x7f80u) gmax = u2f(0x7fc00000u);
         else gmax = fmaxf(mag_to_f32(gm), 1.1754943508222875e-38f);  // clamp_min(tiny)
         if (gmax_out) *gmax_out = gmax;
-        *alpha_out = __fdiv_rn(gmax, 2688.0f);  // gmax / (6 * 448)
+        *alpha_out = nvfp4_alpha(gmax);
         *counter = 0u;
     }
 }
 
-// gmax for an empty tensor (quant.py:99-101): tiny, alpha = tiny / 2688
+// gmax for an empty tensor (quant.py:99-101): tiny, alpha = nvfp4_alpha(tiny)
 __global__ void empty_alpha_kernel(float* gmax_out, float* alpha_out) {
     const float tiny = 1.1754943508222875e-38f;
     if (gmax_out) *gmax_out = tiny;
-    *alpha_out = __fdiv_rn(tiny, 2688.0f);
+    *alpha_out = nvfp4_alpha(tiny);
 }
 
 // ---------------------------------------------------------------------------
@@ -670,13 +685,13 @@ __global__ void __launch_bounds__(kFusedThreads, 2) nvfp4_fused_kernel(
         s_mode = 0;
         if (blockIdx.x == 0) {
             if (gmax_out) *gmax_out = gmax;
-            *alpha_out = __fdiv_rn(gmax, 2688.0f);
+            *alpha_out = nvfp4_alpha(gmax);
         }
     }
     __syncthreads();
     Nvfp4Tensor t;
     t.gmax = s_gmax;
-    t.alpha = __fdiv_rn(t.gmax, 2688.0f);
+    t.alpha = nvfp4_alpha(t.gmax);
     t.markstein = t.gmax >= 0x1p-100f && t.gmax <= 1.0e35f;
     t.yg = t.markstein ? __frcp_rn(t.gmax) : 0.0f;
     {  // 4 lanes per scale byte, one candidate multiplier each
@@ -803,7 +818,7 @@ __global__ void __launch_bounds__(kEncThreads) nvfp4_encode_multi_kernel(const _
         gm = __reduce_max_sync(0xffffffffu, gm);
         Nvfp4Tensor tn;
         tn.gmax = gm > 0x7f80u ? u2f(0x7fc00000u) : fmaxf(u2f(gm << 16), 1.1754943508222875e-38f);
-        tn.alpha = __fdiv_rn(tn.gmax, 2688.0f);
+        tn.alpha = nvfp4_alpha(tn.gmax);
         tn.markstein = tn.gmax >= 0x1p-100f && tn.gmax <= 1.0e35f;
         tn.yg = tn.markstein ? __frcp_rn(tn.gmax) : 0.0f;
         if (c == g.chunk0[ti] && tid == 0) *T.alpha = tn.alpha;
@@ -894,7 +909,7 @@ __device__ __forceinline__ Nvfp4Tensor dual_scale(const cdlb200_nvfp4_dual_tenso
     }
     Nvfp4Tensor tn;
     tn.gmax = gmax;
-    tn.alpha = __fdiv_rn(gmax, 2688.0f);
+    tn.alpha = nvfp4_alpha(gmax);
     tn.markstein = gmax >= 0x1p-100f && gmax <= 1.0e35f;
     tn.yg = tn.markstein ? __frcp_rn(gmax) : 0.0f;
     return tn;

@@ -8,12 +8,15 @@ pass each (forward and backward), keeping the rounding steps of the eager
 modules.  Tensors that are not bf16 on a CUDA device go through the original
 Hugging Face code.  The RMSNorm and SwiGLU outputs feed quantized linears;
 their kernels also produce the output's global amax (``AMAX_ATTR``), so the
-NVFP4 quantize of those activations is a single encode pass.
+NVFP4 quantize of those activations is a single encode pass; the SwiGLU and
+rotary backward kernels do the same for the gradients of the gate / up and
+q / k projections (``grad_amax``).
 """
 
 from __future__ import annotations
 
 import types
+import weakref
 
 import torch
 
@@ -27,6 +30,32 @@ AMAX_ATTR = "_cdlb200_amax"
 
 def attach_amax(t: torch.Tensor, amax: torch.Tensor) -> None:
     setattr(t, AMAX_ATTR, (amax, t._version))
+
+
+# Gradients reach the next autograd node as views made by the engine (the
+# reshape of a linear's output), not as the tensor the kernel wrote, so their
+# amax words are found by address: (weak reference to the written gradient,
+# amax words, its version when written).  While the gradient is alive no
+# other tensor can share its address, and the version check rejects it once
+# something wrote into it.
+_GRAD_AMAX: list = []
+_GRAD_AMAX_MAX = 8
+
+
+def attach_grad_amax(t: torch.Tensor, amax: torch.Tensor) -> None:
+    _GRAD_AMAX.insert(0, (weakref.ref(t), amax, t._version))
+    del _GRAD_AMAX[_GRAD_AMAX_MAX:]
+
+
+def grad_amax(g: torch.Tensor) -> torch.Tensor | None:
+    """The amax words of gradient ``g`` (the tensor a kernel wrote or a view
+    of all of it) if its producer formed them, else None."""
+    for ref, amax, version in _GRAD_AMAX:
+        t = ref()
+        if (t is not None and t.data_ptr() == g.data_ptr() and t.numel() == g.numel() and t.device == g.device
+                and g._version == version and g.is_contiguous()):
+            return amax
+    return None
 
 
 def _cuda_bf16(*ts: torch.Tensor) -> bool:
@@ -74,8 +103,12 @@ class RopeFn(torch.autograd.Function):
             xt = xt.contiguous()
         b, s, h, d = xt.shape
         out = torch.empty_like(xt)
+        # the backward's output is the q / k projection's gradient: form its amax
+        amax = torch.zeros(_lib.AMAX_WORDS, dtype=torch.int32, device=x.device) if backward else None
         _lib.call("cdlb200_rope", _lib.ptr(xt), _lib.ptr(cos), _lib.ptr(sin), b * s, h, d, cos.shape[0] * s,
-                  backward, _lib.ptr(out), _lib.stream(x.device))
+                  backward, _lib.ptr(out), _lib.ptr(amax), _lib.stream(x.device))
+        if amax is not None:
+            attach_grad_amax(out, amax)
         return out.transpose(1, 2)
 
     @staticmethod
@@ -108,8 +141,11 @@ class SwiGLUFn(torch.autograd.Function):
         g, u = ctx.saved_tensors
         dh = dh.contiguous()
         dg, du = torch.empty_like(g), torch.empty_like(u)
+        amax = torch.zeros(2, _lib.AMAX_WORDS, dtype=torch.int32, device=g.device)
         _lib.call("cdlb200_swiglu_bwd", _lib.ptr(dh), _lib.ptr(g), _lib.ptr(u), g.numel(), _lib.ptr(dg), _lib.ptr(du),
-                  _lib.stream(g.device))
+                  _lib.ptr(amax[0]), _lib.ptr(amax[1]), _lib.stream(g.device))
+        attach_grad_amax(dg, amax[0])
+        attach_grad_amax(du, amax[1])
         return dg, du
 
 

@@ -49,6 +49,10 @@ extern "C" {
 #define CDLB200_SCALE_LINEAR 0    /* [rows, nb] row-major */
 #define CDLB200_SCALE_SWIZZLED 1  /* 128x4 tiles, zero-padded */
 
+/* element types of cdlb200_quant_wide's input */
+#define CDLB200_DTYPE_F32 1
+#define CDLB200_DTYPE_F16 2
+
 /* Human-readable name of a status code. */
 const char* cdlb200_status_string(int status);
 
@@ -93,6 +97,22 @@ size_t cdlb200_nvfp4_quant_workspace_bytes(int64_t rows, int64_t k);
 int cdlb200_nvfp4_quant(const void* x, int64_t rows, int64_t k, int64_t ldx, int transpose,
                         void* packed, void* scale, int scale_layout, float* gmax, float* alpha,
                         void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Block-scaled quantize of an fp32 or fp16 matrix (dtype CDLB200_DTYPE_F32 /
+ * CDLB200_DTYPE_F16), format 0 = NVFP4, 1 = MXFP4, 2 = MXFP8.  cdl's `_quant`
+ * (cdl/core/kernel/quant.py:71-123) accepts any floating input: its Triton
+ * kernel casts each block to fp32 and divides, and the NVFP4 global amax is
+ * taken in the input's dtype.  This entry performs those fp32 operations
+ * literally (the bf16 entry points above use bf16-exact shortcuts) and gives
+ * the same codes, scale bytes and alpha.  Arguments as cdlb200_nvfp4_quant /
+ * cdlb200_mx*_quant; alpha (fp32 [1]) and workspace are needed for NVFP4 only
+ * (the global amax is kept in the workspace).  Not tuned: cdl's training step
+ * quantizes bf16 tensors.
+ */
+int cdlb200_quant_wide(const void* x, int dtype, int format, int64_t rows, int64_t k, int64_t ldx, int transpose,
+                       void* packed, void* scale, int scale_layout, float* alpha, void* workspace,
+                       size_t workspace_bytes, void* stream);
 
 /*
  * The global-amax pass of cdlb200_nvfp4_quant on its own: gmax = max|x|

@@ -39,16 +39,23 @@ int cdlb200_rmsnorm_bwd(const void* dy, const void* x, const void* w, const floa
 /* Rotary embedding of x[tokens, heads, head_dim] with cos/sin[cos_tokens,
  * head_dim] (token t uses row t % cos_tokens; head_dim % 16 == 0):
  * forward = x*cos + rotate_half(x)*sin, each product and the sum rounded to
- * bf16; backward = the gradient of that (g*cos + rotate_half^T(g*sin)). */
+ * bf16; backward = the gradient of that (g*cos + rotate_half^T(g*sin)).
+ * amax (optional, CDLB200_AMAX_WORDS words, zero on entry) receives the bf16
+ * magnitude maximum of out, as for the RMSNorm above (the backward's output
+ * is the q / k projections' gradient, which the quantized backward encodes). */
 int cdlb200_rope(const void* x, const void* cos, const void* sin, int64_t tokens, int64_t heads, int64_t head_dim,
-                 int64_t cos_tokens, int backward, void* out, void* stream);
+                 int64_t cos_tokens, int backward, void* out, uint32_t* amax, void* stream);
 
 /* h = bf16(bf16(silu(g)) * u) over n values (n % 8 == 0); amax (optional,
  * CDLB200_AMAX_WORDS words, zero on entry) as for the RMSNorm above. */
 int cdlb200_swiglu_fwd(const void* g, const void* u, int64_t n, void* h, uint32_t* amax, void* stream);
 
-/* dg, du of the SwiGLU product above, given dh. */
-int cdlb200_swiglu_bwd(const void* dh, const void* g, const void* u, int64_t n, void* dg, void* du, void* stream);
+/* dg, du of the SwiGLU product above, given dh; amax_dg / amax_du (optional,
+ * CDLB200_AMAX_WORDS words each, zero on entry) receive the bf16 magnitude
+ * maxima of dg and du, so that their NVFP4 encodings in the quantized
+ * backward skip a separate amax pass. */
+int cdlb200_swiglu_bwd(const void* dh, const void* g, const void* u, int64_t n, void* dg, void* du,
+                       uint32_t* amax_dg, uint32_t* amax_du, void* stream);
 
 /* Cross entropy of bf16 logits[rows, vocab] (contiguous, vocab % 8 == 0)
  * against int64 targets[rows], the per-chunk step of the reference's fused

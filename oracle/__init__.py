@@ -93,7 +93,7 @@ def quant(x: np.ndarray, fmt: int, gmax: float | None = None):
     Returns ``(packed, scale, alpha)`` exactly as the reference's
     ``nvfp4_quant`` / ``mxfp4_quant`` / ``mxfp8_quant`` (quant.py:126-146):
     packed uint8 ``[rows, nb*B/2]`` (FP4) or ``[rows, nb*B]`` (FP8 bytes),
-    scale uint8 ``[rows, nb]``, alpha float32 ``[1]`` (NVFP4: gmax/2688,
+    scale uint8 ``[rows, nb]``, alpha float32 ``[1]`` (NVFP4: gmax/2688 as the device forms it, gmax * RN(1/2688),
     MXFP4: 1.0) or ``None`` (MXFP8).
     """
     lib = _load()

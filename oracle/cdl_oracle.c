@@ -17,7 +17,12 @@
  *   cdl/core/tables.py:8-56       level tables (fp32)
  * and the kernel-side conventions of the reference's Triton path:
  *   cdl/core/kernel/quant.py:34,84   K tail zero-padded to whole blocks
- *   cdl/core/kernel/quant.py:96-101  gmax = max|x| clamped to FLT_MIN, alpha = gmax/2688
+ *   cdl/core/kernel/quant.py:96-101  gmax = max|x| clamped to FLT_MIN, alpha = gmax/2688,
+ *                                    formed on the device, where torch divides a tensor by
+ *                                    a Python float as a multiply by the fp32 reciprocal
+ *                                    (on the CPU the same line divides; the two differ in
+ *                                    the last bit for about a fifth of all gmax values, none
+ *                                    of them in the golden cases)
  *   cdl/core/kernel/dequant.py:6-47  e8m0 byte 0 = 2^-127, dequant = (v*s)*alpha -> bf16
  *   cdl/core/mm/swizzle.py:5-14      128x4 scale-factor tile layout
  *
@@ -110,6 +115,12 @@ static float absmax_bf16(const uint16_t* x, int64_t n, int* has_nan) {
     return m;
 }
 
+/* alpha = gmax / (6 * 448) as torch forms it on the device: gmax * RN(1 / 2688). */
+static inline float nvfp4_alpha(float gmax) {
+    volatile float inv = 1.0f / 2688.0f; /* RN(1/2688), an fp32 constant */
+    return gmax * inv;
+}
+
 /* Global amax and alpha of the NVFP4 path (quant.py:96-101, ecdl.py:52-56). */
 void oracle_nvfp4_global(const uint16_t* x, int64_t n, float* gmax_out, float* alpha_out) {
     int has_nan = 0;
@@ -117,7 +128,7 @@ void oracle_nvfp4_global(const uint16_t* x, int64_t n, float* gmax_out, float* a
     if (has_nan) g = u2f(0x7fc00000u);
     else if (g < FP32_TINY) g = FP32_TINY;
     *gmax_out = g;
-    *alpha_out = g / 2688.0f;                               /* f_max = 6 * 448 */
+    *alpha_out = nvfp4_alpha(g);
 }
 
 /* Shared exponent byte of an MX block (ecdl.py:59-73): clamp(floor(log2(max(bamax,
@@ -147,7 +158,7 @@ void oracle_quant(const uint16_t* x, int64_t rows, int64_t k, int64_t ld, int fm
     const int B = fmt == 0 ? 16 : 32;
     const int64_t nb = (k + B - 1) / B;
     const int64_t pstride = fmt == 2 ? nb * B : nb * B / 2;
-    const float alpha = gmax / 2688.0f;
+    const float alpha = nvfp4_alpha(gmax);
     float v[32];
     for (int64_t r = 0; r < rows; ++r) {
         const uint16_t* xr = x + r * ld;

@@ -48,7 +48,7 @@ def nvfp4_fake_quant(t: torch.Tensor) -> torch.Tensor:
     n = max(1, min(_Pool.threads, x.shape[0]))
     chunks = np.array_split(np.arange(x.shape[0]), n)
     gmax = max(_Pool.ex.map(lambda idx: oracle.nvfp4_global(x[idx[0]: idx[-1] + 1])[0], chunks))
-    alpha = np.float32(gmax) / np.float32(2688.0)  # cdl/core/kernel/quant.py:96-101
+    alpha = np.float32(gmax) * (np.float32(1.0) / np.float32(2688.0))  # quant.py:96-101, as on the device
     outs = list(_Pool.ex.map(lambda idx: oracle.quant(x[idx[0]: idx[-1] + 1], oracle.NVFP4, gmax)[:2], chunks))
     deq = list(_Pool.ex.map(lambda ps: oracle.dequant(ps[0], ps[1], oracle.NVFP4, np.array([alpha], np.float32)),
                             outs))

@@ -192,3 +192,49 @@ def test_epilogue_amax_feeds_single_pass_encode():
         rp, rs, ra = nvfp4_quant(out.reshape(-1, out.shape[-1]).contiguous(), swizzled=True)
         assert torch.equal(p, rp) and torch.equal(s, rs) and torch.equal(a.reshape(-1), ra.reshape(-1))
         assert torch.equal(d, nvfp4_dequant(rp, rs, ra, swizzled=True))
+
+
+def test_swiglu_backward_gradient_amax():
+    """The SwiGLU backward forms the amax words of dg and du; they are found
+    again through the engine's reshape views of the gradients, and the dual
+    encode given them equals the one that computes its own amax."""
+    from cdl_b200.core.kernel.quant import nvfp4_dual_quant
+    from cdl_b200.model.components.fused import SwiGLUFn, grad_amax
+
+    gen = torch.Generator("cuda").manual_seed(12)
+    g = torch.randn(2, 128, 1024, device="cuda", generator=gen).bfloat16().requires_grad_()
+    u = torch.randn(2, 128, 1024, device="cuda", generator=gen).bfloat16().requires_grad_()
+    dh = torch.randn(2, 128, 1024, device="cuda", generator=gen).bfloat16()
+    seen = {}
+    g.register_hook(lambda t: seen.__setitem__("g", t))
+    u.register_hook(lambda t: seen.__setitem__("u", t))
+    SwiGLUFn.apply(g, u).backward(dh)
+    for name in ("g", "u"):
+        grad = seen[name]
+        words = grad_amax(grad.reshape(-1, 1024))
+        assert words is not None
+        want = int((grad.contiguous().view(torch.int16).int() & 0x7FFF).max())
+        assert int(words.max().item()) == want
+        row, col = nvfp4_dual_quant(grad.reshape(-1, 1024), amax=words)
+        row2, col2 = nvfp4_dual_quant(grad.reshape(-1, 1024))
+        for a, b in zip(row + col, row2 + col2):
+            assert torch.equal(a, b)
+    other = torch.zeros(256, 1024, device="cuda", dtype=torch.bfloat16)
+    assert grad_amax(other) is None
+    # rotary backward: the q / k projection's gradient, [B, S, H * D] as the
+    # linear's backward sees it
+    from cdl_b200.model.components.fused import RopeFn
+
+    base = torch.randn(2, 128, 4, 64, device="cuda", generator=gen).bfloat16().requires_grad_()
+    ang = torch.randn(1, 128, 32, device="cuda", generator=gen)
+    cos = torch.cat([ang.cos(), ang.cos()], -1).bfloat16().contiguous()
+    sin = torch.cat([ang.sin(), ang.sin()], -1).bfloat16().contiguous()
+    base.register_hook(lambda t: seen.__setitem__("q", t))
+    RopeFn.apply(base.transpose(1, 2), cos, sin).backward(
+        torch.randn(2, 4, 128, 64, device="cuda", generator=gen).bfloat16())
+    gq = seen["q"].reshape(-1, 256)
+    words = grad_amax(gq)
+    assert words is not None
+    assert int(words.max().item()) == int((gq.contiguous().view(torch.int16).int() & 0x7FFF).max())
+    seen["g"].add_(1)  # written after the kernel: its words no longer hold
+    assert grad_amax(seen["g"].reshape(-1, 1024)) is None

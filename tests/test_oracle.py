@@ -36,6 +36,28 @@ def test_oracle_quant_matches_reference(golden):
             assert alpha.view(np.uint32)[0] == golden[key + "/alpha"].view(np.uint32)[0], key
 
 
+def test_wide_oracle_matches_reference_on_bf16_values(golden):
+    """The fp32 / fp16 oracle (the Triton kernel's fp32 arithmetic) on the
+    golden inputs widened to fp32 gives the reference's golden codes, scales
+    and alpha; on fp16-representable values its fp16 and fp32 inputs agree."""
+    from oracle.wide import quant_wide
+
+    for key in _cases(golden):
+        fmt = FMTS[key.split("/")[0]]
+        x = oracle.bf16_bits_to_f32(golden[key + "/x"])
+        packed, scale, alpha = quant_wide(x, fmt)
+        np.testing.assert_array_equal(packed, golden[key + "/packed"], err_msg=key)
+        np.testing.assert_array_equal(scale, golden[key + "/scale"], err_msg=key)
+        if fmt == oracle.NVFP4:
+            assert alpha.view(np.uint32)[0] == golden[key + "/alpha"].view(np.uint32)[0], key
+    rng = np.random.default_rng(3)
+    h = (rng.standard_normal((64, 96)) * np.exp(rng.standard_normal((64, 1)))).astype(np.float16)
+    for fmt in FMTS.values():
+        for a, b in zip(quant_wide(h, fmt), quant_wide(h.astype(np.float32), fmt)):
+            if a is not None:
+                np.testing.assert_array_equal(a, b)
+
+
 def test_oracle_dequant_matches_reference(golden):
     for key in _cases(golden):
         fmt = FMTS[key.split("/")[0]]

@@ -153,7 +153,7 @@ def test_empty_and_errors():
     e = torch.empty(0, 64, dtype=torch.bfloat16, device="cuda")
     packed, scale, alpha = q[oracle.NVFP4](e)
     assert packed.shape == (0, 32) and scale.shape == (0, 4)
-    assert alpha.cpu().numpy().view(np.uint32)[0] == np.array([np.finfo(np.float32).tiny / np.float32(2688)], np.float32).view(np.uint32)[0]
+    assert alpha.cpu().numpy().view(np.uint32)[0] == np.array([np.finfo(np.float32).tiny * (np.float32(1) / np.float32(2688))], np.float32).view(np.uint32)[0]
     packed, scale, alpha = q[oracle.MXFP8](torch.empty(5, 0, dtype=torch.bfloat16, device="cuda"))
     assert packed.shape == (5, 0) and scale.shape == (5, 0) and alpha is None
     with pytest.raises(ValueError):
