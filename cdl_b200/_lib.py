@@ -63,6 +63,8 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_rmsnorm_fwd": (_I, [_P, _P, _I64, _I64, ctypes.c_float, _P, _P, _P, _P]),
     "cdlb200_rmsnorm_bwd_workspace_bytes": (_I64, [_I64, _I64]),
     "cdlb200_rmsnorm_bwd": (_I, [_P, _P, _P, _P, _I64, _I64, _P, _P, _P, _I64, _P]),
+    "cdlb200_add_rmsnorm_fwd": (_I, [_P, _P, _P, _I64, _I64, ctypes.c_float, _P, _P, _P, _P, _P]),
+    "cdlb200_rmsnorm_bwd_add": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _I64, _P]),
     "cdlb200_rope": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _P, _P, _P]),
     "cdlb200_swiglu_fwd": (_I, [_P, _P, _I64, _P, _P, _P]),
     "cdlb200_swiglu_bwd": (_I, [_P, _P, _P, _I64, _P, _P, _P, _P, _P]),
@@ -134,7 +136,7 @@ def lib() -> ctypes.CDLL:
 
 # kernels one call of an entry point launches (default 1); `launches` counts
 # them over the process, so a benchmark can report how many ran
-KERNELS_PER_CALL = {"cdlb200_rmsnorm_bwd": 2, "cdlb200_clip_adamw": 3, "cdlb200_ecdl_fwd": 2, "cdlb200_ecdl_bwd": 2,
+KERNELS_PER_CALL = {"cdlb200_rmsnorm_bwd": 2, "cdlb200_rmsnorm_bwd_add": 2, "cdlb200_clip_adamw": 3, "cdlb200_ecdl_fwd": 2, "cdlb200_ecdl_bwd": 2,
                     "cdlb200_ccdl_bwd": 2}
 launches = 0
 

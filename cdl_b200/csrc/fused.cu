@@ -82,35 +82,70 @@ __device__ __forceinline__ void cta_amax2(uint32_t m2a, uint32_t* amax_a, uint32
 }
 
 // ---------------------------------------------------------------------------
-// RMSNorm: one warp per row; lane l owns the 8-value vectors l, l + 32, ...
-// (VPL vectors at most, d = 8 * nvec).
+// RMSNorm over rows of d = 8 * nvec bf16 values.  W warps (1, 2 or 4) share a
+// row: lane l of warp w owns the 8-value vectors (32 w + l) + 32 W j, j < VPL;
+// a 256-thread CTA holds R = 8 / W rows at a time.  Few registers per thread,
+// so that many CTAs per SM keep enough loads in flight for HBM.  The row sums
+// are reduced per warp with shuffles, then over the row's W warps in a fixed
+// order through shared memory.
 // ---------------------------------------------------------------------------
+struct RowSplit {
+    int W, R;  // warps per row, rows per CTA pass
+};
+
+__device__ __forceinline__ float row_sum(float v, float (*red)[4], int slot, int wr, int W) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) red[slot][wr] = v;
+    __syncthreads();
+    float t = 0.f;
+    for (int k = 0; k < W; ++k) t += red[slot][k];
+    __syncthreads();  // red is reused by the next row pass
+    return t;
+}
+
+// With `res`, the normalized row is h = bf16(x + res) (the decoder's residual
+// add, as torch adds two bf16 tensors), which is also written to `hout`.
 template <int VPL>
 __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const uint4* __restrict__ x, const uint4* __restrict__ w,
                                                           int64_t rows, int nvec, float eps, uint4* __restrict__ y,
-                                                          float* __restrict__ rstd, uint32_t* __restrict__ amax) {
-    const int lane = threadIdx.x & 31;
+                                                          float* __restrict__ rstd, uint32_t* __restrict__ amax,
+                                                          const uint4* __restrict__ res, uint4* __restrict__ hout,
+                                                          RowSplit rsp) {
+    __shared__ float red[8][4];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int slot = warp / rsp.W, wr = warp - slot * rsp.W;
     uint32_t am = 0;  // max |y| as bf16 magnitude bits (the NVFP4 global amax of the output)
-    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    for (int64_t base = (int64_t)blockIdx.x * rsp.R; base < rows; base += (int64_t)gridDim.x * rsp.R) {
+        const int64_t r = base + slot;
+        const bool live = r < rows;
         uint4 v[VPL];
         float ss = 0.f;
 #pragma unroll
         for (int j = 0; j < VPL; ++j) {
-            const int c = lane + 32 * j;
-            v[j] = c < nvec ? x[r * nvec + c] : make_uint4(0u, 0u, 0u, 0u);
+            const int c = 32 * wr + lane + 32 * rsp.W * j;
+            const bool in = live && c < nvec;
+            v[j] = in ? x[r * nvec + c] : make_uint4(0u, 0u, 0u, 0u);
             float f[8];
             unpack8(v[j], f);
+            if (res != nullptr && in) {
+                float b[8];
+                unpack8(res[r * nvec + c], b);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) f[i] += b[i];
+                v[j] = pack8(f);
+                hout[r * nvec + c] = v[j];
+                unpack8(v[j], f);
+            }
 #pragma unroll
             for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
         }
-        ss = warp_sum(ss);
+        ss = row_sum(ss, red, slot, wr, rsp.W);
         const float rs = rsqrtf(ss / (float)(8 * nvec) + eps);
-        if (lane == 0) rstd[r] = rs;
+        if (live && wr == 0 && lane == 0) rstd[r] = rs;
 #pragma unroll
         for (int j = 0; j < VPL; ++j) {
-            const int c = lane + 32 * j;
-            if (c >= nvec) continue;
+            const int c = 32 * wr + lane + 32 * rsp.W * j;
+            if (!live || c >= nvec) continue;
             float f[8], g[8];
             unpack8(v[j], f);
             unpack8(w[c], g);
@@ -126,13 +161,19 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const uint4* __restric
 
 // dx = bf16(rs * g1 - x * rs^3 * sum(g1 * x) / d) with g1 = bf16(dy * w);
 // dw partial sums (fp32, one row of `part` per CTA) of dy * bf16(x * rs).
+// With `dres`, dx = bf16(dx + dres): the gradient the residual branch adds
+// (autograd's sum of the two bf16 gradients of the residual input); `amax`
+// (optional) receives the bf16 magnitude maximum of dx.
 template <int VPL>
 __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const uint4* __restrict__ dy, const uint4* __restrict__ x,
                                                           const uint4* __restrict__ w, const float* __restrict__ rstd,
                                                           int64_t rows, int nvec, uint4* __restrict__ dx,
-                                                          float* __restrict__ part) {
+                                                          float* __restrict__ part, const uint4* __restrict__ dres,
+                                                          uint32_t* __restrict__ amax, RowSplit rsp) {
     extern __shared__ float dw_s[];  // [8 * nvec]
-    const int lane = threadIdx.x & 31;
+    __shared__ float red[8][4];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int slot = warp / rsp.W, wr = warp - slot * rsp.W;
     for (int i = threadIdx.x; i < 8 * nvec; i += blockDim.x) dw_s[i] = 0.f;
     __syncthreads();
     float acc[VPL][8];
@@ -140,22 +181,25 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const uint4* __restric
     for (int j = 0; j < VPL; ++j)
 #pragma unroll
         for (int i = 0; i < 8; ++i) acc[j][i] = 0.f;
-    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     const float inv_d = 1.0f / (float)(8 * nvec);
-    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
-        const float rs = rstd[r];
+    uint32_t am = 0;
+    for (int64_t base = (int64_t)blockIdx.x * rsp.R; base < rows; base += (int64_t)gridDim.x * rsp.R) {
+        const int64_t r = base + slot;
+        const bool live = r < rows;
+        const float rs = live ? rstd[r] : 0.f;
         uint4 xv[VPL], dv[VPL];  // the row stays in registers as bf16; fp32 values are recomputed
         float dot = 0.f;
 #pragma unroll
         for (int j = 0; j < VPL; ++j) {
-            const int c = lane + 32 * j;
-            xv[j] = c < nvec ? x[r * nvec + c] : make_uint4(0u, 0u, 0u, 0u);
-            dv[j] = c < nvec ? dy[r * nvec + c] : make_uint4(0u, 0u, 0u, 0u);
+            const int c = 32 * wr + lane + 32 * rsp.W * j;
+            const bool in = live && c < nvec;
+            xv[j] = in ? x[r * nvec + c] : make_uint4(0u, 0u, 0u, 0u);
+            dv[j] = in ? dy[r * nvec + c] : make_uint4(0u, 0u, 0u, 0u);
         }
 #pragma unroll
         for (int j = 0; j < VPL; ++j) {
-            const int c = lane + 32 * j;
-            if (c >= nvec) continue;
+            const int c = 32 * wr + lane + 32 * rsp.W * j;
+            if (!live || c >= nvec) continue;
             float xf[8], d8[8], w8[8];
             unpack8(xv[j], xf);
             unpack8(dv[j], d8);
@@ -166,30 +210,39 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const uint4* __restric
                 acc[j][i] = fmaf(d8[i], rbf(xf[i] * rs), acc[j][i]);
             }
         }
-        dot = warp_sum(dot);
+        dot = row_sum(dot, red, slot, wr, rsp.W);
         const float k = rs * rs * rs * dot * inv_d;
 #pragma unroll
         for (int j = 0; j < VPL; ++j) {
-            const int c = lane + 32 * j;
-            if (c >= nvec) continue;
+            const int c = 32 * wr + lane + 32 * rsp.W * j;
+            if (!live || c >= nvec) continue;
             float xf[8], d8[8], w8[8], o[8];
             unpack8(xv[j], xf);
             unpack8(dv[j], d8);
             unpack8(w[c], w8);
 #pragma unroll
             for (int i = 0; i < 8; ++i) o[i] = rs * rbf(d8[i] * w8[i]) - xf[i] * k;
-            dx[r * nvec + c] = pack8(o);
+            if (dres != nullptr) {
+                float r8[8];
+                unpack8(dres[r * nvec + c], r8);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) o[i] = rbf(o[i]) + r8[i];
+            }
+            const uint4 ov = pack8(o);
+            dx[r * nvec + c] = ov;
+            am = mag8(am, ov);
         }
     }
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
-        const int c = lane + 32 * j;
+        const int c = 32 * wr + lane + 32 * rsp.W * j;
         if (c >= nvec) continue;
 #pragma unroll
         for (int i = 0; i < 8; ++i) atomicAdd(&dw_s[8 * c + i], acc[j][i]);
     }
     __syncthreads();
     for (int i = threadIdx.x; i < 8 * nvec; i += blockDim.x) part[(int64_t)blockIdx.x * 8 * nvec + i] = dw_s[i];
+    if (amax) cta_amax(am, amax);
 }
 
 // dw[i] = bf16(sum over the CTA partials): a CTA per 32 columns, its 8 warps
@@ -389,60 +442,94 @@ int grid_for(int64_t items, int per_block) {
 
 using namespace cdlb200;
 
-extern "C" int cdlb200_rmsnorm_fwd(const void* x, const void* w, int64_t rows, int64_t d, float eps, void* y,
-                                   float* rstd, uint32_t* amax, void* stream) {
+namespace {
+// W = the smallest power of two with 64 W >= nvec (at most 4), VPL = vectors per lane
+RowSplit row_split(int nvec, int& vpl) {
+    int W = 1;
+    while (W < 4 && 64 * W < nvec) W *= 2;
+    vpl = (nvec + 32 * W - 1) / (32 * W);
+    return RowSplit{W, 8 / W};
+}
+
+int rmsnorm_fwd_launch(const void* x, const void* res, const void* w, int64_t rows, int64_t d, float eps, void* h,
+                       void* y, float* rstd, uint32_t* amax, void* stream) {
     if (rows < 0 || d <= 0 || (d % 8) != 0 || d > 8 * 32 * 8) return CDLB200_ERR_INVALID_ARG;
     if (rows == 0) return CDLB200_OK;
-    if (!x || !w || !y || !rstd) return CDLB200_ERR_INVALID_ARG;
-    if (!al16(x) || !al16(w) || !al16(y)) return CDLB200_ERR_ALIGNMENT;
-    const int nvec = (int)(d / 8), vpl = (nvec + 31) / 32;
-    const int grid = grid_for(rows, 8);
+    if (!x || !w || !y || !rstd || (res != nullptr) != (h != nullptr)) return CDLB200_ERR_INVALID_ARG;
+    if (!al16(x) || !al16(w) || !al16(y) || !al16(res) || !al16(h)) return CDLB200_ERR_ALIGNMENT;
+    const int nvec = (int)(d / 8);
+    int vpl = 1;
+    const RowSplit rsp = row_split(nvec, vpl);
+    const int grid = grid_for(rows, rsp.R);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     auto args = [&](auto kern) {
         kern<<<grid, 256, 0, st>>>(static_cast<const uint4*>(x), static_cast<const uint4*>(w), rows, nvec, eps,
-                                   static_cast<uint4*>(y), rstd, amax);
+                                   static_cast<uint4*>(y), rstd, amax, static_cast<const uint4*>(res),
+                                   static_cast<uint4*>(h), rsp);
     };
     if (vpl <= 1) args(rmsnorm_fwd_kernel<1>);
-    else if (vpl <= 2) args(rmsnorm_fwd_kernel<2>);
-    else if (vpl <= 4) args(rmsnorm_fwd_kernel<4>);
-    else args(rmsnorm_fwd_kernel<8>);
+    else args(rmsnorm_fwd_kernel<2>);
     CDLB200_CHECK_LAUNCH();
     return CDLB200_OK;
+}
+}  // namespace
+
+extern "C" int cdlb200_rmsnorm_fwd(const void* x, const void* w, int64_t rows, int64_t d, float eps, void* y,
+                                   float* rstd, uint32_t* amax, void* stream) {
+    return rmsnorm_fwd_launch(x, nullptr, w, rows, d, eps, nullptr, y, rstd, amax, stream);
+}
+
+extern "C" int cdlb200_add_rmsnorm_fwd(const void* res, const void* x, const void* w, int64_t rows, int64_t d,
+                                       float eps, void* h, void* y, float* rstd, uint32_t* amax, void* stream) {
+    if (rows > 0 && (!res || !h)) return CDLB200_ERR_INVALID_ARG;
+    return rmsnorm_fwd_launch(x, res, w, rows, d, eps, h, y, rstd, amax, stream);
 }
 
 // the backward runs one persistent CTA per SM (each accumulates its rows' dw
 // in registers, then once into shared memory and one partial row)
-static int bwd_grid(int64_t rows) {
-    const int64_t g = (rows + 7) / 8, cap = num_sms();
+// the backward keeps each CTA's dw in registers and writes one partial row per
+// CTA: 4 CTAs per SM at most (for 2048 columns, 4.8 MB of partials)
+static int bwd_grid(int64_t rows, int64_t d) {
+    int vpl = 1;
+    const RowSplit rsp = row_split((int)(d / 8), vpl);
+    const int64_t g = (rows + rsp.R - 1) / rsp.R, cap = 4 * (int64_t)num_sms();
     return (int)(g < 1 ? 1 : (g < cap ? g : cap));
 }
 
 extern "C" int64_t cdlb200_rmsnorm_bwd_workspace_bytes(int64_t rows, int64_t d) {
     if (rows <= 0 || d <= 0) return 0;
-    return (int64_t)bwd_grid(rows) * d * (int64_t)sizeof(float);
+    return (int64_t)bwd_grid(rows, d) * d * (int64_t)sizeof(float);
 }
 
 extern "C" int cdlb200_rmsnorm_bwd(const void* dy, const void* x, const void* w, const float* rstd, int64_t rows,
                                    int64_t d, void* dx, void* dw, void* workspace, int64_t workspace_bytes,
                                    void* stream) {
+    return cdlb200_rmsnorm_bwd_add(dy, x, w, rstd, nullptr, rows, d, dx, dw, nullptr, workspace, workspace_bytes,
+                                   stream);
+}
+
+extern "C" int cdlb200_rmsnorm_bwd_add(const void* dy, const void* x, const void* w, const float* rstd,
+                                       const void* dres, int64_t rows, int64_t d, void* dx, void* dw, uint32_t* amax,
+                                       void* workspace, int64_t workspace_bytes, void* stream) {
     if (rows < 0 || d <= 0 || (d % 8) != 0 || d > 8 * 32 * 8) return CDLB200_ERR_INVALID_ARG;
     if (rows == 0) return CDLB200_OK;
     if (!dy || !x || !w || !rstd || !dx || !dw || !workspace) return CDLB200_ERR_INVALID_ARG;
-    if (!al16(dy) || !al16(x) || !al16(w) || !al16(dx)) return CDLB200_ERR_ALIGNMENT;
+    if (!al16(dy) || !al16(x) || !al16(w) || !al16(dx) || !al16(dres)) return CDLB200_ERR_ALIGNMENT;
     if (workspace_bytes < cdlb200_rmsnorm_bwd_workspace_bytes(rows, d)) return CDLB200_ERR_WORKSPACE;
-    const int nvec = (int)(d / 8), vpl = (nvec + 31) / 32;
-    const int grid = bwd_grid(rows);
+    const int nvec = (int)(d / 8);
+    int vpl = 1;
+    const RowSplit rsp = row_split(nvec, vpl);
+    const int grid = bwd_grid(rows, d);
     const size_t smem = (size_t)d * sizeof(float);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     float* part = static_cast<float*>(workspace);
     auto args = [&](auto kern) {
         kern<<<grid, 256, smem, st>>>(static_cast<const uint4*>(dy), static_cast<const uint4*>(x),
-                                      static_cast<const uint4*>(w), rstd, rows, nvec, static_cast<uint4*>(dx), part);
+                                      static_cast<const uint4*>(w), rstd, rows, nvec, static_cast<uint4*>(dx), part,
+                                      static_cast<const uint4*>(dres), amax, rsp);
     };
     if (vpl <= 1) args(rmsnorm_bwd_kernel<1>);
-    else if (vpl <= 2) args(rmsnorm_bwd_kernel<2>);
-    else if (vpl <= 4) args(rmsnorm_bwd_kernel<4>);
-    else args(rmsnorm_bwd_kernel<8>);
+    else args(rmsnorm_bwd_kernel<2>);
     CDLB200_CHECK_LAUNCH();
     colsum_kernel<<<(unsigned)((d + 31) / 32), 256, 0, st>>>(part, grid, (int)d, static_cast<uint16_t*>(dw));
     CDLB200_CHECK_LAUNCH();

@@ -91,6 +91,50 @@ class RMSNormFn(torch.autograd.Function):
         return dx.view(ctx.shape), dw, None
 
 
+class ResidualRMSNormFn(torch.autograd.Function):
+    """``h = res + x`` (bf16) and ``y = RMSNorm(h)`` in one pass: the decoder's
+    residual add and the norm after it.  The backward returns one gradient for
+    both inputs -- the norm's input gradient plus the gradient ``h`` receives
+    from its other consumer, summed in the kernel as autograd would sum them
+    -- and forms its amax: it is the gradient of the o / down projection that
+    produced ``x``, which the quantized backward encodes."""
+
+    @staticmethod
+    def forward(ctx, res: torch.Tensor, x: torch.Tensor, w: torch.Tensor, eps: float):
+        d = x.shape[-1]
+        r2 = res.reshape(-1, d).contiguous()
+        x2 = x.reshape(-1, d).contiguous()
+        h = torch.empty_like(x2)
+        y = torch.empty_like(x2)
+        rstd = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device)
+        amax = torch.zeros(_lib.AMAX_WORDS, dtype=torch.int32, device=x.device)
+        _lib.call("cdlb200_add_rmsnorm_fwd", _lib.ptr(r2), _lib.ptr(x2), _lib.ptr(w), x2.shape[0], d, float(eps),
+                  _lib.ptr(h), _lib.ptr(y), _lib.ptr(rstd), _lib.ptr(amax), _lib.stream(x.device))
+        attach_amax(y, amax)
+        ctx.save_for_backward(h, w, rstd)
+        ctx.shape = x.shape
+        return h.view(x.shape), y.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, dh: torch.Tensor | None, dy: torch.Tensor | None):
+        h, w, rstd = ctx.saved_tensors
+        rows, d = h.shape
+        dy2 = (dy if dy is not None else torch.zeros(ctx.shape, dtype=h.dtype, device=h.device))
+        dy2 = dy2.reshape(rows, d).contiguous()
+        dh2 = dh.reshape(rows, d).contiguous() if dh is not None else None
+        dx = torch.empty_like(h)
+        dw = torch.empty_like(w)
+        amax = torch.zeros(_lib.AMAX_WORDS, dtype=torch.int32, device=h.device)
+        nbytes = int(_lib.lib().cdlb200_rmsnorm_bwd_workspace_bytes(rows, d))
+        ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=h.device)
+        _lib.call("cdlb200_rmsnorm_bwd_add", _lib.ptr(dy2), _lib.ptr(h), _lib.ptr(w), _lib.ptr(rstd), _lib.ptr(dh2),
+                  rows, d, _lib.ptr(dx), _lib.ptr(dw), _lib.ptr(amax), _lib.ptr(ws), ws.numel(),
+                  _lib.stream(h.device))
+        attach_grad_amax(dx, amax)
+        g = dx.view(ctx.shape)
+        return g, g, dw, None
+
+
 class RopeFn(torch.autograd.Function):
     """``x * cos + rotate_half(x) * sin`` on ``x[B, H, S, D]`` (a transposed
     view of the ``[B, S, H, D]`` projection output), ``cos/sin[Bc, S, D]``
@@ -173,9 +217,48 @@ def _apply_rotary_pos_emb(q, k, cos, sin, unsqueeze_dim=1):
     return _EAGER_ROPE(q, k, cos, sin, unsqueeze_dim)
 
 
-def patch_llama(model: torch.nn.Module) -> int:
+def _llama_model_forward(self, input_ids=None, attention_mask=None, position_ids=None, past_key_values=None,
+                         inputs_embeds=None, use_cache=None, **kwargs):
+    """``LlamaModel.forward`` with each residual add fused into the RMSNorm
+    that follows it: the two adds of a decoder layer become
+    ``h = x + attn(norm1(x)); y = norm2(h)`` and ``x' = h + mlp(y);
+    y' = norm1'(x')`` (the next layer's input norm, or the final norm) --
+    the same operations in the same order as transformers' loop
+    (``LlamaDecoderLayer.forward``), one pass each.  Inputs the fused path does
+    not cover (a mask, a cache, embeddings not bf16 on a GPU) take the
+    original forward."""
+    from transformers.modeling_outputs import BaseModelOutputWithPast
+
+    layers = self.layers[: self.config.num_hidden_layers]
+    fused = (attention_mask is None and past_key_values is None and not use_cache and len(layers) > 0
+             and self.config.hidden_size % 8 == 0 and self.config.hidden_size <= 2048)
+    if fused:
+        embeds = self.embed_tokens(input_ids) if inputs_embeds is None else inputs_embeds
+        fused = _cuda_bf16(embeds, self.norm.weight)
+    if not fused:
+        return self._cdlb200_eager_forward(input_ids=input_ids, attention_mask=attention_mask,
+                                           position_ids=position_ids, past_key_values=past_key_values,
+                                           inputs_embeds=inputs_embeds, use_cache=use_cache, **kwargs)
+    if position_ids is None:
+        position_ids = torch.arange(embeds.shape[1], device=embeds.device).unsqueeze(0)
+    pos = self.rotary_emb(embeds, position_ids=position_ids)
+    x, y = embeds, layers[0].input_layernorm(embeds)
+    for i, layer in enumerate(layers):
+        a, _ = layer.self_attn(hidden_states=y, attention_mask=None, position_ids=position_ids, past_key_values=None,
+                               use_cache=False, position_embeddings=pos, **kwargs)
+        norm2 = layer.post_attention_layernorm
+        h, y = ResidualRMSNormFn.apply(x, a, norm2.weight, norm2.variance_epsilon)
+        m = layer.mlp(y)
+        nxt = layers[i + 1].input_layernorm if i + 1 < len(layers) else self.norm
+        x, y = ResidualRMSNormFn.apply(h, m, nxt.weight, nxt.variance_epsilon)
+    return BaseModelOutputWithPast(last_hidden_state=y, past_key_values=None)
+
+
+def patch_llama(model: torch.nn.Module, fuse_residual: bool = True) -> int:
     """Route the RMSNorm, rotary and SwiGLU parts of a transformers Llama model
-    through the fused kernels; returns the number of modules patched."""
+    through the fused kernels, and (``fuse_residual``) its decoder loop through
+    the residual-add + RMSNorm kernels; returns the number of modules
+    patched."""
     global _EAGER_ROPE
     from transformers.models.llama import modeling_llama as ml
 
@@ -191,5 +274,10 @@ def patch_llama(model: torch.nn.Module) -> int:
         elif isinstance(m, ml.LlamaMLP) and not getattr(m, "_cdlb200_fused", False):
             m.forward = types.MethodType(_mlp_forward, m)
             m._cdlb200_fused = True
+            count += 1
+        elif (fuse_residual and isinstance(m, ml.LlamaModel) and not hasattr(m, "_cdlb200_eager_forward")
+              and all(type(layer) is ml.LlamaDecoderLayer for layer in m.layers)):
+            m._cdlb200_eager_forward = m.forward
+            m.forward = types.MethodType(_llama_model_forward, m)
             count += 1
     return count

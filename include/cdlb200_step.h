@@ -28,6 +28,13 @@ extern "C" {
 int cdlb200_rmsnorm_fwd(const void* x, const void* w, int64_t rows, int64_t d, float eps, void* y, float* rstd,
                         uint32_t* amax, void* stream);
 
+/* The decoder's residual add fused with the RMSNorm that follows it
+ * (transformers' LlamaDecoderLayer: hidden = residual + branch, then the next
+ * norm of hidden): h = bf16(res + x) is written to h and normalized into y as
+ * above.  Same outputs as a bf16 add followed by cdlb200_rmsnorm_fwd(h). */
+int cdlb200_add_rmsnorm_fwd(const void* res, const void* x, const void* w, int64_t rows, int64_t d, float eps,
+                            void* h, void* y, float* rstd, uint32_t* amax, void* stream);
+
 /* Device scratch (bytes) cdlb200_rmsnorm_bwd needs for rows x d. */
 int64_t cdlb200_rmsnorm_bwd_workspace_bytes(int64_t rows, int64_t d);
 
@@ -35,6 +42,16 @@ int64_t cdlb200_rmsnorm_bwd_workspace_bytes(int64_t rows, int64_t d);
  * of the forward pass. */
 int cdlb200_rmsnorm_bwd(const void* dy, const void* x, const void* w, const float* rstd, int64_t rows, int64_t d,
                         void* dx, void* dw, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* cdlb200_rmsnorm_bwd for cdlb200_add_rmsnorm_fwd: dx = bf16(norm's dx +
+ * dres), the gradient of both inputs of the residual add (dres = the
+ * gradient of h from its other consumer; NULL: none), with amax (optional,
+ * CDLB200_AMAX_WORDS words, zero on entry) receiving the bf16 magnitude
+ * maximum of dx -- the o / down projections' gradient the quantized backward
+ * encodes.  x is the forward's h. */
+int cdlb200_rmsnorm_bwd_add(const void* dy, const void* x, const void* w, const float* rstd, const void* dres,
+                            int64_t rows, int64_t d, void* dx, void* dw, uint32_t* amax, void* workspace,
+                            int64_t workspace_bytes, void* stream);
 
 /* Rotary embedding of x[tokens, heads, head_dim] with cos/sin[cos_tokens,
  * head_dim] (token t uses row t % cos_tokens; head_dim % 16 == 0):

@@ -238,3 +238,63 @@ def test_swiglu_backward_gradient_amax():
     assert int(words.max().item()) == int((gq.contiguous().view(torch.int16).int() & 0x7FFF).max())
     seen["g"].add_(1)  # written after the kernel: its words no longer hold
     assert grad_amax(seen["g"].reshape(-1, 1024)) is None
+
+
+@pytest.mark.parametrize("rows,d", [(1000, 576), (300, 2048), (8, 64)])
+def test_residual_rmsnorm_matches_add_then_rmsnorm(rows, d):
+    """The fused residual add + RMSNorm equals a bf16 add followed by the
+    RMSNorm kernel, forward bit for bit; its backward equals the norm's input
+    gradient plus the residual gradient as autograd sums them, and carries
+    that gradient's amax."""
+    from cdl_b200.model.components.fused import ResidualRMSNormFn, RMSNormFn, grad_amax
+
+    gen = torch.Generator("cuda").manual_seed(rows * 3 + d)
+    w = (1.0 + 0.1 * torch.randn(d, device="cuda", generator=gen)).bfloat16()
+    res = (2.0 * torch.randn(2, rows, d, device="cuda", generator=gen)).bfloat16()
+    x = torch.randn(2, rows, d, device="cuda", generator=gen).bfloat16()
+    dh = torch.randn(2, rows, d, device="cuda", generator=gen).bfloat16()
+    dy = torch.randn(2, rows, d, device="cuda", generator=gen).bfloat16()
+    outs = []
+    for fused in (False, True):
+        r, xx = res.clone().requires_grad_(), x.clone().requires_grad_()
+        ww = w.clone().requires_grad_()
+        if fused:
+            h, y = ResidualRMSNormFn.apply(r, xx, ww, 1e-5)
+        else:
+            h = r + xx
+            y = RMSNormFn.apply(h, ww, 1e-5)
+        seen = {}
+        xx.register_hook(lambda t: seen.__setitem__("x", t))
+        torch.autograd.backward([h, y], [dh, dy])
+        outs.append((h.detach(), y.detach(), r.grad, xx.grad, ww.grad, seen["x"]))
+    (h0, y0, dr0, dx0, dw0, _), (h1, y1, dr1, dx1, dw1, sx) = outs
+    assert torch.equal(h1, h0) and torch.equal(y1, y0)
+    assert torch.equal(dr1, dr0) and torch.equal(dx1, dx0)
+    assert _rel(dw1, dw0) < 1e-2  # per-CTA partial sums: another summation order
+    words = grad_amax(sx.reshape(-1, d))
+    assert words is not None
+    assert int(words.max().item()) == int((dx1.view(torch.int16).int() & 0x7FFF).max())
+
+
+def test_fused_decoder_loop_matches_layer_by_layer():
+    """The patched LlamaModel loop (residual adds fused into the norms) gives
+    the same loss as transformers' decoder loop over the same fused modules,
+    and gradients within float noise."""
+    from cdl_b200.train import qat
+
+    spec = qat.SPECS["tiny"]
+    ids = qat.random_tokens(2, 64, spec.vocab, seed=3, device=torch.device("cuda"))
+    res = []
+    for fuse in (False, True):
+        model = qat.build_model(spec, torch.device("cuda"), seed=1, fused=False)
+        from cdl_b200.model.components.fused import patch_llama
+
+        patch_llama(model, fuse_residual=fuse)
+        hidden = model.model(input_ids=ids, use_cache=False).last_hidden_state
+        loss = hidden.float().square().mean()
+        loss.backward()
+        res.append((hidden.detach(), {n: p.grad.detach().clone() for n, p in model.named_parameters()}))
+    (h0, g0), (h1, g1) = res
+    assert torch.equal(h1, h0)
+    for n in g0:
+        assert _rel(g1[n], g0[n]) < 2e-2, n
