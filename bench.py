@@ -762,19 +762,10 @@ FP4_PEAK_NOTE = ("denominator = 4 x the measured cuBLAS bf16 burst peak: the blo
 
 
 def time_kernel(fn, steps, dev):
-    """Average device time (ms) of ``fn(i)`` over ``steps`` launches on the current stream."""
-    import torch
-
-    for i in range(3):
-        fn(i)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(steps):
-        fn(i)
-    e1.record()
-    torch.cuda.synchronize()
-    return e0.elapsed_time(e1) / steps
+    """Average device time (ms) of ``fn(i)`` over ``steps`` launches replayed
+    from one CUDA graph (so that a short kernel is not timed at the host's
+    launch rate)."""
+    return graph_ms(fn, steps, 3, dev) / steps
 
 
 def reference_qat_gpu(workload, dev, steps, warmup):
