@@ -393,12 +393,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 // TMEM; empty[s] and acc_full are signalled in both CTAs by a multicast
 // tcgen05.commit of the leader.  No TMA load uses multicast.
 // ---------------------------------------------------------------------------
-constexpr int k2Stages = 4;
+constexpr int k2Stages = 5;
 constexpr int k2TileBytes = 128 * kBKBytes;                     // 16 KiB
 constexpr int k2SfaBytes = 4 * kSfAtomBytes;                    // 2 KiB
 constexpr int k2SfbBytes = 8 * kSfAtomBytes;                    // 4 KiB: two 128-column blocks
 constexpr int k2StageBytes = 2 * k2TileBytes + k2SfaBytes + k2SfbBytes;  // 38 KiB
-constexpr int k2OutBytes = 128 * 256 * 2;  // bf16 staging of one CTA's 128 x 256 output tile
+constexpr int k2OutBytes = 128 * 128 * 2;  // bf16 staging of half of one CTA's 128 x 256 output tile
 // TMEM columns: accumulator [0, 256); per stage s the B scales at 256 + 32 s
 // (32 columns) and the A scales at 416 + 16 s (16 columns), so every
 // tcgen05.st / MMA scale address is aligned to its width.
@@ -561,6 +561,54 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int x, int 
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(x),
                  "r"(y), "r"(smem_addr(src))
                  : "memory");
+}
+
+// 64 fp32 accumulator columns of this warp's 32 TMEM lanes (one row per lane).
+// The load completes asynchronously: the registers are valid after
+// tmem_wait_ld.
+__device__ __forceinline__ void tmem_ld64(uint32_t (&v)[64], uint32_t taddr) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,"
+        "%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31]), "=r"(v[32]),
+          "=r"(v[33]), "=r"(v[34]), "=r"(v[35]), "=r"(v[36]), "=r"(v[37]), "=r"(v[38]), "=r"(v[39]), "=r"(v[40]),
+          "=r"(v[41]), "=r"(v[42]), "=r"(v[43]), "=r"(v[44]), "=r"(v[45]), "=r"(v[46]), "=r"(v[47]), "=r"(v[48]),
+          "=r"(v[49]), "=r"(v[50]), "=r"(v[51]), "=r"(v[52]), "=r"(v[53]), "=r"(v[54]), "=r"(v[55]), "=r"(v[56]),
+          "=r"(v[57]), "=r"(v[58]), "=r"(v[59]), "=r"(v[60]), "=r"(v[61]), "=r"(v[62]), "=r"(v[63])
+        : "r"(taddr));
+}
+
+// Waits for this thread's outstanding tcgen05.ld and ties the buffer's
+// registers to the wait, so that no use of them is scheduled before it.
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&v)[64]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 64; ++j) asm volatile("" : "+r"(v[j]));
+}
+
+// 64 accumulator columns (64-column block `blk` of the 256-column tile) of
+// row r: x alpha (packed fp32 multiplies, each lane an IEEE round-to-nearest
+// product), to bf16, into the 128-byte-swizzled staging block `blk`.
+__device__ __forceinline__ void stage_out64(const uint32_t (&v)[64], float alpha, uint8_t* out_s, int r, int blk) {
+    uint64_t aa;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(aa) : "f"(alpha));
+    uint8_t* row = out_s + blk * (128 * 128) + r * 128;
+#pragma unroll
+    for (int chunk = 0; chunk < 8; ++chunk) {  // 16-byte chunk: 8 columns
+        uint32_t pk[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint64_t pv, pr;
+            asm("mov.b64 %0, {%1, %2};" : "=l"(pv) : "r"(v[8 * chunk + 2 * j]), "r"(v[8 * chunk + 2 * j + 1]));
+            asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(pr) : "l"(pv), "l"(aa));
+            asm("{\n.reg .f32 lo, hi;\nmov.b64 {lo, hi}, %1;\ncvt.rn.bf16x2.f32 %0, hi, lo;\n}" : "=r"(pk[j]) : "l"(pr));
+        }
+        *reinterpret_cast<uint4*>(row + ((chunk ^ (r & 7)) * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
 }
 
 constexpr int k2Threads = 320;  // warp 0 TMA, 1 MMA, 2-5 scale factors, 6-9 epilogue
@@ -743,9 +791,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
         const uint32_t lane_off = (uint32_t)(32 * q) << 16;
         const uint32_t acc_empty0 = map_rank(&acc_empty, 0);
         const float alpha = epilogue_alpha(args);
-        // staging: four 64-column blocks of 128 rows x 128 bytes, 16-byte chunk c
-        // of row r at chunk c ^ (r & 7) (the TMA 128-byte swizzle)
+        // staging: two 64-column blocks of 128 rows x 128 bytes (half of the
+        // tile's 256 columns at a time), 16-byte chunk c of row r at chunk
+        // c ^ (r & 7) (the TMA 128-byte swizzle)
         uint8_t* out_s = smem + (size_t)k2Stages * k2StageBytes;
+        auto store_half = [&](int i, int half) {  // thread 192: the staged 128 columns to global memory
+            int m0, n0;
+            tile_origin(i, m0, n0);
+            const int y = m0 + 128 * (int)rank;
+            if (y < args.m) {
+                for (int b = 0; b < 2; ++b) {
+                    const int x = n0 + 128 * half + 64 * b;
+                    if (x < args.n) tma_store_2d(&map_out, x, y, out_s + b * (128 * 128));
+                }
+            }
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        };
         for (int i = 0; i < my_tiles; ++i) {
             const bool ok = mbar_wait(&acc_full, (uint32_t)i & 1u);
             if (!ok) atomicExch(&abort_s, 1);
@@ -753,48 +814,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
             if (threadIdx.x == 192) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
             if (group_any<2>(!ok || aborted())) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-#pragma unroll 1
-            for (int c = 0; c < 8; ++c) {  // 32 columns per step
-                uint32_t v[32];
-                asm volatile(
-                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-                      "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
-                      "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]),
-                      "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]),
-                      "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-                    : "r"(tmem + lane_off + (uint32_t)(32 * c)));
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                uint32_t pk[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const float lo = __fmul_rn(u2f(v[2 * j]), alpha), hi = __fmul_rn(u2f(v[2 * j + 1]), alpha);
-                    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(pk[j]) : "f"(hi), "f"(lo));
-                }
-                uint8_t* blk = out_s + (c >> 1) * (128 * 128) + r * 128;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {  // 16-byte chunks (c & 1) * 4 + j of the 128-byte row
-                    const int chunk = ((c & 1) * 4 + j) ^ (r & 7);
-                    *reinterpret_cast<uint4*>(blk + chunk * 16) =
-                        make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-                }
-            }
-            // accumulator drained: the next tile's MMAs may overwrite it
-            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            // 256 columns in four 64-column loads through two register buffers:
+            // the accumulator is released as soon as its last columns are in
+            // registers, so the next tile's MMAs overlap the second half's
+            // conversion and store
+            uint32_t va[64], vb[64];
+            tmem_ld64(va, tmem + lane_off + 0u);
+            tmem_ld64(vb, tmem + lane_off + 64u);
+            tmem_wait_ld(va);
+            tmem_wait_ld(vb);
+            stage_out64(va, alpha, out_s, r, 0);
+            stage_out64(vb, alpha, out_s, r, 1);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // staging visible to the TMA engine
             group_sync<2>();
-            if (threadIdx.x == 192) {
-                arrive_remote(acc_empty0);
-                int m0, n0;
-                tile_origin(i, m0, n0);
-                const int y = m0 + 128 * (int)rank;
-                if (y < args.m) {
-                    for (int b = 0; b < 4; ++b)
-                        if (n0 + 64 * b < args.n) tma_store_2d(&map_out, n0 + 64 * b, y, out_s + b * (128 * 128));
-                }
-                asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-            }
+            if (threadIdx.x == 192) store_half(i, 0);
+            tmem_ld64(va, tmem + lane_off + 128u);
+            tmem_ld64(vb, tmem + lane_off + 192u);
+            tmem_wait_ld(va);
+            tmem_wait_ld(vb);
+            // accumulator drained: the next tile's MMAs may overwrite it
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            // the first half's stores have finished reading the staging buffer
+            if (threadIdx.x == 192) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+            group_sync<2>();
+            if (threadIdx.x == 192) arrive_remote(acc_empty0);
+            stage_out64(va, alpha, out_s, r, 0);
+            stage_out64(vb, alpha, out_s, r, 1);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            group_sync<2>();
+            if (threadIdx.x == 192) store_half(i, 1);
         }
         if (threadIdx.x == 192) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // output written
     }
