@@ -464,9 +464,9 @@ def quant_workload(name, dev, rank):
         if a is not None:
             host_a.copy_(a, non_blocking=True)
 
-    if tr:
-        kernel, launches = "quant_transpose_kernel" + (" (+ amax_kernel)" if fmt == "nvfp4" else ""), (
-            2 if fmt == "nvfp4" else 1)
+    if tr:  # the C2 shapes take the tiled column kernels (rows % 64 == 0, k % 128 == 0)
+        kernel, launches = (("nvfp4_dual_multi_kernel, column pass (+ amax_kernel)", 2) if fmt == "nvfp4"
+                            else ("mx_col_kernel", 1))
     else:
         kernel, launches = ("nvfp4_fused_kernel" if fmt == "nvfp4" else "quant_flat_kernel"), 1
     w = {

@@ -29,6 +29,7 @@ AMAX_WORDS = 32  # CDLB200_AMAX_WORDS
 SCALE_LINEAR = 0
 SCALE_SWIZZLED = 1
 DTYPE_F32, DTYPE_F16 = 1, 2
+DUAL_ROW_LINEAR, DUAL_COL_LINEAR = 1, 2
 
 _lib = None
 _lock = threading.Lock()
@@ -101,7 +102,7 @@ class Nvfp4DualTensor(ctypes.Structure):
     """``cdlb200_nvfp4_dual_tensor`` (include/cdlb200_step.h)."""
 
     _fields_ = [("x", _P), ("rows", _I64), ("cols", _I64), ("amax", _P), ("gmax", _P),
-                ("amax_words", ctypes.c_int32), ("pad", ctypes.c_int32), ("alpha", _P), ("row_packed", _P),
+                ("amax_words", ctypes.c_int32), ("flags", ctypes.c_int32), ("alpha", _P), ("row_packed", _P),
                 ("row_scale", _P), ("col_packed", _P), ("col_scale", _P)]
 
 

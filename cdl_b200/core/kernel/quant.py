@@ -124,7 +124,7 @@ def nvfp4_amax(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 def nvfp4_dual_quant(x: torch.Tensor, *, amax: torch.Tensor | None = None, gmax: torch.Tensor | None = None,
-                     rows: bool = True, cols: bool = True):
+                     rows: bool = True, cols: bool = True, swizzled: bool = True):
     """NVFP4 encodings of ``x`` (blocks of 16 along dim 1) and of ``x.T``
     (blocks of 16 along dim 0) from one read of ``x``, both with the scales in
     the 128x4 GEMM layout: the same codes, scale bytes and alpha as
@@ -132,7 +132,8 @@ def nvfp4_dual_quant(x: torch.Tensor, *, amax: torch.Tensor | None = None, gmax:
     swizzled=True)``.  ``x``: contiguous bf16 ``[R, C]``, R and C multiples of
     64.  The global amax is given as ``amax`` (int32 words holding bf16
     magnitude bits, e.g. a producer kernel's epilogue words) or ``gmax`` (fp32
-    ``[1]``), else computed here first.  Returns ``(row, col)``, each
+    ``[1]``), else computed here first.  ``swizzled=False`` writes linear
+    scales (``[R, C/16]`` and ``[C, R/16]``).  Returns ``(row, col)``, each
     ``(packed, scale, alpha)`` or None when not requested."""
     if x.ndim != 2:
         raise ValueError(f"expected a 2D tensor [rows, k], got shape {tuple(x.shape)}")
@@ -155,11 +156,13 @@ def nvfp4_dual_quant(x: torch.Tensor, *, amax: torch.Tensor | None = None, gmax:
         t.gmax = gmax.data_ptr()
     if rows:
         row = (torch.empty(r, c // 2, dtype=torch.uint8, device=dev),
-               torch.empty(scale_shape(r, c // 16, True), dtype=torch.uint8, device=dev), alpha)
+               torch.empty(scale_shape(r, c // 16, swizzled), dtype=torch.uint8, device=dev), alpha)
         t.row_packed, t.row_scale = row[0].data_ptr(), row[1].data_ptr()
     if cols:
         col = (torch.empty(c, r // 2, dtype=torch.uint8, device=dev),
-               torch.empty(scale_shape(c, r // 16, True), dtype=torch.uint8, device=dev), alpha)
+               torch.empty(scale_shape(c, r // 16, swizzled), dtype=torch.uint8, device=dev), alpha)
         t.col_packed, t.col_scale = col[0].data_ptr(), col[1].data_ptr()
+    if not swizzled:
+        t.flags = _lib.DUAL_ROW_LINEAR | _lib.DUAL_COL_LINEAR
     _lib.call("cdlb200_nvfp4_dual_multi", ctypes.addressof(t), 1, _lib.stream(dev))
     return row, col

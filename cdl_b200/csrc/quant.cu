@@ -1035,8 +1035,10 @@ __global__ void __launch_bounds__(kDualThreads, 4) nvfp4_dual_multi_kernel(const
                 uint8_t* dst = static_cast<uint8_t*>(T.row_packed) + (row0 + r) * (T.cols / 2) + col0 / 2 + 32 * h;
                 *reinterpret_cast<uint4*>(dst) = make_uint4(o[0].x, o[0].y, o[1].x, o[1].y);
                 *reinterpret_cast<uint4*>(dst + 16) = make_uint4(o[2].x, o[2].y, o[3].x, o[3].y);
-                *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(T.row_scale) +
-                                             swizzle_offset(row0 + r, (col0 + kDualT * h) / 16, T.cols / 64)) = word;
+                const int64_t so = (T.flags & CDLB200_DUAL_ROW_LINEAR)
+                                       ? (row0 + r) * (T.cols / 16) + (col0 + kDualT * h) / 16
+                                       : swizzle_offset(row0 + r, (col0 + kDualT * h) / 16, T.cols / 64);
+                *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(T.row_scale) + so) = word;
             }
         } else if (T.col_packed != nullptr) {
             // ---- x^T, warps 4-7: columns 2p and 2p + 1 of each sub-tile, block b (tile rows 16b .. 16b + 15);
@@ -1076,10 +1078,13 @@ __global__ void __launch_bounds__(kDualThreads, 4) nvfp4_dual_multi_kernel(const
             }
             if (tid < 2 * kDualT) {  // its scale word (blocks row0/16 .. +3)
                 const int h = tid >> 6, c = tid & 63;
-                if (h < nsub)
-                    *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(T.col_scale) +
-                                                 swizzle_offset(col0 + kDualT * h + c, row0 / 16, T.rows / 64)) =
+                if (h < nsub) {
+                    const int64_t so = (T.flags & CDLB200_DUAL_COL_LINEAR)
+                                           ? (col0 + kDualT * h + c) * (T.rows / 16) + row0 / 16
+                                           : swizzle_offset(col0 + kDualT * h + c, row0 / 16, T.rows / 64);
+                    *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(T.col_scale) + so) =
                         *reinterpret_cast<const uint32_t*>(&cscale[256 * h + 4 * c]);
+                }
             }
         }
     }
@@ -1248,6 +1253,88 @@ __global__ void __launch_bounds__(256) quant_transpose_kernel(const uint16_t* __
     }
 }
 
+// ---------------------------------------------------------------------------
+// MX transposed (dim-0) quantize of a contiguous x[rows, k] with rows % 64 == 0
+// and k % 128 == 0: output row c holds column c's blocks of 32 values.  A
+// work item is a 64 x 128 tile staged by cp.async (two stages: the next
+// tile loads while this one is encoded); thread t takes columns 2p, 2p + 1
+// (p = t & 63) of block b = t >> 6: 32 shared-memory words, each holding both
+// columns' values of one row, split with byte permutes into the two columns'
+// packed pairs, then the block is encoded as the row-wise MX path encodes it
+// (hardware conversion of x * 2^-e, nudged for MXFP4) and stored straight
+// from registers: 16 (MXFP4) or 32 (MXFP8) bytes per column block.
+// ---------------------------------------------------------------------------
+constexpr int kMxcR = 64, kMxcC = 128, kMxcPitch = kMxcC + 8;  // staged row: 128 bf16 + 16 bytes of padding
+
+template <int FMT, bool SWZ>
+__device__ __forceinline__ void mx_col_block(const uint32_t (&w)[16], int64_t col, int64_t blk, uint8_t* packed,
+                                             int64_t pstride, uint8_t* scale, int64_t nb, int64_t c4) {
+    const uint32_t M = 0x7fff7fffu;
+    uint32_t m = w[0] & M;
+#pragma unroll
+    for (int i = 1; i < 16; ++i) asm("max.u16x2 %0, %1, %2;" : "=r"(m) : "r"(m), "r"(w[i] & M));
+    const uint32_t byte = e8m0_byte_from_bf16_mag<FmtTraits<FMT>::kEmax>(max(m & 0xffffu, m >> 16));
+    if constexpr (FMT == kMXFP4) {
+        const float c = __fmul_rn(e8m0_inv(byte), 0.99999904632568359375f);  // 2^-e (1 - 2^-20)
+        uint32_t q[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) q[j] = cvt8_scaled(make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]), c);
+        *reinterpret_cast<uint4*>(packed + col * pstride + blk * 16) = make_uint4(q[0], q[1], q[2], q[3]);
+    } else {
+        BlockCode bc;
+        bc.s = e8m0_inv(byte);  // RN(x / 2^e) == x * 2^-e exactly
+        uint2 q[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) q[j] = encode8_fp8(make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]), bc);
+        uint4* dst = reinterpret_cast<uint4*>(packed + col * pstride + blk * 32);
+        dst[0] = make_uint4(q[0].x, q[0].y, q[1].x, q[1].y);
+        dst[1] = make_uint4(q[2].x, q[2].y, q[3].x, q[3].y);
+    }
+    scale[SWZ ? swizzle_offset(col, blk, c4) : col * nb + blk] = (uint8_t)byte;
+}
+
+template <int FMT, bool SWZ>
+__global__ void __launch_bounds__(128) mx_col_kernel(const uint16_t* __restrict__ x, int64_t rows, int64_t k,
+                                                     uint8_t* __restrict__ packed, int64_t pstride,
+                                                     uint8_t* __restrict__ scale, int64_t nb, int64_t c4) {
+    __shared__ __align__(16) uint16_t xs[2][kMxcR * kMxcPitch];
+    const int tid = threadIdx.x;
+    const int64_t tiles_c = k / kMxcC, tiles = (rows / kMxcR) * tiles_c;
+    auto issue = [&](int64_t tile, int s) {
+        if (tile < tiles) {
+            const int64_t r0 = (tile / tiles_c) * kMxcR, c0 = (tile % tiles_c) * kMxcC;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int e = tid + 128 * j, r = e >> 4, c8 = (e & 15) * 8;
+                cp_async16(&xs[s][r * kMxcPitch + c8], x + (r0 + r) * k + c0 + c8);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    issue(blockIdx.x, 0);
+    int it = 0;
+    for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
+        issue(tile + gridDim.x, (it + 1) & 1);
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncthreads();
+        const int64_t r0 = (tile / tiles_c) * kMxcR, c0 = (tile % tiles_c) * kMxcC;
+        const int p = tid & 63, b = tid >> 6;
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(&xs[it & 1][32 * b * kMxcPitch + 2 * p]);
+        uint32_t e[16], o[16];  // columns 2p / 2p + 1, rows (2i, 2i + 1) of the block
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const uint32_t v0 = src[(2 * i) * (kMxcPitch / 2)], v1 = src[(2 * i + 1) * (kMxcPitch / 2)];
+            e[i] = __byte_perm(v0, v1, 0x5410);
+            o[i] = __byte_perm(v0, v1, 0x7632);
+        }
+        const int64_t blk = r0 / 32 + b;
+        mx_col_block<FMT, SWZ>(e, c0 + 2 * p, blk, packed, pstride, scale, nb, c4);
+        mx_col_block<FMT, SWZ>(o, c0 + 2 * p + 1, blk, packed, pstride, scale, nb, c4);
+        __syncthreads();  // the stage is free for the copies issued next
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 bool aligned(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) & (uintptr_t)(a - 1)) == 0; }
 
 int device_ok() {
@@ -1294,6 +1381,13 @@ int launch_encode(const void* x, int64_t rows, int64_t k, int64_t ldx, int trans
         quant_flat_kernel<FMT, SWZ, U><<<(unsigned)grid, 256, 0, st>>>(
             reinterpret_cast<const uint4*>(x), nvec, static_cast<uint8_t*>(packed),
             static_cast<uint8_t*>(scale), nbd, c4, gmax, alpha);
+    } else if (transpose && FMT != kNVFP4 && ldx == k && (rows % kMxcR) == 0 && (k % kMxcC) == 0 &&
+               aligned(x, 16) && aligned(packed, 16)) {
+        const int64_t tiles = (rows / kMxcR) * (k / kMxcC);
+        int64_t grid = tiles < (int64_t)sms * 6 ? tiles : (int64_t)sms * 6;
+        mx_col_kernel<FMT, SWZ><<<(unsigned)grid, 128, 0, st>>>(static_cast<const uint16_t*>(x), rows, k,
+                                                                static_cast<uint8_t*>(packed), pstride,
+                                                                static_cast<uint8_t*>(scale), nb, c4);
     } else if (transpose) {
         const int64_t tiles = ((k + kTrCols - 1) / kTrCols) * ((rows + TrTile<FMT>::kRows - 1) / TrTile<FMT>::kRows);
         int64_t grid = tiles < (int64_t)sms * 4 ? tiles : (int64_t)sms * 4;
@@ -1432,6 +1526,14 @@ int launch_nvfp4_encode(const void* x, int64_t rows, int64_t k, int64_t ldx, int
 
 }  // namespace cdlb200
 
+namespace cdlb200 {
+namespace {
+// Launches the dual NVFP4 encoder over validated tensors (defined with its
+// entry point, cdlb200_nvfp4_dual_multi).
+int launch_dual(const cdlb200_nvfp4_dual_tensor* tensors, int count, cudaStream_t st);
+}  // namespace
+}  // namespace cdlb200
+
 using namespace cdlb200;
 
 extern "C" size_t cdlb200_nvfp4_quant_workspace_bytes(int64_t, int64_t) {
@@ -1459,6 +1561,22 @@ extern "C" int cdlb200_nvfp4_quant(const void* x, int64_t rows, int64_t k, int64
         return launch_nvfp4_fused(x, rows, k, packed, scale, scale_layout, gmax, alpha, ws, st);
     rc = launch_amax(x, rows, k, ldx, partial, counter, g, alpha, st);
     if (rc != CDLB200_OK || rows == 0 || k == 0) return rc;
+    if (transpose && ldx == k && (rows % 64) == 0 && (k % 64) == 0 && aligned(x, 16) && aligned(packed, 16) &&
+        aligned(scale, 4) && (rows / 64) * ((k + 127) / 128) < (1ll << 31)) {
+        // the transposed encode of the dual encoder (its column pass alone):
+        // x is staged in shared memory tile by tile and each column block
+        // encoded from there
+        cdlb200_nvfp4_dual_tensor t{};
+        t.x = x;
+        t.rows = rows;
+        t.cols = k;
+        t.gmax = g;
+        t.alpha = alpha;
+        t.col_packed = packed;
+        t.col_scale = scale;
+        t.flags = scale_layout == CDLB200_SCALE_SWIZZLED ? 0 : CDLB200_DUAL_COL_LINEAR;
+        return launch_dual(&t, 1, st);
+    }
     return launch_nvfp4_encode(x, rows, k, ldx, transpose, packed, scale, scale_layout, g, alpha, st);
 }
 
@@ -1558,6 +1676,7 @@ extern "C" int cdlb200_nvfp4_dual_multi(const cdlb200_nvfp4_dual_tensor* tensors
         if (!t.x || !t.alpha || (!t.amax && !t.gmax) || (t.amax && (t.amax_words < 1 || t.amax_words > 64)))
             return CDLB200_ERR_INVALID_ARG;
         if ((t.row_packed && !t.row_scale) || (t.col_packed && !t.col_scale)) return CDLB200_ERR_INVALID_ARG;
+        if ((t.flags & ~(CDLB200_DUAL_ROW_LINEAR | CDLB200_DUAL_COL_LINEAR)) != 0) return CDLB200_ERR_INVALID_ARG;
         if ((t.rows / kDualT) * (t.cols / kDualT) >= (1ll << 31)) return CDLB200_ERR_INVALID_ARG;
         if (!aligned(t.x, 16) || (t.row_packed && !aligned(t.row_packed, 8)) ||
             (t.col_packed && !aligned(t.col_packed, 16)) || (t.row_scale && !aligned(t.row_scale, 4)) ||
@@ -1566,14 +1685,24 @@ extern "C" int cdlb200_nvfp4_dual_multi(const cdlb200_nvfp4_dual_tensor* tensors
     }
     int rc;
     if ((rc = device_ok()) != CDLB200_OK) return rc;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return launch_dual(tensors, count, static_cast<cudaStream_t>(stream));
+}
+
+namespace cdlb200 {
+namespace {
+int launch_dual(const cdlb200_nvfp4_dual_tensor* tensors, int count, cudaStream_t st) {
+    int rc;
     std::vector<DualGroup> groups;
     int64_t tiles = 0;
     for (int i = 0; i < count; ++i) {
         const cdlb200_nvfp4_dual_tensor& t = tensors[i];
         if (t.rows == 0 || t.cols == 0) continue;
-        if (t.row_packed && (rc = zero_scale_tail(t.row_scale, t.rows, t.cols / 16, st)) != CDLB200_OK) return rc;
-        if (t.col_packed && (rc = zero_scale_tail(t.col_scale, t.cols, t.rows / 16, st)) != CDLB200_OK) return rc;
+        if (t.row_packed && !(t.flags & CDLB200_DUAL_ROW_LINEAR) &&
+            (rc = zero_scale_tail(t.row_scale, t.rows, t.cols / 16, st)) != CDLB200_OK)
+            return rc;
+        if (t.col_packed && !(t.flags & CDLB200_DUAL_COL_LINEAR) &&
+            (rc = zero_scale_tail(t.col_scale, t.cols, t.rows / 16, st)) != CDLB200_OK)
+            return rc;
         const int64_t nt = (t.rows / kDualT) * ((t.cols + kDualW - 1) / kDualW);
         if (groups.empty() || groups.back().count == kDualGroup || tiles + nt >= (1ll << 31)) {
             groups.emplace_back();
@@ -1603,3 +1732,5 @@ extern "C" int cdlb200_nvfp4_dual_multi(const cdlb200_nvfp4_dual_tensor* tensors
     }
     return CDLB200_OK;
 }
+}  // namespace
+}  // namespace cdlb200

@@ -143,18 +143,21 @@ typedef struct {
 int cdlb200_nvfp4_encode_multi(const cdlb200_nvfp4_encode_tensor* tensors, int count, void* stream);
 
 /* One tensor of the dual NVFP4 encoder below. */
+#define CDLB200_DUAL_ROW_LINEAR 1
+#define CDLB200_DUAL_COL_LINEAR 2
 typedef struct {
     const void* x;          /* bf16 [rows, cols], contiguous, 16-byte aligned; rows % 64 == 0, cols % 64 == 0 */
     int64_t rows, cols;
     const uint32_t* amax;   /* bf16 magnitude bits of max|x| (the maximum of amax_words words), or NULL and ... */
     const float* gmax;      /* ... max|x| as fp32 (cdlb200_nvfp4_quant's gmax output, e.g. of its amax pass) */
     int32_t amax_words;     /* 1..64 with amax */
-    int32_t pad;
+    int32_t flags;          /* CDLB200_DUAL_ROW_LINEAR / CDLB200_DUAL_COL_LINEAR: that encoding's scales
+                               linear [rows, cols/16] / [cols, rows/16] instead of the 128x4 layout */
     float* alpha;           /* fp32 [1] output: gmax / 2688, the alpha of both encodings */
     void* row_packed;       /* optional (NULL: skipped): uint8 [rows, cols/2], x in blocks of 16 along cols, 8-byte aligned */
-    void* row_scale;        /* uint8, the 128x4 GEMM layout of [rows, cols/16] (rows padded to 128) */
+    void* row_scale;        /* uint8, the 128x4 GEMM layout of [rows, cols/16] (rows padded to 128), or linear */
     void* col_packed;       /* optional: uint8 [cols, rows/2], x^T in blocks of 16 along rows, 16-byte aligned */
-    void* col_scale;        /* uint8, the 128x4 GEMM layout of [cols, rows/16] (cols padded to 128) */
+    void* col_scale;        /* uint8, the 128x4 GEMM layout of [cols, rows/16] (cols padded to 128), or linear */
 } cdlb200_nvfp4_dual_tensor;
 
 /* NVFP4 encodings of x and of x^T from one read of x, for many tensors in one

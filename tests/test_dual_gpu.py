@@ -48,10 +48,18 @@ def test_dual_matches_single_direction_quantizers(shape):
     x = workloads.c2_mx(*shape, seed=3, device="cuda")
     row, col = nvfp4_dual_quant(x)
     rp, rs, ra = nvfp4_quant(x, swizzled=True)
-    cp, cs, ca = nvfp4_quant(x, transpose=True, swizzled=True)
+    # x^T's encoding by the row-wise quantizer of the transposed copy (the
+    # library's own transposed quantize runs the dual encoder for these shapes)
+    cp, cs, ca = nvfp4_quant(x.t().contiguous(), swizzled=True)
     torch.cuda.synchronize()
     assert torch.equal(row[0], rp) and torch.equal(row[1], rs) and torch.equal(row[2], ra)
     assert torch.equal(col[0], cp) and torch.equal(col[1], cs) and torch.equal(col[2], ca)
+    # the same with linear scale layouts
+    lrow, lcol = nvfp4_dual_quant(x, swizzled=False)
+    lp, ls, _ = nvfp4_quant(x)
+    tp, ts, _ = nvfp4_quant(x.t().contiguous())
+    assert torch.equal(lrow[0], lp) and torch.equal(lrow[1], ls)
+    assert torch.equal(lcol[0], tp) and torch.equal(lcol[1], ts)
 
 
 def test_dual_with_amax_words_and_one_direction():

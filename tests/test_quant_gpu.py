@@ -108,8 +108,11 @@ def test_quant_random_bit_patterns_vs_oracle(fmt):
 
 
 @pytest.mark.parametrize("fmt", [oracle.NVFP4, oracle.MXFP4, oracle.MXFP8])
-@pytest.mark.parametrize("shape", [(64, 256), (300, 96), (33, 1000)])
+@pytest.mark.parametrize("shape", [(64, 256), (300, 96), (33, 1000), (256, 512), (1024, 192)])
 def test_transposed_quant_vs_oracle(fmt, shape):
+    """Shapes with both dimensions multiples of 64 take the dual encoder's
+    column pass for NVFP4 (bf16, contiguous), the others the transposing
+    kernel."""
     x = workloads.c2_mx(*shape, seed=5 + fmt)
     xt_bits = _bits(x.t().contiguous())
     packed, scale, alpha = _q()[fmt](x.cuda(), transpose=True)
