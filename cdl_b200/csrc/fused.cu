@@ -233,14 +233,21 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const uint4* __restric
             am = mag8(am, ov);
         }
     }
+    // the row slots fold their column sums in slot order (not with shared
+    // atomics), so the fp32 partials, and dw, are the same on every run;
+    // within a slot the warps own disjoint columns
+    for (int s = 0; s < rsp.R; ++s) {
+        if (slot == s) {
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-        const int c = 32 * wr + lane + 32 * rsp.W * j;
-        if (c >= nvec) continue;
+            for (int j = 0; j < VPL; ++j) {
+                const int c = 32 * wr + lane + 32 * rsp.W * j;
+                if (c >= nvec) continue;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) atomicAdd(&dw_s[8 * c + i], acc[j][i]);
+                for (int i = 0; i < 8; ++i) dw_s[8 * c + i] += acc[j][i];
+            }
+        }
+        __syncthreads();
     }
-    __syncthreads();
     for (int i = threadIdx.x; i < 8 * nvec; i += blockDim.x) part[(int64_t)blockIdx.x * 8 * nvec + i] = dw_s[i];
     if (amax) cta_amax(am, amax);
 }
