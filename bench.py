@@ -613,7 +613,7 @@ def encode_multi_workload(dev, rank, spec_name="1.7b", with_deq=True):
     n = sum(w.numel() for w in ws)
     bpe = 2 + 0.5 + 1 / 16 + (2 if with_deq else 0)
 
-    def step(i):
+    def step(i=0):
         _lib.call("cdlb200_nvfp4_encode_multi", ctypes.addressof(table), len(ws), _lib.stream(dev))
 
     return {

@@ -75,14 +75,29 @@ struct BlockCode {
     uint32_t byte;   // stored scale byte
 };
 
-// max |x| of 8 bf16 values as bf16 magnitude bits (NaN sorts above Inf).
+// Per 16-bit lane, max(|a|, |b|) of two bf16 pairs: one instruction that
+// propagates NaN (the canonical NaN, magnitude 0x7fff, above every finite
+// value and Inf); the result's sign bits are the XOR of the inputs' and are
+// masked off by the callers.
+__device__ __forceinline__ uint32_t absmax2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t lane_max(uint32_t m) {
+    m &= 0x7fff7fffu;
+    return max(m & 0xffffu, m >> 16);
+}
+
+// max |x| of 8 bf16 values as bf16 magnitude bits (any NaN -> 0x7fff, above Inf).
 __device__ __forceinline__ uint32_t amax8(const uint4& w) {
-    const uint32_t M = 0x7fff7fffu;
-    uint32_t a, b, c;
-    asm("max.u16x2 %0, %1, %2;" : "=r"(a) : "r"(w.x & M), "r"(w.y & M));
-    asm("max.u16x2 %0, %1, %2;" : "=r"(b) : "r"(w.z & M), "r"(w.w & M));
-    asm("max.u16x2 %0, %1, %2;" : "=r"(c) : "r"(a), "r"(b));
-    return max(c & 0xffffu, c >> 16);
+    return lane_max(absmax2(absmax2(w.x, w.y), absmax2(w.z, w.w)));
+}
+
+// max |x| of the 16 bf16 values of one NVFP4 block (two 8-value vectors).
+__device__ __forceinline__ uint32_t amax16(const uint4& a, const uint4& b) {
+    return lane_max(absmax2(absmax2(absmax2(a.x, a.y), absmax2(a.z, a.w)), absmax2(absmax2(b.x, b.y), absmax2(b.z, b.w))));
 }
 
 __device__ __forceinline__ float mag_to_f32(uint32_t mag) { return u2f(mag << 16); }
@@ -177,7 +192,7 @@ __device__ __forceinline__ Nvfp4Tensor nvfp4_tensor(const float* gmax_p, const f
 
 // e4m3 scale byte of a block with bf16 amax bits `mag` (cdl/core/ecdl.py:52-55).
 __device__ __forceinline__ uint32_t nvfp4_scale_byte(uint32_t mag, const Nvfp4Tensor& g) {
-    const float bamax = mag > 0x7f80u ? u2f(0x7fc00000u) : u2f(mag << 16);
+    const float bamax = u2f(mag << 16);  // a NaN magnitude (> 0x7f80) is a NaN float
     const float p = __fmul_rn(bamax, 448.0f);
     float q;
     if (g.markstein) {
@@ -190,29 +205,13 @@ __device__ __forceinline__ uint32_t nvfp4_scale_byte(uint32_t mag, const Nvfp4Te
     return ue4m3_scale_byte(q);
 }
 
-// 8 fp32 values -> 8 e2m1 nibbles, element i at bits 4i..4i+3 (RNE, saturating).
-__device__ __forceinline__ uint32_t cvt_e2m1x8(float f0, float f1, float f2, float f3, float f4,
-                                               float f5, float f6, float f7) {
-    uint32_t out;
-    asm("{\n"
-        ".reg .b8 b0, b1, b2, b3;\n"
-        "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n"
-        "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n"
-        "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n"
-        "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n"
-        "mov.b32 %0, {b0, b1, b2, b3};\n"
-        "}"
-        : "=r"(out)
-        : "f"(f0), "f"(f1), "f"(f2), "f"(f3), "f"(f4), "f"(f5), "f"(f6), "f"(f7));
-    return out;
-}
-
-// 8 bf16 (one uint4: pairs (x0, x1) .. (x6, x7)) times c -> 8 e2m1 nibbles,
-// element i at bits 4i..4i+3.  Each pair is one packed fp32 multiply
+// 8 values (fp32 bit patterns f0..f7, here bf16 values widened) times c -> 8
+// e2m1 nibbles, value i at bits 4i..4i+3.  Each pair is one packed fp32 multiply
 // (mul.rn.f32x2: each lane an IEEE round-to-nearest product, the same as two
 // __fmul_rn) and one hardware conversion (RNE, saturating); the four code
 // bytes are packed by one move.
-__device__ __forceinline__ uint32_t cvt8_scaled(const uint4& w, float c) {
+__device__ __forceinline__ uint32_t cvt8_bits_scaled(uint32_t f0, uint32_t f1, uint32_t f2, uint32_t f3, uint32_t f4,
+                                                     uint32_t f5, uint32_t f6, uint32_t f7, float c) {
     uint32_t out;
     asm("{\n"
         ".reg .b64 cc, p0, p1, p2, p3;\n"
@@ -238,9 +237,23 @@ __device__ __forceinline__ uint32_t cvt8_scaled(const uint4& w, float c) {
         "mov.b32 %0, {b0, b1, b2, b3};\n"
         "}"
         : "=r"(out)
-        : "r"(w.x << 16), "r"(w.x & 0xffff0000u), "r"(w.y << 16), "r"(w.y & 0xffff0000u), "r"(w.z << 16),
-          "r"(w.z & 0xffff0000u), "r"(w.w << 16), "r"(w.w & 0xffff0000u), "f"(c));
+        : "r"(f0), "r"(f1), "r"(f2), "r"(f3), "r"(f4), "r"(f5), "r"(f6), "r"(f7), "f"(c));
     return out;
+}
+
+// 8 bf16 (one uint4: pairs (x0, x1) .. (x6, x7)) times c, element i at bits 4i..
+__device__ __forceinline__ uint32_t cvt8_scaled(const uint4& w, float c) {
+    return cvt8_bits_scaled(w.x << 16, w.x & 0xffff0000u, w.y << 16, w.y & 0xffff0000u, w.z << 16, w.z & 0xffff0000u,
+                            w.w << 16, w.w & 0xffff0000u, c);
+}
+
+// The same for the low (HI = false) or high 16-bit halves of eight words:
+// value i is half HI of v[i] (a column of a row-major bf16 tile, two columns
+// per word), without regrouping the halves first.
+template <bool HI>
+__device__ __forceinline__ uint32_t cvt8_halves_scaled(const uint32_t* v, float c) {
+    auto f = [](uint32_t w) { return HI ? (w & 0xffff0000u) : (w << 16); };
+    return cvt8_bits_scaled(f(v[0]), f(v[1]), f(v[2]), f(v[3]), f(v[4]), f(v[5]), f(v[6]), f(v[7]), c);
 }
 
 // RN(1/s) to within 2^-22 relative: hardware approximation refined by one
@@ -346,7 +359,7 @@ __global__ void __launch_bounds__(512, 2) amax_kernel(const uint16_t* __restrict
         for (; v + 3 * nthr < nvec; v += 4 * nthr) {
             uint4 a = ldg_stream(xv + v), b = ldg_stream(xv + v + nthr);
             uint4 c = ldg_stream(xv + v + 2 * nthr), d = ldg_stream(xv + v + 3 * nthr);
-            m = max(m, max(max(amax8(a), amax8(b)), max(amax8(c), amax8(d))));
+            m = max(m, max(amax16(a, b), amax16(c, d)));
         }
         for (; v < nvec; v += nthr) m = max(m, amax8(ldg_stream(xv + v)));
         for (int64_t i = (nvec << 3) + tid; i < n; i += nthr) m = max(m, (uint32_t)(x[i] & 0x7fffu));
@@ -481,7 +494,7 @@ __global__ void __launch_bounds__(256) nvfp4_flat_kernel(const uint4* __restrict
             const int64_t b = base + u * nthr;
             if (b < nblk) {
                 uint2 out;
-                const uint32_t byte = nvfp4_block16(w0[u], w1[u], max(amax8(w0[u]), amax8(w1[u])), g, out);
+                const uint32_t byte = nvfp4_block16(w0[u], w1[u], amax16(w0[u], w1[u]), g, out);
                 packed[b] = out;
                 int64_t off = b;
                 if constexpr (SWZ) {  // the host guarantees < 2^31 blocks with SWZ
@@ -656,7 +669,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2) nvfp4_fused_kernel(
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             if (!ok[u]) continue;
-            const uint32_t bm = max(amax8(v[2 * u]), amax8(v[2 * u + 1]));
+            const uint32_t bm = amax16(v[2 * u], v[2 * u + 1]);
             if (q0 + u < kAmaxChunks) amax_s[(q0 + u) * kChunkBlocks + tid] = (uint16_t)bm;
             m = max(m, bm);
         }
@@ -727,7 +740,7 @@ __global__ void __launch_bounds__(kFusedThreads, 2) nvfp4_fused_kernel(
             }
             if (b < nblk) {
                 const uint32_t mag = q < kAmaxChunks ? (uint32_t)amax_s[q * kChunkBlocks + tid]
-                                                     : max(amax8(a0), amax8(a1));
+                                                     : amax16(a0, a1);
                 const uint32_t byte = nvfp4_scale_byte(mag, t);
                 const float c = all_search ? -1.0f : ctab[byte];
                 packed[b] = c > 0.0f ? make_uint2(cvt8_scaled(a0, c), cvt8_scaled(a1, c))
@@ -838,7 +851,7 @@ __global__ void __launch_bounds__(kEncThreads) nvfp4_encode_multi_kernel(const _
         for (int j = 0; j < kEncPerThread; ++j) {
             if (b[j] >= nblk) continue;
             uint2 out;
-            const uint32_t byte = nvfp4_block16(w[2 * j], w[2 * j + 1], max(amax8(w[2 * j]), amax8(w[2 * j + 1])),
+            const uint32_t byte = nvfp4_block16(w[2 * j], w[2 * j + 1], amax16(w[2 * j], w[2 * j + 1]),
                                                 tn, out);
             static_cast<uint2*>(T.packed)[b[j]] = out;
             const uint32_t r = nb.div((uint32_t)b[j]);
@@ -943,13 +956,36 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 __device__ __forceinline__ uint32_t table_block16(const uint4& a0, const uint4& a1, const Nvfp4Tensor& tn,
                                                   const ScaleEntry* table, const float* ctab, bool all_search,
                                                   uint2& out) {
-    const uint32_t byte = nvfp4_scale_byte(max(amax8(a0), amax8(a1)), tn) & 127u;
+    const uint32_t byte = nvfp4_scale_byte(amax16(a0, a1), tn) & 127u;
     const float c = all_search ? -1.0f : ctab[byte];
     if (c > 0.0f) {
         out.x = cvt8_scaled(a0, c);
         out.y = cvt8_scaled(a1, c);
     } else {
         out = encode_block(a0, a1, table[byte], all_search);
+    }
+    return byte;
+}
+
+// One column block of a staged tile: v[i] holds row i of columns 2p (low
+// half) and 2p + 1 (high half); HI picks the column, `mag` is its block amax.
+// Same encoding as table_block16; only the rare table paths regroup the
+// halves into pairs.
+template <bool HI>
+__device__ __forceinline__ uint32_t table_col16(const uint32_t (&v)[16], uint32_t mag, const Nvfp4Tensor& tn,
+                                                const ScaleEntry* table, const float* ctab, bool all_search,
+                                                uint2& out) {
+    const uint32_t byte = nvfp4_scale_byte(mag, tn) & 127u;
+    const float c = all_search ? -1.0f : ctab[byte];
+    if (c > 0.0f) {
+        out.x = cvt8_halves_scaled<HI>(v, c);
+        out.y = cvt8_halves_scaled<HI>(v + 8, c);
+    } else {
+        uint32_t e[8];  // rows (2i, 2i + 1) of the column
+#pragma unroll
+        for (int i = 0; i < 8; ++i) e[i] = __byte_perm(v[2 * i], v[2 * i + 1], HI ? 0x7632 : 0x5410);
+        out = encode_block(make_uint4(e[0], e[1], e[2], e[3]), make_uint4(e[4], e[5], e[6], e[7]), table[byte],
+                           all_search);
     }
     return byte;
 }
@@ -1049,17 +1085,16 @@ __global__ void __launch_bounds__(kDualThreads, 4) nvfp4_dual_multi_kernel(const
                 uint32_t v[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) v[i] = src[i * (kDualPitch / 2)];
-                uint32_t e[8], o[8];  // column 2p / 2p + 1, rows (2i, 2i + 1)
+                // both columns' block amax at once: the low / high halves of a pairwise tree
+                uint32_t m[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    e[i] = __byte_perm(v[2 * i], v[2 * i + 1], 0x5410);
-                    o[i] = __byte_perm(v[2 * i], v[2 * i + 1], 0x7632);
-                }
-                const uint4 e0 = make_uint4(e[0], e[1], e[2], e[3]), e1 = make_uint4(e[4], e[5], e[6], e[7]);
-                const uint4 o0 = make_uint4(o[0], o[1], o[2], o[3]), o1 = make_uint4(o[4], o[5], o[6], o[7]);
+                for (int i = 0; i < 8; ++i) m[i] = absmax2(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) m[i] = absmax2(m[2 * i], m[2 * i + 1]);
+                const uint32_t mm = absmax2(absmax2(m[0], m[1]), absmax2(m[2], m[3])) & 0x7fff7fffu;
                 uint2 ce, co;
-                const uint32_t se = table_block16(e0, e1, tn, table, ctab, all_search, ce);
-                const uint32_t so = table_block16(o0, o1, tn, table, ctab, all_search, co);
+                const uint32_t se = table_col16<false>(v, mm & 0xffffu, tn, table, ctab, all_search, ce);
+                const uint32_t so = table_col16<true>(v, mm >> 16, tn, table, ctab, all_search, co);
                 *reinterpret_cast<uint4*>(&ccodes[(4 * h + b) * kDualT + 2 * p]) = make_uint4(ce.x, ce.y, co.x, co.y);
                 cscale[256 * h + 4 * (2 * p) + b] = (uint8_t)se;
                 cscale[256 * h + 4 * (2 * p + 1) + b] = (uint8_t)so;
