@@ -551,6 +551,27 @@ __device__ __forceinline__ void group_sync() {
     asm volatile("bar.sync %0, 128;" ::"n"(ID) : "memory");
 }
 
+// OR of `v` over the 256 threads of the two epilogue groups (named barrier 6).
+__device__ __forceinline__ bool epilogue_any(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n.reg .pred p, q;\nsetp.ne.u32 p, %1, 0;\nbar.red.or.pred q, 6, 256, p;\nselp.u32 %0, 1, 0, q;\n}"
+        : "=r"(r)
+        : "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
+}
+
+// the four warps of epilogue group `hf` (named barriers 2 and 3)
+__device__ __forceinline__ void epilogue_group_sync(int hf) {
+    if (hf == 0) group_sync<2>();
+    else group_sync<3>();
+}
+
+__device__ __forceinline__ void mbar_arrive_local(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 __device__ __forceinline__ void arrive_remote(uint32_t bar_cluster) {
     asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
@@ -590,34 +611,44 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&v)[64]) {
     for (int j = 0; j < 64; ++j) asm volatile("" : "+r"(v[j]));
 }
 
-// 64 accumulator columns (64-column block `blk` of the 256-column tile) of
-// row r: x alpha (packed fp32 multiplies, each lane an IEEE round-to-nearest
-// product), to bf16, into the 128-byte-swizzled staging block `blk`.
-__device__ __forceinline__ void stage_out64(const uint32_t (&v)[64], float alpha, uint8_t* out_s, int r, int blk) {
+// 64 accumulator columns x alpha (packed fp32 multiplies, each lane an IEEE
+// round-to-nearest product) -> 32 bf16 pairs, columns (2j, 2j + 1) in pk[j].
+__device__ __forceinline__ void pack64(const uint32_t (&v)[64], float alpha, uint32_t (&pk)[32]) {
     uint64_t aa;
     asm("mov.b64 %0, {%1, %1};" : "=l"(aa) : "f"(alpha));
-    uint8_t* row = out_s + blk * (128 * 128) + r * 128;
 #pragma unroll
-    for (int chunk = 0; chunk < 8; ++chunk) {  // 16-byte chunk: 8 columns
-        uint32_t pk[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            uint64_t pv, pr;
-            asm("mov.b64 %0, {%1, %2};" : "=l"(pv) : "r"(v[8 * chunk + 2 * j]), "r"(v[8 * chunk + 2 * j + 1]));
-            asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(pr) : "l"(pv), "l"(aa));
-            asm("{\n.reg .f32 lo, hi;\nmov.b64 {lo, hi}, %1;\ncvt.rn.bf16x2.f32 %0, hi, lo;\n}" : "=r"(pk[j]) : "l"(pr));
-        }
-        *reinterpret_cast<uint4*>(row + ((chunk ^ (r & 7)) * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    for (int j = 0; j < 32; ++j) {
+        uint64_t pv, pr;
+        asm("mov.b64 %0, {%1, %2};" : "=l"(pv) : "r"(v[2 * j]), "r"(v[2 * j + 1]));
+        asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(pr) : "l"(pv), "l"(aa));
+        asm("{\n.reg .f32 lo, hi;\nmov.b64 {lo, hi}, %1;\ncvt.rn.bf16x2.f32 %0, hi, lo;\n}" : "=r"(pk[j]) : "l"(pr));
     }
 }
 
-constexpr int k2Threads = 320;  // warp 0 TMA, 1 MMA, 2-5 scale factors, 6-9 epilogue
+// 32 packed bf16 pairs of row r into the 128-byte-swizzled staging block `blk`.
+__device__ __forceinline__ void stage_packed64(const uint32_t (&pk)[32], uint8_t* out_s, int r, int blk) {
+    uint8_t* row = out_s + blk * (128 * 128) + r * 128;
+#pragma unroll
+    for (int chunk = 0; chunk < 8; ++chunk)
+        *reinterpret_cast<uint4*>(row + ((chunk ^ (r & 7)) * 16)) =
+            make_uint4(pk[4 * chunk], pk[4 * chunk + 1], pk[4 * chunk + 2], pk[4 * chunk + 3]);
+}
+
+// warp 0 TMA, 1 MMA (2, 3 idle), 4-7 scale factors, 8-15 epilogue (two groups of
+// four warps, one per 128-column half of the tile)
+constexpr int k2Threads = 512;
 
 // Persistent: cluster c (of gridDim.x / 2) computes pair tiles c, c + C, c + 2C, ...
 // (row-major over 256 x 256 tiles).  The shared-memory stage ring and the
-// scale-factor TMEM buffers run on across tiles; the epilogue warps drain the
-// accumulator into registers, release it (acc_empty) and store while the
-// MMAs of the next tile already run.
+// scale-factor TMEM buffers run on across tiles.  Eight epilogue warps drain
+// the accumulator: each group of four loads its 128-column half into
+// registers, so the accumulator is released (acc_empty) as soon as both
+// halves are loaded, and the two groups then take turns with the one
+// staging buffer (stg_free) while the MMAs of the next tile already run.
+//
+// Registers: 512 threads x 128.  An epilogue warp holds its 128 columns as
+// 64 packed bf16 pairs: the first 64 columns are scaled and packed before
+// the second 64 are loaded.
 template <int KIND>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
     bs_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -630,7 +661,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     __shared__ __align__(8) uint64_t full_bar[k2Stages], empty_bar[k2Stages], sfdata_bar[k2Stages], sffull_bar[k2Stages],
-        acc_full, acc_empty, done_bar;
+        acc_full, acc_empty, done_bar, stg_free[2];
     __shared__ uint32_t tmem_base_s;
     __shared__ int abort_s;
 
@@ -648,8 +679,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
             mbar_init(&sffull_bar[s], 2);
         }
         mbar_init(&acc_full, 1);
-        mbar_init(&acc_empty, 2);
+        mbar_init(&acc_empty, 4);  // one arrival per epilogue group of each CTA
         mbar_init(&done_bar, 1);
+        mbar_init(&stg_free[0], 1);
+        mbar_init(&stg_free[1], 1);
         abort_s = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -678,80 +711,82 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
     auto tile_atoms = [&](int nmma) { return (nmma * kSfPerMma + 3) / 4; };
     auto aborted = [&]() { return *(volatile int*)&abort_s != 0; };
 
-    if (warp == 0) {
-        if (lane == 0) {  // ---- TMA producer (both CTAs)
-            const uint32_t full0 = map_rank(&full_bar[0], 0);
-            int g = 0;
-            for (int i = 0; i < my_tiles && !aborted(); ++i) {
-                int m0, n0;
-                tile_origin(i, m0, n0);
-                const int mblk = (m0 >> 7) + (int)rank, nblk = n0 >> 7;
-                const bool a_ok = mblk * 128 < args.m;
-                const bool b0_ok = nblk * 128 < args.n, b1_ok = (nblk + 1) * 128 < args.n;
-                for (int kt = 0; kt < nk; ++kt, ++g) {
-                    const int s = g % k2Stages;
-                    const uint32_t ph = (uint32_t)(g / k2Stages) & 1u;
-                    if (!mbar_wait(&empty_bar[s], ph ^ 1u)) atomicExch(&abort_s, 1);
-                    if (aborted()) break;
-                    uint8_t* st = smem + (size_t)s * k2StageBytes;
-                    if (rank == 0) mbar_expect_tx(&full_bar[s], 4u * k2TileBytes);
-                    tma_load_2d_pair(st, &map_a, kt * kBKBytes, m0 + 128 * (int)rank, full0 + 8u * s);
-                    tma_load_2d_pair(st + k2TileBytes, &map_b, kt * kBKBytes, n0 + 128 * (int)rank, full0 + 8u * s);
-                    const int natoms = tile_atoms(tile_mmas(kt));
-                    const uint32_t sfb = (uint32_t)(natoms * kSfAtomBytes);
-                    mbar_expect_tx(&sfdata_bar[s], (a_ok ? sfb : 0u) + (b0_ok ? sfb : 0u) + (b1_ok ? sfb : 0u));
-                    uint8_t* sf = st + 2 * k2TileBytes;
-                    const size_t at = (size_t)kt * kCells;
-                    if (a_ok)
-                        bulk_load(sf, args.sfa + ((size_t)mblk * args.c4a + at) * kSfAtomBytes, sfb, &sfdata_bar[s]);
-                    if (b0_ok)
-                        bulk_load(sf + k2SfaBytes, args.sfb + ((size_t)nblk * args.c4b + at) * kSfAtomBytes, sfb,
-                                  &sfdata_bar[s]);
-                    if (b1_ok)
-                        bulk_load(sf + k2SfaBytes + 4 * kSfAtomBytes,
-                                  args.sfb + ((size_t)(nblk + 1) * args.c4b + at) * kSfAtomBytes, sfb, &sfdata_bar[s]);
+    if (warp < 4) {
+        if (warp == 0) {
+            if (lane == 0) {  // ---- TMA producer (both CTAs)
+                const uint32_t full0 = map_rank(&full_bar[0], 0);
+                int g = 0;
+                for (int i = 0; i < my_tiles && !aborted(); ++i) {
+                    int m0, n0;
+                    tile_origin(i, m0, n0);
+                    const int mblk = (m0 >> 7) + (int)rank, nblk = n0 >> 7;
+                    const bool a_ok = mblk * 128 < args.m;
+                    const bool b0_ok = nblk * 128 < args.n, b1_ok = (nblk + 1) * 128 < args.n;
+                    for (int kt = 0; kt < nk; ++kt, ++g) {
+                        const int s = g % k2Stages;
+                        const uint32_t ph = (uint32_t)(g / k2Stages) & 1u;
+                        if (!mbar_wait(&empty_bar[s], ph ^ 1u)) atomicExch(&abort_s, 1);
+                        if (aborted()) break;
+                        uint8_t* st = smem + (size_t)s * k2StageBytes;
+                        if (rank == 0) mbar_expect_tx(&full_bar[s], 4u * k2TileBytes);
+                        tma_load_2d_pair(st, &map_a, kt * kBKBytes, m0 + 128 * (int)rank, full0 + 8u * s);
+                        tma_load_2d_pair(st + k2TileBytes, &map_b, kt * kBKBytes, n0 + 128 * (int)rank, full0 + 8u * s);
+                        const int natoms = tile_atoms(tile_mmas(kt));
+                        const uint32_t sfb = (uint32_t)(natoms * kSfAtomBytes);
+                        mbar_expect_tx(&sfdata_bar[s], (a_ok ? sfb : 0u) + (b0_ok ? sfb : 0u) + (b1_ok ? sfb : 0u));
+                        uint8_t* sf = st + 2 * k2TileBytes;
+                        const size_t at = (size_t)kt * kCells;
+                        if (a_ok)
+                            bulk_load(sf, args.sfa + ((size_t)mblk * args.c4a + at) * kSfAtomBytes, sfb, &sfdata_bar[s]);
+                        if (b0_ok)
+                            bulk_load(sf + k2SfaBytes, args.sfb + ((size_t)nblk * args.c4b + at) * kSfAtomBytes, sfb,
+                                      &sfdata_bar[s]);
+                        if (b1_ok)
+                            bulk_load(sf + k2SfaBytes + 4 * kSfAtomBytes,
+                                      args.sfb + ((size_t)(nblk + 1) * args.c4b + at) * kSfAtomBytes, sfb, &sfdata_bar[s]);
+                    }
                 }
             }
-        }
-    } else if (warp == 1) {
-        if (rank == 0 && lane == 0) {  // ---- MMA issuer (leader CTA only)
-            int g = 0;
-            for (int i = 0; i < my_tiles && !aborted(); ++i) {
-                // both CTAs' epilogues have drained the accumulator of tile i - 1
-                if (i > 0 && !mbar_wait(&acc_empty, (uint32_t)(i - 1) & 1u)) {
-                    atomicExch(&abort_s, 1);
-                    break;
-                }
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                for (int kt = 0; kt < nk; ++kt, ++g) {
-                    const int s = g % k2Stages;
-                    const uint32_t ph = (uint32_t)(g / k2Stages) & 1u;
-                    if (!mbar_wait(&full_bar[s], ph) || !mbar_wait(&sffull_bar[s], ph)) {
+        } else if (warp == 1) {
+            if (rank == 0 && lane == 0) {  // ---- MMA issuer (leader CTA only)
+                int g = 0;
+                for (int i = 0; i < my_tiles && !aborted(); ++i) {
+                    // both CTAs' epilogues have drained the accumulator of tile i - 1
+                    if (i > 0 && !mbar_wait(&acc_empty, (uint32_t)(i - 1) & 1u)) {
                         atomicExch(&abort_s, 1);
                         break;
                     }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const int nmma = tile_mmas(kt);
-                    const uint32_t st = smem_addr(smem + (size_t)s * k2StageBytes);
-                    const uint32_t tsfa0 = tmem + k2SfaCol0 + 16u * (uint32_t)s;
-                    const uint32_t tsfb0 = tmem + k2SfbCol0 + 32u * (uint32_t)s;
-                    for (int kk = 0; kk < nmma; ++kk) {
-                        const uint64_t da = desc_sw128(st + kk * 32);
-                        const uint64_t db = desc_sw128(st + k2TileBytes + kk * 32);
-                        const uint32_t sfi = (uint32_t)(kk * kSfPerMma);
-                        const uint32_t cell = sfi >> 2, byte = sfi & 3u;
-                        mma_issue_pair<KIND>(tmem, da, db, instr_desc_pair<KIND>(byte),
-                                             (tsfa0 + 4u * cell) | (byte << 30), (tsfb0 + 8u * cell) | (byte << 30),
-                                             (kt > 0 || kk > 0) ? 1u : 0u);
+                    for (int kt = 0; kt < nk; ++kt, ++g) {
+                        const int s = g % k2Stages;
+                        const uint32_t ph = (uint32_t)(g / k2Stages) & 1u;
+                        if (!mbar_wait(&full_bar[s], ph) || !mbar_wait(&sffull_bar[s], ph)) {
+                            atomicExch(&abort_s, 1);
+                            break;
+                        }
+                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                        const int nmma = tile_mmas(kt);
+                        const uint32_t st = smem_addr(smem + (size_t)s * k2StageBytes);
+                        const uint32_t tsfa0 = tmem + k2SfaCol0 + 16u * (uint32_t)s;
+                        const uint32_t tsfb0 = tmem + k2SfbCol0 + 32u * (uint32_t)s;
+                        for (int kk = 0; kk < nmma; ++kk) {
+                            const uint64_t da = desc_sw128(st + kk * 32);
+                            const uint64_t db = desc_sw128(st + k2TileBytes + kk * 32);
+                            const uint32_t sfi = (uint32_t)(kk * kSfPerMma);
+                            const uint32_t cell = sfi >> 2, byte = sfi & 3u;
+                            mma_issue_pair<KIND>(tmem, da, db, instr_desc_pair<KIND>(byte),
+                                                 (tsfa0 + 4u * cell) | (byte << 30), (tsfb0 + 8u * cell) | (byte << 30),
+                                                 (kt > 0 || kk > 0) ? 1u : 0u);
+                        }
+                        mma_commit_pair(&empty_bar[s]);
                     }
-                    mma_commit_pair(&empty_bar[s]);
+                    if (aborted()) break;
+                    mma_commit_pair(&acc_full);
                 }
-                if (aborted()) break;
-                mma_commit_pair(&acc_full);
+                mma_commit_pair(&done_bar);  // completes once every MMA issued above has
             }
-            mma_commit_pair(&done_bar);  // completes once every MMA issued above has
         }
-    } else if (warp < 6) {  // ---- warps 2..5: scale factors into TMEM
+    } else if (warp < 8) {  // ---- warps 4..7: scale factors into TMEM
         const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
         const uint32_t lane_off = (uint32_t)(32 * q) << 16;
         const uint32_t sffull0 = map_rank(&sffull_bar[0], 0);
@@ -783,70 +818,72 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             group_sync<1>();
-            if (threadIdx.x == 64) arrive_remote(sffull0 + 8u * s);
+            if (threadIdx.x == 128) arrive_remote(sffull0 + 8u * s);
         }
-    } else {  // ---- warps 6..9: epilogue, 128 rows x 256 columns of this CTA per tile
-        const int q = warp & 3;
-        const int r = 32 * q + lane;  // row of the tile = TMEM lane
+    } else {  // ---- warps 8..15: epilogue, 128 rows x 256 columns of this CTA per tile
+        const int q = warp & 3, hf = (warp >> 2) - 2;  // TMEM lane quarter, 128-column half of the tile
+        const int r = 32 * q + lane;                   // row of the tile = TMEM lane
         const uint32_t lane_off = (uint32_t)(32 * q) << 16;
         const uint32_t acc_empty0 = map_rank(&acc_empty, 0);
+        const bool leader = (threadIdx.x & 127) == 0;  // issues this group's stores
         const float alpha = epilogue_alpha(args);
-        // staging: two 64-column blocks of 128 rows x 128 bytes (half of the
-        // tile's 256 columns at a time), 16-byte chunk c of row r at chunk
-        // c ^ (r & 7) (the TMA 128-byte swizzle)
+        // staging: two 64-column blocks of 128 rows x 128 bytes (one group's
+        // 128 columns), 16-byte chunk c of row r at chunk c ^ (r & 7) (the TMA
+        // 128-byte swizzle); group 0 and group 1 use it in turn
         uint8_t* out_s = smem + (size_t)k2Stages * k2StageBytes;
-        auto store_half = [&](int i, int half) {  // thread 192: the staged 128 columns to global memory
-            int m0, n0;
-            tile_origin(i, m0, n0);
-            const int y = m0 + 128 * (int)rank;
-            if (y < args.m) {
-                for (int b = 0; b < 2; ++b) {
-                    const int x = n0 + 128 * half + 64 * b;
-                    if (x < args.n) tma_store_2d(&map_out, x, y, out_s + b * (128 * 128));
-                }
-            }
-            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-        };
-        for (int i = 0; i < my_tiles; ++i) {
+        int i = 0;
+        for (; i < my_tiles; ++i) {
             const bool ok = mbar_wait(&acc_full, (uint32_t)i & 1u);
             if (!ok) atomicExch(&abort_s, 1);
-            // the TMA stores of tile i - 1 have finished reading the staging buffer
-            if (threadIdx.x == 192) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-            if (group_any<2>(!ok || aborted())) break;
+            if (epilogue_any(!ok || aborted())) break;  // all eight warps leave together
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            // 256 columns in four 64-column loads through two register buffers:
-            // the accumulator is released as soon as its last columns are in
-            // registers, so the next tile's MMAs overlap the second half's
-            // conversion and store
-            uint32_t va[64], vb[64];
-            tmem_ld64(va, tmem + lane_off + 0u);
-            tmem_ld64(vb, tmem + lane_off + 64u);
-            tmem_wait_ld(va);
+            uint32_t pa[32], pb[32];  // the half's 128 columns x alpha, as bf16 pairs
+            {
+                uint32_t v[64];
+                tmem_ld64(v, tmem + lane_off + 128u * (uint32_t)hf);
+                tmem_wait_ld(v);
+                pack64(v, alpha, pa);
+            }
+            uint32_t vb[64];
+            tmem_ld64(vb, tmem + lane_off + 128u * (uint32_t)hf + 64u);
             tmem_wait_ld(vb);
-            stage_out64(va, alpha, out_s, r, 0);
-            stage_out64(vb, alpha, out_s, r, 1);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // staging visible to the TMA engine
-            group_sync<2>();
-            if (threadIdx.x == 192) store_half(i, 0);
-            tmem_ld64(va, tmem + lane_off + 128u);
-            tmem_ld64(vb, tmem + lane_off + 192u);
-            tmem_wait_ld(va);
-            tmem_wait_ld(vb);
-            // accumulator drained: the next tile's MMAs may overwrite it
+            // this group's half is in registers: once both groups of both CTAs
+            // have arrived the next tile's MMAs may overwrite the accumulator
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            // the first half's stores have finished reading the staging buffer
-            if (threadIdx.x == 192) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-            group_sync<2>();
-            if (threadIdx.x == 192) arrive_remote(acc_empty0);
-            stage_out64(va, alpha, out_s, r, 0);
-            stage_out64(vb, alpha, out_s, r, 1);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            group_sync<2>();
-            if (threadIdx.x == 192) store_half(i, 1);
+            epilogue_group_sync(hf);
+            if (leader) arrive_remote(acc_empty0);
+            // the staging buffer is free: group 1 waits for group 0's stores of
+            // this tile, group 0 for group 1's stores of the previous tile
+            bool free_ok = true;
+            if (hf == 1) free_ok = mbar_wait(&stg_free[1], (uint32_t)i & 1u);
+            else if (i > 0) free_ok = mbar_wait(&stg_free[0], (uint32_t)(i - 1) & 1u);
+            if (!free_ok) atomicExch(&abort_s, 1);
+            pack64(vb, alpha, pb);
+            if (free_ok) {
+                stage_packed64(pa, out_s, r, 0);
+                stage_packed64(pb, out_s, r, 1);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // staging visible to the TMA engine
+            }
+            epilogue_group_sync(hf);
+            if (leader) {
+                if (free_ok) {
+                    int m0, n0;
+                    tile_origin(i, m0, n0);
+                    const int y = m0 + 128 * (int)rank;
+                    if (y < args.m) {
+                        for (int b = 0; b < 2; ++b) {
+                            const int x = n0 + 128 * hf + 64 * b;
+                            if (x < args.n) tma_store_2d(&map_out, x, y, out_s + b * (128 * 128));
+                        }
+                    }
+                }
+                asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // staging read
+                mbar_arrive_local(&stg_free[hf ^ 1]);
+            }
         }
-        if (threadIdx.x == 192) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // output written
+        if (leader) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // output written
     }
-
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (threadIdx.x == 0 && abort_s && args.status) atomicExch(args.status, 1u);
