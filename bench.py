@@ -8,8 +8,9 @@ Workloads (synthetic data everywhere):
 * ``qat_1.7b`` (default) -- config C5: one SmolLM2-1.7B NVFP4 QAT training
   step (forward, backward, clip + AdamW) on 4x2048 uniform random tokens per
   rank, backend ``nvfp4_qbwd`` (NVFP4 forward, dgrad and wgrad GEMMs); one
-  CUDA graph per step at N=1, data parallel with an NCCL bf16 gradient
-  all-reduce for N > 1.  Metric: tokens/s over all ranks.  At N=1 the line
+  CUDA graph per step, for N > 1 data parallel with the NCCL bf16 gradient
+  all-reduces (issued from the backward hooks) captured in the same graph.
+  Metric: tokens/s over all ranks.  At N=1 the line
   also carries ``components``: the other BASELINE metrics (NVFP4 quantize
   GB/s on C1 and on a larger-than-L2 tensor, MXFP4 / MXFP8 on C2, the
   transposed requantizes, the optimizer's weight encode, NVFP4 dequantize,
@@ -696,9 +697,9 @@ def qat_workload(name, dev, rank, world, backend="nvfp4", use_graph=True):
 
     spec = qat.SPECS["135m" if name == "qat_135m" else "1.7b"]
     batch, seq = QAT_BATCH[name]
-    # one process per GPU: the whole step is one CUDA graph; data-parallel
-    # steps stay eager (their NCCL all-reduce runs from DDP's backward hooks)
-    graph = world == 1 and use_graph
+    # one process per GPU: the whole step is one CUDA graph, data parallel
+    # too (the NCCL all-reduces issued from the backward hooks are captured)
+    graph = use_graph
     step = qat.QatStep(spec, dev, backend=backend, seed=0, ddp=world > 1, graph=graph)
     qbwd = backend.endswith("_qbwd")
     pool = [qat.random_tokens(batch, seq, spec.vocab, seed=1000 * rank + i, device=dev) for i in range(4)]
@@ -728,6 +729,7 @@ def qat_workload(name, dev, rank, world, backend="nvfp4", use_graph=True):
         "launches_per_step": None, "count_launches": True,
         "graph_launches": (lambda: getattr(step, "graph_launches", 0)) if graph else None,
         "check_status": step.check_status,
+        "release": step.release_graph,
     }
 
 
@@ -1084,6 +1086,9 @@ def main() -> None:
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
+        # a captured step holds NCCL collectives: release it first
+        if "w" in locals() and w.get("release") is not None:
+            w["release"]()
         dist.destroy_process_group()
 
 

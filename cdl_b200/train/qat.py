@@ -21,10 +21,11 @@ freeze policy, the warmup / cosine LR schedule, gradient accumulation, fp32
 master weights, ``evaluate`` (perplexity) and ``run_training`` (its loop with
 checkpoints and evaluation).
 
-Data parallel: one process per GPU; the model is wrapped in
-``DistributedDataParallel`` (NCCL), which all-reduces the bf16 gradients in
-buckets while the backward pass is still running.  Each rank quantizes its
-own activations (per-rank amax, as a single-GPU run would).
+Data parallel: one process per GPU; ``train/dp.py``'s ``GradSync``
+all-reduces (NCCL) each bf16 gradient from a backward hook while the backward
+pass is still running, as torch's ``DistributedDataParallel`` would, and the
+whole step -- all-reduces included -- is one CUDA graph, as on one GPU.  Each rank quantizes its own activations (per-rank amax, as a
+single-GPU run would).
 """
 
 from __future__ import annotations
@@ -343,7 +344,7 @@ class QatStep:
     """One QAT training step: forward, loss, backward (+ DP all-reduce), clip, AdamW."""
 
     def __init__(self, spec: ModelSpec, device: torch.device, backend: str = "nvfp4", lr: float = 3e-4,
-                 grad_clip: float = 1.0, seed: int = 0, ddp: bool = False, bucket_mb: int = 64,
+                 grad_clip: float = 1.0, seed: int = 0, ddp: bool = False,
                  fused: bool | None = None, graph: bool = False, optimizer: str | None = None,
                  activation: str = "ste", weight: str = "ste", quant_lr: float = 3e-4, train_alpha: bool = True,
                  train_kappa: bool = False, use_lora: bool = False, lora_r: int = 8, lora_alpha: int = 16,
@@ -428,11 +429,13 @@ class QatStep:
         self._graph = None
         self.grad_clip = grad_clip
         self.net = LossModule(self.model)
+        # data parallel: gradients averaged over ranks from backward hooks
+        # (train/dp.py), capturable in the step's CUDA graph
+        self.sync = None
         if ddp:
-            from torch.nn.parallel import DistributedDataParallel as DDP
+            from cdl_b200.train.dp import GradSync
 
-            self.net = DDP(self.net, device_ids=[device.index] if device.type == "cuda" else None,
-                           bucket_cap_mb=bucket_mb, gradient_as_bucket_view=True, static_graph=True)
+            self.sync = GradSync(params)
 
     def check_status(self) -> None:
         """Raise ``CdlB200Error`` if a kernel of this step recorded a timed-out
@@ -458,21 +461,32 @@ class QatStep:
             for m in qls:
                 m.set_backend(self.backend)
 
+    def _backward(self, loss: torch.Tensor, scale: float, last: bool) -> None:
+        """``(loss * scale).backward()``; data parallel: the gradients are
+        summed over ranks, the loss pre-scaled by 1 / world, after the last
+        micro-batch only (the earlier ones accumulate locally)."""
+        if self.sync is None:
+            (loss * scale if scale != 1.0 else loss).backward()
+            return
+        self.sync.begin(reduce=last)
+        try:
+            (loss * (scale * self.sync.loss_scale)).backward()
+        finally:
+            self.sync.finish()
+
     def _eager_step(self, input_ids) -> tuple[torch.Tensor, torch.Tensor]:
         if isinstance(input_ids, torch.Tensor):
             loss = self.net(input_ids)
-            loss.backward()
+            self._backward(loss, 1.0, True)
         else:  # gradient accumulation over micro-batches, as cdl's loop (smollm2.py:816-851)
             micro = list(input_ids)
             n = len(micro)
             if n == 0:
                 raise ValueError("no micro-batches")
             loss = None
-            for ids in micro:
-                # with DDP every micro-batch all-reduces: the static-graph DDP
-                # wrapper used here has no no_sync(), and averaging is linear
+            for j, ids in enumerate(micro):
                 part = self.net(ids)
-                (part / n if n > 1 else part).backward()
+                self._backward(part, 1.0 / n if n > 1 else 1.0, j == n - 1)
                 part = part.detach() / n if n > 1 else part.detach()
                 loss = part if loss is None else loss + part
         if self.optimizer == "fused":
@@ -502,8 +516,9 @@ class QatStep:
     def step(self, input_ids) -> tuple[torch.Tensor, torch.Tensor]:
         """One training step on a batch of token ids, or on a list of
         micro-batches whose gradients are accumulated (each loss divided by
-        their count; with data parallelism each one all-reduces) before one
-        optimizer step; the returned loss is their mean.  In graph
+        their count; with data parallelism the gradients are averaged over
+        ranks after the last one) before one optimizer step; the returned
+        loss is their mean.  In graph
         mode (one batch per step) the first call runs warm-up steps
         on a side stream and captures the whole step (forward, backward,
         clipping, AdamW) in a CUDA graph; every call then copies the tokens
@@ -529,10 +544,23 @@ class QatStep:
         torch.cuda.current_stream(self.device).wait_stream(side)
         self._graph = torch.cuda.CUDAGraph()
         launches0 = _lib.launches
-        with torch.cuda.graph(self._graph):
+        # data parallel: the NCCL process group's watchdog thread may query
+        # the events of the warm-up all-reduces while this thread captures;
+        # a thread-local capture keeps its calls legal (the all-reduces
+        # issued from the backward hooks are captured on their streams)
+        mode = "thread_local" if self.sync is not None else "global"
+        with torch.cuda.graph(self._graph, capture_error_mode=mode):
             self._static_out = self._eager_step(self._static_ids)
         # kernels of this library in the captured step (each replay runs them all)
         self.graph_launches = _lib.launches - launches0
+
+    def release_graph(self) -> None:
+        """Drop the captured step.  A graph that holds NCCL collectives must
+        be released before the process group is destroyed."""
+        if self._graph is not None:
+            torch.cuda.synchronize(self.device)
+            self._graph = None
+            self._static_out = None
 
 
 def run_training(step: QatStep, train_batches, *, epochs: int = 1, grad_accum_steps: int = 1, max_steps: int = 0,

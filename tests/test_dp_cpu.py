@@ -1,4 +1,5 @@
-"""Data-parallel step logic on CPU ranks (gloo): DDP-averaged gradients give
+"""Data-parallel step logic on CPU ranks (gloo): gradients averaged by
+``GradSync`` (the loss pre-scaled by 1 / world, summed over ranks) give
 every rank the same parameters, equal to one process stepping on the whole
 batch (world sizes 2, 4 and 8, also with gradient accumulation over
 micro-batches); a late rank only delays the others; a NaN gradient on one

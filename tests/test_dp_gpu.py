@@ -1,10 +1,10 @@
 """The data-parallel QAT step with the fused CUDA path, two ranks sharing one
-GPU over gloo: DistributedDataParallel around the fused decoder loop (residual
-adds in the norms), the quantized backward and the fused optimizer leaves the
-same parameters on both ranks, close to one process stepping on the whole
-batch.  (NCCL needs one GPU per rank; gloo reduces the CUDA gradients through
-the host, which checks the same hooks and buckets.  No kernel waits on another
-rank.)"""
+GPU over gloo: the data-parallel gradient sync (``train/dp.py``) around the
+fused decoder loop (residual adds in the norms), the quantized backward and
+the fused optimizer leaves the same parameters on both ranks, close to one
+process stepping on the whole batch.  (NCCL needs one GPU per rank; gloo
+reduces the CUDA gradients through the host, which checks the same hooks.  No
+kernel waits on another rank.)"""
 
 import os
 import socket
@@ -59,7 +59,7 @@ def test_ddp_fused_step_on_one_gpu(tmp_path, backend):
     assert res[0]["norms"] == res[1]["norms"]
     # one process accumulating the gradients of the same two micro-batches:
     # each micro-batch is quantized with its own amax, as each rank's batch
-    # is, and DDP's bf16 bucket (pre-divided by the world size, a power of
+    # is, and the gradient sync (the loss pre-scaled by 1 / world, a power of
     # two) sums the same two halves the accumulation adds, so the two runs
     # agree bit for bit (measured on B200, both backends).  Only the order of
     # a library's atomic reductions (attention backward) could move a weight;
