@@ -728,9 +728,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
                         if (!mbar_wait(&empty_bar[s], ph ^ 1u)) atomicExch(&abort_s, 1);
                         if (aborted()) break;
                         uint8_t* st = smem + (size_t)s * k2StageBytes;
-                        if (rank == 0) mbar_expect_tx(&full_bar[s], 4u * k2TileBytes);
-                        tma_load_2d_pair(st, &map_a, kt * kBKBytes, m0 + 128 * (int)rank, full0 + 8u * s);
-                        tma_load_2d_pair(st + k2TileBytes, &map_b, kt * kBKBytes, n0 + 128 * (int)rank, full0 + 8u * s);
+                        // the scale atoms first: they land while the A / B
+                        // tiles are still in flight, so the scale warps' TMEM
+                        // stores overlap the operand copies
                         const int natoms = tile_atoms(tile_mmas(kt));
                         const uint32_t sfb = (uint32_t)(natoms * kSfAtomBytes);
                         mbar_expect_tx(&sfdata_bar[s], (a_ok ? sfb : 0u) + (b0_ok ? sfb : 0u) + (b1_ok ? sfb : 0u));
@@ -744,6 +744,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
                         if (b1_ok)
                             bulk_load(sf + k2SfaBytes + 4 * kSfAtomBytes,
                                       args.sfb + ((size_t)(nblk + 1) * args.c4b + at) * kSfAtomBytes, sfb, &sfdata_bar[s]);
+                        if (rank == 0) mbar_expect_tx(&full_bar[s], 4u * k2TileBytes);
+                        tma_load_2d_pair(st, &map_a, kt * kBKBytes, m0 + 128 * (int)rank, full0 + 8u * s);
+                        tma_load_2d_pair(st + k2TileBytes, &map_b, kt * kBKBytes, n0 + 128 * (int)rank, full0 + 8u * s);
                     }
                 }
             }
