@@ -94,6 +94,9 @@ def parse_args():
                          "configuration BASELINE names; nvfp4 = cdl's numerics: bf16 dgrad / wgrad)")
     ap.add_argument("--spinup-s", type=float, default=1.0, help="untimed clock ramp before warm-up")
     ap.add_argument("--no-graph", action="store_true", help="QAT workloads: eager steps even at N=1")
+    ap.add_argument("--comm-sms", type=int, default=16,
+                    help="QAT workloads, N > 1: SMs the backward pass's persistent kernels leave to NCCL "
+                         "(also NCCL_MAX_CTAS unless set)")
     ap.add_argument("--gemm-shape", default="8192,8192,8192", metavar="M,N,K",
                     help="fp4_gemm: the GEMM shape (C3 is 8192^3; its sweep: M in {2048, 16384} x "
                          "(N, K) in {(2048, 8192), (8192, 2048), (49152, 576)})")
@@ -690,7 +693,7 @@ def gemm_workload(dev, rank, shape=(8192, 8192, 8192)):
     }
 
 
-def qat_workload(name, dev, rank, world, backend="nvfp4", use_graph=True):
+def qat_workload(name, dev, rank, world, backend="nvfp4", use_graph=True, comm_sms=16):
     import torch
 
     from cdl_b200.train import qat
@@ -700,7 +703,7 @@ def qat_workload(name, dev, rank, world, backend="nvfp4", use_graph=True):
     # one process per GPU: the whole step is one CUDA graph, data parallel
     # too (the NCCL all-reduces issued from the backward hooks are captured)
     graph = use_graph
-    step = qat.QatStep(spec, dev, backend=backend, seed=0, ddp=world > 1, graph=graph)
+    step = qat.QatStep(spec, dev, backend=backend, seed=0, ddp=world > 1, graph=graph, comm_sms=comm_sms)
     qbwd = backend.endswith("_qbwd")
     pool = [qat.random_tokens(batch, seq, spec.vocab, seed=1000 * rank + i, device=dev) for i in range(4)]
     host_ids = pool[0].cpu().pin_memory()
@@ -718,7 +721,7 @@ def qat_workload(name, dev, rank, world, backend="nvfp4", use_graph=True):
                  f"({step.optimizer})",
         "config": {"workload": f"{name} {'C4' if name == 'qat_135m' else 'C5'} {spec.name} QAT step, "
                                f"{batch}x{seq} tokens per rank, AdamW lr 3e-4, backend {backend}",
-                   "backend": backend,
+                   "backend": backend, "comm_sms": step.comm_sms,
                    "model": spec.name, "global_batch": batch * world, "seq_len": seq,
                    "parallelism": f"dp{world}" if world > 1 else "single", "l2": "activations >> L2"},
         "h2d": host_ids.numel() * 8, "d2h": 4, "bound": "tensor",
@@ -919,6 +922,9 @@ def main() -> None:
     if world > 1:
         import datetime
 
+        if wl.startswith("qat") and args.comm_sms > 0:
+            # NCCL's kernels fit in the SMs the backward pass leaves free
+            os.environ.setdefault("NCCL_MAX_CTAS", str(args.comm_sms))
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
     if wl in QUANT:
@@ -936,7 +942,7 @@ def main() -> None:
     elif wl == "nvfp4_dual":
         w = dual_workload(dev, rank)
     else:
-        w = qat_workload(wl, dev, rank, world, args.backend, not args.no_graph)
+        w = qat_workload(wl, dev, rank, world, args.backend, not args.no_graph, args.comm_sms)
 
     def barrier():
         if world > 1:

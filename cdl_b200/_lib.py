@@ -46,6 +46,7 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_status_string": (ctypes.c_char_p, [_I]),
     "cdlb200_version": (_I, []),
     "cdlb200_set_wait_limit": (ctypes.c_uint32, [ctypes.c_uint32]),
+    "cdlb200_set_persistent_sm_limit": (_I, [_I]),
     "cdlb200_nvfp4_quant_workspace_bytes": (_SZ, [_I64, _I64]),
     "cdlb200_nvfp4_quant": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P, _P, _P, _SZ, _P]),
     "cdlb200_nvfp4_quant_noalloc": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _I, _P, _P, _P]),
@@ -151,6 +152,14 @@ def call(name: str, *args) -> None:
         if status in (ERR_INVALID_ARG, ERR_ALIGNMENT, ERR_WORKSPACE):
             raise ValueError(f"{name}: {msg} (status {status})")
         raise CdlB200Error(name, status, msg)
+
+
+def set_persistent_sm_limit(sms: int) -> None:
+    """Cap the SMs the persistent kernels fill (0: all); a host-side setting,
+    no kernel launch (``cdlb200_set_persistent_sm_limit``)."""
+    status = lib().cdlb200_set_persistent_sm_limit(int(sms))
+    if status != OK:
+        raise ValueError(f"cdlb200_set_persistent_sm_limit({sms}): {lib().cdlb200_status_string(status).decode()}")
 
 
 def ptr(t: torch.Tensor | None) -> int | None:

@@ -184,6 +184,7 @@ __device__ __forceinline__ float bf16hi(uint32_t w) { return u2f(w & 0xffff0000u
 
 int num_sms();  // SM count of the current device (cached per device)
 uint32_t wait_limit();  // poll limit of bounded grid-wide waits (cdlb200_set_wait_limit)
+int persistent_sms();   // SMs a persistent kernel may fill (cdlb200_set_persistent_sm_limit)
 
 }  // namespace cdlb200
 

@@ -988,7 +988,8 @@ int launch_gemm(const void* a, const void* b, const void* sfa, const void* sfb, 
         }
         const int64_t tiles_n = (n + 255) / 256, tiles_m = (m + 255) / 256, tiles = tiles_n * tiles_m;
         if (tiles > (int64_t)INT32_MAX) return CDLB200_ERR_INVALID_ARG;
-        const int64_t clusters = tiles < num_sms() / 2 ? tiles : num_sms() / 2;
+        const int64_t pairs = persistent_sms() / 2;  // SM pairs it may occupy
+        const int64_t clusters = tiles < pairs ? tiles : pairs;
         bs_gemm_pair_kernel<KIND><<<(unsigned)(2 * clusters), k2Threads, smem2, st>>>(ma, mb, mo, args, (int)tiles_n,
                                                                                            (int)tiles);
         CDLB200_CHECK_LAUNCH();

@@ -12,6 +12,10 @@ std::atomic<uint32_t> g_wait_limit{1u << 20};
 
 uint32_t wait_limit() { return g_wait_limit.load(std::memory_order_relaxed); }
 
+// SMs the persistent kernels (the pair GEMM, the dual encoder) may fill; 0 =
+// all (cdlb200_set_persistent_sm_limit).
+std::atomic<int> g_persistent_sm_limit{0};
+
 int num_sms() {
     static int cache[128] = {0};
     int dev = 0;
@@ -22,6 +26,11 @@ int num_sms() {
         cache[dev] = n;
     }
     return cache[dev];
+}
+
+int persistent_sms() {
+    const int n = num_sms(), lim = g_persistent_sm_limit.load(std::memory_order_relaxed);
+    return lim >= 2 && lim < n ? lim : n;
 }
 
 }  // namespace cdlb200
@@ -44,4 +53,10 @@ extern "C" int cdlb200_version(void) { return 101; }
 
 extern "C" uint32_t cdlb200_set_wait_limit(uint32_t polls) {
     return cdlb200::g_wait_limit.exchange(polls, std::memory_order_relaxed);
+}
+
+extern "C" int cdlb200_set_persistent_sm_limit(int sms) {
+    if (sms < 0) return CDLB200_ERR_INVALID_ARG;
+    cdlb200::g_persistent_sm_limit.store(sms, std::memory_order_relaxed);
+    return CDLB200_OK;
 }

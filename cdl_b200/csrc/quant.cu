@@ -1759,7 +1759,7 @@ int launch_dual(const cdlb200_nvfp4_dual_tensor* tensors, int count, cudaStream_
             return CDLB200_ERR_CUDA;
         attr_set = true;
     }
-    const int64_t cap = (int64_t)num_sms() * 4;  // four resident CTAs per SM
+    const int64_t cap = (int64_t)persistent_sms() * 4;  // four resident CTAs per SM
     for (const DualGroup& g : groups) {
         const int64_t n = g.item0[g.count];
         nvfp4_dual_multi_kernel<<<(unsigned)(n < cap ? n : cap), kDualThreads, kDualSmem, st>>>(g);

@@ -351,7 +351,7 @@ class QatStep:
                  freeze_base: bool = False, train_head: bool = True, untie: bool = False, warmup_steps: int = 0,
                  lr_decay: str = "constant", max_steps: int = 0, min_lr_ratio: float = 0.1,
                  fp32_master_weights: bool = False, init_device: torch.device | str | None = None,
-                 **quant_options):
+                 comm_sms: int | None = None, **quant_options):
         self.spec = spec
         self.device = device
         self.backend = backend
@@ -432,10 +432,17 @@ class QatStep:
         # data parallel: gradients averaged over ranks from backward hooks
         # (train/dp.py), capturable in the step's CUDA graph
         self.sync = None
+        # data parallel on CUDA: SMs the backward pass's persistent kernels
+        # (the GEMMs, the dual encoder) leave to NCCL's all-reduce kernels,
+        # which would otherwise queue behind kernels that hold every SM
+        self.comm_sms = 0
         if ddp:
             from cdl_b200.train.dp import GradSync
 
             self.sync = GradSync(params)
+            if on_cuda:
+                self.comm_sms = 16 if comm_sms is None else int(comm_sms)
+                self._sms = torch.cuda.get_device_properties(device).multi_processor_count
 
     def check_status(self) -> None:
         """Raise ``CdlB200Error`` if a kernel of this step recorded a timed-out
@@ -469,9 +476,14 @@ class QatStep:
             (loss * scale if scale != 1.0 else loss).backward()
             return
         self.sync.begin(reduce=last)
+        cap = self.comm_sms > 0 and last
+        if cap:
+            _lib.set_persistent_sm_limit(max(self._sms - self.comm_sms, 2))
         try:
             (loss * (scale * self.sync.loss_scale)).backward()
         finally:
+            if cap:
+                _lib.set_persistent_sm_limit(0)
             self.sync.finish()
 
     def _eager_step(self, input_ids) -> tuple[torch.Tensor, torch.Tensor]:

@@ -71,6 +71,20 @@ int cdlb200_version(void);
 uint32_t cdlb200_set_wait_limit(uint32_t polls);
 
 /*
+ * Caps the SMs that the persistent kernels fill from later launches on: the
+ * pair GEMM behind cdlb200_mm_* (one CTA pair per two SMs) and the dual
+ * encoder cdlb200_nvfp4_dual_multi (four CTAs per SM); 0 (the default), or
+ * any value of at least the device's SM count, means all SMs.  Results do not
+ * depend on it.  The data-parallel training step sets it for its backward
+ * pass, where the gradient all-reduces run beside the GEMMs: the SMs left
+ * free keep NCCL's kernels running instead of queued behind a kernel that
+ * holds every SM.  A launch captured in a CUDA graph keeps the limit that was
+ * set when it was captured.  Process-wide; no counterpart in the reference
+ * (whose step runs on one GPU).  Returns CDLB200_ERR_INVALID_ARG for sms < 0.
+ */
+int cdlb200_set_persistent_sm_limit(int sms);
+
+/*
  * NVFP4 quantize of a bf16 matrix.
  * Replaces cdl/core/kernel/quant.py:126-131 `nvfp4_quant` (its `_quant` host
  * code at quant.py:71-123 with group 16, e4m3 scales, and the torch global

@@ -38,6 +38,10 @@ def test_status_strings_and_version():
     for code in range(-7, 1):
         assert lib.cdlb200_status_string(code)
     assert lib.cdlb200_nvfp4_quant_workspace_bytes(4096, 4096) >= 256
+    # the persistent kernels' SM cap: host-side setting, no GPU involved
+    assert lib.cdlb200_set_persistent_sm_limit(-1) == _lib.ERR_INVALID_ARG
+    assert lib.cdlb200_set_persistent_sm_limit(132) == _lib.OK
+    assert lib.cdlb200_set_persistent_sm_limit(0) == _lib.OK
 
 
 def test_host_side_argument_errors_need_no_gpu():
