@@ -722,39 +722,36 @@ __global__ void __launch_bounds__(kFusedThreads, 2) nvfp4_fused_kernel(
     const bool all_search = s_mode > kMaxSearchEntries;
 
     // ---- phase 2: encode own chunks, last-streamed first (they come from
-    //      L2), the next block's loads in flight while one is encoded
-    {
-        int q = nmine - 1;
-        int64_t b = q >= 0 ? blk(q) : nblk;
-        uint4 a0 = make_uint4(0u, 0u, 0u, 0u), a1 = a0;
-        if (b < nblk) {
-            a0 = ldg_stream(x + 2 * b);
-            a1 = ldg_stream(x + 2 * b + 1);
+    //      L2), four blocks per thread loaded together so that their L2
+    //      round trips overlap
+    for (int q1 = nmine - 1; q1 >= 0; q1 -= 4) {
+        uint4 v[8];
+        int64_t bb[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            bb[u] = q1 - u >= 0 ? blk(q1 - u) : nblk;
+            if (bb[u] < nblk) {
+                v[2 * u] = ldg_stream(x + 2 * bb[u]);
+                v[2 * u + 1] = ldg_stream(x + 2 * bb[u] + 1);
+            }
         }
-        for (; q >= 0; --q) {
-            const int64_t bn = q >= 1 ? blk(q - 1) : nblk;
-            uint4 n0 = make_uint4(0u, 0u, 0u, 0u), n1 = n0;
-            if (bn < nblk) {
-                n0 = ldg_stream(x + 2 * bn);
-                n1 = ldg_stream(x + 2 * bn + 1);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int q = q1 - u;
+            const int64_t b = bb[u];
+            if (b >= nblk) continue;
+            const uint4 a0 = v[2 * u], a1 = v[2 * u + 1];
+            const uint32_t mag = q < kAmaxChunks ? (uint32_t)amax_s[q * kChunkBlocks + tid] : amax16(a0, a1);
+            const uint32_t byte = nvfp4_scale_byte(mag, t);
+            const float c = all_search ? -1.0f : ctab[byte];
+            packed[b] = c > 0.0f ? make_uint2(cvt8_scaled(a0, c), cvt8_scaled(a1, c))
+                                 : encode_block(a0, a1, table[byte], all_search);
+            int64_t off = b;
+            if constexpr (SWZ) {  // with SWZ the host guarantees nblk < 2^31
+                const uint32_t r = nb.div((uint32_t)b);
+                off = swizzle_offset(r, (int64_t)((uint32_t)b - r * nb.d), c4);
             }
-            if (b < nblk) {
-                const uint32_t mag = q < kAmaxChunks ? (uint32_t)amax_s[q * kChunkBlocks + tid]
-                                                     : amax16(a0, a1);
-                const uint32_t byte = nvfp4_scale_byte(mag, t);
-                const float c = all_search ? -1.0f : ctab[byte];
-                packed[b] = c > 0.0f ? make_uint2(cvt8_scaled(a0, c), cvt8_scaled(a1, c))
-                                     : encode_block(a0, a1, table[byte], all_search);
-                int64_t off = b;
-                if constexpr (SWZ) {  // with SWZ the host guarantees nblk < 2^31
-                    const uint32_t r = nb.div((uint32_t)b);
-                    off = swizzle_offset(r, (int64_t)((uint32_t)b - r * nb.d), c4);
-                }
-                scale[off] = (uint8_t)byte;
-            }
-            a0 = n0;
-            a1 = n1;
-            b = bn;
+            scale[off] = (uint8_t)byte;
         }
     }
 
@@ -1006,9 +1003,8 @@ __global__ void __launch_bounds__(kDualThreads, 4) nvfp4_dual_multi_kernel(const
     // copies of item `item` into stage `s`: four 16-byte pieces per thread,
     // whole 128-byte row segments per 8 lanes (a missing second sub-tile is
     // not loaded)
-    auto issue = [&](int32_t item, int s) {
+    auto issue = [&](int32_t item, const DualItem& d, int s) {
         if (item < total) {
-            const DualItem d = dual_locate(g, item);
             const cdlb200_nvfp4_dual_tensor& T = g.t[d.ti];
             const uint16_t* x = static_cast<const uint16_t*>(T.x) + d.row0 * T.cols + d.col0;
             const int ncols = T.cols - d.col0 < kDualW ? kDualT : kDualW;
@@ -1022,16 +1018,21 @@ __global__ void __launch_bounds__(kDualThreads, 4) nvfp4_dual_multi_kernel(const
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
 
-    issue(first, 0);
+    // each item is located once, when its copies are issued, and kept for
+    // its encode in the next iteration
+    DualItem dnext{};
+    if (first < total) dnext = dual_locate(g, first);
+    issue(first, dnext, 0);
     int k = 0, cur_ti = -1;
     Nvfp4Tensor tn;
     bool all_search = false;
     for (int32_t item = first; item < total; item += stride, ++k) {
-        issue(item + stride, (k + 1) % kDualStages);
+        const DualItem d = dnext;
+        if (item + stride < total) dnext = dual_locate(g, item + stride);
+        issue(item + stride, dnext, (k + 1) % kDualStages);
         asm volatile("cp.async.wait_group 1;" ::: "memory");  // this thread's copies of `item` landed
         __syncthreads();                                      // ... and every other thread's
         const uint16_t* xs = xs0 + (k % kDualStages) * (kDualT * kDualPitch);
-        const DualItem d = dual_locate(g, item);
         const cdlb200_nvfp4_dual_tensor& T = g.t[d.ti];
         const int64_t row0 = d.row0, col0 = d.col0;
         const int nsub = T.cols - col0 < kDualW ? 1 : 2;  // sub-tiles of this item
