@@ -61,6 +61,7 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_mm_fp4": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _P, _I64, _P, _P]),
     "cdlb200_mm_mxfp8": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _I64, _P, _P]),
     "cdlb200_mm_fp4_alpha2": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _P, _I64, _P, _P]),
+    "cdlb200_mm_fp4_alpha2_acc": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _P, _I64, _P, _P]),
     # include/cdlb200_step.h
     "cdlb200_rmsnorm_fwd": (_I, [_P, _P, _I64, _I64, ctypes.c_float, _P, _P, _P, _P]),
     "cdlb200_rmsnorm_bwd_workspace_bytes": (_I64, [_I64, _I64]),

@@ -77,6 +77,37 @@ def _dequant_activation(deq, codes, scales, alpha, kw):
     return out
 
 
+# The input gradient of the quantized linears that read one input (q / k / v,
+# gate / up: their activations share one dual encoding, so one codes tensor)
+# is formed in one buffer: the first dgrad GEMM of the backward pass writes
+# it and returns it to autograd; the others add their product to it in their
+# epilogue (bf16(product) + buffer, rounded as autograd's add of the two
+# gradients) and return None, so autograd adds nothing more.  Autograd runs
+# the node that consumes the sum only after all of them, and the buffer
+# reaches it by reference (QLinear's 2-D view of a contiguous input).
+FUSE_DGRAD_SUM = True
+_DGRAD_SUM_ATTR = "_cdlb200_dgrad_sum"
+dgrad_accumulates = 0  # dgrad GEMMs that added into another linear's (diagnostic count)
+
+
+class _DgradSum:
+    __slots__ = ("users", "done", "buf")
+
+    def __init__(self):
+        self.users = 0  # forward calls that need this input's gradient
+        self.done = 0   # dgrad GEMMs of the backward pass so far
+        self.buf = None
+
+
+def _join_dgrad_sum(codes: torch.Tensor) -> _DgradSum:
+    share = getattr(codes, _DGRAD_SUM_ATTR, None)
+    if share is None or share.done > 0:  # none yet, or one whose backward has begun
+        share = _DgradSum()
+        setattr(codes, _DGRAD_SUM_ATTR, share)
+    share.users += 1
+    return share
+
+
 class BlockScaledMatMul(torch.autograd.Function):
     @staticmethod
     def forward(ctx, fmt: str, x: QTensor, x_proxy, w: QTensor, w_proxy, quantized_backward: bool = False):
@@ -92,6 +123,7 @@ class BlockScaledMatMul(torch.autograd.Function):
             (x_row, x_col), (w_row, w_col) = x.encode_dual(), w.encode_dual()
             ctx.dual = True
             ctx.save_for_backward(*x_col, *w_col)
+            ctx.share = _join_dgrad_sum(x_row[0]) if FUSE_DGRAD_SUM and x_proxy.requires_grad else None
             return mm_nvfp4_alpha2(x_row[0], w_row[0].T, x_row[1], w_row[1].T, x_row[2], w_row[2])
         # the quantized backward needs every GEMM dimension to be a multiple of 32
         ctx.qbwd = bool(quantized_backward) and x_proxy is not None and w_proxy is not None and all(
@@ -152,7 +184,22 @@ class BlockScaledMatMul(torch.autograd.Function):
             need_dx, need_dw = ctx.needs_input_grad[2], ctx.needs_input_grad[4]
             g2 = grad_output.reshape(-1, grad_output.shape[-1])
             g_row, g_col = nvfp4_dual_quant(g2, amax=grad_amax(g2), rows=need_dx, cols=need_dw)
-            dx = mm_nvfp4_alpha2(g_row[0], wc_p.T, g_row[1], wc_s.T, g_row[2], wc_a) if need_dx else None
+            dx = None
+            if need_dx:
+                share = ctx.share
+                if share is not None and share.buf is not None:  # add to the first linear's dgrad
+                    global dgrad_accumulates
+                    mm_nvfp4_alpha2(g_row[0], wc_p.T, g_row[1], wc_s.T, g_row[2], wc_a, accumulate_into=share.buf)
+                    dgrad_accumulates += 1
+                    share.done += 1
+                    if share.done == share.users:
+                        share.buf = None
+                else:
+                    dx = mm_nvfp4_alpha2(g_row[0], wc_p.T, g_row[1], wc_s.T, g_row[2], wc_a)
+                    if share is not None:
+                        share.done += 1
+                        if share.users > 1:
+                            share.buf = dx
             dw = mm_nvfp4_alpha2(g_col[0], xc_p.T, g_col[1], xc_s.T, g_col[2], xc_a) if need_dw else None
             return None, None, dx, None, dw, None
         if ctx.qbwd:

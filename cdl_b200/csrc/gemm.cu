@@ -190,7 +190,35 @@ struct GemmArgs {
     int ldo;
     int c4a, c4b;        // scale atoms per 128-row block (ceil(nb/4))
     uint32_t* status;    // optional: non-zero after a timed-out wait
+    const uint16_t* addend;  // optional bf16 [M, ld_add] added to the product (pair kernel: == out)
+    int64_t ld_add;
 };
+
+// Two bf16 pairs added as torch adds two bf16 tensors: the fp32 sum of the
+// widened values (one rounding), rounded to bf16.
+__device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+    const float lo = __fadd_rn(__uint_as_float(a << 16), __uint_as_float(b << 16));
+    const float hi = __fadd_rn(__uint_as_float(a & 0xffff0000u), __uint_as_float(b & 0xffff0000u));
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+// pk[j] (bf16 pairs of 8 * NV consecutive columns) += the addend's values at
+// src (16-byte aligned), the loads issued together
+template <int NV>
+__device__ __forceinline__ void add_addend(uint32_t* pk, const uint16_t* src) {
+    uint4 t[NV];
+#pragma unroll
+    for (int c = 0; c < NV; ++c) t[c] = reinterpret_cast<const uint4*>(src)[c];
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+        pk[4 * c] = add_bf16x2(pk[4 * c], t[c].x);
+        pk[4 * c + 1] = add_bf16x2(pk[4 * c + 1], t[c].y);
+        pk[4 * c + 2] = add_bf16x2(pk[4 * c + 2], t[c].z);
+        pk[4 * c + 3] = add_bf16x2(pk[4 * c + 3], t[c].w);
+    }
+}
 
 // alpha * alpha_b as one fp32 product (what a torch multiply of the two
 // scalars would give)
@@ -343,6 +371,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     uint16_t* dst = args.out + (size_t)row * args.ldo + n0 + c0;
                     const int ncol = args.n - (n0 + c0);
+                    if (args.addend != nullptr && ncol > 0) {
+                        const uint16_t* src = args.addend + (size_t)row * args.ld_add + n0 + c0;
+                        if (ncol >= 32 && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0)) {
+                            add_addend<4>(packed, src);
+                        } else {
+                            for (int i = 0; i < 32 && i < ncol; ++i) {
+                                const uint32_t sh = 16u * (uint32_t)(i & 1);
+                                const uint32_t sum = add_bf16x2(packed[i >> 1] >> sh, (uint32_t)src[i]) & 0xffffu;
+                                packed[i >> 1] = (packed[i >> 1] & ~(0xffffu << sh)) | (sum << sh);
+                            }
+                        }
+                    }
                     if (ncol >= 32 && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
                         uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
@@ -581,6 +621,14 @@ __device__ __forceinline__ void arrive_remote(uint32_t bar_cluster) {
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int x, int y, const void* src) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(x),
                  "r"(y), "r"(smem_addr(src))
+                 : "memory");
+}
+
+// The same box added to the bf16 values already in global memory (the TMA
+// unit's reduce-add: out = bf16(out + staged)), for the accumulating GEMM.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, int x, int y, const void* src) {
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map),
+                 "r"(x), "r"(y), "r"(smem_addr(src))
                  : "memory");
 }
 
@@ -876,7 +924,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(k2Threads, 1)
                     if (y < args.m) {
                         for (int b = 0; b < 2; ++b) {
                             const int x = n0 + 128 * hf + 64 * b;
-                            if (x < args.n) tma_store_2d(&map_out, x, y, out_s + b * (128 * 128));
+                            if (x >= args.n) continue;
+                            // accumulating GEMM (addend == out): the TMA unit adds the
+                            // bf16 tile to out in L2, no loads in the epilogue
+                            if (args.addend != nullptr) tma_reduce_add_2d(&map_out, x, y, out_s + b * (128 * 128));
+                            else tma_store_2d(&map_out, x, y, out_s + b * (128 * 128));
                         }
                     }
                 }
@@ -947,7 +999,7 @@ bool make_out_map(CUtensorMap* map, void* base, int64_t rows, int64_t cols, int6
 template <int KIND>
 int launch_gemm(const void* a, const void* b, const void* sfa, const void* sfb, const float* alpha,
                 const float* alpha_b, int64_t m, int64_t n, int64_t k, void* out, int64_t ldo, void* status,
-                cudaStream_t st) {
+                cudaStream_t st, bool accumulate = false) {
     using T = KindTraits<KIND>;
     const int64_t kbytes = KIND == kMx8 ? k : k / 2;
     CUtensorMap ma, mb;
@@ -973,8 +1025,12 @@ int launch_gemm(const void* a, const void* b, const void* sfa, const void* sfb, 
     const int64_t nb = (k + T::kVec - 1) / T::kVec;
     args.c4a = args.c4b = (int)((nb + 3) / 4);
     args.status = static_cast<uint32_t*>(status);
+    // accumulate: out is read as the addend of the product (out += product)
+    args.addend = accumulate ? static_cast<const uint16_t*>(out) : nullptr;
+    args.ld_add = ldo;
     // pair kernel: 256 x 256 tiles on SM pairs (its TMA store needs a 16-byte
-    // aligned output with a row pitch that is a multiple of 16 bytes)
+    // aligned output with a row pitch that is a multiple of 16 bytes; an
+    // accumulating launch adds into out with the TMA reduce-add)
     CUtensorMap mo;
     if (n > kBN && ((reinterpret_cast<uintptr_t>(out) & 15u) == 0) && (ldo % 8) == 0 &&
         make_out_map(&mo, out, m, n, ldo)) {
@@ -1043,6 +1099,19 @@ extern "C" int cdlb200_mm_fp4_alpha2(const void* a, const void* b, const void* a
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     return use_nvfp4 ? launch_gemm<kNv>(a, b, a_scale, b_scale, alpha_a, alpha_b, m, n, k, out, ldo, status, st)
                      : launch_gemm<kMx4>(a, b, a_scale, b_scale, alpha_a, alpha_b, m, n, k, out, ldo, status, st);
+}
+
+extern "C" int cdlb200_mm_fp4_alpha2_acc(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                                         const float* alpha_a, const float* alpha_b, int64_t m, int64_t n,
+                                         int64_t k, int block_size, int use_nvfp4, void* out, int64_t ldo,
+                                         void* status, void* stream) {
+    if ((use_nvfp4 && block_size != 16) || (!use_nvfp4 && block_size != 32)) return CDLB200_ERR_INVALID_ARG;
+    int rc = gemm_checks(a, b, a_scale, b_scale, m, n, k, 32, out, ldo);
+    if (rc != CDLB200_OK || m == 0 || n == 0) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return use_nvfp4 ? launch_gemm<kNv>(a, b, a_scale, b_scale, alpha_a, alpha_b, m, n, k, out, ldo, status, st, true)
+                     : launch_gemm<kMx4>(a, b, a_scale, b_scale, alpha_a, alpha_b, m, n, k, out, ldo, status, st,
+                                         true);
 }
 
 extern "C" int cdlb200_mm_mxfp8(const void* a, const void* b, const void* a_scale, const void* b_scale,

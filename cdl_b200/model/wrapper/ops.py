@@ -67,19 +67,31 @@ def mm_fp4_direct(
 
 
 def mm_nvfp4_alpha2(a: torch.Tensor, b: torch.Tensor, a_scale: torch.Tensor, b_scale: torch.Tensor,
-                    alpha_a: torch.Tensor, alpha_b: torch.Tensor) -> torch.Tensor:
+                    alpha_a: torch.Tensor, alpha_b: torch.Tensor,
+                    accumulate_into: torch.Tensor | None = None) -> torch.Tensor:
     """NVFP4 ``mm_fp4_direct`` with the two operands' alphas multiplied in the
-    GEMM epilogue (``cdlb200_mm_fp4_alpha2``) instead of by a separate launch."""
+    GEMM epilogue (``cdlb200_mm_fp4_alpha2``) instead of by a separate launch.
+    With ``accumulate_into`` (a contiguous bf16 [m, n] tensor) the product is
+    added to its values in the epilogue, as ``accumulate_into += product``
+    would round it (``cdlb200_mm_fp4_alpha2_acc``), and that tensor is
+    returned."""
     dev = _lib.require_cuda(a, b, a_scale, b_scale, alpha_a, alpha_b)
     a = a.contiguous().view(torch.uint8)
     brows = _storage_rows(b).view(torch.uint8)
     m, k = a.shape[0], a.shape[1] * 2
     n = brows.shape[0]
-    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    if accumulate_into is not None:
+        out = accumulate_into
+        if (out.dtype != torch.bfloat16 or tuple(out.shape) != (m, n) or not out.is_contiguous()
+                or out.device != dev):
+            raise ValueError("accumulate_into must be a contiguous bf16 [m, n] tensor on the operands' device")
+    else:
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
     if m == 0 or n == 0:
         return out
     _lib.call(
-        "cdlb200_mm_fp4_alpha2", _lib.ptr(a), _lib.ptr(brows), _lib.ptr(_flat(a_scale)), _lib.ptr(_flat(b_scale)),
+        "cdlb200_mm_fp4_alpha2_acc" if accumulate_into is not None else "cdlb200_mm_fp4_alpha2",
+        _lib.ptr(a), _lib.ptr(brows), _lib.ptr(_flat(a_scale)), _lib.ptr(_flat(b_scale)),
         _lib.ptr(alpha_a), _lib.ptr(alpha_b), m, n, k, 16, 1, _lib.ptr(out), n, _lib.ptr(_lib.status_word(dev)),
         _lib.stream(dev),
     )

@@ -235,6 +235,20 @@ int cdlb200_mm_fp4_alpha2(const void* a, const void* b, const void* a_scale, con
                           int block_size, int use_nvfp4, void* out, int64_t ldo, void* status, void* stream);
 
 /*
+ * cdlb200_mm_fp4_alpha2 that adds its product to the bf16 values already in
+ * `out`: out = bf16(bf16(alpha_a * alpha_b * acc) + out), the fp32 sum of the
+ * two bf16 values rounded once, i.e. what a torch add of the product to
+ * `out` gives.  Replaces the sum autograd forms when several of cdl's
+ * quantized linears read one input (q / k / v, gate / up: the input gradient
+ * of each is cdl/core/mm/nvfp4.py:55-61's dgrad, and autograd adds them):
+ * the dgrad GEMMs after the first accumulate into the first one's output
+ * instead of writing their own and a separate add reading both.
+ */
+int cdlb200_mm_fp4_alpha2_acc(const void* a, const void* b, const void* a_scale, const void* b_scale,
+                              const float* alpha_a, const float* alpha_b, int64_t m, int64_t n, int64_t k,
+                              int block_size, int use_nvfp4, void* out, int64_t ldo, void* status, void* stream);
+
+/*
  * Block-scaled MXFP8 GEMM (e4m3 elements, e8m0 scales, blocks of 32):
  * replaces cdl/model/wrapper/flashinfer.py:41-52 `cdl::mm_mxfp8` as called by
  * cdl/core/mm/mxfp8.py:36-51.  a: e4m3 [m, k], b: e4m3 [n, k] (storage of the

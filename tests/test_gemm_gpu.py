@@ -115,3 +115,34 @@ def test_gemm_c3_shapes_vs_oracle(fmt_name, shape):
     bound = 2.0 ** -7 * np.abs(ref) + 1e-4 * row_rms
     bad = np.abs(got - ref) > bound
     assert not bad.any(), (int(bad.sum()), np.argwhere(bad)[:5])
+
+
+@pytest.mark.parametrize("shape", [(256, 512, 256), (200, 384, 320), (1000, 2048, 1024), (520, 576, 192),
+                                   (130, 96, 64), (64, 200, 128), (300, 136, 576)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_gemm_accumulate_matches_torch_add(shape):
+    """``cdlb200_mm_fp4_alpha2_acc`` (the dgrad GEMM that adds into the input
+    gradient another linear already wrote) equals the plain GEMM followed by
+    torch's bf16 add, bit for bit: the pair kernel (N a multiple of 64; 576
+    ends in a half-filled tile), the single-CTA kernel (N <= 128, or N not a
+    multiple of 64) and its ragged-column path (N = 200, 136)."""
+    from cdl_b200.core.kernel import quant
+    from cdl_b200.core.mm.swizzle import swizzle_scale_factors
+    from cdl_b200.model.wrapper.ops import mm_nvfp4_alpha2
+
+    m, n, k = shape
+    a, w = workloads.c3_gemm(m, n, k, seed=5)
+    ap, asf, aal = quant.nvfp4_quant(a.cuda())
+    wp, wsf, wal = quant.nvfp4_quant(w.cuda())
+    args = (ap, wp.T, swizzle_scale_factors(asf), swizzle_scale_factors(wsf).T, aal, wal)
+    prior = torch.randn(m, n, generator=torch.Generator().manual_seed(1)).bfloat16().cuda()
+    prior[0, 0] = 0.0
+    prod = mm_nvfp4_alpha2(*args)
+    want = prior + prod
+    buf = prior.clone()
+    got = mm_nvfp4_alpha2(*args, accumulate_into=buf)
+    assert got.data_ptr() == buf.data_ptr()
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    # a second accumulation adds on top, in the order autograd would add
+    mm_nvfp4_alpha2(*args, accumulate_into=buf)
+    assert torch.equal(buf.view(torch.int16), (want + prod).view(torch.int16))

@@ -159,6 +159,34 @@ def test_graph_step_matches_eager():
     assert worst < 5e-3
 
 
+def test_dgrad_sum_in_gemm_epilogue_is_bit_exact():
+    """The quantized backward adds the input gradients of the linears that
+    share an input (q / k / v, gate / up) in the dgrad GEMMs' epilogue
+    instead of leaving the sums to autograd's adds; the step's losses,
+    gradient norms and parameters are the same bits either way."""
+    from cdl_b200.core.mm import blockscaled
+    from cdl_b200.train import qat
+
+    spec = qat.SPECS["tiny"]
+    dev = torch.device("cuda")
+    batches = [qat.random_tokens(4, 256, spec.vocab, seed=300 + i, device=dev) for i in range(3)]
+    runs = []
+    try:
+        for fuse in (True, False):
+            blockscaled.FUSE_DGRAD_SUM = fuse
+            step = qat.QatStep(spec, dev, backend="nvfp4_qbwd", lr=1e-3, seed=0)
+            n0 = blockscaled.dgrad_accumulates
+            out = [tuple(float(v) for v in step.step(b)) for b in batches]
+            # per layer and step: k and v add into q's dgrad, up into gate's
+            assert blockscaled.dgrad_accumulates - n0 == (3 * spec.layers * len(batches) if fuse else 0)
+            flat = torch.cat([p.detach().reshape(-1).view(torch.int16) for p in step.model.parameters()])
+            runs.append((out, flat))
+    finally:
+        blockscaled.FUSE_DGRAD_SUM = True
+    assert runs[0][0] == runs[1][0]
+    assert torch.equal(runs[0][1], runs[1][1])
+
+
 @pytest.mark.parametrize("activation,weight", [("ste", "nvfp4_ccdl"), ("nvfp4_ccdl", "nvfp4_ccdl"),
                                                ("nvfp4_ecdl", "nvfp4_ecdl")])
 def test_qat_step_with_cdl_quantizers(activation, weight):
