@@ -9,7 +9,8 @@ Workloads (synthetic data everywhere):
   step (forward, backward, clip + AdamW) on 4x2048 uniform random tokens per
   rank, backend ``nvfp4_qbwd`` (NVFP4 forward, dgrad and wgrad GEMMs); one
   CUDA graph per step, for N > 1 data parallel with the NCCL bf16 gradient
-  all-reduces (issued from the backward hooks) captured in the same graph.
+  all-reduces (issued from the backward hooks) captured in the same graph,
+  ``--comm-sms`` (16) SMs left to NCCL during the backward pass.
   Metric: tokens/s over all ranks.  At N=1 the line
   also carries ``components``: the other BASELINE metrics (NVFP4 quantize
   GB/s on C1 and on a larger-than-L2 tensor, MXFP4 / MXFP8 on C2, the

@@ -278,15 +278,33 @@ __global__ void __launch_bounds__(256) colsum_kernel(const float* __restrict__ p
 // thread per (token, head, 8-value vector of the first half) handles that
 // vector and its partner in the second half.
 // ---------------------------------------------------------------------------
+// Index math: 32-bit multiply-shift divisions (FastDiv) when the item count
+// is below 2^31 (FAST), else 64-bit divisions.
+struct RopeDivs {
+    FastDiv halfv, heads, cos_tokens;
+};
+
+template <bool FAST>
 __global__ void __launch_bounds__(256) rope_kernel(const uint4* __restrict__ x, const uint4* __restrict__ cosv,
                                                    const uint4* __restrict__ sinv, int64_t tokens, int heads,
                                                    int halfv, int64_t cos_tokens, int backward,
-                                                   uint4* __restrict__ out, uint32_t* __restrict__ amax) {
+                                                   uint4* __restrict__ out, uint32_t* __restrict__ amax,
+                                                   RopeDivs dv) {
     const int64_t total = tokens * heads * halfv;
     uint32_t am = 0;
     for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
-        const int v = (int)(t % halfv);
-        const int64_t th = t / halfv, tok = (th / heads) % cos_tokens;  // cos/sin repeat every cos_tokens
+        int v;
+        int64_t th, tok;  // (token, head) row and the token's cos/sin row (repeating every cos_tokens)
+        if constexpr (FAST) {
+            const uint32_t t32 = (uint32_t)t, th32 = dv.halfv.div(t32), tk = dv.heads.div(th32);
+            v = (int)(t32 - th32 * dv.halfv.d);
+            th = th32;
+            tok = tk - dv.cos_tokens.div(tk) * dv.cos_tokens.d;
+        } else {
+            v = (int)(t % halfv);
+            th = t / halfv;
+            tok = (th / heads) % cos_tokens;
+        }
         const int64_t base = th * 2 * halfv;
         float a[8], b[8], c1[8], c2[8], s1[8], s2[8], o1[8], o2[8];
         unpack8(x[base + v], a);
@@ -554,9 +572,15 @@ extern "C" int cdlb200_rope(const void* x, const void* cos, const void* sin, int
     if (!al16(x) || !al16(cos) || !al16(sin) || !al16(out)) return CDLB200_ERR_ALIGNMENT;
     const int halfv = (int)(head_dim / 16);
     const int64_t items = tokens * heads * halfv;
-    rope_kernel<<<grid_for(items, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const uint4*>(x), static_cast<const uint4*>(cos), static_cast<const uint4*>(sin), tokens,
-        (int)heads, halfv, cos_tokens, backward, static_cast<uint4*>(out), amax);
+    const RopeDivs dv{FastDiv((uint32_t)halfv), FastDiv((uint32_t)(heads < (1ll << 31) ? heads : 1)),
+                      FastDiv((uint32_t)(cos_tokens < (1ll << 31) ? cos_tokens : 1))};
+    auto launch = [&](auto kern) {
+        kern<<<grid_for(items, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const uint4*>(x), static_cast<const uint4*>(cos), static_cast<const uint4*>(sin), tokens,
+            (int)heads, halfv, cos_tokens, backward, static_cast<uint4*>(out), amax, dv);
+    };
+    if (items < (1ll << 31) && cos_tokens < (1ll << 31)) launch(rope_kernel<true>);
+    else launch(rope_kernel<false>);
     CDLB200_CHECK_LAUNCH();
     return CDLB200_OK;
 }

@@ -487,6 +487,18 @@ class QatStep:
             self.sync.finish()
 
     def _eager_step(self, input_ids) -> tuple[torch.Tensor, torch.Tensor]:
+        if self.device.type != "cuda":
+            return self._step_body(input_ids)
+        # the fused kernels' amax words come from one buffer zeroed once per step
+        from cdl_b200.model.components import fused
+
+        fused.begin_step(self.device)
+        try:
+            return self._step_body(input_ids)
+        finally:
+            fused.end_step()
+
+    def _step_body(self, input_ids) -> tuple[torch.Tensor, torch.Tensor]:
         if isinstance(input_ids, torch.Tensor):
             loss = self.net(input_ids)
             self._backward(loss, 1.0, True)
