@@ -340,16 +340,31 @@ __device__ __forceinline__ float sigmoid_f(float g) { return 1.0f / (1.0f + expf
 
 __global__ void __launch_bounds__(256) swiglu_fwd_kernel(const uint4* __restrict__ g, const uint4* __restrict__ u,
                                                          int64_t nvec, uint4* __restrict__ h, uint32_t* __restrict__ amax) {
+    // two vectors per thread and iteration (t and t + stride), both loaded
+    // before either is computed
     uint32_t am = 0;
-    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < nvec; t += (int64_t)gridDim.x * blockDim.x) {
-        float a[8], b[8];
-        unpack8(g[t], a);
-        unpack8(u[t], b);
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < nvec; t += 2 * stride) {
+        const bool two = t + stride < nvec;
+        uint4 gv[2], uv[2];
+        gv[0] = g[t];
+        uv[0] = u[t];
+        if (two) {
+            gv[1] = g[t + stride];
+            uv[1] = u[t + stride];
+        }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) a[i] = rbf(a[i] * sigmoid_f(a[i])) * b[i];
-        const uint4 o = pack8(a);
-        h[t] = o;
-        am = mag8(am, o);
+        for (int k = 0; k < 2; ++k) {
+            if (k == 1 && !two) break;
+            float a[8], b[8];
+            unpack8(gv[k], a);
+            unpack8(uv[k], b);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) a[i] = rbf(a[i] * sigmoid_f(a[i])) * b[i];
+            const uint4 o = pack8(a);
+            h[t + k * stride] = o;
+            am = mag8(am, o);
+        }
     }
     if (amax) cta_amax(am, amax);
 }
@@ -359,23 +374,38 @@ __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const uint4* __restrict
                                                          uint4* __restrict__ dg, uint4* __restrict__ du,
                                                          uint32_t* __restrict__ amax_g, uint32_t* __restrict__ amax_u) {
     uint32_t ag = 0, au = 0;
-    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < nvec; t += (int64_t)gridDim.x * blockDim.x) {
-        float d[8], a[8], b[8], og[8], ou[8];
-        unpack8(dh[t], d);
-        unpack8(g[t], a);
-        unpack8(u[t], b);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float s = sigmoid_f(a[i]);
-            const float ds = rbf(d[i] * b[i]);
-            ou[i] = d[i] * rbf(a[i] * s);
-            og[i] = ds * (s * (1.0f + a[i] * (1.0f - s)));
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < nvec; t += 2 * stride) {
+        const bool two = t + stride < nvec;
+        uint4 dv[2], gv[2], uv[2];
+        dv[0] = dh[t];
+        gv[0] = g[t];
+        uv[0] = u[t];
+        if (two) {
+            dv[1] = dh[t + stride];
+            gv[1] = g[t + stride];
+            uv[1] = u[t + stride];
         }
-        const uint4 pg = pack8(og), pu = pack8(ou);
-        dg[t] = pg;
-        du[t] = pu;
-        ag = mag8(ag, pg);
-        au = mag8(au, pu);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            if (k == 1 && !two) break;
+            float d[8], a[8], b[8], og[8], ou[8];
+            unpack8(dv[k], d);
+            unpack8(gv[k], a);
+            unpack8(uv[k], b);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float s = sigmoid_f(a[i]);
+                const float ds = rbf(d[i] * b[i]);
+                ou[i] = d[i] * rbf(a[i] * s);
+                og[i] = ds * (s * (1.0f + a[i] * (1.0f - s)));
+            }
+            const uint4 pg = pack8(og), pu = pack8(ou);
+            dg[t + k * stride] = pg;
+            du[t + k * stride] = pu;
+            ag = mag8(ag, pg);
+            au = mag8(au, pu);
+        }
     }
     if (amax_g || amax_u) cta_amax2(ag, amax_g, au, amax_u);
 }
