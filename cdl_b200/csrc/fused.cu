@@ -115,21 +115,39 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const uint4* __restric
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int slot = warp / rsp.W, wr = warp - slot * rsp.W;
     uint32_t am = 0;  // max |y| as bf16 magnitude bits (the NVFP4 global amax of the output)
-    for (int64_t base = (int64_t)blockIdx.x * rsp.R; base < rows; base += (int64_t)gridDim.x * rsp.R) {
+    // the next row's x and residual are loaded while this row is reduced
+    const int64_t step = (int64_t)gridDim.x * rsp.R;
+    uint4 nx[VPL], nres[VPL];
+    auto load_row = [&](int64_t r) {
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) {
+            const int c = 32 * wr + lane + 32 * rsp.W * j;
+            const bool in = r < rows && c < nvec;
+            nx[j] = in ? x[r * nvec + c] : make_uint4(0u, 0u, 0u, 0u);
+            nres[j] = in && res != nullptr ? res[r * nvec + c] : make_uint4(0u, 0u, 0u, 0u);
+        }
+    };
+    load_row((int64_t)blockIdx.x * rsp.R + slot);
+    for (int64_t base = (int64_t)blockIdx.x * rsp.R; base < rows; base += step) {
         const int64_t r = base + slot;
         const bool live = r < rows;
-        uint4 v[VPL];
+        uint4 v[VPL], rv[VPL];
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) {
+            v[j] = nx[j];
+            rv[j] = nres[j];
+        }
+        load_row(base + step + slot);
         float ss = 0.f;
 #pragma unroll
         for (int j = 0; j < VPL; ++j) {
             const int c = 32 * wr + lane + 32 * rsp.W * j;
             const bool in = live && c < nvec;
-            v[j] = in ? x[r * nvec + c] : make_uint4(0u, 0u, 0u, 0u);
             float f[8];
             unpack8(v[j], f);
             if (res != nullptr && in) {
                 float b[8];
-                unpack8(res[r * nvec + c], b);
+                unpack8(rv[j], b);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) f[i] += b[i];
                 v[j] = pack8(f);
