@@ -72,6 +72,7 @@ SIGNATURES: dict[str, tuple] = {
     "cdlb200_swiglu_fwd": (_I, [_P, _P, _I64, _P, _P, _P]),
     "cdlb200_swiglu_bwd": (_I, [_P, _P, _P, _I64, _P, _P, _P, _P, _P]),
     "cdlb200_cross_entropy": (_I, [_P, _P, _I64, _I64, _F, _P, _P]),
+    "cdlb200_scale_bf16": (_I, [_P, _I64, _P, _P]),
     "cdlb200_ecdl_fwd": (_I, [_P, _I, _I64, _I64, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P]),
     "cdlb200_ecdl_bwd_workspace_bytes": (_I64, [_I64, _I64, _I]),
     "cdlb200_ecdl_bwd": (_I, [_P, _P, _I, _I64, _I64, _I, _P, _P, _P, _I, _P, _P, _P, _I64, _P]),

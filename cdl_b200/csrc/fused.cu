@@ -510,8 +510,37 @@ int grid_for(int64_t items, int per_block) {
     return (int)(g < 1 ? 1 : (g < cap ? g : cap));
 }
 
+// x *= s in place, as torch multiplies a bf16 tensor by a bf16 scalar (the
+// fp32 product rounded to bf16); s is read on the device, and a launch whose
+// s is 1 leaves x as it is without touching it (x * 1 == x for every value
+// but a NaN's payload), so the multiply costs nothing in the common case.
+__global__ void __launch_bounds__(256) scale_bf16_kernel(uint4* __restrict__ x, int64_t nvec,
+                                                         const uint16_t* __restrict__ s) {
+    const uint32_t sb = *s;
+    if (sb == 0x3f80u) return;
+    const float sc = __uint_as_float(sb << 16);
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < nvec; t += (int64_t)gridDim.x * blockDim.x) {
+        float f[8];
+        unpack8(x[t], f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] *= sc;
+        x[t] = pack8(f);
+    }
+}
 }  // namespace
 }  // namespace cdlb200
+
+extern "C" int cdlb200_scale_bf16(void* x, int64_t n, const void* scale, void* stream) {
+    using namespace cdlb200;
+    if (n < 0 || (n % 8) != 0) return CDLB200_ERR_INVALID_ARG;
+    if (n == 0) return CDLB200_OK;
+    if (!x || !scale) return CDLB200_ERR_INVALID_ARG;
+    if (!al16(x) || (reinterpret_cast<uintptr_t>(scale) & 1u) != 0) return CDLB200_ERR_ALIGNMENT;
+    scale_bf16_kernel<<<grid_for(n / 8, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<uint4*>(x), n / 8, static_cast<const uint16_t*>(scale));
+    CDLB200_CHECK_LAUNCH();
+    return CDLB200_OK;
+}
 
 using namespace cdlb200;
 

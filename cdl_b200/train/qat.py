@@ -284,6 +284,15 @@ class LinearCrossEntropy(torch.autograd.Function):
     def backward(ctx, grad_loss: torch.Tensor):
         grad_h, grad_w = ctx.saved_tensors
         gl = grad_loss.to(grad_h.dtype if grad_h is not None else grad_w.dtype)
+        grads = [g for g in (grad_h, grad_w) if g is not None]
+        if all(g.is_cuda and g.dtype == torch.bfloat16 and g.is_contiguous() and g.numel() % 8 == 0 for g in grads):
+            # scaled in place by the value read on the device (no work when it
+            # is 1: the loss's own backward); the stored gradients are used
+            # once, this backward being the only reader
+            gl = gl.reshape(1).contiguous()
+            for g in grads:
+                _lib.call("cdlb200_scale_bf16", _lib.ptr(g), g.numel(), _lib.ptr(gl), _lib.stream(g.device))
+            return grad_h, grad_w, None, None
         return (grad_h * gl if grad_h is not None else None, grad_w * gl if grad_w is not None else None, None, None)
 
 

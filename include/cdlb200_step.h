@@ -85,6 +85,16 @@ int cdlb200_swiglu_bwd(const void* dh, const void* g, const void* u, int64_t n, 
 int cdlb200_cross_entropy(void* logits, const int64_t* targets, int64_t rows, int64_t vocab, float scale,
                           float* loss, void* stream);
 
+/* x[0..n) *= *scale in place: bf16 x (16-byte aligned, n % 8 == 0) times a
+ * bf16 scalar held in device memory, each product rounded to bf16 as torch
+ * multiplies two bf16 tensors.  The backward of the fused linear cross
+ * entropy above (Liger's, as cdl smollm2.py:667-677 uses it) multiplies the
+ * gradients it stored in the forward by grad_output; this does it in place,
+ * reading the scale on the device, and leaves x untouched when the scale is
+ * 1 (the loss's own backward), which gives the same bits for every value but
+ * a NaN's payload. */
+int cdlb200_scale_bf16(void* x, int64_t n, const void* scale, void* stream);
+
 /* One parameter tensor of the optimizer below: param, its gradient and the
  * two AdamW moments, all bf16, contiguous, 16-byte aligned, numel % 8 == 0. */
 typedef struct {

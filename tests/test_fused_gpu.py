@@ -166,6 +166,43 @@ def test_linear_cross_entropy_matches_plain_loss():
     assert _rel(w.grad, w2.grad) < 1e-2
 
 
+@pytest.mark.parametrize("scale", [1.0, 0.5, 0.3, -2.0])
+def test_scale_kernel_matches_torch_multiply(scale):
+    """``cdlb200_scale_bf16`` (the in-place grad_output scaling of the fused
+    linear cross entropy's backward) gives torch's bf16 product bit for bit;
+    with a scale of 1 it leaves x as it is."""
+    from cdl_b200 import _lib
+
+    g = torch.Generator().manual_seed(4)
+    x = (torch.randn(1000, 264, generator=g) * 3).bfloat16()
+    x[0, :4] = torch.tensor([0.0, -0.0, float("inf"), 1e-40])
+    x = x.cuda()
+    s = torch.tensor([scale], dtype=torch.bfloat16, device="cuda")
+    want = x * s
+    got = x.clone()
+    _lib.call("cdlb200_scale_bf16", _lib.ptr(got), got.numel(), _lib.ptr(s), _lib.stream(got.device))
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+
+
+def test_linear_cross_entropy_backward_scales_by_grad_output():
+    """The chunked loss's gradients under ``(loss * c).backward()`` are c times
+    those of ``loss.backward()`` (c a power of two: exact in bf16)."""
+    from cdl_b200.train import qat
+
+    g = torch.Generator().manual_seed(5)
+    h0 = (torch.randn(512, 256, generator=g) * 0.5).bfloat16().cuda()
+    w0 = (torch.randn(1024, 256, generator=g) * 0.05).bfloat16().cuda()
+    t = torch.randint(0, 1024, (512,), generator=g).cuda()
+    grads = []
+    for c in (1.0, 0.25):
+        h, w = h0.clone().requires_grad_(True), w0.clone().requires_grad_(True)
+        (qat.LinearCrossEntropy.apply(h, w, t, 256) * c).backward()
+        grads.append((h.grad, w.grad))
+    for a, b in zip(grads[0], grads[1]):
+        assert torch.equal((a * 0.25).view(torch.int16), b.view(torch.int16))
+
+
 def test_epilogue_amax_feeds_single_pass_encode():
     """RMSNorm and SwiGLU outputs carry their global amax; the NVFP4 encode of
     such an activation (one pass, with the dequantized copy) equals the
