@@ -182,3 +182,48 @@ def test_run_training_loop_checkpoints_and_resumes(tmp_path):
     # 8 batches = 4 steps per epoch: the resumed run ends its first epoch at step 4
     assert qat.run_training(st2, train, grad_accum_steps=2, start_step=start, max_steps=10) == 4
     assert qat.run_training(st2, train, epochs=2, grad_accum_steps=2, start_step=4, max_steps=6) == 6
+
+
+def test_amax_arena_hands_out_zeroed_words_within_a_step():
+    """The fused kernels' amax words: inside a step, consecutive slices of one
+    buffer zeroed when the step begins; outside a step, or once the buffer is
+    used up, fresh zero-filled tensors."""
+    from cdl_b200 import _lib
+    from cdl_b200.model.components import fused
+
+    dev = torch.device("cpu")
+    outside = fused.new_amax(dev)
+    assert outside.shape == (_lib.AMAX_WORDS,) and not outside.any()
+    fused.begin_step(dev)
+    try:
+        a, b = fused.new_amax(dev), fused.new_amax(dev, 2)
+        assert a.shape == (_lib.AMAX_WORDS,) and b.shape == (2, _lib.AMAX_WORDS)
+        assert a.data_ptr() != b.data_ptr() and not a.any() and not b.any()
+        a.fill_(7)  # a kernel writes its word
+        assert not b.any()
+        rest = fused._ARENA.SLOTS - fused._ARENA.used
+        fused.new_amax(dev, rest)  # the last slots
+        spill = fused.new_amax(dev)  # beyond the buffer: a fresh tensor
+        assert not spill.any() and spill.data_ptr() != a.data_ptr()
+    finally:
+        fused.end_step()
+    fused.begin_step(dev)  # the next step zeroes the words again
+    try:
+        assert not fused.new_amax(dev).any()
+    finally:
+        fused.end_step()
+    assert not fused._ARENA.active
+
+
+def test_dgrad_sum_bookkeeping():
+    """Linears that read one encoded input join one sum: the users are
+    counted in the forward; a new sum starts once a backward has begun."""
+    from cdl_b200.core.mm import blockscaled
+
+    codes = torch.zeros(4, dtype=torch.uint8)
+    s1 = blockscaled._join_dgrad_sum(codes)
+    s2 = blockscaled._join_dgrad_sum(codes)
+    assert s1 is s2 and s1.users == 2 and s1.done == 0
+    s1.done = 1  # the backward of one of them ran
+    s3 = blockscaled._join_dgrad_sum(codes)
+    assert s3 is not s1 and s3.users == 1
