@@ -25,7 +25,8 @@
 // kind::mxf4 block32 with ue8m0; MXFP8 = kind::mxf8f6f4 (e4m3) with ue8m0.
 // Every mbarrier wait is bounded; a timed-out wait sets a status word and
 // the CTA stops issuing work, waits (bounded) for the MMAs it issued, frees
-// TMEM and exits.  No multicast is used anywhere.
+// TMEM and exits.  No TMA load uses multicast (the pair kernel's only
+// multicast is the tcgen05.commit that signals both CTAs).
 #include <cuda.h>
 
 #include "common.cuh"
