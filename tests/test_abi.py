@@ -56,6 +56,17 @@ def test_host_side_argument_errors_need_no_gpu():
     assert lib.cdlb200_mxfp4_quant(None, 0, 16, 16, 0, None, None, 0, None) == _lib.OK
     # ld < k is invalid
     dummy = ctypes.c_void_p(16)
+    # the in-place bf16 scale: n must be a multiple of 8, x 16-byte aligned
+    assert lib.cdlb200_scale_bf16(dummy, 12, dummy, None) == _lib.ERR_INVALID_ARG
+    assert lib.cdlb200_scale_bf16(ctypes.c_void_p(18), 16, dummy, None) == _lib.ERR_ALIGNMENT
+    assert lib.cdlb200_scale_bf16(None, 0, None, None) == _lib.OK
+    # the accumulating GEMM takes the plain GEMM's checks: block size, k % 32, ldo >= n
+    assert lib.cdlb200_mm_fp4_alpha2_acc(dummy, dummy, dummy, dummy, None, None, 64, 64, 64, 32, 1, dummy, 64,
+                                         None, None) == _lib.ERR_INVALID_ARG
+    assert lib.cdlb200_mm_fp4_alpha2_acc(dummy, dummy, dummy, dummy, None, None, 64, 64, 48, 16, 1, dummy, 64,
+                                         None, None) == _lib.ERR_INVALID_ARG
+    assert lib.cdlb200_mm_fp4_alpha2_acc(dummy, dummy, dummy, dummy, None, None, 64, 64, 64, 16, 1, dummy, 32,
+                                         None, None) == _lib.ERR_INVALID_ARG
     assert lib.cdlb200_mxfp4_quant(dummy, 4, 64, 32, 0, dummy, dummy, 0, None) == _lib.ERR_INVALID_ARG
     # NVFP4 needs a workspace of the stated size
     assert lib.cdlb200_nvfp4_quant(dummy, 4, 64, 64, 0, dummy, dummy, 0, None, dummy, dummy, 8, None) in (
